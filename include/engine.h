@@ -1,0 +1,90 @@
+// engine.h — the inference engine of the reference's include/engine.h:1-66:
+// owns weights, KV cache and the architecture; all buffers are allocated in
+// initialize() (zero-allocation decode loop).  forward_token() is one CUDA
+// graph replay (embedding, 22 layers, final norm, LM head and argmax fused
+// into 111 kernels) plus a 4-byte device-to-host copy of the next token.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "architecture.h"
+#include "config.h"
+#include "cublas_wrapper.h"
+#include "kv_cache.h"
+#include "tokenizer.h"
+#include "weights.h"
+
+struct GenerationConfig {
+    int max_new_tokens = 64;
+    float temperature = 0.0f;
+    int top_k = 1;
+    bool stream_stdout = true;
+};
+
+struct GenerationStats {
+    int prompt_tokens = 0;
+    int generated_tokens = 0;
+    double prefill_ms = 0.0;
+    double decode_ms = 0.0;
+    double total_ms = 0.0;
+    double tokens_per_second = 0.0;
+};
+
+class InferenceEngine {
+public:
+    InferenceEngine();
+    ~InferenceEngine();
+
+    // Model directory loading (INFT v1 files) is outside the decode path and
+    // not provided: these throw std::runtime_error.  Use initialize().
+    void load_model(const std::string& model_dir);
+    void load_model(const ModelConfig& config, const std::string& weights_path,
+                    const std::string& tokenizer_path);
+
+    void initialize(const ModelConfig& config, ModelWeights weights, Tokenizer tokenizer);
+
+    std::string generate(const std::string& prompt, const GenerationConfig& gen_config = GenerationConfig(),
+                         GenerationStats* stats = nullptr);
+    // The same loop over token IDs (no tokenizer); returns the generated IDs.
+    std::vector<int> generate_tokens(const std::vector<int>& prompt_tokens,
+                                     const GenerationConfig& gen_config = GenerationConfig(),
+                                     GenerationStats* stats = nullptr);
+
+    // One decode step at `position`: returns the greedy next token.
+    int forward_token(int token_id, int position);
+    // temperature <= 0: the greedy token of the last step (computed by the
+    // fused argmax; no second kernel).  Otherwise the reference's host
+    // sampler (src/engine.cpp:78-104): softmax at the temperature over the
+    // logits and a draw from a static mt19937(1337).
+    int sample_next_token(float temperature = 0.0f);
+
+    // `steps` greedy steps chained on the device from (token_id, position);
+    // writes the produced tokens to tokens_out and returns the device time in ms.
+    float decode_chain(int token_id, int position, int steps, std::vector<int>* tokens_out);
+    // Zero the KV cache.
+    void reset();
+
+    const ModelConfig& config() const;
+    const Tokenizer& tokenizer() const;
+    bool is_loaded() const;
+
+    ModelWeights& weights();
+    KVCache& kv_cache();
+    const Tensor& logits() const;
+    LlamaArchitecture& architecture();
+
+private:
+    ModelConfig config_;
+    ModelWeights weights_;
+    Tokenizer tokenizer_;
+    std::unique_ptr<CublasWrapper> cublas_;
+    std::unique_ptr<LlamaArchitecture> architecture_;
+    KVCache kv_cache_;
+
+    Tensor logits_;
+    Tensor tokens_dev_;
+    int last_token_;
+    bool is_loaded_;
+};

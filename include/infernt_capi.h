@@ -1,0 +1,246 @@
+/*
+ * infernt_capi.h — the C ABI of the B200 decode engine.
+ *
+ * Every entry point takes plain pointers and sizes, an explicit CUDA stream
+ * (`void*` holding a cudaStream_t; NULL = the legacy default stream, the
+ * stream every reference launch uses) and returns an int status (0 = OK).
+ * Nothing here calls exit().  Kernel launches are asynchronous: a 0 status
+ * means the launch was accepted; device-side faults detected by the kernels
+ * themselves (wait timeouts, out-of-range positions or token ids) are
+ * reported by the synchronising calls (infernt_plan_read_token and the
+ * engine calls) as INFERNT_ERR_DEVICE.
+ *
+ * Each function names the reference interface it replaces (paths relative
+ * to the INFERNT repository).  All device pointers must come from
+ * cudaMalloc (256-byte aligned) or be offsets into such memory that keep
+ * the alignment each function states.
+ */
+#ifndef INFERNT_CAPI_H
+#define INFERNT_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define INFERNT_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------- status --- */
+enum {
+    INFERNT_OK = 0,
+    INFERNT_ERR_INVALID_ARGUMENT = 1, /* shape, pointer or range check failed */
+    INFERNT_ERR_UNSUPPORTED = 2,      /* valid but not implemented on this path */
+    INFERNT_ERR_CUDA = 3,             /* a CUDA runtime call failed */
+    INFERNT_ERR_OUT_OF_MEMORY = 4,
+    INFERNT_ERR_DEVICE = 5,           /* a kernel reported an error word */
+    INFERNT_ERR_NO_DEVICE = 6         /* no sm_100 device is visible */
+};
+
+INFERNT_API const char* infernt_status_string(int status);
+/* Detail of the last failing call on this host thread ("" if none). */
+INFERNT_API const char* infernt_last_error(void);
+INFERNT_API int infernt_version(void);
+
+/* ---------------------------------------- include/kernels.h mirrors ---
+ * Same argument meaning as the reference's launch_* functions.          */
+
+/* kernels.h:5-7 (cuda/rmsnorm.cu:29-35): out[b] = in[b] * rsqrt(mean(in[b]^2) + eps) * w */
+INFERNT_API int infernt_rmsnorm(float* out, const float* in, const float* weight, int batch,
+                                int hidden, float eps, void* stream);
+/* kernels.h:9-10 (cuda/residual.cu:12-17): out = a + b (out may alias a or b) */
+INFERNT_API int infernt_residual_add(float* out, const float* a, const float* b, int n,
+                                     void* stream);
+/* kernels.h:12-15 (cuda/rope.cu:37-46): split-half RoPE of q [Nq, D] and k [Nkv, D] in place */
+INFERNT_API int infernt_rope(float* q, float* k, int batch, int num_q_heads, int num_kv_heads,
+                             int head_dim, int position, float theta, void* stream);
+/* kernels.h:17-19 (cuda/softmax.cu:101-106): row softmax of [rows, seq_len], in place allowed */
+INFERNT_API int infernt_softmax(float* out, const float* in, int rows, int seq_len, void* stream);
+/* kernels.h:21-23 (cuda/softmax.cu:108-115): softmax of the first seq_len entries of rows of
+ * total_seq_len, tail zeroed */
+INFERNT_API int infernt_softmax_with_mask(float* out, const float* in, int num_heads,
+                                          int seq_len, int total_seq_len, void* stream);
+/* kernels.h:25-29 (cuda/kv_cache.cu:16-26): cache[h][position][:] = new[h][:] for K and V */
+INFERNT_API int infernt_kv_cache_append(float* k_cache, float* v_cache, const float* k_new,
+                                        const float* v_new, int num_kv_heads, int head_dim,
+                                        int max_seq_len, int position, void* stream);
+/* kernels.h:31-34 (cuda/attention.cu:45-53): scores[qh][p] = scale * q[qh].K[kvh][p],
+ * kvh = qh / (Nq/Nkv), row stride seq_len; every position is computed (no 1024 cap) */
+INFERNT_API int infernt_attention_scores(float* scores, const float* q, const float* k_cache,
+                                         int num_q_heads, int num_kv_heads, int head_dim,
+                                         int seq_len, int max_seq_len, float scale,
+                                         void* stream);
+/* kernels.h:36-39 (cuda/attention.cu:55-64): out[qh][d] = sum_p P[qh][p] V[kvh][p][d] */
+INFERNT_API int infernt_attention_values(float* out, const float* scores, const float* v_cache,
+                                         int num_q_heads, int num_kv_heads, int head_dim,
+                                         int seq_len, int max_seq_len, void* stream);
+/* kernels.h:41-42 (cuda/activation.cu:13-17): out = g / (1 + exp(-g)) * u */
+INFERNT_API int infernt_silu_mul(float* out, const float* gate, const float* up, int n,
+                                 void* stream);
+/* kernels.h:44-46 (cuda/embedding.cu:10-14): out = table[token_id] (row of hidden) */
+INFERNT_API int infernt_embedding_lookup(float* out, const float* table, int token_id,
+                                         int hidden, void* stream);
+/* kernels.h:48-49 (cuda/sampling.cu:38-40): *out_token = argmax(logits), one pass over all
+ * SMs whose last block reduces the per-block winners.  Ties -> lowest index; NaN never wins;
+ * all values <= -1e30 -> 0.  Uses a small per-device workspace allocated on the first call
+ * on each device (make that first call outside stream capture). */
+INFERNT_API int infernt_argmax(int* out_token, const float* logits, int vocab_size,
+                               void* stream);
+
+/* -------------------------------- include/cublas_wrapper.h:23-26 mirror ---
+ * Row-major C[M,N] = alpha * op(A)[M,K] . op(B)[K,N] + beta * C with
+ * lda = trans_a ? M : K, ldb = trans_b ? K : N, ldc = N
+ * (gemm/cublas_wrapper.cu:21-40).  FP32 arithmetic (no TF32).             */
+INFERNT_API int infernt_gemm_f32(const float* A, const float* B, float* C, int M, int N, int K,
+                                 float alpha, float beta, int trans_a, int trans_b,
+                                 void* stream);
+
+/* --------------------------------------------------- fused decode ops ---
+ * Building blocks of the decode step, each one kernel.  `weight_dtype`:
+ * INFERNT_DTYPE_F32 (float weights) or INFERNT_DTYPE_BF16 (bf16 weights,
+ * fp32 accumulation).  Weights are row-major [out, in] (the HF layout the
+ * reference multiplies with trans_b = true, llama_layer.cpp:18-69).
+ * The fast path (TMA-staged weight streaming) needs `in` % 512 == 0 and
+ * 16-byte aligned rows; other shapes run a plain-load kernel.             */
+enum { INFERNT_DTYPE_F32 = 0, INFERNT_DTYPE_BF16 = 1 };
+
+/* y[n] = sum_k W[n][k] * xn[k] with xn = rmsnorm(x, norm_w, eps) when norm_w != NULL
+ * (llama_layer.cpp:11-23 with the rmsnorm fused).  Rows of W0, W1, W2 (any of W1/W2 NULL)
+ * are stacked: y = [W0 x ; W1 x ; W2 x] (the Q, K, V projections in one pass). */
+INFERNT_API int infernt_rmsnorm_gemv(float* y, const void* W0, int n0, const void* W1, int n1,
+                                     const void* W2, int n2, int in_features, int weight_dtype,
+                                     const float* x, const float* norm_w, float eps,
+                                     void* stream);
+/* out[n] = res[n] + sum_k W[n][k] x[k] (llama_layer.cpp:51-55 and :68-72; out may alias res) */
+INFERNT_API int infernt_gemv_residual(float* out, const float* res, const void* W, int n,
+                                      int in_features, int weight_dtype, const float* x,
+                                      void* stream);
+/* out[i] = silu(gate_i) * up_i with gate = Wg xn, up = Wu xn, xn = rmsnorm(x, norm_w)
+ * (llama_layer.cpp:57-66) */
+INFERNT_API int infernt_rmsnorm_gate_up_silu(float* out, const void* Wg, const void* Wu, int n,
+                                             int in_features, int weight_dtype, const float* x,
+                                             const float* norm_w, float eps, void* stream);
+/* RoPE of q and k at `position`, KV append, and split-KV GQA attention with online softmax
+ * over positions [0, position] (llama_layer.cpp:25-48; cuda/rope.cu, kv_cache.cu,
+ * attention.cu, softmax.cu).  qkv = [q (Nq*D) | k (Nkv*D) | v (Nkv*D)] before RoPE; out =
+ * attention output [Nq*D].  workspace: infernt_attention_workspace_bytes() bytes, zeroed
+ * once before first use (the kernel leaves its counters at zero). */
+INFERNT_API size_t infernt_attention_workspace_bytes(int num_q_heads, int num_kv_heads,
+                                                     int head_dim, int splits);
+INFERNT_API int infernt_attention_decode(float* out, const float* qkv, float* k_cache,
+                                         float* v_cache, int num_q_heads, int num_kv_heads,
+                                         int head_dim, int max_seq_len, int position,
+                                         float theta, int splits, void* workspace,
+                                         void* stream);
+/* logits = W rmsnorm(x, norm_w); *out_token = argmax(logits) (llama_model.cpp:58-64 +
+ * cuda/sampling.cu).  workspace: infernt_lm_head_workspace_bytes() bytes, zeroed once. */
+INFERNT_API size_t infernt_lm_head_workspace_bytes(void);
+INFERNT_API int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, const void* W,
+                                               int vocab_size, int in_features,
+                                               int weight_dtype, const float* x,
+                                               const float* norm_w, float eps,
+                                               void* workspace, void* stream);
+
+/* ------------------------------------------------- the decode plan ---
+ * One decoder of a LLaMA-family model over caller-owned weights and KV
+ * cache (the state LlamaArchitecture::forward works on,
+ * architectures/llama/llama_model.cpp:45-65).  The plan owns its scratch
+ * activations (allocated once at creation: the zero-allocation decode
+ * loop) and, when use_graph != 0, CUDA graphs of the whole step.        */
+typedef struct {
+    int vocab_size;
+    int hidden_size;
+    int num_layers;
+    int num_attention_heads;
+    int num_key_value_heads;
+    int intermediate_size;
+    int max_seq_len;
+    int head_dim;
+    float rms_norm_eps;
+    float rope_theta;
+    int weight_dtype; /* INFERNT_DTYPE_F32 or INFERNT_DTYPE_BF16 */
+} infernt_llama_config;
+
+typedef struct infernt_plan infernt_plan;
+
+/* weights: 3 + 9*num_layers device pointers in the order
+ *   embedding [V,h], final_norm [h], lm_head [V,h], then per layer
+ *   attn_norm [h], q [Nq*D,h], k [Nkv*D,h], v [Nkv*D,h], o [h,Nq*D], ffn_norm [h],
+ *   gate [I,h], up [I,h], down [h,I]
+ * (include/weights.h:8-25).  Norm weights and the embedding are always float; the seven
+ * projection matrices and lm_head have weight_dtype.  k_cache / v_cache: num_layers device
+ * pointers to float [Nkv, max_seq_len, D] (include/kv_cache.h:7-15). */
+INFERNT_API int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights,
+                                    float* const* k_cache, float* const* v_cache, int use_graph,
+                                    infernt_plan** out);
+INFERNT_API int infernt_plan_destroy(infernt_plan* plan);
+/* ModelArchitecture::forward (include/architecture.h:15-19): input_embedding [h] at
+ * `position`; writes logits [V] (NULL: the plan's own buffer) and the greedy token
+ * (read it with infernt_plan_read_token). */
+INFERNT_API int infernt_plan_forward(infernt_plan* plan, const float* input_embedding,
+                                     int position, float* logits, void* stream);
+/* InferenceEngine::forward_token's device work (src/engine.cpp:53-66): embedding of
+ * `token` + forward + argmax, asynchronously. */
+INFERNT_API int infernt_plan_decode(infernt_plan* plan, int token, int position, float* logits,
+                                    void* stream);
+/* `steps` decode steps chained on the device: step s consumes the token step s-1
+ * produced, starting from (token, position).  tokens_dev (device int[steps], may be NULL)
+ * receives each produced token.  No host round trip between steps. */
+INFERNT_API int infernt_plan_decode_chain(infernt_plan* plan, int token, int position,
+                                          int steps, int* tokens_dev, void* stream);
+/* Synchronises `stream`, checks the kernels' error word, copies the last greedy token. */
+INFERNT_API int infernt_plan_read_token(infernt_plan* plan, int* token_host, void* stream);
+/* Device pointer of the plan's logits buffer [V]. */
+INFERNT_API float* infernt_plan_logits(infernt_plan* plan);
+/* Number of kernels one decode step launches (for launch accounting). */
+INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
+
+/* ------------------------------------------------ synthetic weights ---
+ * Fill device memory with the seeded values of include/infernt_seed.h
+ * (bit-identical to the host generator).  dtype selects float or bf16
+ * output; bf16 values are the float values rounded to nearest even.     */
+INFERNT_API int infernt_fill_normal(void* dst, size_t n, int dtype, uint64_t seed,
+                                    uint64_t stream_id, float std_dev, void* stream);
+INFERNT_API int infernt_fill_const(float* dst, size_t n, float value, void* stream);
+/* KV prefill: rows [0, n_pos) of every layer's K and V cache get N(0, std) from the
+ * KV streams (element (l, h, p, d) = index ((l*Nkv + h) * 2^20 + p) * D + d). */
+INFERNT_API int infernt_fill_kv(float* const* k_cache, float* const* v_cache, int num_layers,
+                                int num_kv_heads, int max_seq_len, int head_dim, int n_pos,
+                                uint64_t seed, float std_dev, void* stream);
+
+/* --------------------------------------------------- the engine ---
+ * C entry points over the C++ InferenceEngine (include/engine.h), for
+ * hosts that cannot call C++ (ctypes, cgo, JNI).  The engine owns seeded
+ * synthetic weights (weights ~ N(0, std), norms 1.0).                  */
+typedef struct infernt_engine infernt_engine;
+INFERNT_API int infernt_engine_create_seeded(const infernt_llama_config* cfg, uint64_t seed,
+                                             float std_dev, infernt_engine** out);
+INFERNT_API int infernt_engine_destroy(infernt_engine* e);
+/* KVCache::reset (src/kv_cache.cpp:22-30). */
+INFERNT_API int infernt_engine_reset(infernt_engine* e);
+/* InferenceEngine::forward_token (src/engine.cpp:53-66): returns the greedy next token in
+ * *next_token (host). */
+INFERNT_API int infernt_engine_forward_token(infernt_engine* e, int token, int position,
+                                             int* next_token);
+/* InferenceEngine::sample_next_token (src/engine.cpp:68-105). */
+INFERNT_API int infernt_engine_sample_next_token(infernt_engine* e, float temperature,
+                                                 int* token);
+/* Copies the last step's logits [V] to host memory. */
+INFERNT_API int infernt_engine_logits(infernt_engine* e, float* logits_host);
+/* Prefill of KV rows [0, n_pos) with seeded values (benchmark set-up). */
+INFERNT_API int infernt_engine_fill_kv(infernt_engine* e, uint64_t seed, int n_pos,
+                                       float std_dev);
+/* Device-chained decode loop (as infernt_plan_decode_chain) on the engine's stream; writes
+ * `steps` tokens to tokens_host and the device time of the loop (CUDA events) to *ms. */
+INFERNT_API int infernt_engine_decode_chain(infernt_engine* e, int token, int position,
+                                            int steps, int* tokens_host, float* ms);
+/* Device pointers of the engine's weights (3 + 9L, order of infernt_plan_create) and
+ * KV cache (L each), for tests that drive the per-op entry points. */
+INFERNT_API int infernt_engine_weight_ptrs(infernt_engine* e, const void** ptrs, int n);
+INFERNT_API int infernt_engine_kv_ptrs(infernt_engine* e, float** k, float** v, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INFERNT_CAPI_H */

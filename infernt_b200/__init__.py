@@ -1,0 +1,254 @@
+"""infernt_b200 — B200-native decode step of INFERNT behind a C ABI.
+
+The product is the shared library ``infernt_b200/lib/libinfernt_b200.so``
+(CUDA kernels for sm_100a, the C ABI of ``include/infernt_capi.h`` and the
+C++ drop-in classes of ``include/*.h``).  This module binds it with ctypes
+for Python callers (tests, the benchmark).  Importing never falls back to
+anything: if the library is missing, ``lib()`` raises.
+
+Configurations follow the reference's ``ModelConfig`` (include/config.h).
+"""
+import ctypes
+import os
+from dataclasses import dataclass, replace
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libinfernt_b200.so")
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "CUDA error",
+          4: "out of device memory", 5: "device-side error", 6: "no usable CUDA device"}
+
+
+class InferntError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, status, what, detail):
+        super().__init__("%s: %s (%s)" % (what, STATUS.get(status, status), detail))
+        self.status = status
+
+
+class LlamaConfig(ctypes.Structure):
+    """``infernt_llama_config`` (include/infernt_capi.h)."""
+    _fields_ = [("vocab_size", ctypes.c_int), ("hidden_size", ctypes.c_int),
+                ("num_layers", ctypes.c_int), ("num_attention_heads", ctypes.c_int),
+                ("num_key_value_heads", ctypes.c_int), ("intermediate_size", ctypes.c_int),
+                ("max_seq_len", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float),
+                ("weight_dtype", ctypes.c_int)]
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Hyper-parameters of a LLaMA-family decoder (reference include/config.h:22-46)."""
+    vocab_size: int
+    hidden_size: int
+    num_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    intermediate_size: int
+    max_seq_len: int
+    head_dim: int = 0
+    rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    weight_dtype: int = DTYPE_F32
+
+    def __post_init__(self):
+        if self.head_dim == 0:
+            object.__setattr__(self, "head_dim", self.hidden_size // self.num_attention_heads)
+
+    def c(self):
+        return LlamaConfig(self.vocab_size, self.hidden_size, self.num_layers,
+                           self.num_attention_heads, self.num_key_value_heads,
+                           self.intermediate_size, self.max_seq_len, self.head_dim,
+                           self.rms_norm_eps, self.rope_theta, self.weight_dtype)
+
+    def ints(self):
+        return [self.vocab_size, self.hidden_size, self.num_layers, self.num_attention_heads,
+                self.num_key_value_heads, self.intermediate_size, self.max_seq_len, self.head_dim]
+
+    def with_(self, **kw):
+        return replace(self, **kw)
+
+    @property
+    def weight_params(self):
+        """Parameters streamed per decode step (all weights except the embedding table)."""
+        H, I, L, V = self.hidden_size, self.intermediate_size, self.num_layers, self.vocab_size
+        qs = self.num_attention_heads * self.head_dim
+        kvs = self.num_key_value_heads * self.head_dim
+        per_layer = H * (qs + 2 * kvs) + qs * H + 3 * H * I
+        return L * per_layer + V * H
+
+
+# TinyLlama-1.1B shape (FP32 batch-1 greedy decode workload)
+TINYLLAMA = ModelConfig(vocab_size=32000, hidden_size=2048, num_layers=22, num_attention_heads=32,
+                        num_key_value_heads=4, intermediate_size=5632, max_seq_len=2048,
+                        rms_norm_eps=1e-5, rope_theta=10000.0)
+# Llama-3-8B shape (bf16 decode workload)
+LLAMA3_8B = ModelConfig(vocab_size=128256, hidden_size=4096, num_layers=32, num_attention_heads=32,
+                        num_key_value_heads=8, intermediate_size=14336, max_seq_len=8192,
+                        rms_norm_eps=1e-5, rope_theta=500000.0, weight_dtype=DTYPE_BF16)
+
+_lib = None
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+_S = ctypes.c_size_t
+_U64 = ctypes.c_uint64
+
+_SIGS = {
+    "infernt_status_string": (ctypes.c_char_p, [_I]),
+    "infernt_last_error": (ctypes.c_char_p, []),
+    "infernt_version": (_I, []),
+    "infernt_rmsnorm": (_I, [_P, _P, _P, _I, _I, _F, _P]),
+    "infernt_residual_add": (_I, [_P, _P, _P, _I, _P]),
+    "infernt_rope": (_I, [_P, _P, _I, _I, _I, _I, _I, _F, _P]),
+    "infernt_softmax": (_I, [_P, _P, _I, _I, _P]),
+    "infernt_softmax_with_mask": (_I, [_P, _P, _I, _I, _I, _P]),
+    "infernt_kv_cache_append": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "infernt_attention_scores": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P]),
+    "infernt_attention_values": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "infernt_silu_mul": (_I, [_P, _P, _P, _I, _P]),
+    "infernt_embedding_lookup": (_I, [_P, _P, _I, _I, _P]),
+    "infernt_argmax": (_I, [_P, _P, _I, _P]),
+    "infernt_gemm_f32": (_I, [_P, _P, _P, _I, _I, _I, _F, _F, _I, _I, _P]),
+    "infernt_rmsnorm_gemv": (_I, [_P, _P, _I, _P, _I, _P, _I, _I, _I, _P, _P, _F, _P]),
+    "infernt_gemv_residual": (_I, [_P, _P, _P, _I, _I, _I, _P, _P]),
+    "infernt_rmsnorm_gate_up_silu": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P]),
+    "infernt_attention_workspace_bytes": (_S, [_I, _I, _I, _I]),
+    "infernt_attention_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
+    "infernt_lm_head_workspace_bytes": (_S, []),
+    "infernt_rmsnorm_lm_head_argmax": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P, _P]),
+    "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
+                                 ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),
+    "infernt_plan_destroy": (_I, [_P]),
+    "infernt_plan_forward": (_I, [_P, _P, _I, _P, _P]),
+    "infernt_plan_decode": (_I, [_P, _I, _I, _P, _P]),
+    "infernt_plan_decode_chain": (_I, [_P, _I, _I, _I, _P, _P]),
+    "infernt_plan_read_token": (_I, [_P, ctypes.POINTER(_I), _P]),
+    "infernt_plan_logits": (_P, [_P]),
+    "infernt_plan_kernels_per_step": (_I, [_P]),
+    "infernt_fill_normal": (_I, [_P, _S, _I, _U64, _U64, _F, _P]),
+    "infernt_fill_const": (_I, [_P, _S, _F, _P]),
+    "infernt_fill_kv": (_I, [ctypes.POINTER(_P), ctypes.POINTER(_P), _I, _I, _I, _I, _I, _U64, _F, _P]),
+    "infernt_engine_create_seeded": (_I, [ctypes.POINTER(LlamaConfig), _U64, _F, ctypes.POINTER(_P)]),
+    "infernt_engine_destroy": (_I, [_P]),
+    "infernt_engine_reset": (_I, [_P]),
+    "infernt_engine_forward_token": (_I, [_P, _I, _I, ctypes.POINTER(_I)]),
+    "infernt_engine_sample_next_token": (_I, [_P, _F, ctypes.POINTER(_I)]),
+    "infernt_engine_logits": (_I, [_P, _P]),
+    "infernt_engine_fill_kv": (_I, [_P, _U64, _I, _F]),
+    "infernt_engine_decode_chain": (_I, [_P, _I, _I, _I, _P, ctypes.POINTER(_F)]),
+    "infernt_engine_weight_ptrs": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "infernt_engine_kv_ptrs": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), _I]),
+}
+
+
+def exported_symbols():
+    """Names of the C-ABI entry points this module binds."""
+    return sorted(_SIGS)
+
+
+def lib():
+    """The loaded product library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError("%s is missing: run `python -m infernt_b200.build` (or "
+                               "__graft_entry__.build())" % LIB_PATH)
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def check(status, what):
+    if status != 0:
+        raise InferntError(status, what, lib().infernt_last_error().decode())
+    return status
+
+
+def call(name, *args):
+    """Calls a C-ABI entry point and raises InferntError on a non-zero status."""
+    return check(getattr(lib(), name)(*args), name)
+
+
+def ptr(t):
+    """Device pointer of a torch tensor (or pass an int through)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+class Engine:
+    """The C++ InferenceEngine (include/engine.h) through its C entry points,
+    with seeded synthetic weights (include/infernt_seed.h)."""
+
+    def __init__(self, cfg: ModelConfig, seed: int = 0, std: float = 0.02):
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        call("infernt_engine_create_seeded", ctypes.byref(cfg.c()), seed, std, ctypes.byref(h))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().infernt_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        call("infernt_engine_reset", self._h)
+
+    def forward_token(self, token: int, position: int) -> int:
+        out = ctypes.c_int()
+        call("infernt_engine_forward_token", self._h, token, position, ctypes.byref(out))
+        return out.value
+
+    def sample_next_token(self, temperature: float = 0.0) -> int:
+        out = ctypes.c_int()
+        call("infernt_engine_sample_next_token", self._h, temperature, ctypes.byref(out))
+        return out.value
+
+    def logits(self):
+        import numpy as np
+        out = np.empty(self.cfg.vocab_size, dtype=np.float32)
+        call("infernt_engine_logits", self._h, out.ctypes.data)
+        return out
+
+    def fill_kv(self, seed: int, n_pos: int, std: float = 1.0):
+        call("infernt_engine_fill_kv", self._h, seed, n_pos, std)
+
+    def decode_chain(self, token: int, position: int, steps: int):
+        """Device-chained greedy decode; returns (tokens, device ms)."""
+        import numpy as np
+        toks = np.zeros(max(steps, 1), dtype=np.int32)
+        ms = ctypes.c_float()
+        call("infernt_engine_decode_chain", self._h, token, position, steps, toks.ctypes.data,
+             ctypes.byref(ms))
+        return toks[:steps].tolist(), ms.value
+
+    def weight_ptrs(self):
+        n = 3 + 9 * self.cfg.num_layers
+        arr = (ctypes.c_void_p * n)()
+        call("infernt_engine_weight_ptrs", self._h, arr, n)
+        return [arr[i] for i in range(n)]
+
+    def kv_ptrs(self):
+        n = self.cfg.num_layers
+        k = (ctypes.c_void_p * n)()
+        v = (ctypes.c_void_p * n)()
+        call("infernt_engine_kv_ptrs", self._h, k, v, n)
+        return [k[i] for i in range(n)], [v[i] for i in range(n)]
