@@ -58,12 +58,21 @@ public:
     // Kernels per decode step (launch accounting).
     int kernels_per_step() const;
 
+    // The decode plan bound to these weights and this cache (created on first use).
+    infernt_plan* plan_for(const ModelWeights& weights, KVCache& kv_cache) { return bind(weights, kv_cache); }
+
+    // INFERNT_MODE_* for the following steps (rebinds the plan).
+    void set_decode_mode(int mode);
+    // The mode in use: the bound plan's, or the requested one before any step.
+    int decode_mode() const;
+
 private:
     infernt_plan* bind(const ModelWeights& weights, KVCache& kv_cache);
 
     CublasWrapper& cublas_;
     ModelConfig config_;
     int max_batch_size_;
+    int mode_;
     infernt_plan* plan_;
     std::vector<const void*> bound_weights_;
     std::vector<float*> bound_k_;

@@ -147,7 +147,15 @@ INFERNT_API int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, co
  * cache (the state LlamaArchitecture::forward works on,
  * architectures/llama/llama_model.cpp:45-65).  The plan owns its scratch
  * activations (allocated once at creation: the zero-allocation decode
- * loop) and, when use_graph != 0, CUDA graphs of the whole step.        */
+ * loop).  Execution modes:
+ *   INFERNT_MODE_EAGER       5 kernels per layer + 1, launched per step;
+ *   INFERNT_MODE_GRAPH       the same kernels replayed as one CUDA graph;
+ *   INFERNT_MODE_PERSISTENT  one cooperative launch of the persistent decode
+ *                            kernel per call (a whole chain of steps too);
+ *                            falls back to GRAPH when the shapes do not allow
+ *                            it (projection inputs not multiples of 512,
+ *                            unaligned weights).                          */
+enum { INFERNT_MODE_EAGER = 0, INFERNT_MODE_GRAPH = 1, INFERNT_MODE_PERSISTENT = 2 };
 typedef struct {
     int vocab_size;
     int hidden_size;
@@ -172,9 +180,11 @@ typedef struct infernt_plan infernt_plan;
  * projection matrices and lm_head have weight_dtype.  k_cache / v_cache: num_layers device
  * pointers to float [Nkv, max_seq_len, D] (include/kv_cache.h:7-15). */
 INFERNT_API int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights,
-                                    float* const* k_cache, float* const* v_cache, int use_graph,
+                                    float* const* k_cache, float* const* v_cache, int mode,
                                     infernt_plan** out);
 INFERNT_API int infernt_plan_destroy(infernt_plan* plan);
+/* The mode the plan runs in (PERSISTENT may have fallen back to GRAPH). */
+INFERNT_API int infernt_plan_mode(const infernt_plan* plan);
 /* ModelArchitecture::forward (include/architecture.h:15-19): input_embedding [h] at
  * `position`; writes logits [V] (NULL: the plan's own buffer) and the greedy token
  * (read it with infernt_plan_read_token). */
@@ -195,6 +205,15 @@ INFERNT_API int infernt_plan_read_token(infernt_plan* plan, int* token_host, voi
 INFERNT_API float* infernt_plan_logits(infernt_plan* plan);
 /* Number of kernels one decode step launches (for launch accounting). */
 INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
+/* Phase timeline of the persistent decode kernel.  Phases per step:
+ * 5 per layer (qkv, attention, o, gate/up, down) + the LM head.  With a
+ * device buffer of infernt_plan_trace_entries(plan, steps) uint64 set, the
+ * following launches record %globaltimer nanoseconds for CTA 0 and the last
+ * CTA per (step, phase): [phase start, input loaded, work done, grid barrier
+ * passed, producer issued the phase's last tile], layout
+ * [cta (2)][step][phase][5].  NULL turns it off.  PERSISTENT mode only. */
+INFERNT_API size_t infernt_plan_trace_entries(const infernt_plan* plan, int steps);
+INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* trace_dev);
 
 /* ------------------------------------------------ synthetic weights ---
  * Fill device memory with the seeded values of include/infernt_seed.h
@@ -217,6 +236,15 @@ typedef struct infernt_engine infernt_engine;
 INFERNT_API int infernt_engine_create_seeded(const infernt_llama_config* cfg, uint64_t seed,
                                              float std_dev, infernt_engine** out);
 INFERNT_API int infernt_engine_destroy(infernt_engine* e);
+/* Decode execution mode (INFERNT_MODE_*) for the following steps; the default is
+ * PERSISTENT, or the INFERNT_DECODE_MODE environment variable (eager | graph |
+ * persistent) when set.  infernt_engine_mode reports the mode in use (after a step). */
+INFERNT_API int infernt_engine_set_mode(infernt_engine* e, int mode);
+INFERNT_API int infernt_engine_mode(infernt_engine* e, int* mode);
+/* A device-chained decode of `steps` steps with the phase timeline recorded
+ * (infernt_plan_set_trace layout) into host_out (n entries). */
+INFERNT_API int infernt_engine_trace_chain(infernt_engine* e, int token, int position, int steps,
+                                           unsigned long long* host_out, size_t n);
 /* KVCache::reset (src/kv_cache.cpp:22-30). */
 INFERNT_API int infernt_engine_reset(infernt_engine* e);
 /* InferenceEngine::forward_token (src/engine.cpp:53-66): returns the greedy next token in

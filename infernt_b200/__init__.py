@@ -18,6 +18,10 @@ LIB_PATH = os.path.join(HERE, "lib", "libinfernt_b200.so")
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
+MODE_EAGER = 0
+MODE_GRAPH = 1
+MODE_PERSISTENT = 2
+
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "CUDA error",
           4: "out of device memory", 5: "device-side error", 6: "no usable CUDA device"}
 
@@ -131,6 +135,12 @@ _SIGS = {
     "infernt_plan_read_token": (_I, [_P, ctypes.POINTER(_I), _P]),
     "infernt_plan_logits": (_P, [_P]),
     "infernt_plan_kernels_per_step": (_I, [_P]),
+    "infernt_plan_mode": (_I, [_P]),
+    "infernt_plan_trace_entries": (_S, [_P, _I]),
+    "infernt_plan_set_trace": (_I, [_P, _P]),
+    "infernt_engine_trace_chain": (_I, [_P, _I, _I, _I, _P, _S]),
+    "infernt_engine_set_mode": (_I, [_P, _I]),
+    "infernt_engine_mode": (_I, [_P, ctypes.POINTER(_I)]),
     "infernt_fill_normal": (_I, [_P, _S, _I, _U64, _U64, _F, _P]),
     "infernt_fill_const": (_I, [_P, _S, _F, _P]),
     "infernt_fill_kv": (_I, [ctypes.POINTER(_P), ctypes.POINTER(_P), _I, _I, _I, _I, _I, _U64, _F, _P]),
@@ -212,6 +222,16 @@ class Engine:
     def reset(self):
         call("infernt_engine_reset", self._h)
 
+    def set_mode(self, mode: int):
+        """MODE_EAGER / MODE_GRAPH / MODE_PERSISTENT for the following steps."""
+        call("infernt_engine_set_mode", self._h, mode)
+
+    @property
+    def mode(self) -> int:
+        out = ctypes.c_int()
+        call("infernt_engine_mode", self._h, ctypes.byref(out))
+        return out.value
+
     def forward_token(self, token: int, position: int) -> int:
         out = ctypes.c_int()
         call("infernt_engine_forward_token", self._h, token, position, ctypes.byref(out))
@@ -239,6 +259,17 @@ class Engine:
         call("infernt_engine_decode_chain", self._h, token, position, steps, toks.ctypes.data,
              ctypes.byref(ms))
         return toks[:steps].tolist(), ms.value
+
+    def trace_chain(self, token: int, position: int, steps: int):
+        """Device-chained decode with the persistent kernel's phase timeline.
+        Returns an int64 array [cta (0 = first, 1 = last)][step][phase][5]
+        of %globaltimer ns: phase start, input loaded, work done, barrier
+        passed, producer issued the phase's last tile."""
+        import numpy as np
+        nph = 5 * self.cfg.num_layers + 1
+        out = np.zeros(2 * steps * nph * 5, dtype=np.uint64)
+        call("infernt_engine_trace_chain", self._h, token, position, steps, out.ctypes.data, out.size)
+        return out.reshape(2, steps, nph, 5).astype(np.int64)
 
     def weight_ptrs(self):
         n = 3 + 9 * self.cfg.num_layers

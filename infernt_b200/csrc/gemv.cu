@@ -22,8 +22,8 @@ cudaError_t launch_one(const GemvArgs& a, bool fast, int grid, cudaStream_t stre
     }
     if (fast) {
         cfg.blockDim = dim3(kGemvThreads);
-        cfg.dynamicSmemBytes = gemv_tma_smem_bytes(a.K);
-        return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<WT, EPI>, a);
+        cfg.dynamicSmemBytes = gemv_tma_smem_bytes(a.K, kGemvStages);
+        return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<WT, EPI, kGemvStages>, a);
     }
     cfg.blockDim = dim3(kPlainThreads);
     cfg.dynamicSmemBytes = a.K * 4;
@@ -32,11 +32,10 @@ cudaError_t launch_one(const GemvArgs& a, bool fast, int grid, cudaStream_t stre
 
 template <typename WT, int EPI>
 cudaError_t set_max_smem() {
-    cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WT, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+    cudaError_t e =
+        raise_dynamic_smem_limit(reinterpret_cast<const void*>(gemv_tma_kernel<WT, EPI, kGemvStages>));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(gemv_plain_kernel<WT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kMaxDynSmem);
+    return raise_dynamic_smem_limit(reinterpret_cast<const void*>(gemv_plain_kernel<WT, EPI>));
 }
 
 bool g_prepared[64] = {false};
@@ -53,10 +52,21 @@ cudaError_t launch_dtype(const GemvArgs& a, int epi, bool fast, int grid, cudaSt
 
 }  // namespace
 
+cudaError_t raise_dynamic_smem_limit(const void* kernel) {
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, current_device());
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - (int)fa.sharedSizeBytes);
+}
+
 bool gemv_fast_path_ok(const GemvArgs& a, int weight_dtype, int epi) {
     (void)weight_dtype;
     if (a.K <= 0 || a.K % kPiece != 0) return false;
-    if (gemv_tma_smem_bytes(a.K) > 227 * 1024) return false;
+    if (gemv_tma_smem_bytes(a.K, kGemvStages) > kMaxDynSmem) return false;
     const int nseg = epi == kEpiSwiGLU ? 2 : a.nseg;
     for (int s = 0; s < nseg; ++s)
         if (!aligned16(a.seg_ptr[s])) return false;

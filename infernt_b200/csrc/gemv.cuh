@@ -11,9 +11,8 @@
 // producer thread streams the CTA's contiguous block of rows into a ring
 // of shared-memory slots with 1-D bulk copies (cp.async.bulk, the TMA
 // engine) and mbarrier transaction counts; four consumer warps multiply
-// the slots against the input vector held in shared memory.  Rows are
-// consumed in groups of four so one cross-warp reduction covers four rows.
-// The producer starts before griddepcontrol.wait, so under programmatic
+// the slots against the input vector held in shared memory (slot layout
+// below).  The producer starts before griddepcontrol.wait, so under programmatic
 // dependent launch a kernel's weights stream in while the previous kernel
 // is still finishing.
 //
@@ -39,12 +38,12 @@ enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiArgmax
 constexpr int kPiece = 512;          // weight elements per piece (one float4/bf16x4 per thread)
 constexpr int kGemvConsumers = 128;  // four consumer warps
 constexpr int kGemvThreads = 160;    // plus one producer warp
-constexpr int kGemvGroup = 4;        // rows per cross-warp reduction
-constexpr int kSlotBytes = 8192;     // ring slot
-constexpr int kStages = 8;           // ring depth (64 KB in flight per SM)
+constexpr int kSlotBytes = 16384;    // ring slot: one 512-column block of 8 FP32 / 16 bf16 rows
+constexpr int kGemvStages = 8;       // ring depth of the standalone kernels (128 KB in flight per SM)
 constexpr int kArgmaxMaxBlocks = 1024;
 constexpr int kPlainThreads = 256;
-constexpr int kMaxDynSmem = 227 * 1024;  // opt-in dynamic shared memory per CTA on sm_100
+constexpr int kMaxDynSmem = 226 * 1024;  // dynamic shared memory the launchers plan with (opt-in 227 KB
+                                         // minus room for the kernels' static shared memory)
 
 struct GemvArgs {
     const void* seg_ptr[3];  // matrices stacked in one virtual row space (Q|K|V)
@@ -70,29 +69,6 @@ struct GemvArgs {
     int* token_hist;       // optional history, written at state[2]
     unsigned* err;
 };
-
-__device__ __forceinline__ float dot_piece(const float* wp, const float* xp, int t, float acc) {
-    const float4 w = reinterpret_cast<const float4*>(wp)[t];
-    const float4 x = reinterpret_cast<const float4*>(xp)[t];
-    acc = fmaf(w.x, x.x, acc);
-    acc = fmaf(w.y, x.y, acc);
-    acc = fmaf(w.z, x.z, acc);
-    acc = fmaf(w.w, x.w, acc);
-    return acc;
-}
-
-__device__ __forceinline__ float dot_piece(const __nv_bfloat16* wp, const float* xp, int t,
-                                           float acc) {
-    const uint2 raw = reinterpret_cast<const uint2*>(wp)[t];
-    const float4 x = reinterpret_cast<const float4*>(xp)[t];
-    const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-    const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-    acc = fmaf(w01.x, x.x, acc);
-    acc = fmaf(w01.y, x.y, acc);
-    acc = fmaf(w23.x, x.z, acc);
-    acc = fmaf(w23.y, x.w, acc);
-    return acc;
-}
 
 // Resolve the input row (explicit vector or the embedding row of *token).
 __device__ __forceinline__ const float* gemv_input(const GemvArgs& a) {
@@ -157,85 +133,83 @@ __device__ __forceinline__ void argmax_finish(const GemvArgs& a, float bv, int b
 
 // ---------------------------------------------------------------------------
 // Fast path: TMA ring
+//
+// Work of one CTA: the contiguous units [ub, ue) (rows, or gate/up row
+// pairs), taken in groups of G = R / NS units.  A ring slot holds one
+// 512-column block j of every row of the group: piece i = s * G + g is row
+// g of segment s (gate/up) at columns [512 j, 512 j + 512).  So a consumer
+// thread loads one float4 of x per slot and R independent weight vectors,
+// accumulating into R registers; a group's rows are reduced across the
+// four warps once, after its last column block.  The producer issues one
+// bulk copy per piece (2 KB FP32 / 1 KB bf16); slot bytes are R pieces.
 // ---------------------------------------------------------------------------
 
-struct RingProducer {
-    unsigned char* ring;
-    uint64_t* full;
-    uint64_t* empty;
-    uint64_t total_bytes;
-    uint64_t policy;
-    unsigned* err;
-    uint32_t slot_fill;
-    uint32_t slot_idx;
-    bool ok;
-
-    __device__ __forceinline__ void emit(const unsigned char* src, uint64_t nbytes) {
-        while (nbytes > 0 && ok) {
-            const uint32_t s = slot_idx % kStages;
-            if (slot_fill == 0) {
-                const uint32_t use = slot_idx / kStages;
-                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1u, err)) {
-                    ok = false;
-                    return;
-                }
-                const uint64_t rem = total_bytes - (uint64_t)slot_idx * kSlotBytes;
-                mbar_arrive_expect_tx(&full[s], rem < (uint64_t)kSlotBytes ? (uint32_t)rem
-                                                                            : (uint32_t)kSlotBytes);
-            }
-            const uint64_t room = (uint64_t)(kSlotBytes - slot_fill);
-            const uint32_t n = (uint32_t)(nbytes < room ? nbytes : room);
-            bulk_g2s(ring + s * kSlotBytes + slot_fill, src, n, &full[s], policy);
-            src += n;
-            nbytes -= n;
-            slot_fill += n;
-            if (slot_fill == kSlotBytes) {
-                slot_fill = 0;
-                ++slot_idx;
-            }
-        }
-    }
-
-    // After a failed wait: let every armed slot's copies land before exit.
-    __device__ __forceinline__ void drain() {
-        const uint32_t armed = slot_idx + (slot_fill ? 1u : 0u);
-        const uint32_t first = armed > (uint32_t)kStages ? armed - kStages : 0u;
-        for (uint32_t sl = first; sl < armed; ++sl)
-            mbar_wait(&full[sl % kStages], (sl / kStages) & 1u, err);
-    }
+template <typename WT>
+struct TmaShape {
+    static constexpr int EB = WeightTraits<WT>::kBytes;
+    static constexpr int PB = kPiece * EB;                 // piece bytes
+    static constexpr int R = kSlotBytes / PB;              // pieces (rows) per slot: 8 FP32, 16 bf16
 };
 
+// Global address of unit-row `row` of segment space `s` (SwiGLU: 0 gate, 1
+// up; otherwise the stacked virtual row space).
 template <typename WT>
-__host__ __device__ constexpr int gemv_tma_smem_bytes_const() {
-    return kStages * kSlotBytes;
+__device__ __forceinline__ const unsigned char* tma_row(const GemvArgs& a, int ns, int s, int row) {
+    const size_t rb = (size_t)a.K * WeightTraits<WT>::kBytes;
+    if (ns == 2) return static_cast<const unsigned char*>(a.seg_ptr[s]) + (size_t)row * rb;
+    int base = 0;
+    for (int q = 0; q < a.nseg; ++q) {
+        if (row < base + a.seg_rows[q])
+            return static_cast<const unsigned char*>(a.seg_ptr[q]) + (size_t)(row - base) * rb;
+        base += a.seg_rows[q];
+    }
+    return static_cast<const unsigned char*>(a.seg_ptr[0]);
 }
 
-__host__ __device__ inline int gemv_tma_smem_bytes(int K) {
-    // ring | x [K] | reduction [2][4][8] | 2*kStages mbarriers
-    return kStages * kSlotBytes + K * 4 + 2 * 4 * 8 * 4 + 2 * kStages * 8;
+__host__ __device__ inline int gemv_tma_smem_bytes(int K, int stages) {
+    // ring | x [K] | reduction [2][4][16] | 2*stages mbarriers
+    return stages * kSlotBytes + K * 4 + 2 * 4 * 16 * 4 + 2 * stages * 8;
 }
 
-template <typename WT, int EPI>
+__device__ __forceinline__ void dot_slot_piece(const float* wp, const float4& x, int t, float& acc) {
+    const float4 w = reinterpret_cast<const float4*>(wp)[t];
+    acc = fmaf(w.x, x.x, acc);
+    acc = fmaf(w.y, x.y, acc);
+    acc = fmaf(w.z, x.z, acc);
+    acc = fmaf(w.w, x.w, acc);
+}
+
+__device__ __forceinline__ void dot_slot_piece(const __nv_bfloat16* wp, const float4& x, int t, float& acc) {
+    const uint2 raw = reinterpret_cast<const uint2*>(wp)[t];
+    const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    acc = fmaf(w01.x, x.x, acc);
+    acc = fmaf(w01.y, x.y, acc);
+    acc = fmaf(w23.x, x.z, acc);
+    acc = fmaf(w23.y, x.w, acc);
+}
+
+template <typename WT, int EPI, int STAGES>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArgs a) {
-    constexpr int EB = WeightTraits<WT>::kBytes;
-    constexpr int PIECE_BYTES = kPiece * EB;
-    constexpr int PPS = kSlotBytes / PIECE_BYTES;
+    using S = TmaShape<WT>;
+    constexpr int PB = S::PB;
+    constexpr int R = S::R;
     constexpr int NS = (EPI == kEpiSwiGLU) ? 2 : 1;
-    constexpr int G = kGemvGroup;
+    constexpr int G = R / NS;
 
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* ring = smem;
-    float* xs = reinterpret_cast<float*>(smem + kStages * kSlotBytes);
-    float* red = xs + a.K;  // [2][4][8]
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 64);
-    uint64_t* empty = full + kStages;
+    float* xs = reinterpret_cast<float*>(smem + STAGES * kSlotBytes);
+    float* red = xs + a.K;  // [2][4][16]
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * 4 * 16);
+    uint64_t* empty = full + STAGES;
     __shared__ float s_ss[4];
     __shared__ float s_amv[G];
     __shared__ int s_ami[G];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kGemvConsumers / 32);
         }
@@ -247,39 +221,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
     const int ub = (int)((long long)a.units * blockIdx.x / gridDim.x);
     const int ue = (int)((long long)a.units * (blockIdx.x + 1) / gridDim.x);
     const int PPR = a.K / kPiece;
-    const long long total_pieces = (long long)(ue - ub) * NS * PPR;
 
     if (warp == kGemvConsumers / 32) {
         // ---------------- producer: weights do not depend on the previous kernel
-        if (lane == 0 && total_pieces > 0) {
-            RingProducer pr{ring, full, empty, (uint64_t)total_pieces * PIECE_BYTES,
-                            l2_evict_first_policy(), a.err, 0u, 0u, true};
-            const uint64_t row_bytes = (uint64_t)a.K * EB;
-            for (int u0 = ub; u0 < ue && pr.ok; u0 += G) {
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            uint32_t sl = 0;
+            bool ok = true;
+            for (int u0 = ub; u0 < ue && ok; u0 += G) {
                 const int ng = min(G, ue - u0);
-                if (NS == 2) {
-                    pr.emit(static_cast<const unsigned char*>(a.seg_ptr[0]) + (uint64_t)u0 * row_bytes,
-                            (uint64_t)ng * row_bytes);
-                    pr.emit(static_cast<const unsigned char*>(a.seg_ptr[1]) + (uint64_t)u0 * row_bytes,
-                            (uint64_t)ng * row_bytes);
-                } else {
-                    int r = u0, left = ng, base = 0;
-                    for (int s = 0; s < a.nseg && left > 0; ++s) {
-                        const int rows = a.seg_rows[s];
-                        if (r < base + rows) {
-                            const int lr = r - base;
-                            const int take = min(left, base + rows - r);
-                            pr.emit(static_cast<const unsigned char*>(a.seg_ptr[s]) +
-                                        (uint64_t)lr * row_bytes,
-                                    (uint64_t)take * row_bytes);
-                            r += take;
-                            left -= take;
-                        }
-                        base += rows;
+                for (int j = 0; j < PPR && ok; ++j, ++sl) {
+                    const int s = (int)(sl % STAGES);
+                    const uint32_t use = sl / STAGES;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1u, a.err)) {
+                        ok = false;
+                        break;
                     }
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(ng * NS * PB));
+                    unsigned char* dst = ring + s * kSlotBytes;
+#pragma unroll
+                    for (int q = 0; q < NS; ++q)
+                        for (int g = 0; g < ng; ++g)
+                            bulk_g2s(dst + (q * G + g) * PB,
+                                     tma_row<WT>(a, NS, q, u0 + g) + (size_t)j * PB, PB, &full[s], pol);
                 }
             }
-            if (!pr.ok) pr.drain();
+            if (!ok) {  // let every armed slot's copies land before the CTA can exit
+                const uint32_t first = sl > (uint32_t)STAGES ? sl - STAGES : 0u;
+                for (uint32_t q = first; q < sl; ++q) mbar_wait(&full[q % STAGES], (q / STAGES) & 1u, a.err);
+            }
         }
         return;
     }
@@ -291,7 +261,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
     if (a.norm_w) {
         float ss = 0.0f;
         for (int i = tid * 4; i < a.K; i += kGemvConsumers * 4) {
-            const float4 v = *reinterpret_cast<const float4*>(xsrc + i);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(xsrc + i));
             ss = fmaf(v.x, v.x, ss);
             ss = fmaf(v.y, v.y, ss);
             ss = fmaf(v.z, v.z, ss);
@@ -304,7 +274,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
         rms = rsqrtf(tot / (float)a.K + a.eps);
     }
     for (int i = tid * 4; i < a.K; i += kGemvConsumers * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(xsrc + i);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(xsrc + i));
         float4 o = v;
         if (a.norm_w) {
             const float4 w = *reinterpret_cast<const float4*>(a.norm_w + i);
@@ -318,55 +288,41 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
     }
     named_sync(1, kGemvConsumers);
 
-    long long piece = 0;
+    uint32_t sl = 0;
     bool failed = false;
     int buf = 0;
     float am_v = -1e30f;
     int am_i = 0;
     for (int u0 = ub; u0 < ue; u0 += G) {
         const int ng = min(G, ue - u0);
-        float acc[NS][G];
+        float acc[R];
 #pragma unroll
-        for (int s = 0; s < NS; ++s)
+        for (int i = 0; i < R; ++i) acc[i] = 0.0f;
+        for (int j = 0; j < PPR; ++j, ++sl) {
+            const int s = (int)(sl % STAGES);
+            if (!failed) failed = !mbar_wait(&full[s], (sl / STAGES) & 1u, a.err);
+            const float4 xv = reinterpret_cast<const float4*>(xs + j * kPiece)[tid];
+            const unsigned char* slot = ring + s * kSlotBytes;
 #pragma unroll
-            for (int g = 0; g < G; ++g) acc[s][g] = 0.0f;
-#pragma unroll
-        for (int s = 0; s < NS; ++s) {
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                if (g < ng) {
-                    for (int j = 0; j < PPR; ++j, ++piece) {
-                        const uint32_t sl = (uint32_t)(piece / PPS);
-                        const int slot = (int)(sl % kStages);
-                        const int within = (int)(piece - (long long)sl * PPS);
-                        if (within == 0 && !failed)
-                            failed = !mbar_wait(&full[slot], (sl / kStages) & 1u, a.err);
-                        const WT* wp =
-                            reinterpret_cast<const WT*>(ring + slot * kSlotBytes + within * PIECE_BYTES);
-                        acc[s][g] = dot_piece(wp, xs + j * kPiece, tid, acc[s][g]);
-                        if (within == PPS - 1 || piece == total_pieces - 1) {
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&empty[slot]);
-                        }
-                    }
-                }
-            }
+            for (int i = 0; i < R; ++i)
+                dot_slot_piece(reinterpret_cast<const WT*>(slot + i * PB), xv, tid, acc[i]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        float* rb = red + buf * 32;
+        float* rb = red + buf * 64;  // [4 warps][16]
 #pragma unroll
-        for (int s = 0; s < NS; ++s)
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float v = warp_sum(acc[s][g]);
-                if (lane == 0) rb[warp * 8 + s * G + g] = v;
-            }
+        for (int i = 0; i < R; ++i) {
+            const float v = warp_sum(acc[i]);
+            if (lane == 0) rb[warp * 16 + i] = v;
+        }
         named_sync(1, kGemvConsumers);
         if (tid < ng) {
             float y[2] = {0.0f, 0.0f};
 #pragma unroll
-            for (int s = 0; s < NS; ++s)
-                y[s] = ((rb[0 * 8 + s * G + tid] + rb[1 * 8 + s * G + tid]) + rb[2 * 8 + s * G + tid]) +
-                       rb[3 * 8 + s * G + tid];
+            for (int q = 0; q < NS; ++q) {
+                const int i = q * G + tid;
+                y[q] = ((rb[0 * 16 + i] + rb[1 * 16 + i]) + rb[2 * 16 + i]) + rb[3 * 16 + i];
+            }
             gemv_epilogue<EPI>(a, u0 + tid, y[0], y[1], am_v, am_i);
         }
         buf ^= 1;
@@ -390,6 +346,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
         }
     }
 }
+
 
 // ---------------------------------------------------------------------------
 // Plain path: any K, scalar loads, one warp per output unit
@@ -475,6 +432,9 @@ __global__ void __launch_bounds__(kPlainThreads) gemv_plain_kernel(const GemvArg
 // current device (once per device; call outside stream capture).
 cudaError_t gemv_prepare();
 cudaError_t attention_prepare();
+// Sets a kernel's dynamic shared-memory limit to the device's opt-in
+// maximum minus the kernel's static shared memory.
+cudaError_t raise_dynamic_smem_limit(const void* kernel);
 
 // Host launcher (gemv.cu).  `weight_dtype` INFERNT_DTYPE_*, `epi` EpiKind.
 // `pdl` enables programmatic dependent launch on the stream.

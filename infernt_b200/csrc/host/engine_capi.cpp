@@ -103,6 +103,43 @@ int infernt_engine_destroy(infernt_engine* e) {
     return INFERNT_OK;
 }
 
+int infernt_engine_set_mode(infernt_engine* e, int mode) {
+    INFERNT_REQUIRE(e, "engine_set_mode: null engine");
+    INFERNT_REQUIRE(mode >= INFERNT_MODE_EAGER && mode <= INFERNT_MODE_PERSISTENT, "engine_set_mode: mode %d", mode);
+    e->engine.architecture().set_decode_mode(mode);
+    return INFERNT_OK;
+}
+
+int infernt_engine_mode(infernt_engine* e, int* mode) {
+    INFERNT_REQUIRE(e && mode, "engine_mode: null argument");
+    *mode = e->engine.architecture().decode_mode();
+    return INFERNT_OK;
+}
+
+int infernt_engine_trace_chain(infernt_engine* e, int token, int position, int steps, unsigned long long* host_out,
+                               size_t n) {
+    INFERNT_REQUIRE(e && host_out && steps > 0, "engine_trace_chain: bad arguments");
+    try {
+        infernt_plan* plan = e->engine.architecture().plan_for(e->engine.weights(), e->engine.kv_cache());
+        const size_t need = infernt_plan_trace_entries(plan, steps);
+        INFERNT_REQUIRE(need > 0, "engine_trace_chain: the plan does not run the persistent kernel");
+        INFERNT_REQUIRE(n >= need, "engine_trace_chain: need %zu entries", need);
+        unsigned long long* dev = nullptr;
+        INFERNT_CUDA_TRY(cudaMalloc(&dev, need * sizeof(unsigned long long)));
+        cudaMemset(dev, 0, need * sizeof(unsigned long long));
+        int s = infernt_plan_set_trace(plan, dev);
+        if (!s) e->engine.decode_chain(token, position, steps, nullptr);
+        infernt_plan_set_trace(plan, nullptr);
+        cudaError_t ce = cudaMemcpy(host_out, dev, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+        cudaFree(dev);
+        if (s) return s;
+        INFERNT_CUDA_TRY(ce);
+    } catch (const std::exception& ex) {
+        return infernt::fail(INFERNT_ERR_INVALID_ARGUMENT, "%s", ex.what());
+    }
+    return INFERNT_OK;
+}
+
 int infernt_engine_reset(infernt_engine* e) {
     INFERNT_REQUIRE(e, "engine_reset: null engine");
     try {

@@ -1,7 +1,9 @@
 // llama_architecture.cpp — LlamaArchitecture over the fused decode plan.
 // The reference's forward (architectures/llama/llama_model.cpp:45-65 and
 // llama_layer.cpp:5-73: ~400 launches, 23 blocking copies) becomes one
-// graph replay of the plan bound to these weights and this KV cache.
+// launch of the persistent decode kernel (or one graph replay) of the plan
+// bound to these weights and this KV cache.
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -23,7 +25,31 @@ const void* ptr(const Tensor& t, const char* name, DType want) {
 }
 }  // namespace
 
-LlamaArchitecture::LlamaArchitecture(CublasWrapper& cublas) : cublas_(cublas), max_batch_size_(1), plan_(nullptr) {}
+namespace {
+// INFERNT_DECODE_MODE = eager | graph | persistent (default persistent).
+int default_mode() {
+    const char* m = std::getenv("INFERNT_DECODE_MODE");
+    if (!m) return INFERNT_MODE_PERSISTENT;
+    const std::string s(m);
+    if (s == "eager") return INFERNT_MODE_EAGER;
+    if (s == "graph") return INFERNT_MODE_GRAPH;
+    return INFERNT_MODE_PERSISTENT;
+}
+}  // namespace
+
+LlamaArchitecture::LlamaArchitecture(CublasWrapper& cublas)
+    : cublas_(cublas), max_batch_size_(1), mode_(default_mode()), plan_(nullptr) {}
+
+void LlamaArchitecture::set_decode_mode(int mode) {
+    if (mode < INFERNT_MODE_EAGER || mode > INFERNT_MODE_PERSISTENT)
+        throw std::invalid_argument("set_decode_mode: unknown mode");
+    mode_ = mode;
+    infernt_plan_destroy(plan_);
+    plan_ = nullptr;
+    bound_weights_.clear();
+}
+
+int LlamaArchitecture::decode_mode() const { return plan_ ? infernt_plan_mode(plan_) : mode_; }
 
 LlamaArchitecture::~LlamaArchitecture() { infernt_plan_destroy(plan_); }
 
@@ -81,7 +107,7 @@ infernt_plan* LlamaArchitecture::bind(const ModelWeights& w, KVCache& kv) {
     pc.rms_norm_eps = c.rms_norm_eps;
     pc.rope_theta = c.rope_theta;
     pc.weight_dtype = wd == DType::BF16 ? INFERNT_DTYPE_BF16 : INFERNT_DTYPE_F32;
-    check(infernt_plan_create(&pc, wp.data(), kp.data(), vp.data(), 1, &plan_), "infernt_plan_create");
+    check(infernt_plan_create(&pc, wp.data(), kp.data(), vp.data(), mode_, &plan_), "infernt_plan_create");
     bound_weights_ = wp;
     bound_k_ = kp;
     bound_v_ = vp;
@@ -122,4 +148,6 @@ int LlamaArchitecture::last_token() {
 
 cudaStream_t LlamaArchitecture::stream() const { return cublas_.handle(); }
 
-int LlamaArchitecture::kernels_per_step() const { return 5 * config_.num_layers + 1; }
+int LlamaArchitecture::kernels_per_step() const {
+    return plan_ ? infernt_plan_kernels_per_step(plan_) : 5 * config_.num_layers + 1;
+}

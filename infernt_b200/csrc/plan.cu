@@ -1,30 +1,37 @@
-// plan.cu — the decode step: 5 kernels per decoder layer + 1 for the head.
+// plan.cu — the decode step over caller-owned weights and KV cache.
 //
-//   qkv     RMSNorm(attn_norm) + [Wq;Wk;Wv] x          (layer 0: embedding row of the token)
-//   attn    RoPE + KV append + split-KV GQA attention   -> attn_out
-//   o       hidden += Wo attn_out
-//   gateup  RMSNorm(ffn_norm) + SiLU(Wg x) * (Wu x)     -> act
-//   down    hidden += Wd act
-//   head    RMSNorm(final_norm) + logits = Wlm x + argmax -> token, state advanced
+// Two executions of the same step (architectures/llama/llama_layer.cpp:5-73,
+// llama_model.cpp:45-65, src/engine.cpp:53-76):
 //
-// (architectures/llama/llama_layer.cpp:5-73, llama_model.cpp:45-65,
-// src/engine.cpp:53-76).  The residual stream is updated in place, so the
-// reference's 23 hidden-state copies per token (llama_model.cpp:48, :55)
-// disappear.  Token, position and step live in a small device state block:
-// the attention kernel reads the position from it and the head kernel
-// writes the next token and position into it, so a chain of steps needs no
-// host round trip.  Every kernel is launched with programmatic stream
-// serialisation, so the next kernel's CTAs start streaming their weights
-// while the previous kernel drains; the step is captured once into a CUDA
-// graph and replayed.
+// * persistent (default when the shapes allow it): one cooperative launch
+//   of the persistent decode kernel (decode_kernel.cu) runs every layer and
+//   the LM head, and a chain of steps, with the weight stream never stopping
+//   at phase boundaries;
+// * kernel sequence: 5 kernels per layer + 1 for the head, chained with
+//   programmatic dependent launch and replayed as a CUDA graph:
+//     qkv     RMSNorm(attn_norm) + [Wq;Wk;Wv] x      (layer 0: embedding row of the token)
+//     attn    RoPE + KV append + split-KV GQA attention
+//     o       hidden += Wo attn_out
+//     gateup  RMSNorm(ffn_norm) + SiLU(Wg x) * (Wu x)
+//     down    hidden += Wd act
+//     head    RMSNorm(final_norm) + logits = Wlm x + argmax
+//
+// The residual stream is updated in place, so the reference's 23 hidden-
+// state copies per token (llama_model.cpp:48, :55) disappear.  Token,
+// position and step live in a small device state block: attention reads the
+// position from it and the head writes the next token and position into it,
+// so a chain of steps needs no host round trip.
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
 
-#include "common.cuh"
 #include "attention.cuh"
+#include "common.cuh"
+#include "decode_kernel.cuh"
 #include "gemv.cuh"
 #include "internal.h"
+#include "tensormap.h"
 
 namespace infernt {
 
@@ -56,12 +63,13 @@ struct infernt_plan {
     float* act = nullptr;
     float* hidden = nullptr;
     float* logits = nullptr;
-    int* state = nullptr;     // {token, position, step, last token}
+    int* state = nullptr;  // {token, position, step, last token}
     unsigned* err = nullptr;
     float* attn_part = nullptr;
     unsigned* attn_counter = nullptr;
     LmWs* lm_ws = nullptr;
-    bool use_graph = true;
+    int mode = INFERNT_MODE_PERSISTENT;
+    // kernel-sequence path
     cudaStream_t cap_stream = nullptr;
     struct Entry {
         int mode;
@@ -71,21 +79,23 @@ struct infernt_plan {
         cudaGraphExec_t exec;
     };
     std::vector<Entry> graphs;
+    // persistent path
+    void* mega_mem = nullptr;
+    MegaParams mega;
+    int mega_ctas = 0;
 };
 
 namespace {
 
-const int kModeInput = 0;  // layer 0 reads an input embedding vector
-const int kModeToken = 1;  // layer 0 reads the embedding row of state[0]
+const int kInputVector = 0;  // layer 0 reads an input embedding vector
+const int kInputToken = 1;   // layer 0 reads the embedding row of state[0]
 
-int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits,
-                int* hist) {
+int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist) {
     const infernt_llama_config& c = p->cfg;
     const int H = c.hidden_size, I = c.intermediate_size, L = c.num_layers;
     const int dt = c.weight_dtype;
     for (int l = 0; l < L; ++l) {
         const void* const* lw = p->w.data() + 3 + 9 * l;
-        // qkv
         GemvArgs a;
         memset(&a, 0, sizeof(a));
         a.seg_ptr[0] = lw[1];
@@ -98,7 +108,7 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         a.units = p->qs + 2 * p->kvs;
         a.K = H;
         if (l == 0) {
-            a.x = mode == kModeInput ? input : nullptr;
+            a.x = mode == kInputVector ? input : nullptr;
             a.emb = static_cast<const float*>(p->w[0]);
             a.token = p->state;
             a.vocab = c.vocab_size;
@@ -112,7 +122,6 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         a.err = p->err;
         INFERNT_CUDA_TRY(launch_gemv(a, dt, kEpiStore, st, true, nullptr));
 
-        // attention
         AttnArgs at;
         memset(&at, 0, sizeof(at));
         at.qkv = p->qkv;
@@ -132,7 +141,6 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         at.err = p->err;
         INFERNT_CUDA_TRY(launch_attention_decode(at, st, true));
 
-        // o projection + residual
         memset(&a, 0, sizeof(a));
         a.seg_ptr[0] = lw[4];
         a.seg_rows[0] = H;
@@ -145,7 +153,6 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         a.err = p->err;
         INFERNT_CUDA_TRY(launch_gemv(a, dt, kEpiResidual, st, true, nullptr));
 
-        // gate/up + SiLU
         memset(&a, 0, sizeof(a));
         a.seg_ptr[0] = lw[6];
         a.seg_ptr[1] = lw[7];
@@ -160,7 +167,6 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         a.err = p->err;
         INFERNT_CUDA_TRY(launch_gemv(a, dt, kEpiSwiGLU, st, true, nullptr));
 
-        // down + residual
         memset(&a, 0, sizeof(a));
         a.seg_ptr[0] = lw[8];
         a.seg_rows[0] = H;
@@ -173,7 +179,6 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         a.err = p->err;
         INFERNT_CUDA_TRY(launch_gemv(a, dt, kEpiResidual, st, true, nullptr));
     }
-    // final norm + LM head + argmax
     GemvArgs a;
     memset(&a, 0, sizeof(a));
     a.seg_ptr[0] = p->w[2];
@@ -196,9 +201,8 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
     return INFERNT_OK;
 }
 
-int run_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist) {
-    if (!logits) logits = p->logits;
-    if (!p->use_graph) return record_step(p, st, mode, input, logits, hist);
+int run_graph_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist) {
+    if (p->mode == INFERNT_MODE_EAGER) return record_step(p, st, mode, input, logits, hist);
     for (auto& e : p->graphs)
         if (e.mode == mode && e.input == input && e.logits == logits && e.hist == hist) {
             INFERNT_CUDA_TRY(cudaGraphLaunch(e.exec, st));
@@ -227,15 +231,31 @@ int run_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, flo
     return INFERNT_OK;
 }
 
+// `steps` decode steps from the current device state.
+int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist, int steps) {
+    if (!logits) logits = p->logits;
+    if (p->mode == INFERNT_MODE_PERSISTENT) {
+        MegaParams m = p->mega;
+        m.input = mode == kInputVector ? input : nullptr;
+        m.logits = logits;
+        m.hist = hist;
+        m.steps = steps;
+        INFERNT_CUDA_TRY(launch_mega(m, p->cfg.weight_dtype, p->mega_ctas, st));
+        return INFERNT_OK;
+    }
+    for (int s = 0; s < steps; ++s)
+        if (int r = run_graph_step(p, st, mode, input, logits, hist)) return r;
+    return INFERNT_OK;
+}
+
 int validate_config(const infernt_llama_config* c) {
     INFERNT_REQUIRE(c, "plan: null config");
-    INFERNT_REQUIRE(c->vocab_size > 0 && c->hidden_size > 0 && c->num_layers > 0 &&
-                        c->num_attention_heads > 0 && c->num_key_value_heads > 0 &&
-                        c->intermediate_size > 0 && c->max_seq_len > 0 && c->head_dim > 0,
+    INFERNT_REQUIRE(c->vocab_size > 0 && c->hidden_size > 0 && c->num_layers > 0 && c->num_attention_heads > 0 &&
+                        c->num_key_value_heads > 0 && c->intermediate_size > 0 && c->max_seq_len > 0 &&
+                        c->head_dim > 0,
                     "plan: every dimension must be positive");
     INFERNT_REQUIRE(c->hidden_size % 4 == 0 && c->intermediate_size % 4 == 0,
-                    "plan: hidden %d and intermediate %d must be multiples of 4", c->hidden_size,
-                    c->intermediate_size);
+                    "plan: hidden %d and intermediate %d must be multiples of 4", c->hidden_size, c->intermediate_size);
     INFERNT_REQUIRE(c->weight_dtype == INFERNT_DTYPE_F32 || c->weight_dtype == INFERNT_DTYPE_BF16,
                     "plan: weight_dtype %d", c->weight_dtype);
     INFERNT_REQUIRE(c->vocab_size <= 1 << 30 && (long long)c->max_seq_len * c->head_dim < (1ll << 31),
@@ -243,20 +263,196 @@ int validate_config(const infernt_llama_config* c) {
     return attention_shape_check(c->num_attention_heads, c->num_key_value_heads, c->head_dim, 1);
 }
 
+// Whether the persistent kernel applies: projection inputs in 512-column
+// blocks, 16-byte aligned weights, and the shared memory budget.
+bool mega_eligible(const infernt_plan* p) {
+    const infernt_llama_config& c = p->cfg;
+    if (c.hidden_size % kPiece || p->qs % kPiece || c.intermediate_size % kPiece) return false;
+    for (const void* w : p->w)
+        if (!aligned16(w)) return false;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, current_device());
+    return coop != 0;
+}
+
+int build_mega(infernt_plan* p) {
+    const infernt_llama_config& c = p->cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, L = c.num_layers, V = c.vocab_size;
+    const int dt = c.weight_dtype;
+    const int EB = dt == INFERNT_DTYPE_BF16 ? 2 : 4;
+    const int R = mega_tile_rows(dt);
+    const int G = c.num_attention_heads / c.num_key_value_heads;
+    auto groups = [](int rows, int r) { return (rows + r - 1) / r; };
+
+    // tensor maps: per layer q k v o down (R-row boxes), gate up (R/2-row boxes); lm_head
+    std::vector<CUtensorMap> maps(7 * L + 1);
+    for (int l = 0; l < L; ++l) {
+        const void* const* lw = p->w.data() + 3 + 9 * l;
+        CUtensorMap* m = &maps[7 * l];
+        INFERNT_CUDA_TRY(encode_weight_map(&m[0], lw[1], p->qs, H, EB, R));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[1], lw[2], p->kvs, H, EB, R));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[2], lw[3], p->kvs, H, EB, R));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[3], lw[4], H, p->qs, EB, R));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[4], lw[6], I, H, EB, R / 2));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[5], lw[7], I, H, EB, R / 2));
+        INFERNT_CUDA_TRY(encode_weight_map(&m[6], lw[8], H, I, EB, R));
+    }
+    INFERNT_CUDA_TRY(encode_weight_map(&maps[7 * L], p->w[2], V, H, EB, R));
+
+    std::vector<MegaPhase> ph;
+    long long max_groups = 1;
+    auto gemv = [&](int epi, int ns, std::initializer_list<int> map, std::initializer_list<int> rows, int units,
+                    int K, const float* x, const float* norm, float* out, const float* res, float* x_copy) {
+        MegaPhase P;
+        memset(&P, 0, sizeof(P));
+        P.kind = kPhGemv;
+        P.epi = epi;
+        P.ns = ns;
+        P.nseg = (int)map.size();
+        int i = 0;
+        for (int m : map) P.map[i++] = m;
+        i = 0;
+        P.groups = 0;
+        for (int r : rows) {
+            P.seg_rows[i] = r;
+            P.seg_groups[i] = ns == 2 ? groups(r, R / 2) : groups(r, R);
+            if (ns == 1 || i == 0) P.groups += P.seg_groups[i];
+            ++i;
+        }
+        P.units = units;
+        P.K = K;
+        P.cb = K / kPiece;
+        P.tiles = (long long)P.groups * P.cb;
+        P.x = x;
+        P.norm_w = norm;
+        P.eps = c.rms_norm_eps;
+        P.out = out;
+        P.res = res;
+        P.x_copy = x_copy;
+        if (P.groups > max_groups) max_groups = P.groups;
+        ph.push_back(P);
+    };
+    for (int l = 0; l < L; ++l) {
+        const void* const* lw = p->w.data() + 3 + 9 * l;
+        const int m = 7 * l;
+        gemv(kEpiStore, 1, {m + 0, m + 1, m + 2}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
+             l == 0 ? nullptr : p->hidden, static_cast<const float*>(lw[0]), p->qkv, nullptr,
+             l == 0 ? p->hidden : nullptr);
+        MegaPhase A;
+        memset(&A, 0, sizeof(A));
+        A.kind = kPhAttn;
+        A.layer = l;
+        ph.push_back(A);
+        gemv(kEpiResidual, 1, {m + 3}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
+        gemv(kEpiSwiGLU, 2, {m + 4, m + 5}, {I, I}, I, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
+             nullptr, nullptr);
+        gemv(kEpiResidual, 1, {m + 6}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
+    }
+    gemv(kEpiArgmax, 1, {7 * L}, {V}, V, H, p->hidden, static_cast<const float*>(p->w[1]), nullptr, nullptr,
+         nullptr);
+
+    int x_floats = H;
+    if (p->qs > x_floats) x_floats = p->qs;
+    if (I > x_floats) x_floats = I;
+    const int af = attn_smem_floats(G, c.head_dim);
+    if (af > x_floats) x_floats = af;
+    x_floats = (x_floats + 3) / 4 * 4;
+
+    INFERNT_CUDA_TRY(mega_prepare());
+    int optin = 0;
+    INFERNT_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, current_device()));
+    int slots = 16;
+    while (slots >= 4 && mega_smem_bytes(slots, x_floats) > optin - 1024) --slots;
+    INFERNT_REQUIRE(slots >= 4, "persistent decode: shared memory budget too small");
+    const int smem = mega_smem_bytes(slots, x_floats);
+    const int per_sm = mega_occupancy(dt, smem);
+    INFERNT_REQUIRE(per_sm >= 1, "persistent decode: kernel does not fit on an SM");
+    const int ctas = sm_count();
+
+    // device memory: maps | phases | cache pointers | barrier | split-K partials | tickets | argmax
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t b_maps = al(sizeof(CUtensorMap) * maps.size());
+    const size_t b_ph = al(sizeof(MegaPhase) * ph.size());
+    const size_t b_kv = al(sizeof(float*) * 2 * L);
+    const size_t b_bar = 256;
+    const size_t b_part = al(sizeof(float) * ctas * 2 * 16);
+    const size_t b_cnt = al(sizeof(unsigned) * max_groups);
+    const size_t b_am = al(sizeof(float) * ctas) + al(sizeof(int) * ctas) + 256;
+    const size_t total = b_maps + b_ph + b_kv + b_bar + b_part + b_cnt + b_am;
+    INFERNT_CUDA_TRY(cudaMalloc(&p->mega_mem, total));
+    INFERNT_CUDA_TRY(cudaMemset(p->mega_mem, 0, total));
+    char* b = static_cast<char*>(p->mega_mem);
+    CUtensorMap* d_maps = reinterpret_cast<CUtensorMap*>(b);
+    INFERNT_CUDA_TRY(cudaMemcpy(d_maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice));
+    b += b_maps;
+    MegaPhase* d_ph = reinterpret_cast<MegaPhase*>(b);
+    INFERNT_CUDA_TRY(cudaMemcpy(d_ph, ph.data(), sizeof(MegaPhase) * ph.size(), cudaMemcpyHostToDevice));
+    b += b_ph;
+    float** d_kv = reinterpret_cast<float**>(b);
+    std::vector<float*> kvp(p->kc);
+    kvp.insert(kvp.end(), p->vc.begin(), p->vc.end());
+    INFERNT_CUDA_TRY(cudaMemcpy(d_kv, kvp.data(), sizeof(float*) * 2 * L, cudaMemcpyHostToDevice));
+    b += b_kv;
+    unsigned* d_bar = reinterpret_cast<unsigned*>(b);
+    b += b_bar;
+    float* d_part = reinterpret_cast<float*>(b);
+    b += b_part;
+    unsigned* d_cnt = reinterpret_cast<unsigned*>(b);
+    b += b_cnt;
+    float* d_amv = reinterpret_cast<float*>(b);
+    b += al(sizeof(float) * ctas);
+    int* d_ami = reinterpret_cast<int*>(b);
+    b += al(sizeof(int) * ctas);
+    unsigned* d_amc = reinterpret_cast<unsigned*>(b);
+
+    MegaParams& m = p->mega;
+    memset(&m, 0, sizeof(m));
+    m.phases = d_ph;
+    m.nphases = (int)ph.size();
+    m.maps = d_maps;
+    m.emb = static_cast<const float*>(p->w[0]);
+    m.vocab = V;
+    m.kc = d_kv;
+    m.vc = d_kv + L;
+    m.attn.qkv = p->qkv;
+    m.attn.out = p->attn;
+    m.attn.part = p->attn_part;
+    m.attn.counter = p->attn_counter;
+    m.attn.nq = c.num_attention_heads;
+    m.attn.nkv = c.num_key_value_heads;
+    m.attn.D = c.head_dim;
+    m.attn.max_seq = c.max_seq_len;
+    m.attn.splits = p->splits;
+    m.attn.theta = c.rope_theta;
+    m.attn.scale = 1.0f / sqrtf((float)c.head_dim);
+    m.attn.err = p->err;
+    m.state = p->state;
+    m.err = p->err;
+    m.bar = d_bar;
+    m.part = d_part;
+    m.gcnt = d_cnt;
+    m.am_val = d_amv;
+    m.am_idx = d_ami;
+    m.am_cnt = d_amc;
+    m.ring_slots = slots;
+    m.x_floats = x_floats;
+    p->mega_ctas = ctas;
+    return INFERNT_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
-int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights,
-                        float* const* k_cache, float* const* v_cache, int use_graph,
-                        infernt_plan** out) {
+int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights, float* const* k_cache,
+                        float* const* v_cache, int mode, infernt_plan** out) {
     INFERNT_REQUIRE(out, "plan_create: null output");
     *out = nullptr;
     if (int s = validate_config(cfg)) return s;
     INFERNT_REQUIRE(weights && k_cache && v_cache, "plan_create: null weights or cache");
+    INFERNT_REQUIRE(mode >= INFERNT_MODE_EAGER && mode <= INFERNT_MODE_PERSISTENT, "plan_create: mode %d", mode);
     const int L = cfg->num_layers;
-    for (int i = 0; i < 3 + 9 * L; ++i)
-        INFERNT_REQUIRE(weights[i], "plan_create: weight pointer %d is null", i);
+    for (int i = 0; i < 3 + 9 * L; ++i) INFERNT_REQUIRE(weights[i], "plan_create: weight pointer %d is null", i);
     for (int l = 0; l < L; ++l) INFERNT_REQUIRE(k_cache[l] && v_cache[l], "plan_create: cache layer %d null", l);
     INFERNT_CUDA_TRY(gemv_prepare());
 
@@ -268,8 +464,8 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     p->vc.assign(v_cache, v_cache + L);
     p->qs = cfg->num_attention_heads * cfg->head_dim;
     p->kvs = cfg->num_key_value_heads * cfg->head_dim;
-    p->use_graph = use_graph != 0;
-    int splits = sm_count() / cfg->num_key_value_heads;
+    p->mode = mode;
+    const int splits = sm_count() / cfg->num_key_value_heads;
     p->splits = splits < 1 ? 1 : splits;
 
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
@@ -279,27 +475,28 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     const size_t b_hid = al(sizeof(float) * cfg->hidden_size);
     const size_t b_log = al(sizeof(float) * cfg->vocab_size);
     const size_t b_state = 256;
-    const size_t b_aws = attention_workspace_bytes(cfg->num_attention_heads, cfg->num_key_value_heads,
-                                                   cfg->head_dim, p->splits);
+    const size_t b_aws =
+        attention_workspace_bytes(cfg->num_attention_heads, cfg->num_key_value_heads, cfg->head_dim, p->splits);
     const size_t b_lm = al(sizeof(LmWs));
     const size_t total = b_qkv + b_attn + b_act + b_hid + b_log + b_state + b_aws + b_lm;
     cudaError_t e = cudaMalloc(&p->scratch, total);
-    if (e != cudaSuccess) {
-        delete p;
-        return cuda_fail(e, "cudaMalloc(plan scratch)");
-    }
-    e = cudaMemset(p->scratch, 0, total);
+    if (e == cudaSuccess) e = cudaMemset(p->scratch, 0, total);
     if (e != cudaSuccess) {
         cudaFree(p->scratch);
         delete p;
-        return cuda_fail(e, "cudaMemset(plan scratch)");
+        return cuda_fail(e, "plan scratch allocation");
     }
     char* b = static_cast<char*>(p->scratch);
-    p->qkv = reinterpret_cast<float*>(b); b += b_qkv;
-    p->attn = reinterpret_cast<float*>(b); b += b_attn;
-    p->act = reinterpret_cast<float*>(b); b += b_act;
-    p->hidden = reinterpret_cast<float*>(b); b += b_hid;
-    p->logits = reinterpret_cast<float*>(b); b += b_log;
+    p->qkv = reinterpret_cast<float*>(b);
+    b += b_qkv;
+    p->attn = reinterpret_cast<float*>(b);
+    b += b_attn;
+    p->act = reinterpret_cast<float*>(b);
+    b += b_act;
+    p->hidden = reinterpret_cast<float*>(b);
+    b += b_hid;
+    p->logits = reinterpret_cast<float*>(b);
+    b += b_log;
     p->state = reinterpret_cast<int*>(b);
     p->err = reinterpret_cast<unsigned*>(b + 64);
     b += b_state;
@@ -309,6 +506,17 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     p->attn_counter = reinterpret_cast<unsigned*>(b + al(part));
     b += b_aws;
     p->lm_ws = reinterpret_cast<LmWs*>(b);
+
+    if (p->mode == INFERNT_MODE_PERSISTENT) {
+        if (mega_eligible(p)) {
+            if (int s = build_mega(p)) {
+                infernt_plan_destroy(p);
+                return s;
+            }
+        } else {
+            p->mode = INFERNT_MODE_GRAPH;
+        }
+    }
     *out = p;
     return INFERNT_OK;
 }
@@ -317,47 +525,48 @@ int infernt_plan_destroy(infernt_plan* p) {
     if (!p) return INFERNT_OK;
     for (auto& e : p->graphs) cudaGraphExecDestroy(e.exec);
     if (p->cap_stream) cudaStreamDestroy(p->cap_stream);
+    cudaFree(p->mega_mem);
     cudaFree(p->scratch);
     delete p;
     return INFERNT_OK;
 }
 
-int infernt_plan_forward(infernt_plan* p, const float* input_embedding, int position, float* logits,
-                         void* stream) {
+int infernt_plan_mode(const infernt_plan* p) { return p ? p->mode : -1; }
+
+int infernt_plan_forward(infernt_plan* p, const float* input_embedding, int position, float* logits, void* stream) {
     INFERNT_REQUIRE(p && input_embedding, "plan_forward: null argument");
-    INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len,
-                    "plan_forward: position %d outside [0, %d)", position, p->cfg.max_seq_len);
+    INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len, "plan_forward: position %d outside [0, %d)",
+                    position, p->cfg.max_seq_len);
+    INFERNT_REQUIRE(aligned16(input_embedding), "plan_forward: input must be 16-byte aligned");
     cudaStream_t st = (cudaStream_t)stream;
     set_state_kernel<<<1, 1, 0, st>>>(p->state, 0, position);
     INFERNT_CUDA_TRY(cudaGetLastError());
-    return run_step(p, st, kModeInput, input_embedding, logits, nullptr);
+    return run_steps(p, st, kInputVector, input_embedding, logits, nullptr, 1);
 }
 
 int infernt_plan_decode(infernt_plan* p, int token, int position, float* logits, void* stream) {
     INFERNT_REQUIRE(p, "plan_decode: null plan");
     INFERNT_REQUIRE(token >= 0 && token < p->cfg.vocab_size, "plan_decode: token %d outside [0, %d)", token,
                     p->cfg.vocab_size);
-    INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len,
-                    "plan_decode: position %d outside [0, %d)", position, p->cfg.max_seq_len);
+    INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len, "plan_decode: position %d outside [0, %d)",
+                    position, p->cfg.max_seq_len);
     cudaStream_t st = (cudaStream_t)stream;
     set_state_kernel<<<1, 1, 0, st>>>(p->state, token, position);
     INFERNT_CUDA_TRY(cudaGetLastError());
-    return run_step(p, st, kModeToken, nullptr, logits, nullptr);
+    return run_steps(p, st, kInputToken, nullptr, logits, nullptr, 1);
 }
 
-int infernt_plan_decode_chain(infernt_plan* p, int token, int position, int steps, int* tokens_dev,
-                              void* stream) {
+int infernt_plan_decode_chain(infernt_plan* p, int token, int position, int steps, int* tokens_dev, void* stream) {
     INFERNT_REQUIRE(p, "plan_decode_chain: null plan");
     INFERNT_REQUIRE(token >= 0 && token < p->cfg.vocab_size, "plan_decode_chain: token %d", token);
     INFERNT_REQUIRE(steps >= 0 && position >= 0 && (long long)position + steps <= p->cfg.max_seq_len,
-                    "plan_decode_chain: positions [%d, %d) exceed max_seq_len %d", position,
-                    position + steps, p->cfg.max_seq_len);
+                    "plan_decode_chain: positions [%d, %d) exceed max_seq_len %d", position, position + steps,
+                    p->cfg.max_seq_len);
+    if (steps == 0) return INFERNT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     set_state_kernel<<<1, 1, 0, st>>>(p->state, token, position);
     INFERNT_CUDA_TRY(cudaGetLastError());
-    for (int s = 0; s < steps; ++s)
-        if (int r = run_step(p, st, kModeToken, nullptr, nullptr, tokens_dev)) return r;
-    return INFERNT_OK;
+    return run_steps(p, st, kInputToken, nullptr, nullptr, tokens_dev, steps);
 }
 
 int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
@@ -370,8 +579,8 @@ int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
     INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
     if (err) {
         cudaMemsetAsync(p->err, 0, sizeof(unsigned), st);
-        return fail(INFERNT_ERR_DEVICE, "decode kernels reported error word 0x%x (1: wait timeout, 2: position, "
-                    "4: token id)", err);
+        return fail(INFERNT_ERR_DEVICE,
+                    "decode kernels reported error word 0x%x (1: wait timeout, 2: position, 4: token id)", err);
     }
     *token_host = buf[3];
     return INFERNT_OK;
@@ -379,6 +588,21 @@ int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
 
 float* infernt_plan_logits(infernt_plan* p) { return p ? p->logits : nullptr; }
 
-int infernt_plan_kernels_per_step(const infernt_plan* p) { return p ? 5 * p->cfg.num_layers + 1 : 0; }
+size_t infernt_plan_trace_entries(const infernt_plan* p, int steps) {
+    if (!p || p->mode != INFERNT_MODE_PERSISTENT || steps <= 0) return 0;
+    return (size_t)2 * steps * p->mega.nphases * kTraceFields;
+}
+
+int infernt_plan_set_trace(infernt_plan* p, unsigned long long* trace_dev) {
+    INFERNT_REQUIRE(p, "plan_set_trace: null plan");
+    INFERNT_REQUIRE(p->mode == INFERNT_MODE_PERSISTENT || !trace_dev, "plan_set_trace: persistent mode only");
+    p->mega.trace = trace_dev;
+    return INFERNT_OK;
+}
+
+int infernt_plan_kernels_per_step(const infernt_plan* p) {
+    if (!p) return 0;
+    return p->mode == INFERNT_MODE_PERSISTENT ? 1 : 5 * p->cfg.num_layers + 1;
+}
 
 }  // extern "C"

@@ -20,6 +20,9 @@ int fail(int status, const char* fmt, ...) {
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
+    // the error is reported here; clear the runtime's last-error slot so a
+    // later launch check does not report it a second time
+    cudaGetLastError();
     if (e == cudaErrorMemoryAllocation)
         return fail(INFERNT_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
     if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver)

@@ -56,7 +56,8 @@ def test_status_strings():
     lambda l: l.infernt_rmsnorm_gemv(8, 8, 4, None, 0, None, 0, 512, 7, 8, None, 1e-5, None),
     lambda l: l.infernt_attention_decode(8, 8, 8, 8, 32, 4, 64, 16, 16, 1e4, 4, 8, None),
     lambda l: l.infernt_attention_decode(8, 8, 8, 8, 32, 5, 64, 16, 3, 1e4, 4, 8, None),
-    lambda l: l.infernt_attention_decode(8, 8, 8, 8, 32, 4, 48, 16, 3, 1e4, 4, 8, None),
+    lambda l: l.infernt_attention_decode(8, 8, 8, 8, 32, 4, 47, 16, 3, 1e4, 4, 8, None),
+    lambda l: l.infernt_attention_decode(8, 8, 8, 8, 32, 4, 256, 16, 3, 1e4, 4, 8, None),
     lambda l: l.infernt_kv_cache_append(8, 8, 8, 8, 2, 4, 8, 8, None),
 ])
 def test_bad_arguments_are_rejected_without_a_launch(call):

@@ -34,8 +34,10 @@ def top2_gap(logits):
     return float(s[-1] - s[-2])
 
 
-def run_parity(cfg, seed, steps, bf16=False, start_tokens=4):
+def run_parity(cfg, seed, steps, bf16=False, start_tokens=4, mode=None, expect_mode=None):
     eng = ib.Engine(cfg, seed=seed)
+    if mode is not None:
+        eng.set_mode(mode)
     orc = O.LlamaOracle(cfg, seed=seed, round_bf16=bf16)
     prompt = O.prompt(start_tokens, seed, 3, cfg.vocab_size)
     near_ties = []
@@ -49,23 +51,42 @@ def run_parity(cfg, seed, steps, bf16=False, start_tokens=4):
             assert top2_gap(want_logits) < 1e-4, (pos, mine, want_tok)
             near_ties.append(pos)
         tok = want_tok  # follow the oracle's path
+    if expect_mode is not None:
+        assert eng.mode == expect_mode
     eng.close()
     return near_ties
 
 
-@pytest.mark.parametrize("cfg", [SMALL_FAST, SMALL_PLAIN], ids=["tma_path", "plain_path"])
-def test_decode_matches_oracle(cfg):
-    run_parity(cfg, seed=5, steps=20)
+@pytest.mark.parametrize("cfg,mode,expect", [
+    (SMALL_FAST, ib.MODE_PERSISTENT, ib.MODE_PERSISTENT),
+    (SMALL_FAST, ib.MODE_GRAPH, ib.MODE_GRAPH),
+    (SMALL_FAST, ib.MODE_EAGER, ib.MODE_EAGER),
+    (SMALL_PLAIN, ib.MODE_PERSISTENT, ib.MODE_GRAPH),  # h=128: falls back to the kernel sequence
+], ids=["persistent", "graph_tma", "eager_tma", "graph_plain"])
+def test_decode_matches_oracle(cfg, mode, expect):
+    run_parity(cfg, seed=5, steps=20, mode=mode, expect_mode=expect)
 
 
-def test_decode_bf16_matches_oracle_on_rounded_weights():
-    run_parity(SMALL_FAST.with_(weight_dtype=ib.DTYPE_BF16), seed=6, steps=12, bf16=True)
+@pytest.mark.parametrize("mode", [ib.MODE_PERSISTENT, ib.MODE_GRAPH], ids=["persistent", "graph"])
+def test_decode_bf16_matches_oracle_on_rounded_weights(mode):
+    run_parity(SMALL_FAST.with_(weight_dtype=ib.DTYPE_BF16), seed=6, steps=12, bf16=True, mode=mode,
+               expect_mode=mode)
 
 
-def test_chain_equals_stepwise():
+def test_persistent_split_groups_match_oracle():
+    """Shapes whose tile count is not a multiple of the CTA count, so row
+    groups are shared between CTAs and merged by the split-K ticket."""
+    cfg = ib.ModelConfig(vocab_size=3001, hidden_size=1024, num_layers=2, num_attention_heads=16,
+                         num_key_value_heads=4, intermediate_size=2560, max_seq_len=96)
+    run_parity(cfg, seed=12, steps=10, mode=ib.MODE_PERSISTENT, expect_mode=ib.MODE_PERSISTENT)
+
+
+@pytest.mark.parametrize("mode", [ib.MODE_PERSISTENT, ib.MODE_GRAPH], ids=["persistent", "graph"])
+def test_chain_equals_stepwise(mode):
     """Device-chained decode produces the same tokens as host-driven steps."""
     cfg = SMALL_FAST
     eng = ib.Engine(cfg, seed=7)
+    eng.set_mode(mode)
     toks = []
     t = 11
     for pos in range(30):

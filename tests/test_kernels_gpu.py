@@ -18,9 +18,23 @@ pytestmark = pytest.mark.gpu
 REL = 1e-5
 
 
+_KEEP = []  # device buffers stay alive until the test's kernels are done
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    if _KEEP:
+        import torch
+        torch.cuda.synchronize()
+        _KEEP.clear()
+
+
 def dev(torch, a, dtype=None):
     t = torch.as_tensor(np.asarray(a, dtype=np.float32)).cuda()
-    return t if dtype is None else t.to(dtype)
+    t = t if dtype is None else t.to(dtype)
+    _KEEP.append(t)
+    return t
 
 
 def host(torch, t):
@@ -310,5 +324,7 @@ def test_attention_decode_vs_oracle(cuda, nq, nkv, D, pos, splits):
         sc = O.attention_scores(q, kc2, nq, nkv, D, pos + 1, ms, 1.0 / np.sqrt(np.float32(D)))
         want = O.attention_values(O.softmax(sc, nq, pos + 1), vc2, nq, nkv, D, pos + 1, ms)
         close(host(cuda, out), want, rel=2e-5)
-        close(host(cuda, kd), kc2, rel=1e-6)
+        # RoPE angle = position * freq: one ulp of freq (powf differs by an ulp
+        # between the device and glibc) moves the angle by ~position ulps
+        close(host(cuda, kd), kc2, rel=1e-6 + 2e-7 * pos)
         assert np.array_equal(host(cuda, vd), vc2)
