@@ -18,6 +18,11 @@ LIB_PATH = os.path.join(HERE, "lib", "libinfernt_b200.so")
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
+# Phase-timeline fields (infernt_plan_set_trace): phase start, input loaded,
+# work done, barrier passed, producer issued last tile (ns); consumer wait
+# cycles, producer wait cycles.
+TRACE_FIELDS = 7
+
 MODE_EAGER = 0
 MODE_GRAPH = 1
 MODE_PERSISTENT = 2
@@ -267,9 +272,9 @@ class Engine:
         passed, producer issued the phase's last tile."""
         import numpy as np
         nph = 5 * self.cfg.num_layers + 1
-        out = np.zeros(2 * steps * nph * 5, dtype=np.uint64)
+        out = np.zeros(2 * steps * nph * TRACE_FIELDS, dtype=np.uint64)
         call("infernt_engine_trace_chain", self._h, token, position, steps, out.ctypes.data, out.size)
-        return out.reshape(2, steps, nph, 5).astype(np.int64)
+        return out.reshape(2, steps, nph, TRACE_FIELDS).astype(np.int64)
 
     def weight_ptrs(self):
         n = 3 + 9 * self.cfg.num_layers

@@ -47,11 +47,34 @@ struct AttnArgs {
     int nq, nkv, D, max_seq, splits;
     float theta, scale;
     unsigned* err;
+    const float2* rope;  // optional (cos, sin) table [max_seq][D/2]; NULL: computed in place
 };
+
+// The (cos, sin) RoPE factors of pair d at `pos` (cuda/rope.cu:13-16).
+__device__ __forceinline__ float2 rope_factors(int d, int D, int pos, float theta) {
+    const float freq = 1.0f / powf(theta, (float)(2 * d) / (float)D);
+    const float angle = (float)pos * freq;
+    return make_float2(cosf(angle), sinf(angle));
+}
+
+// cuda/rope.cu:21-24 with precomputed factors.
+__device__ __forceinline__ void rope_apply(float& a, float& b, float2 cs) {
+    const float a0 = a, b0 = b;
+    a = a0 * cs.x - b0 * cs.y;
+    b = b0 * cs.x + a0 * cs.y;
+}
 
 __host__ __device__ inline int attn_smem_floats(int G, int D) {
     // q [G][D] | K tile [T][D+1] | V tile [T][D] | p [G][T] | k_new [D] | v_new [D] | flag
     return G * D + kAttnTile * (D + 1) + kAttnTile * D + G * kAttnTile + 2 * D + 4;
+}
+
+// Positions per K/V tile of the bulk-copy variant in the persistent kernel.
+constexpr int kAttnBulkTile = 32;
+
+__host__ __device__ inline int attn_bulk_smem_floats(int G, int D) {
+    // q [G][D] | K tile [T][D] | V tile [T][D] | p [G][T] | RoPE row [D] | k_new [D] | v_new [D] | flag
+    return G * D + 2 * kAttnBulkTile * D + G * kAttnBulkTile + 3 * D + 4;
 }
 
 __device__ __forceinline__ void rope_pair(float& a, float& b, int d, int D, int pos, float theta) {
@@ -100,7 +123,7 @@ __device__ void attention_item(const AttnArgs& a, int kvh, int split, int pos, f
     for (int i = tid; i < G * half; i += NT) {
         const int h = i / half, d = i % half;
         float x0 = __ldcg(qsrc + h * D + d), x1 = __ldcg(qsrc + h * D + d + half);
-        rope_pair(x0, x1, d, D, pos, a.theta);
+        rope_apply(x0, x1, a.rope ? __ldg(a.rope + (size_t)pos * half + d) : rope_factors(d, D, pos, a.theta));
         qs[h * D + d] = x0;
         qs[h * D + d + half] = x1;
     }
@@ -111,7 +134,7 @@ __device__ void attention_item(const AttnArgs& a, int kvh, int split, int pos, f
         float* vdst = a.v_cache + ((size_t)kvh * a.max_seq + pos) * D;
         for (int d = tid; d < half; d += NT) {
             float x0 = __ldcg(ksrc + d), x1 = __ldcg(ksrc + d + half);
-            rope_pair(x0, x1, d, D, pos, a.theta);
+            rope_apply(x0, x1, a.rope ? __ldg(a.rope + (size_t)pos * half + d) : rope_factors(d, D, pos, a.theta));
             knew[d] = x0;
             knew[d + half] = x1;
             kdst[d] = x0;
@@ -139,19 +162,36 @@ __device__ void attention_item(const AttnArgs& a, int kvh, int split, int pos, f
     for (int t0 = c0; t0 < c1; t0 += kAttnTile) {
         const int tl = min(kAttnTile, c1 - t0);
         // stage K and V rows of the tile (the row at `pos` comes from this item's copy)
-        for (int i = tid; i < tl * D; i += NT) {
-            const int p = i / D, d = i % D;
-            const int gp = t0 + p;
-            float kv, vv;
-            if (gp == pos) {
-                kv = knew[d];
-                vv = vnew[d];
-            } else {
-                kv = __ldcg(kbase + (size_t)gp * D + d);
-                vv = __ldcg(vbase + (size_t)gp * D + d);
+        if ((D & 3) == 0) {
+            const int n4 = tl * D / 4;
+#pragma unroll 4
+            for (int i = tid; i < n4; i += NT) {
+                const int p = (4 * i) / D, d = (4 * i) % D;
+                const int gp = t0 + p;
+                float4 kv, vv;
+                if (gp == pos) {
+                    kv = make_float4(knew[d], knew[d + 1], knew[d + 2], knew[d + 3]);
+                    vv = make_float4(vnew[d], vnew[d + 1], vnew[d + 2], vnew[d + 3]);
+                } else {
+                    kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)gp * D + d));
+                    vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)gp * D + d));
+                }
+                float* kd = ks + p * (D + 1) + d;
+                kd[0] = kv.x;
+                kd[1] = kv.y;
+                kd[2] = kv.z;
+                kd[3] = kv.w;
+                *reinterpret_cast<float4*>(vs + p * D + d) = vv;
             }
-            ks[p * (D + 1) + d] = kv;
-            vs[p * D + d] = vv;
+        } else {
+            for (int i = tid; i < tl * D; i += NT) {
+                const int p = i / D, d = i % D;
+                const int gp = t0 + p;
+                const float kv = gp == pos ? knew[d] : __ldcg(kbase + (size_t)gp * D + d);
+                const float vv = gp == pos ? vnew[d] : __ldcg(vbase + (size_t)gp * D + d);
+                ks[p * (D + 1) + d] = kv;
+                vs[p * D + d] = vv;
+            }
         }
         named_sync(1, NT);
 #pragma unroll

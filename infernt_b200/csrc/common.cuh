@@ -88,6 +88,28 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// 1-D bulk copy global -> shared without an L2 hint (data reused in L2).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) writes to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Orders generic-proxy writes to global memory that this thread has
+// observed (its own, or other threads' through an acquire) before its later
+// async-proxy (bulk copy) reads of the same memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // 2-D tiled TMA load of one box at element coordinates (x inner, y outer)
 // from the tensor map at `map` (global or parameter memory) into shared
 // memory, completion signalled on `bar`.  x * element size must be a
@@ -99,6 +121,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, i
         "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// 2-D tiled TMA prefetch of one box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_map(const void* map) {

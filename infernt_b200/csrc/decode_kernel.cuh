@@ -13,7 +13,7 @@ enum MegaKind : int { kPhGemv = 0, kPhAttn = 1 };
 // One phase of a decode step.  GEMV phases stream their weights through the
 // shared-memory ring as tiles of (R rows x 512 columns); R = 8 FP32 / 16
 // bf16 (gate/up tiles carry R/2 rows of each).
-struct MegaPhase {
+struct alignas(16) MegaPhase {
     int kind;           // MegaKind
     int epi;            // EpiKind (gemv.cuh)
     int ns;             // 1, or 2 for paired gate/up
@@ -33,7 +33,11 @@ struct MegaPhase {
     const float* res;   // residual source (out = res + y)
     float* x_copy;      // layer 0: the raw input row is copied here (residual stream)
     int layer;          // attention phases: KV-cache layer
+    float* kc;          // attention phases: the layer's K and V caches [N_kv, max_seq, D]
+    float* vc;
 };
+// descriptors are bulk-copied into shared memory ahead of their phase
+static_assert(sizeof(MegaPhase) % 16 == 0, "MegaPhase must be a multiple of 16 bytes");
 
 struct MegaParams {
     const MegaPhase* phases;
@@ -53,27 +57,33 @@ struct MegaParams {
     // scratch
     int* state;          // {token, position, step, last token}
     unsigned* err;
-    unsigned* bar;       // grid barrier: [0] arrivals, [32] generation
-    float* part;         // split-K partials [gridDim][2][16]
-    unsigned* gcnt;      // split-K group tickets
+    unsigned long long* bar;       // grid-barrier arrivals (only ever grows)
+    unsigned long long bar_base;   // its value when this launch starts
     float* am_val;       // LM-head argmax partials [gridDim]
     int* am_idx;
     unsigned* am_cnt;
     int ring_slots;
     int x_floats;        // shared floats for the input vector / attention scratch
+    int l2_prefetch_tiles;  // tiles the L2 prefetch runs ahead of the ring loads
     // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
     // last CTA, per (step, phase): [phase start, input loaded, work done,
-    // barrier passed, producer issued the phase's last tile]
+    // barrier passed, producer issued the phase's last tile, SM cycles
+    // consumer warp 0 waited for full slots, SM cycles the producer waited
+    // for free slots while issuing the phase's tiles]
     unsigned long long* trace;
 };
 
-constexpr int kTraceFields = 5;
+constexpr int kTraceFields = 7;
 
 // Rows per tile for a weight type.
 inline int mega_tile_rows(int weight_dtype) { return weight_dtype == 1 ? 16 : 8; }
 
 // Dynamic shared memory of the persistent kernel.
 int mega_smem_bytes(int ring_slots, int x_floats);
+// Largest ring the kernel's group hand-off supports.
+int mega_max_ring_slots();
+// Static shared memory of the kernel instantiation.
+int mega_static_smem(int weight_dtype);
 
 // Launches the cooperative persistent kernel (grid = `ctas`).
 cudaError_t launch_mega(const MegaParams& p, int weight_dtype, int ctas, cudaStream_t stream);

@@ -35,6 +35,15 @@
 
 namespace infernt {
 
+// (cos, sin) RoPE factors for every position and pair, with the same device
+// functions the attention would otherwise evaluate per step.
+__global__ void rope_table_kernel(float2* tab, int max_seq, int D, float theta) {
+    const int half = D / 2;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)max_seq * half;
+         i += (long long)gridDim.x * blockDim.x)
+        tab[i] = rope_factors((int)(i % half), D, (int)(i / half), theta);
+}
+
 __global__ void set_state_kernel(int* state, int token, int pos) {
     state[0] = token;
     state[1] = pos;
@@ -63,6 +72,7 @@ struct infernt_plan {
     float* act = nullptr;
     float* hidden = nullptr;
     float* logits = nullptr;
+    float2* rope = nullptr;  // (cos, sin) table [max_seq][D/2]
     int* state = nullptr;  // {token, position, step, last token}
     unsigned* err = nullptr;
     float* attn_part = nullptr;
@@ -83,6 +93,7 @@ struct infernt_plan {
     void* mega_mem = nullptr;
     MegaParams mega;
     int mega_ctas = 0;
+    unsigned long long bar_epoch = 0;  // grid-barrier counter value at the next launch
 };
 
 namespace {
@@ -139,6 +150,7 @@ int record_step(infernt_plan* p, cudaStream_t st, int mode, const float* input, 
         at.theta = c.rope_theta;
         at.scale = 1.0f / sqrtf((float)c.head_dim);
         at.err = p->err;
+        at.rope = p->rope;
         INFERNT_CUDA_TRY(launch_attention_decode(at, st, true));
 
         memset(&a, 0, sizeof(a));
@@ -240,6 +252,8 @@ int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, fl
         m.logits = logits;
         m.hist = hist;
         m.steps = steps;
+        m.bar_base = p->bar_epoch;
+        p->bar_epoch += (unsigned long long)steps * m.nphases * p->mega_ctas;
         INFERNT_CUDA_TRY(launch_mega(m, p->cfg.weight_dtype, p->mega_ctas, st));
         return INFERNT_OK;
     }
@@ -270,6 +284,10 @@ bool mega_eligible(const infernt_plan* p) {
     if (c.hidden_size % kPiece || p->qs % kPiece || c.intermediate_size % kPiece) return false;
     for (const void* w : p->w)
         if (!aligned16(w)) return false;
+    // attention inputs arrive by bulk copies: whole rows of 16-byte multiples
+    if (c.head_dim % 4) return false;
+    for (int l = 0; l < c.num_layers; ++l)
+        if (!aligned16(p->kc[l]) || !aligned16(p->vc[l])) return false;
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, current_device());
     return coop != 0;
@@ -300,7 +318,7 @@ int build_mega(infernt_plan* p) {
     INFERNT_CUDA_TRY(encode_weight_map(&maps[7 * L], p->w[2], V, H, EB, R));
 
     std::vector<MegaPhase> ph;
-    long long max_groups = 1;
+
     auto gemv = [&](int epi, int ns, std::initializer_list<int> map, std::initializer_list<int> rows, int units,
                     int K, const float* x, const float* norm, float* out, const float* res, float* x_copy) {
         MegaPhase P;
@@ -329,7 +347,7 @@ int build_mega(infernt_plan* p) {
         P.out = out;
         P.res = res;
         P.x_copy = x_copy;
-        if (P.groups > max_groups) max_groups = P.groups;
+
         ph.push_back(P);
     };
     for (int l = 0; l < L; ++l) {
@@ -342,6 +360,8 @@ int build_mega(infernt_plan* p) {
         memset(&A, 0, sizeof(A));
         A.kind = kPhAttn;
         A.layer = l;
+        A.kc = p->kc[l];
+        A.vc = p->vc[l];
         ph.push_back(A);
         gemv(kEpiResidual, 1, {m + 3}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
         gemv(kEpiSwiGLU, 2, {m + 4, m + 5}, {I, I}, I, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
@@ -351,18 +371,21 @@ int build_mega(infernt_plan* p) {
     gemv(kEpiArgmax, 1, {7 * L}, {V}, V, H, p->hidden, static_cast<const float*>(p->w[1]), nullptr, nullptr,
          nullptr);
 
-    int x_floats = H;
+    // input vector + the norm weights behind it (RMSNorm phases), or the
+    // attention scratch, whichever is larger
+    int x_floats = 2 * H;
     if (p->qs > x_floats) x_floats = p->qs;
     if (I > x_floats) x_floats = I;
-    const int af = attn_smem_floats(G, c.head_dim);
+    const int af = attn_bulk_smem_floats(G, c.head_dim);
     if (af > x_floats) x_floats = af;
     x_floats = (x_floats + 3) / 4 * 4;
 
     INFERNT_CUDA_TRY(mega_prepare());
     int optin = 0;
     INFERNT_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, current_device()));
-    int slots = 16;
-    while (slots >= 4 && mega_smem_bytes(slots, x_floats) > optin - 1024) --slots;
+    int slots = mega_max_ring_slots();
+    const int budget = optin - mega_static_smem(dt) - 256;
+    while (slots >= 4 && mega_smem_bytes(slots, x_floats) > budget) --slots;
     INFERNT_REQUIRE(slots >= 4, "persistent decode: shared memory budget too small");
     const int smem = mega_smem_bytes(slots, x_floats);
     const int per_sm = mega_occupancy(dt, smem);
@@ -375,10 +398,8 @@ int build_mega(infernt_plan* p) {
     const size_t b_ph = al(sizeof(MegaPhase) * ph.size());
     const size_t b_kv = al(sizeof(float*) * 2 * L);
     const size_t b_bar = 256;
-    const size_t b_part = al(sizeof(float) * ctas * 2 * 16);
-    const size_t b_cnt = al(sizeof(unsigned) * max_groups);
     const size_t b_am = al(sizeof(float) * ctas) + al(sizeof(int) * ctas) + 256;
-    const size_t total = b_maps + b_ph + b_kv + b_bar + b_part + b_cnt + b_am;
+    const size_t total = b_maps + b_ph + b_kv + b_bar + b_am;
     INFERNT_CUDA_TRY(cudaMalloc(&p->mega_mem, total));
     INFERNT_CUDA_TRY(cudaMemset(p->mega_mem, 0, total));
     char* b = static_cast<char*>(p->mega_mem);
@@ -393,12 +414,8 @@ int build_mega(infernt_plan* p) {
     kvp.insert(kvp.end(), p->vc.begin(), p->vc.end());
     INFERNT_CUDA_TRY(cudaMemcpy(d_kv, kvp.data(), sizeof(float*) * 2 * L, cudaMemcpyHostToDevice));
     b += b_kv;
-    unsigned* d_bar = reinterpret_cast<unsigned*>(b);
+    unsigned long long* d_bar = reinterpret_cast<unsigned long long*>(b);
     b += b_bar;
-    float* d_part = reinterpret_cast<float*>(b);
-    b += b_part;
-    unsigned* d_cnt = reinterpret_cast<unsigned*>(b);
-    b += b_cnt;
     float* d_amv = reinterpret_cast<float*>(b);
     b += al(sizeof(float) * ctas);
     int* d_ami = reinterpret_cast<int*>(b);
@@ -426,16 +443,20 @@ int build_mega(infernt_plan* p) {
     m.attn.theta = c.rope_theta;
     m.attn.scale = 1.0f / sqrtf((float)c.head_dim);
     m.attn.err = p->err;
+    m.attn.rope = p->rope;
     m.state = p->state;
     m.err = p->err;
     m.bar = d_bar;
-    m.part = d_part;
-    m.gcnt = d_cnt;
     m.am_val = d_amv;
     m.am_idx = d_ami;
     m.am_cnt = d_amc;
     m.ring_slots = slots;
     m.x_floats = x_floats;
+    // L2 prefetch window per CTA in 16 KB tiles (default 32: 512 KB per SM,
+    // ~76 MB in flight over 148 SMs, well inside the 126 MB L2)
+    m.l2_prefetch_tiles = 0;
+    if (const char* env = std::getenv("INFERNT_L2_PREFETCH_TILES")) m.l2_prefetch_tiles = std::atoi(env);
+    if (m.l2_prefetch_tiles < 0) m.l2_prefetch_tiles = 0;
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
@@ -478,7 +499,8 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     const size_t b_aws =
         attention_workspace_bytes(cfg->num_attention_heads, cfg->num_key_value_heads, cfg->head_dim, p->splits);
     const size_t b_lm = al(sizeof(LmWs));
-    const size_t total = b_qkv + b_attn + b_act + b_hid + b_log + b_state + b_aws + b_lm;
+    const size_t b_rope = al(sizeof(float2) * (size_t)cfg->max_seq_len * (cfg->head_dim / 2));
+    const size_t total = b_qkv + b_attn + b_act + b_hid + b_log + b_state + b_aws + b_lm + b_rope;
     cudaError_t e = cudaMalloc(&p->scratch, total);
     if (e == cudaSuccess) e = cudaMemset(p->scratch, 0, total);
     if (e != cudaSuccess) {
@@ -506,6 +528,15 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     p->attn_counter = reinterpret_cast<unsigned*>(b + al(part));
     b += b_aws;
     p->lm_ws = reinterpret_cast<LmWs*>(b);
+    b += b_lm;
+    p->rope = reinterpret_cast<float2*>(b);
+    rope_table_kernel<<<sm_count() * 4, 256>>>(p->rope, cfg->max_seq_len, cfg->head_dim, cfg->rope_theta);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        infernt_plan_destroy(p);
+        return cuda_fail(e, "RoPE table");
+    }
 
     if (p->mode == INFERNT_MODE_PERSISTENT) {
         if (mega_eligible(p)) {
@@ -579,6 +610,11 @@ int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
     INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
     if (err) {
         cudaMemsetAsync(p->err, 0, sizeof(unsigned), st);
+        if (p->mega.bar) {  // an aborted launch leaves the barrier count short: restart it
+            cudaMemsetAsync(p->mega.bar, 0, sizeof(unsigned long long), st);
+            p->bar_epoch = 0;
+        }
+        cudaStreamSynchronize(st);
         return fail(INFERNT_ERR_DEVICE,
                     "decode kernels reported error word 0x%x (1: wait timeout, 2: position, 4: token id)", err);
     }

@@ -74,8 +74,8 @@ def test_decode_bf16_matches_oracle_on_rounded_weights(mode):
 
 
 def test_persistent_split_groups_match_oracle():
-    """Shapes whose tile count is not a multiple of the CTA count, so row
-    groups are shared between CTAs and merged by the split-K ticket."""
+    """Shapes whose row-group counts are not multiples of the CTA count
+    (uneven group ranges per CTA, a ragged last group in the LM head)."""
     cfg = ib.ModelConfig(vocab_size=3001, hidden_size=1024, num_layers=2, num_attention_heads=16,
                          num_key_value_heads=4, intermediate_size=2560, max_seq_len=96)
     run_parity(cfg, seed=12, steps=10, mode=ib.MODE_PERSISTENT, expect_mode=ib.MODE_PERSISTENT)
@@ -135,6 +135,26 @@ def test_tinyllama_first_steps_match_oracle():
         want_tok, want_logits = orc.decode_token(int(prompt[pos]), pos)
         check_logits(eng.logits(), want_logits, pos)
         assert mine == want_tok or top2_gap(want_logits) < 1e-4
+    eng.close()
+
+
+@pytest.mark.parametrize("mode", [ib.MODE_PERSISTENT, ib.MODE_GRAPH], ids=["persistent", "graph"])
+def test_mid_context_positions_match_oracle(mode):
+    """One layer at the TinyLlama shape, KV prefilled up to each position:
+    1 to 10 key splits per KV head, tile edges (31, 32, 33, 64) and the
+    bench's positions (40..296)."""
+    cfg = ib.TINYLLAMA.with_(num_layers=1, max_seq_len=512)
+    eng = ib.Engine(cfg, seed=2)
+    eng.set_mode(mode)
+    orc = O.LlamaOracle(cfg, seed=2)
+    for pos in (31, 32, 33, 40, 64, 100, 131, 200, 296, 511):
+        eng.fill_kv(seed=pos, n_pos=pos, std=1.0)
+        orc.fill_kv(seed=pos, n_pos=pos, std=1.0)
+        mine = eng.forward_token(77 + pos, pos)
+        want_tok, want_logits = orc.decode_token(77 + pos, pos)
+        check_logits(eng.logits(), want_logits, pos)
+        assert mine == want_tok or top2_gap(want_logits) < 1e-4
+    assert eng.mode == mode
     eng.close()
 
 
