@@ -133,6 +133,25 @@ INFERNT_API int infernt_attention_decode(float* out, const float* qkv, float* k_
                                          int head_dim, int max_seq_len, int position,
                                          float theta, int splits, void* workspace,
                                          void* stream);
+/* No counterpart in the reference.  infernt_attention_decode without the workspace argument,
+ * for callers that cannot allocate device memory for it: the kernel and its results are the
+ * same, but the split partials and tickets live in a fixed 512 KiB static device array inside
+ * this library, so the call allocates nothing (no cudaMalloc / cudaFree, no allocating
+ * library routine).  Limits and rules:
+ *  - a shape whose infernt_attention_workspace_bytes() exceeds 512 KiB is rejected with
+ *    INFERNT_ERR_INVALID_ARGUMENT (lower `splits`);
+ *  - the tickets in that array must be zero when a call starts: static storage starts
+ *    zeroed and every completed call leaves them at zero;
+ *  - there is one array per device: calls that overlap in time on one device (different
+ *    streams, or different host threads without ordering) race on it and give wrong
+ *    results.  Issue them on one stream, or order them;
+ *  - the first call on each device looks up the array's address (cudaGetSymbolAddress);
+ *    make that first call before any stream capture on the device. */
+INFERNT_API int infernt_attention_decode_noalloc(float* out, const float* qkv, float* k_cache,
+                                                 float* v_cache, int num_q_heads,
+                                                 int num_kv_heads, int head_dim,
+                                                 int max_seq_len, int position, float theta,
+                                                 int splits, void* stream);
 /* logits = W rmsnorm(x, norm_w); *out_token = argmax(logits) (llama_model.cpp:58-64 +
  * cuda/sampling.cu).  workspace: infernt_lm_head_workspace_bytes() bytes, zeroed once. */
 INFERNT_API size_t infernt_lm_head_workspace_bytes(void);

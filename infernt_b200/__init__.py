@@ -129,6 +129,7 @@ _SIGS = {
     "infernt_rmsnorm_gate_up_silu": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P]),
     "infernt_attention_workspace_bytes": (_S, [_I, _I, _I, _I]),
     "infernt_attention_decode": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
+    "infernt_attention_decode_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P]),
     "infernt_lm_head_workspace_bytes": (_S, []),
     "infernt_rmsnorm_lm_head_argmax": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),

@@ -2,6 +2,7 @@
 // (KV head, split) work item; the device code is attention.cuh).
 #include <cmath>
 #include <cstring>
+#include <mutex>
 
 #include "attention.cuh"
 #include "gemv.cuh"
@@ -67,6 +68,43 @@ size_t attention_workspace_bytes(int nq, int nkv, int D, int splits) {
 
 }  // namespace infernt
 
+// Scratch of infernt_attention_decode_noalloc: the per-KV-head tickets (up
+// to 64 heads) at a fixed place at the start, so calls of different shapes
+// find them where the previous call left them at zero; then the error word;
+// then the split partials from offset 512.  512 KiB covers every split
+// count up to the SM count for the usual LLaMA shapes (TinyLlama: 313 KB of
+// partials at 37 splits; Llama-3-8B: 300 KB at 18).  Static storage starts
+// zeroed when the module loads, which is what the tickets need; each
+// completed call leaves them at zero again.  The partials need no zeroing.
+static constexpr size_t kAttnStaticScratchBytes = 512 * 1024;
+static constexpr int kAttnStaticTickets = 64;
+static constexpr size_t kAttnStaticPartOffset = 512;
+static __device__ __align__(256) unsigned char g_attn_static_scratch[kAttnStaticScratchBytes];
+
+namespace infernt {
+namespace {
+
+std::mutex g_static_mu;
+void* g_static_addr[64] = {nullptr};
+
+// Device address of the static scratch on the current device, looked up
+// once per device.
+int attn_static_scratch(void** out) {
+    const int d = current_device();
+    INFERNT_REQUIRE(d >= 0 && d < 64, "attention_decode_noalloc: device ordinal %d out of range", d);
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_addr[d]) {
+        void* p = nullptr;
+        INFERNT_CUDA_TRY(cudaGetSymbolAddress(&p, g_attn_static_scratch));
+        g_static_addr[d] = p;
+    }
+    *out = g_static_addr[d];
+    return INFERNT_OK;
+}
+
+}  // namespace
+}  // namespace infernt
+
 using namespace infernt;
 
 extern "C" {
@@ -95,6 +133,43 @@ int infernt_attention_decode(float* out, const float* qkv, float* k_cache, float
     a.part = static_cast<float*>(workspace);
     a.counter = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + part_al);
     a.err = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + part_al + cnt_al);
+    a.pos = position;
+    a.nq = num_q_heads;
+    a.nkv = num_kv_heads;
+    a.D = head_dim;
+    a.max_seq = max_seq_len;
+    a.splits = splits;
+    a.theta = theta;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    INFERNT_CUDA_TRY(launch_attention_decode(a, (cudaStream_t)stream, false));
+    return INFERNT_OK;
+}
+
+int infernt_attention_decode_noalloc(float* out, const float* qkv, float* k_cache, float* v_cache, int num_q_heads,
+                                     int num_kv_heads, int head_dim, int max_seq_len, int position, float theta,
+                                     int splits, void* stream) {
+    if (int s = attention_shape_check(num_q_heads, num_kv_heads, head_dim, splits)) return s;
+    const size_t need = attention_workspace_bytes(num_q_heads, num_kv_heads, head_dim, splits);
+    INFERNT_REQUIRE(num_kv_heads <= kAttnStaticTickets && need <= kAttnStaticScratchBytes,
+                    "attention_decode_noalloc: %d KV heads x %d splits need %zu bytes of scratch, the static "
+                    "scratch holds %zu (and tickets for %d KV heads); use fewer splits or "
+                    "infernt_attention_decode with a workspace",
+                    num_kv_heads, splits, need, kAttnStaticScratchBytes, kAttnStaticTickets);
+    INFERNT_REQUIRE(out && qkv && k_cache && v_cache, "attention_decode_noalloc: null pointer");
+    INFERNT_REQUIRE(position >= 0 && position < max_seq_len,
+                    "attention_decode_noalloc: position %d outside [0, %d)", position, max_seq_len);
+    void* ws = nullptr;
+    if (int s = attn_static_scratch(&ws)) return s;
+    char* base = static_cast<char*>(ws);
+    AttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.qkv = qkv;
+    a.k_cache = k_cache;
+    a.v_cache = v_cache;
+    a.out = out;
+    a.counter = reinterpret_cast<unsigned*>(base);
+    a.err = reinterpret_cast<unsigned*>(base + kAttnStaticTickets * sizeof(unsigned));
+    a.part = reinterpret_cast<float*>(base + kAttnStaticPartOffset);
     a.pos = position;
     a.nq = num_q_heads;
     a.nkv = num_kv_heads;
