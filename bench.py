@@ -256,7 +256,7 @@ def run_ours(args):
     launch_bytes = step_bytes * K
     achieved = launch_bytes / (ms / 1e3) / 1e9
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
+    tfile = os.path.join(ROOT, "profiles", "decode_mega_kernel_f32_tinyllama_traffic.txt")
     if os.path.exists(tfile):
         for line in open(tfile):
             if line.startswith("decode_mega_kernel_f32_tinyllama_per_step"):

@@ -1,0 +1,43 @@
+"""A decode run sized for profilers: one seeded engine, a short prompt, then
+one chained launch of the persistent decode kernel.
+
+    python -m infernt_b200.profile_case --layers 4 --steps 8
+
+The TinyLlama-1.1B shape with `--layers` decoder layers (the LM head and
+the per-layer matrices keep their full size), seeded N(0, 0.02) weights.
+Launch order on the device: `--prompt` single-step launches (the prompt),
+then one warm-up chain and one measured chain of `--steps` steps, so a
+profiler that skips `--prompt + 1` launches of the decode kernel captures
+the measured chain."""
+import argparse
+import sys
+
+import infernt_b200 as ib
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--prompt", type=int, default=2)
+    ap.add_argument("--bf16", action="store_true", help="bf16 weights (FP32 activations)")
+    args = ap.parse_args(argv)
+    cfg = ib.TINYLLAMA.with_(num_layers=args.layers)
+    if args.bf16:
+        cfg = cfg.with_(weight_dtype=ib.DTYPE_BF16)
+    eng = ib.Engine(cfg, seed=0)
+    t = 5
+    for pos in range(args.prompt):
+        t = eng.forward_token(t, pos)
+    eng.decode_chain(t, args.prompt, args.steps)
+    toks, ms = eng.decode_chain(t, args.prompt, args.steps)
+    wbytes = cfg.weight_params * (2 if args.bf16 else 4)
+    print("layers=%d steps=%d mode=%d: %.4f ms/step, %.0f tok/s, weights %.3f GB -> %.1f GB/s"
+          % (args.layers, args.steps, eng.mode, ms / args.steps, args.steps * 1e3 / ms, wbytes / 1e9,
+             wbytes / (ms / args.steps / 1e3) / 1e9))
+    eng.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
