@@ -110,29 +110,6 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-// 2-D tiled TMA load of one box at element coordinates (x inner, y outer)
-// from the tensor map at `map` (global or parameter memory) into shared
-// memory, completion signalled on `bar`.  x * element size must be a
-// multiple of 16 bytes; y may run past the tensor (rows read as zero).
-__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, int y, uint64_t* bar,
-                                            uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
-        : "memory");
-}
-
-// 2-D tiled TMA prefetch of one box into L2 (no shared memory, no completion).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* map, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_map(const void* map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
 // Programmatic dependent launch: let the next kernel in the stream start
 // its prologue, and wait for the previous kernel's results.
 __device__ __forceinline__ void pdl_launch_dependents() {

@@ -6,31 +6,36 @@
 // gate/up + SiLU, down projection + residual; then RMSNorm + LM head +
 // argmax.  Phases are separated by a grid barrier among the consumer warps.
 //
-// Warps 0-3 consume; warp 4 produces: lanes 0-3 stream the CTA's share of
-// every GEMV phase's weights, tile by tile, into a ring of 16 KB shared-
-// memory slots with 2-D TMA box loads (8 KB per instruction).  Weights do
-// not depend on activations, so the producer runs ahead across phase
-// boundaries and layers while the consumers wait at grid barriers or compute
-// attention.  Warp 5 keeps an L2 prefetch window (cp.async.bulk.prefetch
-// .tensor) a fixed number of tiles ahead of the producer, so HBM keeps
-// streaming for longer than the shared-memory ring alone could buffer.
+// Warps 0-3 consume; lane 0 of warp 4 produces: it streams the CTA's share
+// of every GEMV phase's weights into a ring of 16 KB shared-memory slots with
+// 1-D bulk copies (cp.async.bulk).  A GEMV phase gives CTA b the output units
+// [U b / P, U (b + 1) / P), whose weight rows are contiguous in row-major
+// memory, so every slot is one contiguous 16 KB run of HBM (two runs where
+// it straddles a matrix or gate/up boundary): the access pattern that
+// streams fastest, and a split balanced to one row per CTA.  Weights do not
+// depend on activations, so the producer runs ahead across phase boundaries
+// and layers while the consumers wait at grid barriers or compute attention.
 //
-// A GEMV phase of G row groups (R rows each, R = 8 FP32 / 16 bf16; a tile is
-// one 512-column block of a group) gives CTA b the groups
-// [G b / P, G (b + 1) / P): every group is reduced inside one CTA, in a
-// fixed order, so results do not depend on timing and no cross-CTA merge
-// sits on the critical path.
+// Consumers walk the stream in 512-element pieces, each thread covering 4
+// columns of every piece, in batches of R rows (R = 8 FP32 / 16 bf16; for
+// gate/up R / 2 units, gate rows then up rows), which fill exactly K / 512
+// slots.  Each thread adds a row's pieces in column order into one
+// accumulator per row; for the usual widths the (row, column block) of every
+// piece of a batch is known at compile time and the input columns stay in
+// registers.  A batch ends with one reduce-scatter over the warp, and the
+// four warps' row sums are added in warp order in the batches' epilogue.
+// Every output is reduced inside one CTA in a fixed order, so results do
+// not depend on timing and no cross-CTA merge sits on the critical path.
 //
-// Every wait (ring slots, grid barrier, prefetch pacing) is bounded by a
-// clock budget; on expiry the CTA sets kErrWaitTimeout in the error word,
-// marks itself aborted and runs the remaining control flow without waiting,
-// so the kernel always terminates and the host reports INFERNT_ERR_DEVICE.
+// Every wait (ring slots, grid barrier, bulk copies) is bounded by a clock
+// budget; on expiry the CTA sets kErrWaitTimeout in the error word, marks
+// itself aborted and runs the remaining control flow without waiting, so the
+// kernel always terminates and the host reports INFERNT_ERR_DEVICE.
 #include <cstring>
 
 #include "decode_kernel.cuh"
 #include "gemv.cuh"
 #include "internal.h"
-#include "tensormap.h"
 
 namespace infernt {
 
@@ -39,33 +44,31 @@ namespace {
 constexpr int kMegaSlot = 16384;
 constexpr int kMegaConsumers = 128;
 constexpr int kProducerWarp = 4;
-constexpr int kPrefetchWarp = 5;
-constexpr int kMegaThreads = 192;  // 4 consumer warps, the producer warp, the L2 prefetch warp
+constexpr int kMegaThreads = 160;  // 4 consumer warps and the producer warp
 constexpr long long kWaitCycles = 4000000000ll;  // about 2 s at the maximum SM clock
 constexpr int kResRows = 128;                    // residual rows a CTA stages per phase
 
 template <typename WT>
 struct MegaRows {
     static constexpr int EB = WeightTraits<WT>::kBytes;
-    static constexpr int R = kMegaSlot / (kPiece * EB);  // 8 FP32, 16 bf16
+    static constexpr int R = kMegaSlot / (kPiece * EB);  // rows per batch: 8 FP32, 16 bf16
+    static constexpr int PB = kPiece * EB;               // bytes per 512-element piece
+    static constexpr int PT = kMegaSlot / PB;            // pieces per slot (= R)
 };
 
-constexpr int kGroupSlots = 16;  // group hand-off slots (> ring slots, see finish_group)
+constexpr int kGroupBatch = 16;  // batches whose row sums are held before their epilogue runs
 constexpr int kMaxRingSlots = 14;
 
 struct MegaShared {
     int abort;
-    unsigned loaded;  // tiles the producer has issued (paces the prefetch warp)
-    int producer_done;
     float ss[4];
-    float amv[64];  // LM-head candidates [warp][lane < R]
-    int ami[64];
+    float amv[4];  // LM-head candidate of each consumer warp
+    int ami[4];
     int res_base;  // first staged residual row
     int res_n;     // staged rows
     float res[kResRows];
-    int gcnt[kGroupSlots];           // warps that have deposited a group's partials
-    float gred[kGroupSlots][4][16];  // per-warp partial sums of a group's rows
-    uint64_t xbar;                   // completion of the input-vector bulk copy
+    float gpart[4][kGroupBatch][16];  // per-warp row sums of up to kGroupBatch batches
+    uint64_t xbar;                    // completion of the input-vector bulk copy
     uint64_t pbar;                   // completion of the next phase descriptor's bulk copy
 };
 
@@ -142,12 +145,10 @@ __device__ __forceinline__ void grid_sync(const MegaParams& p, volatile int* abo
     named_sync(1, kMegaConsumers);
 }
 
-// Tiles [t0, t1) of this CTA: whole row groups [G b / P, G (b + 1) / P).
-__device__ __forceinline__ void phase_range(const MegaPhase& P, long long& t0, long long& t1) {
-    const long long g0 = (long long)P.groups * blockIdx.x / gridDim.x;
-    const long long g1 = (long long)P.groups * (blockIdx.x + 1) / gridDim.x;
-    t0 = g0 * P.cb;
-    t1 = g1 * P.cb;
+// Output units [u0, u1) of this CTA: [U b / P, U (b + 1) / P).
+__device__ __forceinline__ void unit_range(const MegaPhase& P, int& u0, int& u1) {
+    u0 = (int)((long long)P.units * blockIdx.x / gridDim.x);
+    u1 = (int)((long long)P.units * (blockIdx.x + 1) / gridDim.x);
 }
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -167,54 +168,34 @@ __device__ __forceinline__ void trace_mark(const MegaParams& p, long long base, 
     if (base >= 0) p.trace[base + field] = global_ns();
 }
 
-// Segment and local group of group g in the stacked row space.
-__device__ __forceinline__ int seg_of(const MegaPhase& P, int g, int& lg, int& rowbase) {
-    int q = 0;
-    lg = g;
-    rowbase = 0;
-    while (q < P.nseg - 1 && lg >= P.seg_groups[q]) {
-        lg -= P.seg_groups[q];
-        rowbase += P.seg_rows[q];
-        ++q;
-    }
-    return q;
-}
-
 // -------------------------------------------------------------- consumers
 
-template <typename WT, int NS>
-__device__ __forceinline__ void tile_fma(const unsigned char* slot, const float4& xv, int tid, float* acc) {
-    constexpr int R = MegaRows<WT>::R;
-    constexpr int EB = MegaRows<WT>::EB;
-    constexpr int BR = R / NS;
-    const int h = tid >> 6;
-    const unsigned char* base = slot + (size_t)(h * BR) * kBoxCols * EB + (size_t)(tid & 63) * 4 * EB;
-#pragma unroll
-    for (int a = 0; a < R; ++a) {
-        const int s2 = a / BR, i = a % BR;
-        const unsigned char* wp = base + (size_t)(s2 * 2 * BR + i) * kBoxCols * EB;
-        if (EB == 4) {
-            const float4 w = *reinterpret_cast<const float4*>(wp);
-            acc[a] = fmaf(w.x, xv.x, acc[a]);
-            acc[a] = fmaf(w.y, xv.y, acc[a]);
-            acc[a] = fmaf(w.z, xv.z, acc[a]);
-            acc[a] = fmaf(w.w, xv.w, acc[a]);
-        } else {
-            const uint2 raw = *reinterpret_cast<const uint2*>(wp);
-            const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-            const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-            acc[a] = fmaf(w01.x, xv.x, acc[a]);
-            acc[a] = fmaf(w01.y, xv.y, acc[a]);
-            acc[a] = fmaf(w23.x, xv.z, acc[a]);
-            acc[a] = fmaf(w23.y, xv.w, acc[a]);
-        }
+// The dot product of 4 weights at wp with 4 inputs, in element order.
+template <typename WT>
+__device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4& xv) {
+    float acc = 0.0f;
+    if (WeightTraits<WT>::kBytes == 4) {
+        const float4 w = *reinterpret_cast<const float4*>(wp);
+        acc = fmaf(w.x, xv.x, acc);
+        acc = fmaf(w.y, xv.y, acc);
+        acc = fmaf(w.z, xv.z, acc);
+        acc = fmaf(w.w, xv.w, acc);
+    } else {
+        const uint2 raw = *reinterpret_cast<const uint2*>(wp);
+        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+        acc = fmaf(w01.x, xv.x, acc);
+        acc = fmaf(w01.y, xv.y, acc);
+        acc = fmaf(w23.x, xv.z, acc);
+        acc = fmaf(w23.y, xv.w, acc);
     }
+    return acc;
 }
 
 // Input vector of a GEMV phase into shared memory (RMSNorm applied when set).
-// Residual phases also stage the residual rows of the CTA's row groups
-// (R rows per group) in sh.res, so the epilogue needs no L2 round trip.
-__device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, int R,
+// Residual phases also stage the residual rows of the CTA's units in sh.res,
+// so the epilogue needs no L2 round trip.
+__device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, int u0, int u1,
                        uint32_t& xphase, int tok) {
     const int warp = tid >> 5, lane = tid & 31;
     const float* src = P.x;
@@ -240,21 +221,11 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         bulk_g2s_plain(xs, src, bytes, &sh.xbar);
         if (P.norm_w) bulk_g2s_plain(xs + P.K, P.norm_w, bytes, &sh.xbar);
     }
-    int staged = 0, staged_base = 0;
-    if (P.epi == kEpiResidual) {
-        long long t0, t1;
-        phase_range(P, t0, t1);
-        if (t1 > t0) {
-            const long long r0 = (t0 / P.cb) * R;
-            long long r1 = (t1 / P.cb) * R;
-            if (r1 > P.units) r1 = P.units;
-            const int n = (int)(r1 - r0);
-            if (n > 0 && n <= kResRows) {
-                for (int i = tid; i < n; i += kMegaConsumers) sh.res[i] = __ldcg(P.res + r0 + i);
-                staged = n;
-                staged_base = (int)r0;
-            }
-        }
+    int staged = 0;
+    const int staged_base = u0;
+    if (P.epi == kEpiResidual && u1 - u0 <= kResRows) {
+        for (int i = tid; i < u1 - u0; i += kMegaConsumers) sh.res[i] = __ldcg(P.res + u0 + i);
+        staged = u1 - u0;
     }
     if (tid == 0) {  // one writer; read after the named barrier at the end
         sh.res_n = staged;
@@ -294,73 +265,85 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
     named_sync(1, kMegaConsumers);
 }
 
-// A warp's share of a finished group: its R row sums (xor-shuffle trees)
-// go to the group's hand-off slot; the fourth warp to deposit adds the four
-// shares in warp order and runs the epilogue.  No CTA-wide barrier, so the
-// warps keep streaming tiles.  A slot is reused kGroupSlots groups later,
-// and no warp runs more than the ring's slot count of tiles (at least one
-// tile per group) ahead of the slowest warp, so kGroupSlots > ring slots
-// keeps a slot's readers ahead of its next writers.
-template <typename WT, int NS>
-__device__ __forceinline__ void finish_group(const MegaParams& p, const MegaPhase& P, long long g, const float* acc,
-                             MegaShared& sh, int gslot, int tid, float& am_v, int& am_i) {
-    constexpr int R = MegaRows<WT>::R;
-    constexpr int BR = R / NS;
-    const int warp = tid >> 5, lane = tid & 31;
-    float(*slot)[16] = sh.gred[gslot];
+// Warp sums of N per-lane values by a reduce-scatter butterfly (N - 1
+// exchanges that halve the values held per lane, then the remaining xor
+// steps on one value): lane L returns the warp sum of value L / (32 / N).
+// Every value is added along the same xor tree as a full butterfly (16, 8,
+// 4, 2, 1), for N - 1 + log2(32 / N) shuffles instead of 5 N.
+template <int N>
+__device__ __forceinline__ float warp_reduce_scatter(const float* in, int lane) {
+    float a[N];
 #pragma unroll
-    for (int a = 0; a < R; ++a) {
-        const float v = warp_sum(acc[a]);
-        if (lane == a) slot[warp][a] = v;
-    }
-    __threadfence_block();
-    int ticket = 0;
-    if (lane == 0) ticket = atomicAdd(&sh.gcnt[gslot], 1);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket != kMegaConsumers / 32 - 1) return;
-    __threadfence_block();
-    if (NS == 2) {
-        if (lane < BR) {
-            const float yg = ((slot[0][lane] + slot[1][lane]) + slot[2][lane]) + slot[3][lane];
-            const int u = BR + lane;
-            const float yu = ((slot[0][u] + slot[1][u]) + slot[2][u]) + slot[3][u];
-            const long long unit = g * BR + lane;
-            if (unit < P.units) P.out[unit] = silu_mul(yg, yu);
+    for (int i = 0; i < N; ++i) a[i] = in[i];
+    int o = 16;
+#pragma unroll
+    for (int n = N; n > 1; n >>= 1, o >>= 1) {
+        const bool hi = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float send = hi ? a[i] : a[i + n / 2];
+            const float keep = hi ? a[i + n / 2] : a[i];
+            a[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
-    } else if (lane < R) {
-        const float v = ((slot[0][lane] + slot[1][lane]) + slot[2][lane]) + slot[3][lane];
-        int lg, rowbase;
-        const int q = seg_of(P, (int)g, lg, rowbase);
-        const int local = lg * R + lane;
-        if (local < P.seg_rows[q]) {
-            const int row = rowbase + local;
-            if (P.epi == kEpiStore) {
-                P.out[row] = v;
-            } else if (P.epi == kEpiResidual) {
-                const int ri = row - sh.res_base;
-                const float r = (ri >= 0 && ri < sh.res_n) ? sh.res[ri] : __ldcg(P.res + row);
-                P.out[row] = r + v;
-            } else {
-                float* lo = P.out ? P.out : p.logits;
-                lo[row] = v;
-                if (argmax_better(v, row, am_v, am_i)) {
-                    am_v = v;
-                    am_i = row;
-                }
+    }
+#pragma unroll
+    for (; o > 0; o >>= 1) a[0] += __shfl_xor_sync(0xffffffffu, a[0], o);
+    return a[0];
+}
+
+// Epilogue of n batches whose first unit is ub (their row sums in gpart
+// slots [0, n)), units below u1: the four warps' sums added in warp order,
+// then store / residual add / SwiGLU / logits + argmax candidate.  All
+// consumer threads take part; called between named barriers.  Units of a
+// Q|K|V phase are rows of the stacked [q | k | v] output, so the stacked row
+// is the output index.
+template <typename WT, int NS>
+__device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaShared& sh, int ub, int n, int u1,
+                                int tid, float& am_v, int& am_i) {
+    constexpr int BU = MegaRows<WT>::R / NS;
+    for (int idx = tid; idx < n * BU; idx += kMegaConsumers) {
+        const int sl = idx / BU, i = idx % BU;
+        const int row = ub + idx;
+        if (row >= u1) continue;
+        const float v = ((sh.gpart[0][sl][i] + sh.gpart[1][sl][i]) + sh.gpart[2][sl][i]) + sh.gpart[3][sl][i];
+        if (NS == 2) {
+            const int u = BU + i;
+            const float yu = ((sh.gpart[0][sl][u] + sh.gpart[1][sl][u]) + sh.gpart[2][sl][u]) + sh.gpart[3][sl][u];
+            P.out[row] = silu_mul(v, yu);
+        } else if (P.epi == kEpiStore) {
+            P.out[row] = v;
+        } else if (P.epi == kEpiResidual) {
+            const int ri = row - sh.res_base;
+            const float r = (ri >= 0 && ri < sh.res_n) ? sh.res[ri] : __ldcg(P.res + row);
+            P.out[row] = r + v;
+        } else {
+            float* lo = P.out ? P.out : p.logits;
+            lo[row] = v;
+            if (argmax_better(v, row, am_v, am_i)) {
+                am_v = v;
+                am_i = row;
             }
         }
     }
-    __syncwarp();
-    if (lane == 0) sh.gcnt[gslot] = 0;
 }
 
 // Winner of the CTA -> partial; the last CTA reduces all partials in CTA
 // order, writes the token and advances the decode state.
-__device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, float am_v, int am_i, int R) {
+__device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, float am_v, int am_i) {
     const int warp = tid >> 5, lane = tid & 31;
-    if (lane < R) {
-        sh.amv[warp * 16 + lane] = am_v;
-        sh.ami[warp * 16 + lane] = am_i;
+    // the order is total, so any reduction tree picks the same winner
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, am_v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, am_i, o);
+        if (argmax_better(ov, oi, am_v, am_i)) {
+            am_v = ov;
+            am_i = oi;
+        }
+    }
+    if (lane == 0) {
+        sh.amv[warp] = am_v;
+        sh.ami[warp] = am_i;
     }
     named_sync(1, kMegaConsumers);
     if (warp != 0) return;
@@ -369,11 +352,10 @@ __device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, f
         float bv = -1e30f;
         int bi = 0;
         for (int w = 0; w < kMegaConsumers / 32; ++w)
-            for (int i = 0; i < R; ++i)
-                if (argmax_better(sh.amv[w * 16 + i], sh.ami[w * 16 + i], bv, bi)) {
-                    bv = sh.amv[w * 16 + i];
-                    bi = sh.ami[w * 16 + i];
-                }
+            if (argmax_better(sh.amv[w], sh.ami[w], bv, bi)) {
+                bv = sh.amv[w];
+                bi = sh.ami[w];
+            }
         p.am_val[blockIdx.x] = bv;
         p.am_idx[blockIdx.x] = bi;
         last = atom_add_acq_rel(p.am_cnt, 1u) == gridDim.x - 1;
@@ -411,48 +393,171 @@ __device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, f
     *p.am_cnt = 0u;
 }
 
-template <typename WT, int NS>
-__device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned char* ring, uint64_t* full,
-                           uint64_t* empty, RingPos& rp, uint32_t& gcount, uint32_t& xphase, float* xs,
-                           MegaShared& sh, int tid, long long tb, int tok) {
-    constexpr int R = MegaRows<WT>::R;
-    const int lane = tid & 31;
-    const int slots = p.ring_slots;
-    load_x(p, P, xs, sh, tid, R, xphase, tok);
-    if (tid == 0) trace_mark(p, tb, 1);
-    long long t0, t1;
-    phase_range(P, t0, t1);
-    float acc[R];
-#pragma unroll
-    for (int a = 0; a < R; ++a) acc[a] = 0.0f;
-    float am_v = -1e30f;
-    int am_i = 0;
-    long long g = t0 / P.cb;
-    int j = 0;
-    long long waited = 0;
-    for (long long t = t0; t < t1; ++t, rp.advance(slots)) {
-        const int s = rp.s;
-        if (tb >= 0) {
+// A consumer's view of the ring: the next slot to take, and the wait
+// accounting of the phase timeline.
+struct SlotReader {
+    unsigned char* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    RingPos* rp;
+    int slots;
+    volatile int* abort;
+    unsigned* err;
+    bool timed;
+    long long waited;
+
+    // Waits for the next slot; returns this thread's first byte in it.
+    __device__ __forceinline__ const unsigned char* take(int tid, int eb) {
+        if (timed) {
             const long long c0 = clock64();
-            mega_wait(&full[s], rp.ph, &sh.abort, p.err);
+            mega_wait(&full[rp->s], rp->ph, abort, err);
             waited += clock64() - c0;
         } else {
-            mega_wait(&full[s], rp.ph, &sh.abort, p.err);
+            mega_wait(&full[rp->s], rp->ph, abort, err);
         }
-        const float4 xv = reinterpret_cast<const float4*>(xs + j * kPiece)[tid];
-        tile_fma<WT, NS>(ring + (size_t)s * kMegaSlot, xv, tid, acc);
+        return ring + (size_t)rp->s * kMegaSlot + (size_t)tid * 4 * eb;
+    }
+    // Hands the slot back to the producer (after the warp's last read of it).
+    __device__ __forceinline__ void release(int lane) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (++j == P.cb) {
-            finish_group<WT, NS>(p, P, g, acc, sh, (int)(gcount++ % kGroupSlots), tid, am_v, am_i);
+        if (lane == 0) mbar_arrive(&empty[rp->s]);
+        rp->advance(slots);
+    }
+};
+
+// A full batch (R rows, or R / 2 gate/up units) of a phase with cb == CB:
+// CB slots whose pieces map to (row, column block) at compile time, so each
+// piece's product goes straight to its row's accumulator.  The input columns
+// stay in registers (CB <= 11) or are read from shared memory.
+template <typename WT, int CB>
+__device__ __forceinline__ void batch_static(SlotReader& rd, const float* xt, const float4* xr, float* acc, int tid,
+                                             int lane) {
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
 #pragma unroll
-            for (int a = 0; a < R; ++a) acc[a] = 0.0f;
-            j = 0;
-            ++g;
+    for (int j = 0; j < CB; ++j) {
+        const unsigned char* wp = rd.take(tid, EB);
+        float pv[PT];
+#pragma unroll
+        for (int i = 0; i < PT; ++i) {
+            constexpr int kRegs = CB <= 11;
+            const int q = (j * PT + i) % CB;
+            const float4 xv = kRegs ? xr[q] : *reinterpret_cast<const float4*>(xt + q * kPiece);
+            pv[i] = piece_dot<WT>(wp + i * PB, xv);
+        }
+        rd.release(lane);
+#pragma unroll
+        for (int i = 0; i < PT; ++i) acc[(j * PT + i) / CB] += pv[i];
+    }
+}
+
+// Any batch, any cb: the pieces of each slot as independent products, added
+// to a running row sum in stream order; a finished row moves to its
+// accumulator.  Pieces past the batch's end (a short last batch) are not
+// in the stream.
+template <typename WT, int NS>
+__device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, float* acc, int tid, int lane) {
+    constexpr int R = MegaRows<WT>::R, BU = R / NS;
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
+    const int npieces = (NS == 2 ? 2 * nb : nb) * cb;
+    int q = 0;  // column block of the next piece
+    int r = 0;  // row (stream order) of the next piece
+    float racc = 0.0f;
+    for (int p0 = 0; p0 < npieces; p0 += PT) {
+        const unsigned char* wp = rd.take(tid, EB);
+        const int n = min(PT, npieces - p0);
+        float pv[PT];
+        int qi = q;
+#pragma unroll
+        for (int i = 0; i < PT; ++i) {
+            // bytes past n are stale but inside the slot: read, then dropped
+            const float d = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + qi * kPiece));
+            pv[i] = i < n ? d : 0.0f;
+            if (++qi == cb) qi = 0;
+        }
+        rd.release(lane);
+#pragma unroll
+        for (int i = 0; i < PT; ++i) {
+            if (i < n) {
+                racc += pv[i];
+                if (++q == cb) {
+                    // stream row r -> accumulator: gate rows first, then up rows
+                    const int k = (NS == 2 && r >= nb) ? BU + (r - nb) : r;
+#pragma unroll
+                    for (int m = 0; m < R; ++m)
+                        if (m == k) acc[m] = racc;
+                    racc = 0.0f;
+                    q = 0;
+                    ++r;
+                }
+            }
         }
     }
-    if (tb >= 0) p.trace[tb + 5] = (unsigned long long)waited;
-    if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i, R);
+}
+
+template <typename WT, int NS, int CB>
+__device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& rd, const float* xs, MegaShared& sh,
+                          int tid, int u0, int u1) {
+    constexpr int R = MegaRows<WT>::R;
+    constexpr int BU = R / NS;  // units per batch
+    static_assert(MegaRows<WT>::PT == R, "a batch of R rows fills whole slots");
+    const int warp = tid >> 5, lane = tid & 31;
+    const float* xt = xs + tid * 4;  // this thread's 4 columns of every piece
+    constexpr int NXR = (CB > 0 && CB <= 11) ? CB : 1;
+    float4 xr[NXR];
+    if (CB > 0 && CB <= 11) {
+#pragma unroll
+        for (int c = 0; c < NXR; ++c) xr[c] = *reinterpret_cast<const float4*>(xt + c * kPiece);
+    }
+    float am_v = -1e30f;
+    int am_i = 0;
+    int bi = 0;  // batches finished in this phase
+    for (int ub = u0; ub < u1; ub += BU) {
+        const int nb = min(BU, u1 - ub);
+        float acc[R];
+#pragma unroll
+        for (int a = 0; a < R; ++a) acc[a] = 0.0f;
+        if (CB > 0 && nb == BU)
+            batch_static<WT, CB>(rd, xt, xr, acc, tid, lane);
+        else
+            batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, tid, lane);
+        // the warp's sum of each row; lane L holds row L / (32 / R)
+        const float v = warp_reduce_scatter<R>(acc, lane);
+        constexpr int kLanesPerRow = 32 / R;
+        if (lane % kLanesPerRow == 0) sh.gpart[warp][bi % kGroupBatch][lane / kLanesPerRow] = v;
+        // kGroupBatch batches held: every warp has summed them (all walk the
+        // same rows); run their epilogue before the slots are reused
+        if (++bi % kGroupBatch == 0) {
+            named_sync(1, kMegaConsumers);
+            combine_batches<WT, NS>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v, am_i);
+            named_sync(1, kMegaConsumers);
+        }
+    }
+    const int rest = bi % kGroupBatch;
+    if (rest) {
+        named_sync(1, kMegaConsumers);
+        combine_batches<WT, NS>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i);
+    }
+    if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i);
+}
+
+template <typename WT, int NS>
+__device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned char* ring, uint64_t* full,
+                           uint64_t* empty, RingPos& rp, uint32_t& xphase, float* xs, MegaShared& sh, int tid,
+                           long long tb, int tok) {
+    int u0, u1;
+    unit_range(P, u0, u1);
+    load_x(p, P, xs, sh, tid, u0, u1, xphase, tok);
+    if (tid == 0) trace_mark(p, tb, 1);
+    SlotReader rd{ring, full, empty, &rp, p.ring_slots, &sh.abort, p.err, tb >= 0, 0};
+    // the stream pattern of the usual widths at compile time (every thread
+    // takes the same branch: P is shared)
+    switch (P.cb) {
+        case 4: gemv_body<WT, NS, 4>(p, P, rd, xs, sh, tid, u0, u1); break;
+        case 8: gemv_body<WT, NS, 8>(p, P, rd, xs, sh, tid, u0, u1); break;
+        case 11: gemv_body<WT, NS, 11>(p, P, rd, xs, sh, tid, u0, u1); break;
+        default: gemv_body<WT, NS, 0>(p, P, rd, xs, sh, tid, u0, u1); break;
+    }
+    if (tb >= 0) p.trace[tb + 5] = (unsigned long long)rd.waited;
 }
 
 // One (KV head, split) item of decode attention inside the persistent
@@ -702,174 +807,129 @@ __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* 
 
 // ---------------------------------------------------------------- producer
 
-// Position in a CTA's weight stream: (step, phase, tile) over the GEMV
-// phases, in the order the consumers use them.  The phase's fields the
-// producer needs are cached in registers when the cursor enters a phase,
-// so a tile costs no global-memory reads.
-struct TileCursor {
-    int step, ph;
-    long long t, t1;
-    int g, j, cb, ns, q, lg;
-    int segg[3];
-    const CUtensorMap* m[3];
-    bool done;
+// A CTA's weight stream of one GEMV phase as consecutive byte ranges of the
+// weight matrices, in the order the consumers walk the rows: NS == 1, the
+// rows [u0, u1) of the stacked matrices (one range per matrix crossed);
+// NS == 2, per batch of bu units, the batch's gate rows then its up rows.
+struct StreamRanges {
+    const unsigned char* w[3];
+    int seg_rows[3];
+    int nseg, ns, bu;
+    long long rowbytes;
+    int u, u1;      // next unit, end of the CTA's units
+    int seg, seg0;  // NS == 1: matrix of unit u and its first stacked row
+    bool up;        // NS == 2: the next range is the up half of the batch at u
+    const unsigned char* addr;  // rest of the current range
+    long long left;
 
-    __device__ void start(const MegaParams& p) {
-        step = 0;
-        ph = -1;
-        done = false;
-        next_phase(p);
-    }
-    __device__ void next_phase(const MegaParams& p) {
-        while (true) {
-            if (++ph == p.nphases) {
-                ph = 0;
-                if (++step >= p.steps) {
-                    done = true;
-                    return;
-                }
-            }
-            const MegaPhase& P = p.phases[ph];
-            if (P.kind != kPhGemv) continue;
-            long long t0;
-            phase_range(P, t0, t1);
-            if (t0 == t1) continue;
-            t = t0;
-            cb = P.cb;
-            ns = P.ns;
-            g = (int)(t0 / cb);
-            j = 0;
-            const int nm = ns == 2 ? 2 : P.nseg;
-            for (int i = 0; i < 3; ++i) {
-                segg[i] = P.seg_groups[i];
-                m[i] = &p.maps[P.map[i < nm ? i : 0]];
-            }
-            q = 0;
-            lg = g;
-            if (ns == 1)
-                while (q < P.nseg - 1 && lg >= segg[q]) {
-                    lg -= segg[q];
-                    ++q;
-                }
-            return;
+    __device__ void start(const MegaPhase& P, int eb, int u0, int uend, int units_per_batch) {
+        for (int i = 0; i < 3; ++i) {
+            w[i] = static_cast<const unsigned char*>(P.w[i]);
+            seg_rows[i] = P.seg_rows[i];
         }
+        nseg = P.nseg;
+        ns = P.ns;
+        bu = units_per_batch;
+        rowbytes = (long long)P.K * eb;
+        u = u0;
+        u1 = uend;
+        seg = 0;
+        seg0 = 0;
+        up = false;
+        addr = nullptr;
+        left = 0;
     }
-    __device__ __forceinline__ void next(const MegaParams& p) {
-        ++t;
-        if (++j == cb) {
-            j = 0;
-            ++g;
-            if (++lg == segg[q] && ns == 1) {
-                ++q;
-                lg = 0;
+    // Moves to the next range; false when the phase's stream has ended.
+    __device__ bool next() {
+        if (u >= u1) return false;
+        if (ns == 1) {
+            while (seg < nseg - 1 && u >= seg0 + seg_rows[seg]) {
+                seg0 += seg_rows[seg];
+                ++seg;
             }
+            const int end = min(u1, seg0 + seg_rows[seg]);
+            addr = w[seg] + (long long)(u - seg0) * rowbytes;
+            left = (long long)(end - u) * rowbytes;
+            u = end;
+            return true;
         }
-        if (t == t1) next_phase(p);
+        const int nb = min(bu, u1 - u);
+        addr = w[up ? 1 : 0] + (long long)u * rowbytes;
+        left = (long long)nb * rowbytes;
+        if (up) u += nb;
+        up = !up;
+        return true;
     }
 };
 
-// Box `box` (0..3) of the tile at cursor c: tensor map and coordinates.
+// One thread streams every GEMV phase's weights of this CTA, across phases
+// and steps, into the ring: each slot takes the next min(16 KB, rest of the
+// phase) bytes of the phase's ranges with one or more bulk copies (a slot
+// straddles at most a matrix or gate/up boundary), completing on the slot's
+// full barrier.  A phase starts a new slot.  From the second lap on it waits
+// until the consumers released the slot.
 template <typename WT>
-__device__ __forceinline__ const CUtensorMap* tile_box(const TileCursor& c, int box, int& x, int& y) {
-    constexpr int R = MegaRows<WT>::R;
-    x = c.j * kPiece + (box & 1) * kBoxCols;
-    if (c.ns == 1) {
-        y = c.lg * R;
-        return c.m[c.q];
-    }
-    y = c.g * (R / 2);
-    return c.m[box >> 1];
-}
-
-template <typename WT>
-__device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full, uint64_t* empty,
-                        MegaShared& sh, int lane) {
+__device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full, uint64_t* empty, MegaShared& sh) {
     constexpr int R = MegaRows<WT>::R;
     constexpr int EB = MegaRows<WT>::EB;
     volatile int* abort = &sh.abort;
     const int slots = p.ring_slots;
     const uint64_t pol = l2_evict_first_policy();
-    TileCursor ld;
-    ld.start(p);
-    uint32_t sl = 0;
-    int ok = 1;
+    uint32_t sl = 0;  // slots armed so far
+    bool ok = true;
     RingPos wp{0, 0u};
-    long long pwait = 0;  // cycles waited for free slots in the current phase (trace)
-    while (!ld.done && ok) {
-        const int s = wp.s;
-        if (lane == 0) {
-            // from the second lap on, wait until the consumers released the slot
-            const long long c0 = clock64();
-            if (sl >= (uint32_t)slots && !mega_wait(&empty[s], wp.ph ^ 1u, abort, p.err))
-                ok = 0;
-            else
-                mbar_arrive_expect_tx(&full[s], kMegaSlot);
-            pwait += clock64() - c0;
-        }
-        ok = __shfl_sync(0xFu, ok, 0);
-        if (ok) {
-            // ns == 1: box h at h*R rows; ns == 2: box (s2, h) at (s2*2 + h)*(R/2) rows
-            const int BR = R / ld.ns;
-            if (lane < (ld.ns == 1 ? 2 : 4)) {
-                int x, y;
-                const CUtensorMap* m = tile_box<WT>(ld, lane, x, y);
-                tma_load_2d(ring + (size_t)s * kMegaSlot + (size_t)lane * BR * kBoxCols * EB, m, x, y, &full[s], pol);
-            }
-            const int ph_before = ld.ph, step_before = ld.step;
-            ld.next(p);
-            ++sl;
-            wp.advance(slots);
-            if (lane == 0) {
-                *reinterpret_cast<volatile unsigned*>(&sh.loaded) = sl;
-                if (ld.done || ld.ph != ph_before || ld.step != step_before)
-                {
-                    const long long tbp = trace_base(p, step_before, ph_before);
-                    trace_mark(p, tbp, 4);
-                    if (tbp >= 0) p.trace[tbp + 6] = (unsigned long long)pwait;
-                    pwait = 0;
+    for (int step = 0; step < p.steps && ok; ++step) {
+        for (int ph = 0; ph < p.nphases && ok; ++ph) {
+            const MegaPhase& P = p.phases[ph];
+            if (P.kind != kPhGemv) continue;
+            int u0, u1;
+            unit_range(P, u0, u1);
+            if (u0 >= u1) continue;
+            StreamRanges st;
+            st.start(P, EB, u0, u1, R / P.ns);
+            long long total = (long long)(u1 - u0) * st.rowbytes * P.ns;
+            long long pwait = 0;  // cycles waited for free slots (trace)
+            while (total > 0) {
+                const uint32_t sb = (uint32_t)(total < kMegaSlot ? total : kMegaSlot);
+                const long long c0 = clock64();
+                if (sl >= (uint32_t)slots && !mega_wait(&empty[wp.s], wp.ph ^ 1u, abort, p.err)) {
+                    ok = false;
+                    break;
                 }
+                pwait += clock64() - c0;
+                mbar_arrive_expect_tx(&full[wp.s], sb);
+                unsigned char* dst = ring + (size_t)wp.s * kMegaSlot;
+                uint32_t fill = 0;
+                while (fill < sb) {
+                    if (st.left == 0 && !st.next()) {
+                        // the ranges ended before the phase's byte count (a
+                        // descriptor error): the slot's consumers time out
+                        atomicOr(p.err, kErrWaitTimeout);
+                        *abort = 1;
+                        break;
+                    }
+                    const long long room = (long long)(sb - fill);
+                    const uint32_t n = (uint32_t)(st.left < room ? st.left : room);
+                    bulk_g2s(dst + fill, st.addr, n, &full[wp.s], pol);
+                    st.addr += n;
+                    st.left -= n;
+                    fill += n;
+                }
+                total -= sb;
+                ++sl;
+                wp.advance(slots);
             }
+            const long long tbp = trace_base(p, step, ph);
+            trace_mark(p, tbp, 4);
+            if (tbp >= 0) p.trace[tbp + 6] = (unsigned long long)pwait;
         }
-        __syncwarp(0xFu);
     }
-    if (lane == 0) *reinterpret_cast<volatile int*>(&sh.producer_done) = 1;
-    if (!ok && lane == 0) {
-        // slot sl was not armed; let the copies of every armed slot land
-        // before the CTA can exit
+    if (!ok) {
+        // the next slot was not armed; let the copies of every armed slot
+        // land before the CTA can exit
         const uint32_t first = sl > (uint32_t)slots ? sl - slots : 0u;
         volatile int no_abort = 0;
         for (uint32_t q = first; q < sl; ++q) mega_wait(&full[q % slots], (q / slots) & 1u, &no_abort, p.err);
-    }
-}
-
-// L2 prefetch window: tile n of the stream is prefetched once the producer
-// has issued tile n - window.  Prefetches have no completion to wait for.
-template <typename WT>
-__device__ void prefetch_l2(const MegaParams& p, MegaShared& sh) {
-    const int window = p.l2_prefetch_tiles;
-    if (window <= 0) return;
-    volatile unsigned* loaded = &sh.loaded;
-    volatile int* done = &sh.producer_done;
-    volatile int* abort = &sh.abort;
-    TileCursor pf;
-    pf.start(p);
-    unsigned n = 0;
-    while (!pf.done) {
-        if (n >= *loaded + (unsigned)window) {
-            const long long t0 = clock64();
-            while (n >= *loaded + (unsigned)window) {
-                if (*done || *abort || clock64() - t0 > kWaitCycles) return;
-                __nanosleep(200);
-            }
-        }
-        const int nb = pf.ns == 1 ? 2 : 4;
-        for (int b = 0; b < nb; ++b) {
-            int x, y;
-            const CUtensorMap* m = tile_box<WT>(pf, b, x, y);
-            tma_prefetch_l2_2d(m, x, y);
-        }
-        pf.next(p);
-        ++n;
     }
 }
 
@@ -895,23 +955,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         sP[0] = p.phases[0];
         sP[1] = p.phases[p.nphases > 1 ? 1 : 0];
         sh.abort = 0;
-        sh.loaded = 0;
-        sh.producer_done = 0;
-        for (int i = 0; i < kGroupSlots; ++i) sh.gcnt[i] = 0;
     }
     __syncthreads();
 
     if (warp == kProducerWarp) {
-        if (lane < 4) produce<WT>(p, ring, full, empty, sh, lane);
-        return;
-    }
-    if (warp == kPrefetchWarp) {
-        if (lane == 0) prefetch_l2<WT>(p, sh);
+        if (lane == 0) produce<WT>(p, ring, full, empty, sh);
         return;
     }
 
     RingPos rp{0, 0u};
-    uint32_t gcount = 0, xphase = 0, pphase = 0;
+    uint32_t xphase = 0, pphase = 0;
     unsigned long long target = p.bar_base;
     int cur = 0;
     long long n = 0;  // phases started so far
@@ -946,9 +999,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             if (P.kind == kPhAttn) {
                 attention_phase(p, P, xs, sh, tid, xphase, pos);
             } else if (P.ns == 2) {
-                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, gcount, xphase, xs, sh, tid, tb, tok);
+                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
             } else {
-                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, gcount, xphase, xs, sh, tid, tb, tok);
+                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
             }
             trace_mark(p, tb, 2);
             target += gridDim.x;

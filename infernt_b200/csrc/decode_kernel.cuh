@@ -2,30 +2,27 @@
 // entry points (decode_kernel.cu).
 #pragma once
 
-#include <cuda.h>
-
 #include "attention.cuh"
 
 namespace infernt {
 
 enum MegaKind : int { kPhGemv = 0, kPhAttn = 1 };
 
-// One phase of a decode step.  GEMV phases stream their weights through the
-// shared-memory ring as tiles of (R rows x 512 columns); R = 8 FP32 / 16
-// bf16 (gate/up tiles carry R/2 rows of each).
+// One phase of a decode step.  A GEMV phase gives CTA b the output units
+// [units b / P, units (b + 1) / P) and streams the weight rows of those units
+// (contiguous in row-major memory) through the shared-memory ring in 16 KB
+// slots: one to three byte ranges for a stacked Q|K|V phase, two ranges per
+// batch of units for gate/up.
 struct alignas(16) MegaPhase {
     int kind;           // MegaKind
     int epi;            // EpiKind (gemv.cuh)
     int ns;             // 1, or 2 for paired gate/up
-    int nseg;           // segments stacked in the row space (Q|K|V = 3)
-    int map[3];         // tensor-map index of each segment (ns == 2: gate, up)
-    int seg_groups[3];  // tile rows groups per segment (ns == 1)
+    int nseg;           // matrices stacked in the row space (Q|K|V = 3); ns == 2: gate, up
+    const void* w[3];   // the matrices, row-major [seg_rows][K]
     int seg_rows[3];
     int units;          // output rows (ns == 2: gate/up pairs)
     int K;              // input features, a multiple of 512
     int cb;             // K / 512
-    int groups;
-    long long tiles;    // groups * cb
     const float* x;     // input vector; NULL: the per-launch input (layer 0)
     const float* norm_w;  // RMSNorm weight or NULL
     float eps;
@@ -42,7 +39,6 @@ static_assert(sizeof(MegaPhase) % 16 == 0, "MegaPhase must be a multiple of 16 b
 struct MegaParams {
     const MegaPhase* phases;
     int nphases;
-    const CUtensorMap* maps;
     // per launch
     const float* input;  // NULL: embedding row of the state's token
     float* logits;
@@ -51,9 +47,7 @@ struct MegaParams {
     // model
     const float* emb;
     int vocab;
-    float* const* kc;    // device array of per-layer K caches
-    float* const* vc;
-    AttnArgs attn;       // qkv, out, part, counter, shape, theta, scale (caches per layer)
+    AttnArgs attn;       // qkv, out, part, counter, shape, theta, scale (caches per phase)
     // scratch
     int* state;          // {token, position, step, last token}
     unsigned* err;
@@ -64,23 +58,22 @@ struct MegaParams {
     unsigned* am_cnt;
     int ring_slots;
     int x_floats;        // shared floats for the input vector / attention scratch
-    int l2_prefetch_tiles;  // tiles the L2 prefetch runs ahead of the ring loads
     // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
     // last CTA, per (step, phase): [phase start, input loaded, work done,
-    // barrier passed, producer issued the phase's last tile, SM cycles
+    // barrier passed, producer issued the phase's last slot, SM cycles
     // consumer warp 0 waited for full slots, SM cycles the producer waited
-    // for free slots while issuing the phase's tiles]
+    // for free slots while issuing the phase's slots]
     unsigned long long* trace;
 };
 
 constexpr int kTraceFields = 7;
 
-// Rows per tile for a weight type.
-inline int mega_tile_rows(int weight_dtype) { return weight_dtype == 1 ? 16 : 8; }
+// Rows of a consumer batch: 8 FP32 / 16 bf16 (a batch is whole 16 KB slots).
+inline int mega_batch_rows(int weight_dtype) { return weight_dtype == 1 ? 16 : 8; }
 
 // Dynamic shared memory of the persistent kernel.
 int mega_smem_bytes(int ring_slots, int x_floats);
-// Largest ring the kernel's group hand-off supports.
+// Largest ring the kernel uses.
 int mega_max_ring_slots();
 // Static shared memory of the kernel instantiation.
 int mega_static_smem(int weight_dtype);

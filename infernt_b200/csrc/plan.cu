@@ -31,7 +31,6 @@
 #include "decode_kernel.cuh"
 #include "gemv.cuh"
 #include "internal.h"
-#include "tensormap.h"
 
 namespace infernt {
 
@@ -297,50 +296,28 @@ int build_mega(infernt_plan* p) {
     const infernt_llama_config& c = p->cfg;
     const int H = c.hidden_size, I = c.intermediate_size, L = c.num_layers, V = c.vocab_size;
     const int dt = c.weight_dtype;
-    const int EB = dt == INFERNT_DTYPE_BF16 ? 2 : 4;
-    const int R = mega_tile_rows(dt);
     const int G = c.num_attention_heads / c.num_key_value_heads;
-    auto groups = [](int rows, int r) { return (rows + r - 1) / r; };
-
-    // tensor maps: per layer q k v o down (R-row boxes), gate up (R/2-row boxes); lm_head
-    std::vector<CUtensorMap> maps(7 * L + 1);
-    for (int l = 0; l < L; ++l) {
-        const void* const* lw = p->w.data() + 3 + 9 * l;
-        CUtensorMap* m = &maps[7 * l];
-        INFERNT_CUDA_TRY(encode_weight_map(&m[0], lw[1], p->qs, H, EB, R));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[1], lw[2], p->kvs, H, EB, R));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[2], lw[3], p->kvs, H, EB, R));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[3], lw[4], H, p->qs, EB, R));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[4], lw[6], I, H, EB, R / 2));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[5], lw[7], I, H, EB, R / 2));
-        INFERNT_CUDA_TRY(encode_weight_map(&m[6], lw[8], H, I, EB, R));
-    }
-    INFERNT_CUDA_TRY(encode_weight_map(&maps[7 * L], p->w[2], V, H, EB, R));
 
     std::vector<MegaPhase> ph;
 
-    auto gemv = [&](int epi, int ns, std::initializer_list<int> map, std::initializer_list<int> rows, int units,
-                    int K, const float* x, const float* norm, float* out, const float* res, float* x_copy) {
+    // a GEMV phase over the matrices `mats` stacked in the row space (ns ==
+    // 2: gate, up)
+    auto gemv = [&](int epi, int ns, std::initializer_list<const void*> mats, std::initializer_list<int> rows,
+                    int units, int K, const float* x, const float* norm, float* out, const float* res,
+                    float* x_copy) {
         MegaPhase P;
         memset(&P, 0, sizeof(P));
         P.kind = kPhGemv;
         P.epi = epi;
         P.ns = ns;
-        P.nseg = (int)map.size();
+        P.nseg = (int)mats.size();
         int i = 0;
-        for (int m : map) P.map[i++] = m;
+        for (const void* m : mats) P.w[i++] = m;
         i = 0;
-        P.groups = 0;
-        for (int r : rows) {
-            P.seg_rows[i] = r;
-            P.seg_groups[i] = ns == 2 ? groups(r, R / 2) : groups(r, R);
-            if (ns == 1 || i == 0) P.groups += P.seg_groups[i];
-            ++i;
-        }
+        for (int r : rows) P.seg_rows[i++] = r;
         P.units = units;
         P.K = K;
         P.cb = K / kPiece;
-        P.tiles = (long long)P.groups * P.cb;
         P.x = x;
         P.norm_w = norm;
         P.eps = c.rms_norm_eps;
@@ -352,8 +329,7 @@ int build_mega(infernt_plan* p) {
     };
     for (int l = 0; l < L; ++l) {
         const void* const* lw = p->w.data() + 3 + 9 * l;
-        const int m = 7 * l;
-        gemv(kEpiStore, 1, {m + 0, m + 1, m + 2}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
+        gemv(kEpiStore, 1, {lw[1], lw[2], lw[3]}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
              l == 0 ? nullptr : p->hidden, static_cast<const float*>(lw[0]), p->qkv, nullptr,
              l == 0 ? p->hidden : nullptr);
         MegaPhase A;
@@ -363,12 +339,12 @@ int build_mega(infernt_plan* p) {
         A.kc = p->kc[l];
         A.vc = p->vc[l];
         ph.push_back(A);
-        gemv(kEpiResidual, 1, {m + 3}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
-        gemv(kEpiSwiGLU, 2, {m + 4, m + 5}, {I, I}, I, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
+        gemv(kEpiResidual, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
+        gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {I, I}, I, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
              nullptr, nullptr);
-        gemv(kEpiResidual, 1, {m + 6}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
+        gemv(kEpiResidual, 1, {lw[8]}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
     }
-    gemv(kEpiArgmax, 1, {7 * L}, {V}, V, H, p->hidden, static_cast<const float*>(p->w[1]), nullptr, nullptr,
+    gemv(kEpiArgmax, 1, {p->w[2]}, {V}, V, H, p->hidden, static_cast<const float*>(p->w[1]), nullptr, nullptr,
          nullptr);
 
     // input vector + the norm weights behind it (RMSNorm phases), or the
@@ -392,28 +368,18 @@ int build_mega(infernt_plan* p) {
     INFERNT_REQUIRE(per_sm >= 1, "persistent decode: kernel does not fit on an SM");
     const int ctas = sm_count();
 
-    // device memory: maps | phases | cache pointers | barrier | split-K partials | tickets | argmax
+    // device memory: phases | barrier | argmax partials | argmax ticket
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
-    const size_t b_maps = al(sizeof(CUtensorMap) * maps.size());
     const size_t b_ph = al(sizeof(MegaPhase) * ph.size());
-    const size_t b_kv = al(sizeof(float*) * 2 * L);
     const size_t b_bar = 256;
     const size_t b_am = al(sizeof(float) * ctas) + al(sizeof(int) * ctas) + 256;
-    const size_t total = b_maps + b_ph + b_kv + b_bar + b_am;
+    const size_t total = b_ph + b_bar + b_am;
     INFERNT_CUDA_TRY(cudaMalloc(&p->mega_mem, total));
     INFERNT_CUDA_TRY(cudaMemset(p->mega_mem, 0, total));
     char* b = static_cast<char*>(p->mega_mem);
-    CUtensorMap* d_maps = reinterpret_cast<CUtensorMap*>(b);
-    INFERNT_CUDA_TRY(cudaMemcpy(d_maps, maps.data(), sizeof(CUtensorMap) * maps.size(), cudaMemcpyHostToDevice));
-    b += b_maps;
     MegaPhase* d_ph = reinterpret_cast<MegaPhase*>(b);
     INFERNT_CUDA_TRY(cudaMemcpy(d_ph, ph.data(), sizeof(MegaPhase) * ph.size(), cudaMemcpyHostToDevice));
     b += b_ph;
-    float** d_kv = reinterpret_cast<float**>(b);
-    std::vector<float*> kvp(p->kc);
-    kvp.insert(kvp.end(), p->vc.begin(), p->vc.end());
-    INFERNT_CUDA_TRY(cudaMemcpy(d_kv, kvp.data(), sizeof(float*) * 2 * L, cudaMemcpyHostToDevice));
-    b += b_kv;
     unsigned long long* d_bar = reinterpret_cast<unsigned long long*>(b);
     b += b_bar;
     float* d_amv = reinterpret_cast<float*>(b);
@@ -426,11 +392,8 @@ int build_mega(infernt_plan* p) {
     memset(&m, 0, sizeof(m));
     m.phases = d_ph;
     m.nphases = (int)ph.size();
-    m.maps = d_maps;
     m.emb = static_cast<const float*>(p->w[0]);
     m.vocab = V;
-    m.kc = d_kv;
-    m.vc = d_kv + L;
     m.attn.qkv = p->qkv;
     m.attn.out = p->attn;
     m.attn.part = p->attn_part;
@@ -452,11 +415,6 @@ int build_mega(infernt_plan* p) {
     m.am_cnt = d_amc;
     m.ring_slots = slots;
     m.x_floats = x_floats;
-    // L2 prefetch window per CTA in 16 KB tiles (default 32: 512 KB per SM,
-    // ~76 MB in flight over 148 SMs, well inside the 126 MB L2)
-    m.l2_prefetch_tiles = 0;
-    if (const char* env = std::getenv("INFERNT_L2_PREFETCH_TILES")) m.l2_prefetch_tiles = std::atoi(env);
-    if (m.l2_prefetch_tiles < 0) m.l2_prefetch_tiles = 0;
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
