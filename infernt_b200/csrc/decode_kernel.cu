@@ -425,28 +425,101 @@ struct SlotReader {
     }
 };
 
-// A full batch (R rows, or R / 2 gate/up units) of a phase with cb == CB:
-// CB slots whose pieces map to (row, column block) at compile time, so each
-// piece's product goes straight to its row's accumulator.  The input columns
-// stay in registers (CB <= 11) or are read from shared memory.
-template <typename WT, int CB>
-__device__ __forceinline__ void batch_static(SlotReader& rd, const float* xt, const float4* xr, float* acc, int tid,
-                                             int lane) {
-    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
+// Stream row s of a batch of nb units -> its accumulator: gate rows first,
+// then up rows (NS == 2).
+template <int NS, int BU>
+__device__ __forceinline__ int stream_row_acc(int s, int nb) {
+    return (NS == 2 && s >= nb) ? BU + (s - nb) : s;
+}
+
+// acc[k] = v with k only known at run time, without indexing the register
+// array dynamically.
+template <int R>
+__device__ __forceinline__ void acc_set(float* acc, int k, float v) {
 #pragma unroll
-    for (int j = 0; j < CB; ++j) {
+    for (int m = 0; m < R; ++m)
+        if (m == k) acc[m] = v;
+}
+
+// A batch when CB = K / 512 divides the pieces of a slot: every slot holds
+// PT / CB whole rows and the same column blocks in the same places, so a
+// slot's rows are summed with compile-time indexing and the input columns
+// stay in registers (xr).  Rows past `rows` (a short last batch) are not
+// in the stream; the tail of its last slot is computed and dropped.
+template <typename WT, int NS, int CB>
+__device__ __forceinline__ void batch_regs(SlotReader& rd, const float4* xr, float* acc, int rows, int nb, int tid,
+                                           int lane) {
+    constexpr int R = MegaRows<WT>::R, BU = R / NS;
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
+    constexpr int RS = PT / CB;  // rows per slot
+    static_assert(PT % CB == 0, "CB divides the slot");
+    const int nslots = (rows + RS - 1) / RS;
+    const bool full = rows == R;
+#pragma unroll
+    for (int j = 0; j < R / RS; ++j) {
+        if (j < nslots) {
+            const unsigned char* wp = rd.take(tid, EB);
+            float pv[PT];
+#pragma unroll
+            for (int i = 0; i < PT; ++i) pv[i] = piece_dot<WT>(wp + i * PB, xr[i % CB]);
+            rd.release(lane);
+#pragma unroll
+            for (int k = 0; k < RS; ++k) {
+                float v = 0.0f;
+#pragma unroll
+                for (int c = 0; c < CB; ++c) v += pv[k * CB + c];
+                const int s = j * RS + k;  // stream row
+                if (full)
+                    acc[s] = v;  // a full batch: stream row s is accumulator s
+                else if (s < rows)
+                    acc_set<R>(acc, stream_row_acc<NS, BU>(s, nb), v);
+            }
+        }
+    }
+}
+
+// A batch when K / 512 >= the pieces of a slot: a slot holds the end of one
+// row and at most the start of the next.  Both partial sums are formed
+// without branches (pieces in column order), the running row sum carries
+// over slots, and a finished row goes to its accumulator.  The input columns
+// are read from shared memory.
+template <typename WT, int NS>
+__device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int cb, int rows, int nb, float* acc,
+                                            int tid, int lane) {
+    constexpr int R = MegaRows<WT>::R, BU = R / NS;
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
+    const int npieces = rows * cb;
+    int q0 = 0;  // column block of the slot's first piece
+    int s = 0;   // stream row of the slot's first piece
+    float run = 0.0f;
+    for (int p0 = 0; p0 < npieces; p0 += PT) {
         const unsigned char* wp = rd.take(tid, EB);
+        const int n = min(PT, npieces - p0);
+        const int split = cb - q0;  // pieces of row s in this slot (>= 1)
         float pv[PT];
 #pragma unroll
         for (int i = 0; i < PT; ++i) {
-            constexpr int kRegs = CB <= 11;
-            const int q = (j * PT + i) % CB;
-            const float4 xv = kRegs ? xr[q] : *reinterpret_cast<const float4*>(xt + q * kPiece);
-            pv[i] = piece_dot<WT>(wp + i * PB, xv);
+            const int q = q0 + i >= cb ? q0 + i - cb : q0 + i;
+            pv[i] = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + q * kPiece));
         }
         rd.release(lane);
+        float nxt = 0.0f;
 #pragma unroll
-        for (int i = 0; i < PT; ++i) acc[(j * PT + i) / CB] += pv[i];
+        for (int i = 0; i < PT; ++i) {
+            const float v = i < n ? pv[i] : 0.0f;
+            if (i < split)
+                run += v;
+            else
+                nxt += v;
+        }
+        if (split <= n) {  // row s ends in this slot
+            acc_set<R>(acc, stream_row_acc<NS, BU>(s, nb), run);
+            run = nxt;
+            ++s;
+            q0 = n - split;
+        } else {
+            q0 += n;
+        }
     }
 }
 
@@ -480,11 +553,7 @@ __device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, f
             if (i < n) {
                 racc += pv[i];
                 if (++q == cb) {
-                    // stream row r -> accumulator: gate rows first, then up rows
-                    const int k = (NS == 2 && r >= nb) ? BU + (r - nb) : r;
-#pragma unroll
-                    for (int m = 0; m < R; ++m)
-                        if (m == k) acc[m] = racc;
+                    acc_set<R>(acc, stream_row_acc<NS, BU>(r, nb), racc);
                     racc = 0.0f;
                     q = 0;
                     ++r;
@@ -502,22 +571,26 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
     static_assert(MegaRows<WT>::PT == R, "a batch of R rows fills whole slots");
     const int warp = tid >> 5, lane = tid & 31;
     const float* xt = xs + tid * 4;  // this thread's 4 columns of every piece
-    constexpr int NXR = (CB > 0 && CB <= 11) ? CB : 1;
+    constexpr int NXR = CB > 0 ? CB : 1;
     float4 xr[NXR];
-    if (CB > 0 && CB <= 11) {
+    if (CB > 0) {
 #pragma unroll
         for (int c = 0; c < NXR; ++c) xr[c] = *reinterpret_cast<const float4*>(xt + c * kPiece);
     }
+    const bool split = CB == 0 && P.cb >= MegaRows<WT>::PT;
     float am_v = -1e30f;
     int am_i = 0;
     int bi = 0;  // batches finished in this phase
     for (int ub = u0; ub < u1; ub += BU) {
         const int nb = min(BU, u1 - ub);
+        const int rows = NS * nb;  // stream rows of the batch
         float acc[R];
 #pragma unroll
         for (int a = 0; a < R; ++a) acc[a] = 0.0f;
-        if (CB > 0 && nb == BU)
-            batch_static<WT, CB>(rd, xt, xr, acc, tid, lane);
+        if (CB > 0)
+            batch_regs<WT, NS, NXR>(rd, xr, acc, rows, nb, tid, lane);
+        else if (split)
+            batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, tid, lane);
         else
             batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, tid, lane);
         // the warp's sum of each row; lane L holds row L / (32 / R)
@@ -549,12 +622,11 @@ __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned cha
     load_x(p, P, xs, sh, tid, u0, u1, xphase, tok);
     if (tid == 0) trace_mark(p, tb, 1);
     SlotReader rd{ring, full, empty, &rp, p.ring_slots, &sh.abort, p.err, tb >= 0, 0};
-    // the stream pattern of the usual widths at compile time (every thread
-    // takes the same branch: P is shared)
+    // widths that divide a slot's pieces keep their input columns in
+    // registers (every thread takes the same branch: P is shared)
     switch (P.cb) {
         case 4: gemv_body<WT, NS, 4>(p, P, rd, xs, sh, tid, u0, u1); break;
         case 8: gemv_body<WT, NS, 8>(p, P, rd, xs, sh, tid, u0, u1); break;
-        case 11: gemv_body<WT, NS, 11>(p, P, rd, xs, sh, tid, u0, u1); break;
         default: gemv_body<WT, NS, 0>(p, P, rd, xs, sh, tid, u0, u1); break;
     }
     if (tb >= 0) p.trace[tb + 5] = (unsigned long long)rd.waited;
@@ -811,30 +883,29 @@ __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* 
 // weight matrices, in the order the consumers walk the rows: NS == 1, the
 // rows [u0, u1) of the stacked matrices (one range per matrix crossed);
 // NS == 2, per batch of bu units, the batch's gate rows then its up rows.
+// Scalar fields only (no arrays indexed at run time), so it stays in
+// registers.
 struct StreamRanges {
-    const unsigned char* w[3];
-    int seg_rows[3];
-    int nseg, ns, bu;
+    const unsigned char *w0, *w1, *w2;
+    int r0, r1;  // rows of the first two stacked matrices
+    int ns, bu;
     long long rowbytes;
-    int u, u1;      // next unit, end of the CTA's units
-    int seg, seg0;  // NS == 1: matrix of unit u and its first stacked row
-    bool up;        // NS == 2: the next range is the up half of the batch at u
+    int u, u1;  // next unit (NS == 2: first unit of the batch), end of the CTA's units
+    bool up;    // NS == 2: the next range is the batch's up rows
     const unsigned char* addr;  // rest of the current range
     long long left;
 
     __device__ void start(const MegaPhase& P, int eb, int u0, int uend, int units_per_batch) {
-        for (int i = 0; i < 3; ++i) {
-            w[i] = static_cast<const unsigned char*>(P.w[i]);
-            seg_rows[i] = P.seg_rows[i];
-        }
-        nseg = P.nseg;
+        w0 = static_cast<const unsigned char*>(P.w[0]);
+        w1 = static_cast<const unsigned char*>(P.w[1]);
+        w2 = static_cast<const unsigned char*>(P.w[2]);
+        r0 = P.nseg > 1 ? P.seg_rows[0] : P.units;
+        r1 = P.nseg > 2 ? P.seg_rows[1] : P.units;
         ns = P.ns;
         bu = units_per_batch;
         rowbytes = (long long)P.K * eb;
         u = u0;
         u1 = uend;
-        seg = 0;
-        seg0 = 0;
         up = false;
         addr = nullptr;
         left = 0;
@@ -843,18 +914,30 @@ struct StreamRanges {
     __device__ bool next() {
         if (u >= u1) return false;
         if (ns == 1) {
-            while (seg < nseg - 1 && u >= seg0 + seg_rows[seg]) {
-                seg0 += seg_rows[seg];
-                ++seg;
+            // stacked rows: [0, r0) of w0, [r0, r0 + r1) of w1, the rest of w2
+            const unsigned char* w;
+            int first, end;
+            if (u < r0) {
+                w = w0;
+                first = 0;
+                end = r0;
+            } else if (u < r0 + r1) {
+                w = w1;
+                first = r0;
+                end = r0 + r1;
+            } else {
+                w = w2;
+                first = r0 + r1;
+                end = u1;
             }
-            const int end = min(u1, seg0 + seg_rows[seg]);
-            addr = w[seg] + (long long)(u - seg0) * rowbytes;
+            end = min(end, u1);
+            addr = w + (long long)(u - first) * rowbytes;
             left = (long long)(end - u) * rowbytes;
             u = end;
             return true;
         }
         const int nb = min(bu, u1 - u);
-        addr = w[up ? 1 : 0] + (long long)u * rowbytes;
+        addr = (up ? w1 : w0) + (long long)u * rowbytes;
         left = (long long)nb * rowbytes;
         if (up) u += nb;
         up = !up;
@@ -862,66 +945,112 @@ struct StreamRanges {
     }
 };
 
+// Position in this CTA's weight stream: the GEMV phases of every step, in
+// consumer order, as byte ranges; `pos` counts the bytes passed since the
+// launch started.
+template <typename WT>
+struct StreamCursor {
+    int step, ph;
+    long long left;  // bytes left in the current phase
+    long long pos;
+    bool done;
+    StreamRanges st;
+
+    __device__ void start(const MegaParams& p) {
+        step = 0;
+        ph = -1;
+        pos = 0;
+        left = 0;
+        done = false;
+        next_phase(p);
+    }
+    // Moves to the next GEMV phase with units for this CTA.
+    __device__ void next_phase(const MegaParams& p) {
+        while (true) {
+            if (++ph == p.nphases) {
+                ph = 0;
+                if (++step >= p.steps) {
+                    done = true;
+                    left = 0;
+                    return;
+                }
+            }
+            const MegaPhase& P = p.phases[ph];
+            if (P.kind != kPhGemv) continue;
+            int u0, u1;
+            unit_range(P, u0, u1);
+            if (u0 >= u1) continue;
+            st.start(P, MegaRows<WT>::EB, u0, u1, MegaRows<WT>::R / P.ns);
+            left = (long long)(u1 - u0) * st.rowbytes * P.ns;
+            return;
+        }
+    }
+    // The next contiguous run of at most `max` bytes of the current phase;
+    // false at the end of the phase's ranges.
+    __device__ bool chunk(uint32_t max, const unsigned char*& addr, uint32_t& n) {
+        if (st.left == 0 && !st.next()) return false;
+        n = (uint32_t)(st.left < (long long)max ? st.left : (long long)max);
+        addr = st.addr;
+        st.addr += n;
+        st.left -= n;
+        left -= n;
+        pos += n;
+        return true;
+    }
+};
+
 // One thread streams every GEMV phase's weights of this CTA, across phases
 // and steps, into the ring: each slot takes the next min(16 KB, rest of the
-// phase) bytes of the phase's ranges with one or more bulk copies (a slot
-// straddles at most a matrix or gate/up boundary), completing on the slot's
-// full barrier.  A phase starts a new slot.  From the second lap on it waits
-// until the consumers released the slot.
+// phase) bytes with one or more bulk copies (a slot straddles at most a
+// matrix or gate/up boundary), completing on the slot's full barrier; a
+// phase starts a new slot.  From the second lap on it waits until the
+// consumers released the slot.  (Prefetching the stream further ahead into
+// L2 while the ring is full was measured slower: the extra queueing
+// lengthens the latency-bound synchronisation between phases.)
 template <typename WT>
 __device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full, uint64_t* empty, MegaShared& sh) {
-    constexpr int R = MegaRows<WT>::R;
-    constexpr int EB = MegaRows<WT>::EB;
     volatile int* abort = &sh.abort;
     const int slots = p.ring_slots;
     const uint64_t pol = l2_evict_first_policy();
     uint32_t sl = 0;  // slots armed so far
     bool ok = true;
     RingPos wp{0, 0u};
-    for (int step = 0; step < p.steps && ok; ++step) {
-        for (int ph = 0; ph < p.nphases && ok; ++ph) {
-            const MegaPhase& P = p.phases[ph];
-            if (P.kind != kPhGemv) continue;
-            int u0, u1;
-            unit_range(P, u0, u1);
-            if (u0 >= u1) continue;
-            StreamRanges st;
-            st.start(P, EB, u0, u1, R / P.ns);
-            long long total = (long long)(u1 - u0) * st.rowbytes * P.ns;
-            long long pwait = 0;  // cycles waited for free slots (trace)
-            while (total > 0) {
-                const uint32_t sb = (uint32_t)(total < kMegaSlot ? total : kMegaSlot);
-                const long long c0 = clock64();
-                if (sl >= (uint32_t)slots && !mega_wait(&empty[wp.s], wp.ph ^ 1u, abort, p.err)) {
-                    ok = false;
-                    break;
-                }
-                pwait += clock64() - c0;
-                mbar_arrive_expect_tx(&full[wp.s], sb);
-                unsigned char* dst = ring + (size_t)wp.s * kMegaSlot;
-                uint32_t fill = 0;
-                while (fill < sb) {
-                    if (st.left == 0 && !st.next()) {
-                        // the ranges ended before the phase's byte count (a
-                        // descriptor error): the slot's consumers time out
-                        atomicOr(p.err, kErrWaitTimeout);
-                        *abort = 1;
-                        break;
-                    }
-                    const long long room = (long long)(sb - fill);
-                    const uint32_t n = (uint32_t)(st.left < room ? st.left : room);
-                    bulk_g2s(dst + fill, st.addr, n, &full[wp.s], pol);
-                    st.addr += n;
-                    st.left -= n;
-                    fill += n;
-                }
-                total -= sb;
-                ++sl;
-                wp.advance(slots);
+    StreamCursor<WT> lc;
+    lc.start(p);
+    long long pwait = 0;  // cycles waited for free slots in the phase (trace)
+    while (!lc.done && ok) {
+        const uint32_t sb = (uint32_t)(lc.left < kMegaSlot ? lc.left : kMegaSlot);
+        const long long c0 = clock64();
+        if (sl >= (uint32_t)slots && !mega_wait(&empty[wp.s], wp.ph ^ 1u, abort, p.err)) {
+            ok = false;
+            break;
+        }
+        pwait += clock64() - c0;
+        mbar_arrive_expect_tx(&full[wp.s], sb);
+        unsigned char* dst = ring + (size_t)wp.s * kMegaSlot;
+        uint32_t fill = 0;
+        while (fill < sb) {
+            const unsigned char* a;
+            uint32_t n;
+            if (!lc.chunk(sb - fill, a, n)) {
+                // the ranges ended before the phase's byte count (a
+                // descriptor error): the slot's consumers time out
+                atomicOr(p.err, kErrWaitTimeout);
+                *abort = 1;
+                ok = false;
+                break;
             }
-            const long long tbp = trace_base(p, step, ph);
+            bulk_g2s(dst + fill, a, n, &full[wp.s], pol);
+            fill += n;
+        }
+        ++sl;
+        wp.advance(slots);
+        if (lc.left == 0) {
+            const long long tbp = trace_base(p, lc.step, lc.ph);
             trace_mark(p, tbp, 4);
             if (tbp >= 0) p.trace[tbp + 6] = (unsigned long long)pwait;
+            pwait = 0;
+            lc.next_phase(p);
         }
     }
     if (!ok) {

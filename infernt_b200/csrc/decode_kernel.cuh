@@ -57,8 +57,7 @@ struct MegaParams {
     int* am_idx;
     unsigned* am_cnt;
     int ring_slots;
-    int x_floats;        // shared floats for the input vector / attention scratch
-    // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
+    int x_floats;        // shared floats for the input vector / attention scratch    // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
     // last CTA, per (step, phase): [phase start, input loaded, work done,
     // barrier passed, producer issued the phase's last slot, SM cycles
     // consumer warp 0 waited for full slots, SM cycles the producer waited
