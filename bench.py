@@ -15,8 +15,10 @@ Our arm prints one JSON line with
            (infernt_engine_forward_token -> InferenceEngine::forward_token):
            token and position in as kernel arguments, next token out by a
            4-byte device-to-host copy, one host sync per step;
-  roofline the dominant kernel (RMSNorm + gate/up + SiLU GEMV) timed alone
-           with CUDA events over every layer's weights;
+  roofline the dominant kernel, the persistent decode kernel (one launch
+           runs the K chained steps): algorithmic bytes of K steps over its
+           CUDA-event time, against the measured HBM copy bandwidth; traffic
+           from the ncu summary under profiles/;
   cpu_baseline  the CPU oracle (oracle/, scalar C, all host threads) on a
            bounded sample of the same decode, rank 0 at N=1 only.
 With N > 1 (torchrun, one process per GPU) every rank decodes its own
@@ -48,6 +50,23 @@ METRIC = "decode tok/s (TinyLlama-1.1B FP32 batch-1 greedy)"
 def env_rank():
     return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), \
         int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def max_over_ranks(torch, x, device):
+    """The largest value of x over all ranks (x itself without a process
+    group): timings are reported as the slowest rank's."""
+    import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized() or dist.get_world_size() == 1:
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_tokens_per_s(world, steps, ms_max):
+    """Whole-job throughput: every rank decodes `steps` tokens of its own
+    sequence; the job takes the slowest rank's time."""
+    return world * steps / (ms_max / 1e3)
 
 
 def peaks():
@@ -214,12 +233,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_max = float(t.item())
-    value = world * K / (ms_max / 1e3)
+    ms_max = max_over_ranks(torch, ms, "cuda")
+    value = job_tokens_per_s(world, K, ms_max)
 
     # ---- end to end through the public C API (same positions)
     first = prefill()
@@ -237,12 +252,8 @@ def run_ours(args):
     b.record()
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = a.elapsed_time(b)
-    if world > 1:
-        tt = torch.tensor([e2e_ms], device="cuda")
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
-    e2e_value = world * K / (e2e_ms / 1e3)
+    e2e_ms = max_over_ranks(torch, a.elapsed_time(b), "cuda")
+    e2e_value = job_tokens_per_s(world, K, e2e_ms)
     same_tokens = e2e_toks == toks
 
     # ---- roofline of the dominant kernel: the persistent decode kernel runs
@@ -351,17 +362,110 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_layer_ops(args):
+    """Single-layer decode microbench at the TinyLlama shape (FP32): one token
+    at position 4095 with the KV cache filled with seeded N(0,1) values for
+    4095 positions; every op of the layer launched alone through the C ABI,
+    L2 flushed (a 256 MB write) before each timed launch, CUDA events around
+    the launch on its stream; median over --steps launches after --warmup.
+    Each op's algorithmic bytes (weights, inputs, outputs, K/V rows read)
+    over its time, against the measured HBM bandwidth."""
+    import torch
+    import infernt_b200 as ib
+    torch.cuda.set_device(0)
+    H, I, Nq, Nkv, D, V = 2048, 5632, 32, 4, 64, 32000
+    pos, max_seq, eps, theta = 4095, 4096, 1e-5, 10000.0
+    qs, kvs = Nq * D, Nkv * D
+    f32 = 0
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+
+    def randn(*shape, std=1.0):
+        return torch.randn(*shape, device="cuda", generator=g) * std
+
+    x, nw = randn(H), torch.ones(H, device="cuda")
+    wq, wk, wv = randn(qs, H, std=STD), randn(kvs, H, std=STD), randn(kvs, H, std=STD)
+    wo, wg, wu, wd = randn(H, qs, std=STD), randn(I, H, std=STD), randn(I, H, std=STD), randn(H, I, std=STD)
+    kc, vc = randn(Nkv, max_seq, D), randn(Nkv, max_seq, D)
+    qkv, attn, act, hid, y = (torch.zeros(n, device="cuda") for n in (qs + 2 * kvs, qs, I, H, H))
+    logits = randn(V)
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    splits = torch.cuda.get_device_properties(0).multi_processor_count // Nkv
+    ws = torch.zeros(ib.lib().infernt_attention_workspace_bytes(Nq, Nkv, D, splits), dtype=torch.uint8,
+                     device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    P = lambda t: t.data_ptr()  # noqa: E731
+    ops = [
+        ("rmsnorm", 3 * H * 4, lambda: ib.call("infernt_rmsnorm", P(y), P(x), P(nw), 1, H, eps, sp)),
+        ("qkv_rmsnorm_gemv", (qs + 2 * kvs) * H * 4 + 2 * H * 4 + (qs + 2 * kvs) * 4,
+         lambda: ib.call("infernt_rmsnorm_gemv", P(qkv), P(wq), qs, P(wk), kvs, P(wv), kvs, H, f32, P(x), P(nw),
+                         eps, sp)),
+        ("rope", 2 * (qs + kvs) * 4, lambda: ib.call("infernt_rope", P(qkv), P(qkv) + qs * 4, 1, Nq, Nkv, D, pos,
+                                                     theta, sp)),
+        ("kv_cache_append", 4 * kvs * 4, lambda: ib.call("infernt_kv_cache_append", P(kc), P(vc), P(qkv) + qs * 4,
+                                                         P(qkv) + (qs + kvs) * 4, Nkv, D, max_seq, pos, sp)),
+        ("attention_decode", 2 * Nkv * (pos + 1) * D * 4 + (qs + 2 * kvs) * 4 + qs * 4,
+         lambda: ib.call("infernt_attention_decode", P(attn), P(qkv), P(kc), P(vc), Nq, Nkv, D, max_seq, pos, theta,
+                         splits, P(ws), sp)),
+        ("o_gemv_residual", H * qs * 4 + qs * 4 + 2 * H * 4,
+         lambda: ib.call("infernt_gemv_residual", P(hid), P(x), P(wo), H, qs, f32, P(attn), sp)),
+        ("gate_up_rmsnorm_silu", 2 * I * H * 4 + 2 * H * 4 + I * 4,
+         lambda: ib.call("infernt_rmsnorm_gate_up_silu", P(act), P(wg), P(wu), I, H, f32, P(hid), P(nw), eps, sp)),
+        ("down_gemv_residual", H * I * 4 + I * 4 + 2 * H * 4,
+         lambda: ib.call("infernt_gemv_residual", P(y), P(hid), P(wd), H, I, f32, P(act), sp)),
+        ("residual_add", 3 * H * 4, lambda: ib.call("infernt_residual_add", P(y), P(hid), P(x), H, sp)),
+        ("argmax", V * 4 + 4, lambda: ib.call("infernt_argmax", P(tok), P(logits), V, sp)),
+    ]
+    hbm, src = peaks()
+    res = {}
+    for name, nbytes, op in ops:
+        for _ in range(args.warmup):
+            op()
+        times = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            op()
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        times.sort()
+        ms = times[len(times) // 2]
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4)}
+    total_us = sum(r["us"] for r in res.values())
+    total_bytes = sum(r["bytes"] for r in res.values())
+    print(json.dumps({
+        "metric": "single-layer decode ops at position 4095 (TinyLlama shape, FP32)", "unit": "us",
+        "value": round(total_us, 2), "higher_is_better": False, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "dtype": "f32", "data": "synthetic: torch.randn seeded 0 (weights x0.02), "
+        "KV cache N(0,1) for 4095 positions, logits N(0,1)",
+        "config": {"workload": "tinyllama-layer-ops-pos4095", "position": pos, "attention_splits": splits,
+                   "l2": "flushed before every timed launch (256 MB write)"},
+        "ops": res, "layer_bytes": total_bytes,
+        "layer_gbs": round(total_bytes / (total_us / 1e6) / 1e9, 1),
+        "peak": {"hbm_gbs": hbm, "source": src},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "layer-ops"], default="decode",
+                    help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
+                         "at position 4095, timed alone")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.workload == "layer-ops":
+        run_layer_ops(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

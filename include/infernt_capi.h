@@ -173,7 +173,8 @@ INFERNT_API int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, co
  *                            kernel per call (a whole chain of steps too);
  *                            falls back to GRAPH when the shapes do not allow
  *                            it (projection inputs not multiples of 512,
- *                            unaligned weights).                          */
+ *                            weights or caches not 16-byte aligned, head_dim
+ *                            not a multiple of 4).                        */
 enum { INFERNT_MODE_EAGER = 0, INFERNT_MODE_GRAPH = 1, INFERNT_MODE_PERSISTENT = 2 };
 typedef struct {
     int vocab_size;
@@ -227,10 +228,12 @@ INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
 /* Phase timeline of the persistent decode kernel.  Phases per step:
  * 5 per layer (qkv, attention, o, gate/up, down) + the LM head.  With a
  * device buffer of infernt_plan_trace_entries(plan, steps) uint64 set, the
- * following launches record %globaltimer nanoseconds for CTA 0 and the last
- * CTA per (step, phase): [phase start, input loaded, work done, grid barrier
- * passed, producer issued the phase's last tile], layout
- * [cta (2)][step][phase][5].  NULL turns it off.  PERSISTENT mode only. */
+ * following launches record, for CTA 0 and the last CTA per (step, phase):
+ * [phase start, input loaded, work done, grid barrier passed, producer issued
+ * the phase's last slot] as %globaltimer nanoseconds, then the SM cycles the
+ * first consumer thread waited for weight slots and the SM cycles the
+ * producer waited for free slots; layout [cta (2)][step][phase][7].  NULL
+ * turns it off.  PERSISTENT mode only. */
 INFERNT_API size_t infernt_plan_trace_entries(const infernt_plan* plan, int steps);
 INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* trace_dev);
 
