@@ -450,21 +450,101 @@ def run_layer_ops(args):
     }), flush=True)
 
 
+def run_llama8b_tp(args):
+    """Llama-3-8B-shaped bf16 greedy decode, batch 1, tensor-parallel over
+    the torchrun ranks (one per GPU; 1 without torchrun): seeded weights
+    (seed 1), a 512-token seeded prompt, then --steps chained decode steps
+    timed with CUDA events on each rank, max over ranks.  The O and down
+    all-reduces and the argmax exchange run inside the persistent kernel over
+    NVLink peer memory; torch.distributed only swaps the exchange-region
+    handles and lines the ranks up.  value: the sequence's tokens/s (strong
+    scaling: the same sequence on more GPUs)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import infernt_b200 as ib
+    import oracle as O
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    prompt_len = 512
+    cfg = ib.LLAMA3_8B.with_(max_seq_len=prompt_len + args.warmup + args.steps + 8)
+    seed = 1
+    eng = ib.TPEngine(cfg, rank, world, seed=seed, std=STD)
+    if world > 1:
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.xchg_handle())
+        eng.set_peers(handles)
+        dist.barrier()
+    prompt = [int(t) for t in O.prompt(prompt_len, seed, 3, cfg.vocab_size)]
+    t = None
+    for pos, tok in enumerate(prompt):
+        t = eng.forward_token(tok, pos)
+    toks_w, _ = eng.decode_chain(t, prompt_len, args.warmup)
+    start_tok, start_pos = toks_w[-1], prompt_len + args.warmup
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    toks, ms = eng.decode_chain(start_tok, start_pos, args.steps)
+    clocks = sampler.stop()
+    ms_max = max_over_ranks(torch, ms, "cuda")
+    K = args.steps
+    value = K / (ms_max / 1e3)
+    # per-GPU algorithmic bytes per token: this rank's weight shards (bf16),
+    # its KV rows read by attention, the embedding row
+    H, L, D = cfg.hidden_size, cfg.num_layers, cfg.head_dim
+    d = eng.dims
+    per_layer = (d[0] * D + 2 * d[1] * D) * H + H * d[0] * D + 2 * d[2] * H + H * d[3]
+    wbytes = 2 * (L * per_layer + d[5] * H)
+    ctx_mean = start_pos + K / 2.0
+    kv = 2 * L * d[1] * D * 4 * (ctx_mean + 1)
+    bytes_gpu = wbytes + kv + H * 4
+    hbm, src = peaks()
+    achieved = bytes_gpu * K / (ms_max / 1e3) / 1e9
+    result = {
+        "metric": "decode tok/s (Llama-3-8B shape, bf16 weights, batch 1, tensor parallel)", "value": round(value, 3),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_max / K, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 weights, f32 math",
+        "data": "synthetic: seeded weights N(0,0.02) seed 1, norms 1.0, 512-token seeded prompt",
+        "config": {"workload": "llama3-8b-bf16-b1-tp%d" % world, "hidden": H, "layers": L, "q_heads": 32,
+                   "kv_heads": 8, "head_dim": D, "intermediate": cfg.intermediate_size, "vocab": cfg.vocab_size,
+                   "prompt_tokens": prompt_len, "positions": [start_pos, start_pos + K],
+                   "parallelism": "tp%d" % world, "l2": "no flush: %.2f GB of weights per GPU per step"
+                   % (wbytes / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "decode_mega_kernel<bf16> (persistent, per GPU)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "peak_source": src, "bytes_per_gpu_per_step": bytes_gpu},
+        "clocks": clocks,
+    }
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "layer-ops"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp"], default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
-                         "at position 4095, timed alone")
+                         "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
+                         "tensor-parallel over the torchrun ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.workload == "layer-ops":
         run_layer_ops(args)
+    elif args.workload == "llama8b-tp":
+        run_llama8b_tp(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

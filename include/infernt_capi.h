@@ -237,12 +237,80 @@ INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
 INFERNT_API size_t infernt_plan_trace_entries(const infernt_plan* plan, int steps);
 INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* trace_dev);
 
+/* ----------------------------------------- tensor parallelism ---
+ * The 8B-class configuration decoded by tp_size GPUs, one process per GPU
+ * (the reference has a single-GPU engine only; this extends
+ * LlamaArchitecture::forward, architectures/llama/llama_model.cpp:45-65,
+ * Megatron-style).  Rank t of T holds
+ *   q/k/v: the rows of its Nq/T query heads and Nkv/T KV heads,
+ *   o:     the columns of its query heads, [h, Nq*D/T],
+ *   gate/up: rows [t*I/T, (t+1)*I/T),
+ *   down:  the matching columns, [h, Ip] with Ip = I/T rounded up to 512 and
+ *          the extra columns zero,
+ *   lm_head: vocabulary rows [V*t/T, V*(t+1)/T), the embedding in full,
+ * and its KV heads' caches [Nkv/T, max_seq, D].  The O and down products are
+ * all-reduced inside the persistent decode kernel: each rank writes its
+ * partial rows into every rank's exchange region over NVLink (peer memory
+ * mapped by CUDA IPC) and the ranks meet at a bounded system-scope flag
+ * barrier; the next phase adds the partials in rank order, so every rank
+ * holds bit-identical activations.  The greedy token is agreed the same
+ * way.  Every rank must run the same calls in the same order.
+ *
+ * infernt_tp_shard_dims: dims[6] = {Nq/T, Nkv/T, I/T, Ip, first vocabulary
+ * row, vocabulary rows} of rank t.  infernt_plan_create_tp: `cfg` is the
+ * whole model's; weights/caches are the rank's shards in the order of
+ * infernt_plan_create.  Then exchange the ranks' 64-byte handles
+ * (infernt_plan_xchg_handle) by any host channel and pass all of them, in
+ * rank order, to infernt_plan_set_peers before the first decode call.
+ * Decode calls (forward, decode, decode_chain) then work as for a single
+ * GPU; logits hold the rank's vocabulary rows. */
+#define INFERNT_IPC_HANDLE_BYTES 64
+INFERNT_API int infernt_tp_shard_dims(const infernt_llama_config* cfg, int tp_rank, int tp_size,
+                                      int* dims);
+INFERNT_API int infernt_plan_create_tp(const infernt_llama_config* cfg, const void* const* weights,
+                                       float* const* k_cache, float* const* v_cache, int tp_rank,
+                                       int tp_size, infernt_plan** out);
+INFERNT_API int infernt_plan_xchg_handle(infernt_plan* plan, void* handle_out);
+INFERNT_API int infernt_plan_set_peers(infernt_plan* plan, const void* handles);
+
+/* One rank of a tensor-parallel decoder with seeded synthetic weights: the
+ * rank's shards are windows of the matrices infernt_engine_create_seeded
+ * generates for the same seed (norms 1.0), its KV caches start at zero.
+ * Exchange handles and set peers as for the plan; forward_token runs one
+ * greedy step (every rank returns the same token); decode_chain runs
+ * `steps` chained steps and reports their device time (CUDA events);
+ * logits copies the rank's vocabulary rows (dims: infernt_tp_shard_dims). */
+typedef struct infernt_tp_engine infernt_tp_engine;
+INFERNT_API int infernt_tp_engine_create_seeded(const infernt_llama_config* cfg, uint64_t seed,
+                                                float std_dev, int tp_rank, int tp_size,
+                                                infernt_tp_engine** out);
+INFERNT_API int infernt_tp_engine_destroy(infernt_tp_engine* e);
+INFERNT_API int infernt_tp_engine_xchg_handle(infernt_tp_engine* e, void* handle_out);
+INFERNT_API int infernt_tp_engine_set_peers(infernt_tp_engine* e, const void* handles);
+INFERNT_API int infernt_tp_engine_forward_token(infernt_tp_engine* e, int token, int position,
+                                                int* next_token);
+INFERNT_API int infernt_tp_engine_decode_chain(infernt_tp_engine* e, int token, int position,
+                                               int steps, int* tokens_host, float* ms);
+INFERNT_API int infernt_tp_engine_logits(infernt_tp_engine* e, float* logits_host, int n);
+INFERNT_API int infernt_tp_engine_dims(infernt_tp_engine* e, int* dims);
+/* decode_chain with the phase timeline of infernt_plan_set_trace recorded into host_out
+ * (infernt_plan_trace_entries entries). */
+INFERNT_API int infernt_tp_engine_trace_chain(infernt_tp_engine* e, int token, int position,
+                                              int steps, unsigned long long* host_out, size_t n);
+
 /* ------------------------------------------------ synthetic weights ---
  * Fill device memory with the seeded values of include/infernt_seed.h
  * (bit-identical to the host generator).  dtype selects float or bf16
  * output; bf16 values are the float values rounded to nearest even.     */
 INFERNT_API int infernt_fill_normal(void* dst, size_t n, int dtype, uint64_t seed,
                                     uint64_t stream_id, float std_dev, void* stream);
+/* dst [rows][ld_dst] = rows row0.. and columns col0..col0+cols-1 of the seeded matrix with
+ * src_ld columns that infernt_fill_normal(seed, stream_id) would produce (its element
+ * (r, c) has index r*src_ld + c); columns cols..ld_dst-1 are zero.  For weight shards. */
+INFERNT_API int infernt_fill_normal_window(void* dst, int rows, int cols, int ld_dst,
+                                           uint64_t src_ld, uint64_t row0, uint64_t col0,
+                                           int dtype, uint64_t seed, uint64_t stream_id,
+                                           float std_dev, void* stream);
 INFERNT_API int infernt_fill_const(float* dst, size_t n, float value, void* stream);
 /* KV prefill: rows [0, n_pos) of every layer's K and V cache get N(0, std) from the
  * KV streams (element (l, h, p, d) = index ((l*Nkv + h) * 2^20 + p) * D + d). */

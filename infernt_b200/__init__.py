@@ -160,7 +160,24 @@ _SIGS = {
     "infernt_engine_decode_chain": (_I, [_P, _I, _I, _I, _P, ctypes.POINTER(_F)]),
     "infernt_engine_weight_ptrs": (_I, [_P, ctypes.POINTER(_P), _I]),
     "infernt_engine_kv_ptrs": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_P), _I]),
+    "infernt_fill_normal_window": (_I, [_P, _I, _I, _I, _U64, _U64, _U64, _I, _U64, _U64, _F, _P]),
+    "infernt_tp_shard_dims": (_I, [ctypes.POINTER(LlamaConfig), _I, _I, ctypes.POINTER(_I)]),
+    "infernt_plan_create_tp": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P), ctypes.POINTER(_P),
+                                    ctypes.POINTER(_P), _I, _I, ctypes.POINTER(_P)]),
+    "infernt_plan_xchg_handle": (_I, [_P, _P]),
+    "infernt_plan_set_peers": (_I, [_P, _P]),
+    "infernt_tp_engine_create_seeded": (_I, [ctypes.POINTER(LlamaConfig), _U64, _F, _I, _I, ctypes.POINTER(_P)]),
+    "infernt_tp_engine_destroy": (_I, [_P]),
+    "infernt_tp_engine_xchg_handle": (_I, [_P, _P]),
+    "infernt_tp_engine_set_peers": (_I, [_P, _P]),
+    "infernt_tp_engine_forward_token": (_I, [_P, _I, _I, ctypes.POINTER(_I)]),
+    "infernt_tp_engine_decode_chain": (_I, [_P, _I, _I, _I, _P, ctypes.POINTER(_F)]),
+    "infernt_tp_engine_logits": (_I, [_P, _P, _I]),
+    "infernt_tp_engine_dims": (_I, [_P, ctypes.POINTER(_I)]),
+    "infernt_tp_engine_trace_chain": (_I, [_P, _I, _I, _I, _P, _S]),
 }
+
+IPC_HANDLE_BYTES = 64
 
 
 def exported_symbols():
@@ -268,9 +285,10 @@ class Engine:
 
     def trace_chain(self, token: int, position: int, steps: int):
         """Device-chained decode with the persistent kernel's phase timeline.
-        Returns an int64 array [cta (0 = first, 1 = last)][step][phase][5]
-        of %globaltimer ns: phase start, input loaded, work done, barrier
-        passed, producer issued the phase's last tile."""
+        Returns an int64 array [cta (0 = first, 1 = last)][step][phase][7]:
+        %globaltimer ns of phase start, input loaded, work done, barrier
+        passed, producer issued the phase's last slot; then the SM cycles
+        the first consumer waited for slots and the producer for free ones."""
         import numpy as np
         nph = 5 * self.cfg.num_layers + 1
         out = np.zeros(2 * steps * nph * TRACE_FIELDS, dtype=np.uint64)
@@ -289,3 +307,73 @@ class Engine:
         v = (ctypes.c_void_p * n)()
         call("infernt_engine_kv_ptrs", self._h, k, v, n)
         return [k[i] for i in range(n)], [v[i] for i in range(n)]
+
+
+class TPEngine:
+    """One rank of a tensor-parallel decoder (infernt_tp_engine_* in
+    include/infernt_capi.h) with seeded synthetic weights: the rank's shards
+    of the model Engine(cfg, seed) would hold.  All ranks construct, swap
+    xchg_handle() bytes by any host channel, and call set_peers(handles in
+    rank order) before decoding; then every call must be made on every rank
+    in the same order."""
+
+    def __init__(self, cfg: ModelConfig, rank: int, world: int, seed: int = 0, std: float = 0.02):
+        self.cfg, self.rank, self.world = cfg, rank, world
+        h = ctypes.c_void_p()
+        call("infernt_tp_engine_create_seeded", ctypes.byref(cfg.c()), seed, std, rank, world, ctypes.byref(h))
+        self._h = h
+        d = (ctypes.c_int * 6)()
+        call("infernt_tp_engine_dims", self._h, d)
+        self.dims = list(d)
+        self.vocab_range = (d[4], d[4] + d[5])
+
+    def close(self):
+        if self._h:
+            lib().infernt_tp_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def xchg_handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        call("infernt_tp_engine_xchg_handle", self._h, buf)
+        return buf.raw
+
+    def set_peers(self, handles):
+        blob = b"".join(handles)
+        assert len(blob) == IPC_HANDLE_BYTES * self.world
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        call("infernt_tp_engine_set_peers", self._h, buf)
+
+    def forward_token(self, token: int, position: int) -> int:
+        out = ctypes.c_int()
+        call("infernt_tp_engine_forward_token", self._h, token, position, ctypes.byref(out))
+        return out.value
+
+    def decode_chain(self, token: int, position: int, steps: int):
+        """Device-chained greedy decode; returns (tokens, device ms)."""
+        import numpy as np
+        toks = np.zeros(steps, dtype=np.int32)
+        ms = ctypes.c_float()
+        call("infernt_tp_engine_decode_chain", self._h, token, position, steps, toks.ctypes.data, ctypes.byref(ms))
+        return toks.tolist(), ms.value
+
+    def logits(self):
+        """This rank's vocabulary rows [vocab_range) of the last step's logits."""
+        import numpy as np
+        out = np.empty(self.dims[5], dtype=np.float32)
+        call("infernt_tp_engine_logits", self._h, out.ctypes.data, out.size)
+        return out
+
+    def trace_chain(self, token: int, position: int, steps: int):
+        """decode_chain with the persistent kernel's phase timeline (as
+        Engine.trace_chain)."""
+        import numpy as np
+        nph = 5 * self.cfg.num_layers + 1
+        out = np.zeros(2 * steps * nph * TRACE_FIELDS, dtype=np.uint64)
+        call("infernt_tp_engine_trace_chain", self._h, token, position, steps, out.ctypes.data, out.size)
+        return out.reshape(2, steps, nph, TRACE_FIELDS).astype(np.int64)

@@ -68,6 +68,7 @@ struct MegaShared {
     int res_n;     // staged rows
     float res[kResRows];
     float gpart[4][kGroupBatch][16];  // per-warp row sums of up to kGroupBatch batches
+    unsigned long long xe;            // tensor parallelism: epoch of the phase's exchange
     uint64_t xbar;                    // completion of the input-vector bulk copy
     uint64_t pbar;                   // completion of the next phase descriptor's bulk copy
 };
@@ -119,17 +120,70 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
     return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Publishes exchange epoch e to every rank (after this rank's data writes,
+// which the caller has fenced at system scope) and waits, bounded, until
+// every rank has published e.  Returns false on timeout.
+__device__ bool exchange_flags(const MegaParams& p, unsigned long long e, volatile int* abort) {
+    for (int r = 0; r < p.tp_size; ++r)
+        st_release_sys64(reinterpret_cast<unsigned long long*>(p.peers[r] + kXchFlags) + p.tp_rank, e);
+    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + kXchFlags);
+    const long long t0 = clock64();
+    for (int r = 0; r < p.tp_size; ++r) {
+        while (ld_acquire_sys64(own + r) < e) {
+            if (*abort || (ld_acquire(p.err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
+                atomicOr(p.err, kErrWaitTimeout);
+                *abort = 1;
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
 // Grid barrier of the consumer warps: every CTA adds 1 (release) to a 64-bit
 // counter that only grows, and polls (acquire) until it reaches `target`
 // (the launch's base plus gridDim.x per barrier passed).  One atomic per
 // CTA, no reset and no last-arriver hop.  The named barrier orders the other
 // consumer threads' writes before thread 0's release, which is cumulative,
 // so no separate fence is needed.
+//
+// After an exchange phase (xe > 0) the barrier also crosses the GPUs: once
+// every local CTA has arrived (each fenced its writes into the peers'
+// regions at system scope first), CTA 0 publishes epoch xe to every rank,
+// waits for every rank's, and adds one more arrival; the other CTAs wait for
+// that one too (target counts it).
 __device__ __forceinline__ void grid_sync(const MegaParams& p, volatile int* abort, int tid,
-                                          unsigned long long target) {
+                                          unsigned long long target, unsigned long long xe = 0) {
     named_sync(1, kMegaConsumers);
     if (tid == 0 && !*abort) {
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p.bar) : "memory");
+        if (xe && blockIdx.x == 0) {
+            const long long t0 = clock64();
+            while (ld_acquire64(p.bar) < target - 1) {
+                if ((ld_acquire(p.err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
+                    atomicOr(p.err, kErrWaitTimeout);
+                    *abort = 1;
+                    break;
+                }
+            }
+            if (!*abort) {
+                __threadfence_system();
+                exchange_flags(p, xe, abort);
+            }
+            // the extra arrival is made even after a failure, so no CTA waits
+            // on it in vain
+            asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p.bar) : "memory");
+        }
         if (ld_acquire64(p.bar) < target) {
             const long long t0 = clock64();
             while (ld_acquire64(p.bar) < target) {
@@ -210,16 +264,43 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
             src = p.emb + (size_t)t * P.K;
         }
     }
-    if (tid == 0) {
-        // the input vector (and the norm weights behind it) in one bulk copy
-        // each, issued first so the residual loads below overlap them; the
-        // vector was written by generic stores (after the grid barrier's
-        // acquire), read here through the async proxy
+    // the input vector (and the norm weights behind it) in one bulk copy
+    // each, issued first so the residual loads below overlap them; the
+    // vector was written by generic stores (after the grid barrier's
+    // acquire), read here through the async proxy.  A summed input (tensor
+    // parallelism) is formed by the threads instead.
+    const bool sum = P.nsum > 0;
+    const uint32_t vbytes = (uint32_t)P.K * 4u;
+    const uint32_t bytes = (sum ? 0u : vbytes) + (P.norm_w ? vbytes : 0u);
+    if (tid == 0 && bytes) {
         fence_proxy_async_global();
-        const uint32_t bytes = (uint32_t)P.K * 4u;
-        mbar_arrive_expect_tx(&sh.xbar, P.norm_w ? 2u * bytes : bytes);
-        bulk_g2s_plain(xs, src, bytes, &sh.xbar);
-        if (P.norm_w) bulk_g2s_plain(xs + P.K, P.norm_w, bytes, &sh.xbar);
+        mbar_arrive_expect_tx(&sh.xbar, bytes);
+        if (!sum) bulk_g2s_plain(xs, src, vbytes, &sh.xbar);
+        if (P.norm_w) bulk_g2s_plain(xs + P.K, P.norm_w, vbytes, &sh.xbar);
+    }
+    if (sum) {
+        // x = src + the ranks' partials in rank order (every rank forms the
+        // same sum); this CTA also stores its share of the result for later
+        // phases' residual reads
+        const int s0 = (int)((long long)P.K * blockIdx.x / gridDim.x);
+        const int s1 = (int)((long long)P.K * (blockIdx.x + 1) / gridDim.x);
+        for (int i = tid * 4; i < P.K; i += kMegaConsumers * 4) {
+            float4 v = __ldcg(reinterpret_cast<const float4*>(src + i));
+            for (int r = 0; r < P.nsum; ++r) {
+                const float4 w = __ldcg(reinterpret_cast<const float4*>(P.xsum + (size_t)r * P.K + i));
+                v.x += w.x;
+                v.y += w.y;
+                v.z += w.z;
+                v.w += w.w;
+            }
+            *reinterpret_cast<float4*>(xs + i) = v;
+            if (P.xout) {
+                const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (i + j >= s0 && i + j < s1) P.xout[i + j] = e[j];
+            }
+        }
     }
     int staged = 0;
     const int staged_base = u0;
@@ -231,8 +312,10 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         sh.res_n = staged;
         sh.res_base = staged_base;
     }
-    mega_wait(&sh.xbar, xphase & 1u, &sh.abort, p.err);
-    ++xphase;
+    if (bytes) {
+        mega_wait(&sh.xbar, xphase & 1u, &sh.abort, p.err);
+        ++xphase;
+    }
     constexpr int STRIDE = kMegaConsumers * 4;
     if (P.x_copy && blockIdx.x == 0)
         for (int i = tid * 4; i < P.K; i += STRIDE)
@@ -316,12 +399,17 @@ __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaSha
             const int ri = row - sh.res_base;
             const float r = (ri >= 0 && ri < sh.res_n) ? sh.res[ri] : __ldcg(P.res + row);
             P.out[row] = r + v;
+        } else if (P.epi == kEpiExchange) {
+            // this rank's partial of the row, into every rank's slot for it
+            for (int r = 0; r < p.tp_size; ++r)
+                reinterpret_cast<float*>(p.peers[r] + P.xch_off)[(size_t)p.tp_rank * P.units + row] = v;
         } else {
             float* lo = P.out ? P.out : p.logits;
             lo[row] = v;
-            if (argmax_better(v, row, am_v, am_i)) {
+            const int id = P.row_base + row;
+            if (argmax_better(v, id, am_v, am_i)) {
                 am_v = v;
-                am_i = row;
+                am_i = id;
             }
         }
     }
@@ -384,6 +472,28 @@ __device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, f
         }
     }
     if (lane != 0) return;
+    if (p.tp_size > 1) {
+        // this rank's winner (over its vocabulary rows) to every rank, then
+        // the winner of all ranks' (the order is total: every rank agrees)
+        const unsigned long long mine =
+            (unsigned long long)__float_as_uint(v) | ((unsigned long long)(unsigned)id << 32);
+        for (int r = 0; r < p.tp_size; ++r)
+            reinterpret_cast<unsigned long long*>(p.peers[r] + kXchArgmax)[p.tp_rank] = mine;
+        __threadfence_system();
+        if (exchange_flags(p, sh.xe, &sh.abort)) {
+            const unsigned long long* slots =
+                reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + kXchArgmax);
+            for (int r = 0; r < p.tp_size; ++r) {
+                const unsigned long long s = __ldcg(slots + r);
+                const float rv = __uint_as_float((unsigned)(s & 0xffffffffull));
+                const int ri = (int)(unsigned)(s >> 32);
+                if (argmax_better(rv, ri, v, id)) {
+                    v = rv;
+                    id = ri;
+                }
+            }
+        }
+    }
     const int step = __ldcg(p.state + 2);
     if (p.hist) p.hist[step] = id;
     p.state[3] = id;
@@ -1094,6 +1204,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
 
     RingPos rp{0, 0u};
     uint32_t xphase = 0, pphase = 0;
+    unsigned long long xe = p.xe_base;  // exchange epochs so far
     unsigned long long target = p.bar_base;
     int cur = 0;
     long long n = 0;  // phases started so far
@@ -1122,6 +1233,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
                 bulk_g2s_plain(&sP[cur ^ 1], p.phases + nph, (uint32_t)sizeof(MegaPhase), &sh.pbar);
             }
             const MegaPhase& P = sP[cur];
+            // tensor parallelism: the partial-sum phases and the LM head
+            // exchange with the other ranks, each under a new epoch
+            const bool xdata = p.tp_size > 1 && P.kind == kPhGemv && P.xch_off >= 0;
+            if (xdata || (p.tp_size > 1 && P.kind == kPhGemv && P.epi == kEpiArgmax)) ++xe;
+            if (tid == 0) sh.xe = xe;
             // every consumer thread takes the same branches here (no branch on the
             // abort flag, which the producer may set at any moment): the phases
             // contain named barriers
@@ -1133,8 +1249,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
                 gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
             }
             trace_mark(p, tb, 2);
-            target += gridDim.x;
-            grid_sync(p, &sh.abort, tid, target);
+            if (xdata) __threadfence_system();  // this CTA's writes into the peers' regions
+            target += gridDim.x + (xdata ? 1 : 0);
+            grid_sync(p, &sh.abort, tid, target, xdata ? xe : 0);
             trace_mark(p, tb, 3);
             cur ^= 1;
             ++n;

@@ -32,6 +32,14 @@ struct alignas(16) MegaPhase {
     int layer;          // attention phases: KV-cache layer
     float* kc;          // attention phases: the layer's K and V caches [N_kv, max_seq, D]
     float* vc;
+    // tensor parallelism
+    int nsum;           // > 0: the input vector is x + the nsum partial vectors at xsum (rank order)
+    int xch_off;        // >= 0: epilogue writes its rows to every rank's exchange region at this
+                        // byte offset, slot [this rank][units]; -1: none
+    const float* xsum;  // [nsum][K] partials of the previous exchange (this rank's region)
+    float* xout;        // the summed input's rows [K b/P, K (b+1)/P) are written here (or NULL)
+    int row_base;       // LM head: global index of the first local row (argmax ids)
+    int pad_;
 };
 // descriptors are bulk-copied into shared memory ahead of their phase
 static_assert(sizeof(MegaPhase) % 16 == 0, "MegaPhase must be a multiple of 16 bytes");
@@ -57,7 +65,13 @@ struct MegaParams {
     int* am_idx;
     unsigned* am_cnt;
     int ring_slots;
-    int x_floats;        // shared floats for the input vector / attention scratch    // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
+    int x_floats;        // shared floats for the input vector / attention scratch
+    // tensor parallelism over tp_size GPUs (tp_size 1: none): every rank's
+    // exchange region (flags at kXchFlags, argmax slots at kXchArgmax, the
+    // partial buffers at the phases' xch_off), mapped into this process
+    int tp_rank, tp_size;
+    unsigned char* const* peers;   // [tp_size] region base pointers (own included)
+    unsigned long long xe_base;    // exchange epoch before this launch's first exchange    // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
     // last CTA, per (step, phase): [phase start, input loaded, work done,
     // barrier passed, producer issued the phase's last slot, SM cycles
     // consumer warp 0 waited for full slots, SM cycles the producer waited
@@ -66,6 +80,14 @@ struct MegaParams {
 };
 
 constexpr int kTraceFields = 7;
+
+// Exchange region layout (one per rank, cudaMalloc'd, shared by IPC):
+// flags [8] u64 (the last exchange epoch each rank has published), argmax
+// slots [8] u64 (float value bits | index << 32), then the partial buffers.
+constexpr int kMaxTp = 8;
+constexpr int kXchFlags = 0;
+constexpr int kXchArgmax = 256;
+constexpr int kXchData = 512;
 
 // Rows of a consumer batch: 8 FP32 / 16 bf16 (a batch is whole 16 KB slots).
 inline int mega_batch_rows(int weight_dtype) { return weight_dtype == 1 ? 16 : 8; }

@@ -18,6 +18,22 @@ __global__ void fill_normal_bf16(__nv_bfloat16* dst, size_t n, uint64_t key, flo
         dst[i] = __float2bfloat16_rn(infernt_normal_std(key, i, std_dev));
 }
 
+// dst [rows][ld_dst] = the window (row0.., col0..) of a seeded matrix with
+// src_ld columns; columns cols..ld_dst-1 are zero (padding)
+template <typename T>
+__global__ void fill_window(T* dst, int rows, int cols, int ld_dst, uint64_t src_ld, uint64_t row0, uint64_t col0,
+                            uint64_t key, float std_dev) {
+    const size_t n = (size_t)rows * ld_dst;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / ld_dst), c = (int)(i % ld_dst);
+        const float v = c < cols ? infernt_normal_std(key, (row0 + r) * src_ld + col0 + c, std_dev) : 0.0f;
+        if constexpr (sizeof(T) == 2)
+            dst[i] = __float2bfloat16_rn(v);
+        else
+            dst[i] = v;
+    }
+}
+
 __global__ void fill_const_f32(float* dst, size_t n, float v) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         dst[i] = v;
@@ -62,6 +78,26 @@ int infernt_fill_normal(void* dst, size_t n, int dtype, uint64_t seed, uint64_t 
                                                                        std_dev);
     else
         return fail(INFERNT_ERR_INVALID_ARGUMENT, "fill_normal: dtype %d", dtype);
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
+int infernt_fill_normal_window(void* dst, int rows, int cols, int ld_dst, uint64_t src_ld, uint64_t row0,
+                               uint64_t col0, int dtype, uint64_t seed, uint64_t stream_id, float std_dev,
+                               void* stream) {
+    INFERNT_REQUIRE(dst && rows >= 0 && cols >= 0 && ld_dst >= cols && col0 + (uint64_t)cols <= src_ld,
+                    "fill_normal_window: bad window");
+    const size_t n = (size_t)rows * ld_dst;
+    if (n == 0) return INFERNT_OK;
+    const uint64_t key = infernt_stream_key(seed, stream_id);
+    if (dtype == INFERNT_DTYPE_BF16)
+        fill_window<__nv_bfloat16><<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(
+            static_cast<__nv_bfloat16*>(dst), rows, cols, ld_dst, src_ld, row0, col0, key, std_dev);
+    else if (dtype == INFERNT_DTYPE_F32)
+        fill_window<float><<<grid_for(n), 256, 0, (cudaStream_t)stream>>>(static_cast<float*>(dst), rows, cols,
+                                                                           ld_dst, src_ld, row0, col0, key, std_dev);
+    else
+        return fail(INFERNT_ERR_INVALID_ARGUMENT, "fill_normal_window: dtype %d", dtype);
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }

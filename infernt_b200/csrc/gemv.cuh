@@ -33,7 +33,9 @@
 
 namespace infernt {
 
-enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiArgmax = 3 };
+// kEpiExchange (persistent kernel, tensor parallelism): the rows go to every
+// rank's exchange buffer, to be summed by the next phase.
+enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiArgmax = 3, kEpiExchange = 4 };
 
 constexpr int kPiece = 512;          // weight elements per piece (one float4/bf16x4 per thread)
 constexpr int kGemvConsumers = 128;  // four consumer warps

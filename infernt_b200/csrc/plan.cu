@@ -93,6 +93,20 @@ struct infernt_plan {
     MegaParams mega;
     int mega_ctas = 0;
     unsigned long long bar_epoch = 0;  // grid-barrier counter value at the next launch
+    // tensor parallelism (tp_size 1: none).  cfg holds this rank's shapes:
+    // its heads, its gate/up rows padded to a multiple of 512 (down's K), its
+    // vocabulary rows
+    int tp_rank = 0, tp_size = 1;
+    int vocab_global = 0;  // embedding rows (token ids)
+    int iloc = 0;          // gate/up rows of this rank (<= cfg.intermediate_size)
+    int v0 = 0;            // first vocabulary row of this rank
+    float* hmid = nullptr;  // residual stream after the O all-reduce
+    void* xch_mem = nullptr;  // this rank's exchange region
+    size_t xch_bytes = 0;
+    std::vector<void*> opened;  // peers' regions mapped into this process
+    unsigned char** peer_tab = nullptr;  // device copy of the region pointers
+    bool peers_set = false;
+    unsigned long long xepoch = 0;  // exchange epochs published so far
 };
 
 namespace {
@@ -246,13 +260,24 @@ int run_graph_step(infernt_plan* p, cudaStream_t st, int mode, const float* inpu
 int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist, int steps) {
     if (!logits) logits = p->logits;
     if (p->mode == INFERNT_MODE_PERSISTENT) {
+        INFERNT_REQUIRE(p->tp_size == 1 || p->peers_set,
+                        "tensor-parallel plan: infernt_plan_set_peers has not been called");
         MegaParams m = p->mega;
         m.input = mode == kInputVector ? input : nullptr;
         m.logits = logits;
         m.hist = hist;
         m.steps = steps;
         m.bar_base = p->bar_epoch;
-        p->bar_epoch += (unsigned long long)steps * m.nphases * p->mega_ctas;
+        // per step: one arrival per CTA and phase, plus one per all-reduce;
+        // exchange epochs: two all-reduces per layer and the argmax
+        const int L = p->cfg.num_layers;
+        const unsigned long long xch = p->tp_size > 1 ? 2ull * L : 0ull;
+        p->bar_epoch += (unsigned long long)steps * ((unsigned long long)m.nphases * p->mega_ctas + xch);
+        if (p->tp_size > 1) {
+            m.peers = p->peer_tab;
+            m.xe_base = p->xepoch;
+            p->xepoch += (unsigned long long)steps * (2ull * L + 1ull);
+        }
         INFERNT_CUDA_TRY(launch_mega(m, p->cfg.weight_dtype, p->mega_ctas, st));
         return INFERNT_OK;
     }
@@ -297,6 +322,13 @@ int build_mega(infernt_plan* p) {
     const int H = c.hidden_size, I = c.intermediate_size, L = c.num_layers, V = c.vocab_size;
     const int dt = c.weight_dtype;
     const int G = c.num_attention_heads / c.num_key_value_heads;
+    const bool tp = p->tp_size > 1;
+    const int T = p->tp_size;
+    // exchange buffers of the O and down partials (kept apart: a rank may
+    // write one while a slower rank still reads the other)
+    const int off_o = kXchData, off_d = kXchData + T * H * 4;
+    const float* xch_o = tp ? reinterpret_cast<const float*>(static_cast<char*>(p->xch_mem) + off_o) : nullptr;
+    const float* xch_d = tp ? reinterpret_cast<const float*>(static_cast<char*>(p->xch_mem) + off_d) : nullptr;
 
     std::vector<MegaPhase> ph;
 
@@ -304,7 +336,7 @@ int build_mega(infernt_plan* p) {
     // 2: gate, up)
     auto gemv = [&](int epi, int ns, std::initializer_list<const void*> mats, std::initializer_list<int> rows,
                     int units, int K, const float* x, const float* norm, float* out, const float* res,
-                    float* x_copy) {
+                    float* x_copy) -> MegaPhase& {
         MegaPhase P;
         memset(&P, 0, sizeof(P));
         P.kind = kPhGemv;
@@ -324,28 +356,49 @@ int build_mega(infernt_plan* p) {
         P.out = out;
         P.res = res;
         P.x_copy = x_copy;
-
+        P.xch_off = -1;
         ph.push_back(P);
+        return ph.back();
     };
+    // with tensor parallelism the input of a phase after an all-reduce is
+    // the residual stream plus every rank's partial
+    auto summed = [&](MegaPhase& P, const float* parts, float* share) {
+        P.nsum = T;
+        P.xsum = parts;
+        P.xout = share;
+    };
+    const int Iu = p->iloc;  // gate/up rows (down's K may be padded past them)
     for (int l = 0; l < L; ++l) {
         const void* const* lw = p->w.data() + 3 + 9 * l;
-        gemv(kEpiStore, 1, {lw[1], lw[2], lw[3]}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
-             l == 0 ? nullptr : p->hidden, static_cast<const float*>(lw[0]), p->qkv, nullptr,
-             l == 0 ? p->hidden : nullptr);
+        const float* qkv_in = l == 0 ? nullptr : (tp ? p->hmid : p->hidden);
+        MegaPhase& Q = gemv(kEpiStore, 1, {lw[1], lw[2], lw[3]}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
+                            qkv_in, static_cast<const float*>(lw[0]), p->qkv, nullptr, l == 0 ? p->hidden : nullptr);
+        if (tp && l > 0) summed(Q, xch_d, p->hidden);
         MegaPhase A;
         memset(&A, 0, sizeof(A));
         A.kind = kPhAttn;
         A.layer = l;
         A.kc = p->kc[l];
         A.vc = p->vc[l];
+        A.xch_off = -1;
         ph.push_back(A);
-        gemv(kEpiResidual, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
-        gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {I, I}, I, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
-             nullptr, nullptr);
-        gemv(kEpiResidual, 1, {lw[8]}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
+        if (tp) {
+            gemv(kEpiExchange, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, nullptr, nullptr, nullptr).xch_off = off_o;
+            MegaPhase& U = gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, p->hidden,
+                                static_cast<const float*>(lw[5]), p->act, nullptr, nullptr);
+            summed(U, xch_o, p->hmid);
+            gemv(kEpiExchange, 1, {lw[8]}, {H}, H, I, p->act, nullptr, nullptr, nullptr, nullptr).xch_off = off_d;
+        } else {
+            gemv(kEpiResidual, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
+            gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
+                 nullptr, nullptr);
+            gemv(kEpiResidual, 1, {lw[8]}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
+        }
     }
-    gemv(kEpiArgmax, 1, {p->w[2]}, {V}, V, H, p->hidden, static_cast<const float*>(p->w[1]), nullptr, nullptr,
-         nullptr);
+    MegaPhase& LM = gemv(kEpiArgmax, 1, {p->w[2]}, {V}, V, H, tp ? p->hmid : p->hidden,
+                         static_cast<const float*>(p->w[1]), nullptr, nullptr, nullptr);
+    LM.row_base = p->v0;
+    if (tp) summed(LM, xch_d, nullptr);
 
     // input vector + the norm weights behind it (RMSNorm phases), or the
     // attention scratch, whichever is larger
@@ -393,7 +446,7 @@ int build_mega(infernt_plan* p) {
     m.phases = d_ph;
     m.nphases = (int)ph.size();
     m.emb = static_cast<const float*>(p->w[0]);
-    m.vocab = V;
+    m.vocab = p->vocab_global;  // embedding rows (V is this rank's LM-head rows)
     m.attn.qkv = p->qkv;
     m.attn.out = p->attn;
     m.attn.part = p->attn_part;
@@ -415,6 +468,9 @@ int build_mega(infernt_plan* p) {
     m.am_cnt = d_amc;
     m.ring_slots = slots;
     m.x_floats = x_floats;
+    m.tp_rank = p->tp_rank;
+    m.tp_size = p->tp_size;
+    m.peers = p->peer_tab;  // set by infernt_plan_set_peers (tensor parallelism)
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
@@ -423,13 +479,18 @@ int build_mega(infernt_plan* p) {
 
 extern "C" {
 
-int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights, float* const* k_cache,
-                        float* const* v_cache, int mode, infernt_plan** out) {
-    INFERNT_REQUIRE(out, "plan_create: null output");
-    *out = nullptr;
-    if (int s = validate_config(cfg)) return s;
-    INFERNT_REQUIRE(weights && k_cache && v_cache, "plan_create: null weights or cache");
-    INFERNT_REQUIRE(mode >= INFERNT_MODE_EAGER && mode <= INFERNT_MODE_PERSISTENT, "plan_create: mode %d", mode);
+}  // extern "C"
+
+namespace {
+
+// Tensor-parallel rank description for plan_create_impl (rank 0 of 1: none).
+struct TpShard {
+    int rank = 0, size = 1;
+    int vocab_global = 0, iloc = 0, v0 = 0;
+};
+
+int plan_create_impl(const infernt_llama_config* cfg, const void* const* weights, float* const* k_cache,
+                     float* const* v_cache, int mode, const TpShard& tp, infernt_plan** out) {
     const int L = cfg->num_layers;
     for (int i = 0; i < 3 + 9 * L; ++i) INFERNT_REQUIRE(weights[i], "plan_create: weight pointer %d is null", i);
     for (int l = 0; l < L; ++l) INFERNT_REQUIRE(k_cache[l] && v_cache[l], "plan_create: cache layer %d null", l);
@@ -438,6 +499,11 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     infernt_plan* p = new (std::nothrow) infernt_plan();
     INFERNT_REQUIRE(p, "plan_create: host allocation failed");
     p->cfg = *cfg;
+    p->tp_rank = tp.rank;
+    p->tp_size = tp.size;
+    p->vocab_global = tp.vocab_global;
+    p->iloc = tp.iloc;
+    p->v0 = tp.v0;
     p->w.assign(weights, weights + 3 + 9 * L);
     p->kc.assign(k_cache, k_cache + L);
     p->vc.assign(v_cache, v_cache + L);
@@ -458,7 +524,7 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
         attention_workspace_bytes(cfg->num_attention_heads, cfg->num_key_value_heads, cfg->head_dim, p->splits);
     const size_t b_lm = al(sizeof(LmWs));
     const size_t b_rope = al(sizeof(float2) * (size_t)cfg->max_seq_len * (cfg->head_dim / 2));
-    const size_t total = b_qkv + b_attn + b_act + b_hid + b_log + b_state + b_aws + b_lm + b_rope;
+    const size_t total = b_qkv + b_attn + b_act + 2 * b_hid + b_log + b_state + b_aws + b_lm + b_rope;
     cudaError_t e = cudaMalloc(&p->scratch, total);
     if (e == cudaSuccess) e = cudaMemset(p->scratch, 0, total);
     if (e != cudaSuccess) {
@@ -474,6 +540,8 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     p->act = reinterpret_cast<float*>(b);
     b += b_act;
     p->hidden = reinterpret_cast<float*>(b);
+    b += b_hid;
+    p->hmid = reinterpret_cast<float*>(b);
     b += b_hid;
     p->logits = reinterpret_cast<float*>(b);
     b += b_log;
@@ -496,6 +564,22 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
         return cuda_fail(e, "RoPE table");
     }
 
+    if (p->tp_size > 1) {
+        // the all-reduces run inside the persistent kernel only
+        if (p->mode != INFERNT_MODE_PERSISTENT || !mega_eligible(p)) {
+            infernt_plan_destroy(p);
+            return fail(INFERNT_ERR_UNSUPPORTED, "tensor-parallel plan: shapes not eligible for the persistent "
+                                                 "kernel (K multiples of 512, 16-byte aligned, head_dim %% 4)");
+        }
+        p->xch_bytes = kXchData + 2 * (size_t)p->tp_size * cfg->hidden_size * sizeof(float);
+        e = cudaMalloc(&p->xch_mem, p->xch_bytes);
+        if (e == cudaSuccess) e = cudaMemset(p->xch_mem, 0, p->xch_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&p->peer_tab), sizeof(void*) * kMaxTp);
+        if (e != cudaSuccess) {
+            infernt_plan_destroy(p);
+            return cuda_fail(e, "tensor-parallel exchange region");
+        }
+    }
     if (p->mode == INFERNT_MODE_PERSISTENT) {
         if (mega_eligible(p)) {
             if (int s = build_mega(p)) {
@@ -510,10 +594,102 @@ int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weig
     return INFERNT_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int infernt_plan_create(const infernt_llama_config* cfg, const void* const* weights, float* const* k_cache,
+                        float* const* v_cache, int mode, infernt_plan** out) {
+    INFERNT_REQUIRE(out, "plan_create: null output");
+    *out = nullptr;
+    if (int s = validate_config(cfg)) return s;
+    INFERNT_REQUIRE(weights && k_cache && v_cache, "plan_create: null weights or cache");
+    INFERNT_REQUIRE(mode >= INFERNT_MODE_EAGER && mode <= INFERNT_MODE_PERSISTENT, "plan_create: mode %d", mode);
+    TpShard tp;
+    tp.vocab_global = cfg->vocab_size;
+    tp.iloc = cfg->intermediate_size;
+    return plan_create_impl(cfg, weights, k_cache, v_cache, mode, tp, out);
+}
+
+int infernt_tp_shard_dims(const infernt_llama_config* cfg, int tp_rank, int tp_size, int* dims) {
+    INFERNT_REQUIRE(cfg && dims, "tp_shard_dims: null argument");
+    if (int s = validate_config(cfg)) return s;
+    INFERNT_REQUIRE(tp_size >= 1 && tp_size <= kMaxTp && tp_rank >= 0 && tp_rank < tp_size,
+                    "tp_shard_dims: rank %d of %d (at most %d ranks)", tp_rank, tp_size, kMaxTp);
+    INFERNT_REQUIRE(cfg->num_key_value_heads % tp_size == 0 && cfg->intermediate_size % tp_size == 0,
+                    "tp_shard_dims: %d KV heads and intermediate %d must divide among %d ranks",
+                    cfg->num_key_value_heads, cfg->intermediate_size, tp_size);
+    const int il = cfg->intermediate_size / tp_size;
+    dims[0] = cfg->num_attention_heads / tp_size;
+    dims[1] = cfg->num_key_value_heads / tp_size;
+    dims[2] = il;
+    dims[3] = (il + kPiece - 1) / kPiece * kPiece;
+    dims[4] = (int)((long long)cfg->vocab_size * tp_rank / tp_size);
+    dims[5] = (int)((long long)cfg->vocab_size * (tp_rank + 1) / tp_size) - dims[4];
+    return INFERNT_OK;
+}
+
+int infernt_plan_create_tp(const infernt_llama_config* cfg, const void* const* weights, float* const* k_cache,
+                           float* const* v_cache, int tp_rank, int tp_size, infernt_plan** out) {
+    INFERNT_REQUIRE(out, "plan_create_tp: null output");
+    *out = nullptr;
+    int d[6];
+    if (int s = infernt_tp_shard_dims(cfg, tp_rank, tp_size, d)) return s;
+    INFERNT_REQUIRE(weights && k_cache && v_cache, "plan_create_tp: null weights or cache");
+    infernt_llama_config local = *cfg;
+    local.num_attention_heads = d[0];
+    local.num_key_value_heads = d[1];
+    local.intermediate_size = d[3];
+    local.vocab_size = d[5];
+    if (int s = validate_config(&local)) return s;
+    TpShard tp;
+    tp.rank = tp_rank;
+    tp.size = tp_size;
+    tp.vocab_global = cfg->vocab_size;
+    tp.iloc = d[2];
+    tp.v0 = d[4];
+    return plan_create_impl(&local, weights, k_cache, v_cache, INFERNT_MODE_PERSISTENT, tp, out);
+}
+
+int infernt_plan_xchg_handle(infernt_plan* p, void* handle_out) {
+    INFERNT_REQUIRE(p && handle_out, "plan_xchg_handle: null argument");
+    INFERNT_REQUIRE(p->tp_size > 1 && p->xch_mem, "plan_xchg_handle: not a tensor-parallel plan");
+    cudaIpcMemHandle_t h;
+    INFERNT_CUDA_TRY(cudaIpcGetMemHandle(&h, p->xch_mem));
+    static_assert(sizeof(h) == INFERNT_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    return INFERNT_OK;
+}
+
+int infernt_plan_set_peers(infernt_plan* p, const void* handles) {
+    INFERNT_REQUIRE(p && handles, "plan_set_peers: null argument");
+    INFERNT_REQUIRE(p->tp_size > 1 && p->xch_mem, "plan_set_peers: not a tensor-parallel plan");
+    INFERNT_REQUIRE(!p->peers_set, "plan_set_peers: peers are already set");
+    std::vector<unsigned char*> tab(kMaxTp, nullptr);
+    for (int r = 0; r < p->tp_size; ++r) {
+        if (r == p->tp_rank) {
+            tab[r] = static_cast<unsigned char*>(p->xch_mem);
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + (size_t)r * INFERNT_IPC_HANDLE_BYTES, sizeof(h));
+        void* ptr = nullptr;
+        INFERNT_CUDA_TRY(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        p->opened.push_back(ptr);
+        tab[r] = static_cast<unsigned char*>(ptr);
+    }
+    INFERNT_CUDA_TRY(cudaMemcpy(p->peer_tab, tab.data(), sizeof(void*) * kMaxTp, cudaMemcpyHostToDevice));
+    p->peers_set = true;
+    return INFERNT_OK;
+}
+
 int infernt_plan_destroy(infernt_plan* p) {
     if (!p) return INFERNT_OK;
     for (auto& e : p->graphs) cudaGraphExecDestroy(e.exec);
     if (p->cap_stream) cudaStreamDestroy(p->cap_stream);
+    for (void* ptr : p->opened) cudaIpcCloseMemHandle(ptr);
+    cudaFree(p->peer_tab);
+    cudaFree(p->xch_mem);
     cudaFree(p->mega_mem);
     cudaFree(p->scratch);
     delete p;
@@ -535,8 +711,8 @@ int infernt_plan_forward(infernt_plan* p, const float* input_embedding, int posi
 
 int infernt_plan_decode(infernt_plan* p, int token, int position, float* logits, void* stream) {
     INFERNT_REQUIRE(p, "plan_decode: null plan");
-    INFERNT_REQUIRE(token >= 0 && token < p->cfg.vocab_size, "plan_decode: token %d outside [0, %d)", token,
-                    p->cfg.vocab_size);
+    INFERNT_REQUIRE(token >= 0 && token < p->vocab_global, "plan_decode: token %d outside [0, %d)", token,
+                    p->vocab_global);
     INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len, "plan_decode: position %d outside [0, %d)",
                     position, p->cfg.max_seq_len);
     cudaStream_t st = (cudaStream_t)stream;
@@ -547,7 +723,7 @@ int infernt_plan_decode(infernt_plan* p, int token, int position, float* logits,
 
 int infernt_plan_decode_chain(infernt_plan* p, int token, int position, int steps, int* tokens_dev, void* stream) {
     INFERNT_REQUIRE(p, "plan_decode_chain: null plan");
-    INFERNT_REQUIRE(token >= 0 && token < p->cfg.vocab_size, "plan_decode_chain: token %d", token);
+    INFERNT_REQUIRE(token >= 0 && token < p->vocab_global, "plan_decode_chain: token %d", token);
     INFERNT_REQUIRE(steps >= 0 && position >= 0 && (long long)position + steps <= p->cfg.max_seq_len,
                     "plan_decode_chain: positions [%d, %d) exceed max_seq_len %d", position, position + steps,
                     p->cfg.max_seq_len);
