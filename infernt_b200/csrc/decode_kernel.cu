@@ -22,8 +22,9 @@
 // slots.  Each thread adds a row's pieces in column order into one
 // accumulator per row; for the usual widths the (row, column block) of every
 // piece of a batch is known at compile time and the input columns stay in
-// registers.  A batch ends with one reduce-scatter over the warp, and the
-// four warps' row sums are added in warp order in the batches' epilogue.
+// registers.  Row sums are reduced over the warp by a reduce-scatter (per
+// slot in that case, else once per batch), and the four warps' row sums are
+// added in warp order in the batches' epilogue.
 // Every output is reduced inside one CTA in a fixed order, so results do
 // not depend on timing and no cross-CTA merge sits on the critical path.
 //
@@ -235,13 +236,13 @@ __device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4
         acc = fmaf(w.z, xv.z, acc);
         acc = fmaf(w.w, xv.w, acc);
     } else {
+        // a bf16 value is the top half of the FP32 with the same bits, so
+        // widening is a shift (low element) or a mask (high element)
         const uint2 raw = *reinterpret_cast<const uint2*>(wp);
-        const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-        const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-        acc = fmaf(w01.x, xv.x, acc);
-        acc = fmaf(w01.y, xv.y, acc);
-        acc = fmaf(w23.x, xv.z, acc);
-        acc = fmaf(w23.y, xv.w, acc);
+        acc = fmaf(__uint_as_float(raw.x << 16), xv.x, acc);
+        acc = fmaf(__uint_as_float(raw.x & 0xffff0000u), xv.y, acc);
+        acc = fmaf(__uint_as_float(raw.y << 16), xv.z, acc);
+        acc = fmaf(__uint_as_float(raw.y & 0xffff0000u), xv.w, acc);
     }
     return acc;
 }
@@ -552,40 +553,62 @@ __device__ __forceinline__ void acc_set(float* acc, int k, float v) {
 }
 
 // A batch when CB = K / 512 divides the pieces of a slot: every slot holds
-// PT / CB whole rows and the same column blocks in the same places, so a
-// slot's rows are summed with compile-time indexing and the input columns
-// stay in registers (xr).  Rows past `rows` (a short last batch) are not
-// in the stream; the tail of its last slot is computed and dropped.
+// RS = PT / CB whole rows and the same column blocks in the same places, so
+// the input columns stay in registers (xr) and a slot's rows are summed with
+// compile-time indexing.  Each slot's RS row sums are reduced over the warp
+// at once (the same xor tree as a reduction of the whole batch, so the same
+// bits) and land in the warp's row-sum slots `gp`, indexed by accumulator.
+// The slot loop stays rolled: its body is one slot, small enough for the
+// instruction cache (an unrolled batch stalled the warps on instruction
+// fetch).  The warp reduction of a slot runs one slot late, beside the next
+// slot's loads and products, so the latency of its shuffle chain is hidden.
+// Rows past `rows` (a short last batch) are not in the stream; the tail of
+// its last slot is computed and dropped.
+template <typename WT, int CB>
+__device__ __forceinline__ void slot_row_sums(const unsigned char* wp, const float4* xr, float* v) {
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB;
+    constexpr int RS = PT / CB;
+    float pv[PT];
+#pragma unroll
+    for (int i = 0; i < PT; ++i) pv[i] = piece_dot<WT>(wp + i * PB, xr[i % CB]);
+#pragma unroll
+    for (int k = 0; k < RS; ++k) {
+        float t = 0.0f;
+#pragma unroll
+        for (int c = 0; c < CB; ++c) t += pv[k * CB + c];
+        v[k] = t;
+    }
+}
+
 template <typename WT, int NS, int CB>
-__device__ __forceinline__ void batch_regs(SlotReader& rd, const float4* xr, float* acc, int rows, int nb, int tid,
+__device__ __forceinline__ void batch_regs(SlotReader& rd, const float4* xr, float* gp, int rows, int nb, int tid,
                                            int lane) {
     constexpr int R = MegaRows<WT>::R, BU = R / NS;
-    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
-    constexpr int RS = PT / CB;  // rows per slot
+    constexpr int PT = MegaRows<WT>::PT, EB = MegaRows<WT>::EB;
+    constexpr int RS = PT / CB;    // rows per slot
+    constexpr int LPR = 32 / RS;   // lanes per row after the reduce-scatter
     static_assert(PT % CB == 0, "CB divides the slot");
     const int nslots = (rows + RS - 1) / RS;
-    const bool full = rows == R;
+    const int srow = lane / LPR;   // this lane's row within a slot after the reduction
+    const bool writer = lane % LPR == 0;
+    float v[RS];
+    slot_row_sums<WT, CB>(rd.take(tid, EB), xr, v);
+    rd.release(lane);
+#pragma unroll 1
+    for (int j = 1; j < nslots; ++j) {
+        const unsigned char* wp = rd.take(tid, EB);
+        float vn[RS];
+        slot_row_sums<WT, CB>(wp, xr, vn);
+        const float r = warp_reduce_scatter<RS>(v, lane);  // slot j - 1
+        const int s = (j - 1) * RS + srow;
+        if (writer && s < rows) gp[stream_row_acc<NS, BU>(s, nb)] = r;
+        rd.release(lane);
 #pragma unroll
-    for (int j = 0; j < R / RS; ++j) {
-        if (j < nslots) {
-            const unsigned char* wp = rd.take(tid, EB);
-            float pv[PT];
-#pragma unroll
-            for (int i = 0; i < PT; ++i) pv[i] = piece_dot<WT>(wp + i * PB, xr[i % CB]);
-            rd.release(lane);
-#pragma unroll
-            for (int k = 0; k < RS; ++k) {
-                float v = 0.0f;
-#pragma unroll
-                for (int c = 0; c < CB; ++c) v += pv[k * CB + c];
-                const int s = j * RS + k;  // stream row
-                if (full)
-                    acc[s] = v;  // a full batch: stream row s is accumulator s
-                else if (s < rows)
-                    acc_set<R>(acc, stream_row_acc<NS, BU>(s, nb), v);
-            }
-        }
+        for (int k = 0; k < RS; ++k) v[k] = vn[k];
     }
+    const float r = warp_reduce_scatter<RS>(v, lane);
+    const int s = (nslots - 1) * RS + srow;
+    if (writer && s < rows) gp[stream_row_acc<NS, BU>(s, nb)] = r;
 }
 
 // A batch when K / 512 >= the pieces of a slot: a slot holds the end of one
@@ -694,19 +717,22 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
     for (int ub = u0; ub < u1; ub += BU) {
         const int nb = min(BU, u1 - ub);
         const int rows = NS * nb;  // stream rows of the batch
-        float acc[R];
+        float* gp = sh.gpart[warp][bi % kGroupBatch];
+        if (CB > 0) {
+            batch_regs<WT, NS, NXR>(rd, xr, gp, rows, nb, tid, lane);
+        } else {
+            float acc[R];
 #pragma unroll
-        for (int a = 0; a < R; ++a) acc[a] = 0.0f;
-        if (CB > 0)
-            batch_regs<WT, NS, NXR>(rd, xr, acc, rows, nb, tid, lane);
-        else if (split)
-            batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, tid, lane);
-        else
-            batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, tid, lane);
-        // the warp's sum of each row; lane L holds row L / (32 / R)
-        const float v = warp_reduce_scatter<R>(acc, lane);
-        constexpr int kLanesPerRow = 32 / R;
-        if (lane % kLanesPerRow == 0) sh.gpart[warp][bi % kGroupBatch][lane / kLanesPerRow] = v;
+            for (int a = 0; a < R; ++a) acc[a] = 0.0f;
+            if (split)
+                batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, tid, lane);
+            else
+                batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, tid, lane);
+            // the warp's sum of each row; lane L holds row L / (32 / R)
+            const float v = warp_reduce_scatter<R>(acc, lane);
+            constexpr int kLanesPerRow = 32 / R;
+            if (lane % kLanesPerRow == 0) gp[lane / kLanesPerRow] = v;
+        }
         // kGroupBatch batches held: every warp has summed them (all walk the
         // same rows); run their epilogue before the slots are reused
         if (++bi % kGroupBatch == 0) {

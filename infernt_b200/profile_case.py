@@ -3,8 +3,10 @@ one chained launch of the persistent decode kernel.
 
     python -m infernt_b200.profile_case --layers 4 --steps 8
 
-The TinyLlama-1.1B shape with `--layers` decoder layers (the LM head and
-the per-layer matrices keep their full size), seeded N(0, 0.02) weights.
+The TinyLlama-1.1B shape (or, with `--shape llama3-8b`, the Llama-3-8B
+shape) with `--layers` decoder layers (the per-layer matrices keep their
+full size; `--vocab` shrinks the embedding and LM head), seeded N(0, 0.02)
+weights.
 Launch order on the device: `--prompt` single-step launches (the prompt),
 then one warm-up chain and one measured chain of `--steps` steps, so a
 profiler that skips `--prompt + 1` launches of the decode kernel captures
@@ -21,8 +23,13 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--prompt", type=int, default=2)
     ap.add_argument("--bf16", action="store_true", help="bf16 weights (FP32 activations)")
+    ap.add_argument("--shape", choices=["tinyllama", "llama3-8b"], default="tinyllama")
+    ap.add_argument("--vocab", type=int, default=0, help="vocabulary size (0: the shape's own)")
     args = ap.parse_args(argv)
-    cfg = ib.TINYLLAMA.with_(num_layers=args.layers)
+    base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B.with_(max_seq_len=1024)
+    cfg = base.with_(num_layers=args.layers)
+    if args.vocab:
+        cfg = cfg.with_(vocab_size=args.vocab)
     if args.bf16:
         cfg = cfg.with_(weight_dtype=ib.DTYPE_BF16)
     eng = ib.Engine(cfg, seed=0)
