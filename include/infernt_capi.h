@@ -228,14 +228,19 @@ INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
 /* Phase timeline of the persistent decode kernel.  Phases per step:
  * 5 per layer (qkv, attention, o, gate/up, down) + the LM head.  With a
  * device buffer of infernt_plan_trace_entries(plan, steps) uint64 set, the
- * following launches record, for CTA 0 and the last CTA per (step, phase):
- * [phase start, input loaded, work done, grid barrier passed, producer issued
- * the phase's last slot] as %globaltimer nanoseconds, then the SM cycles the
- * first consumer thread waited for weight slots and the SM cycles the
- * producer waited for free slots; layout [cta (2)][step][phase][7].  NULL
- * turns it off.  PERSISTENT mode only. */
+ * following launches record, for every CTA per (step, phase): [phase start,
+ * input loaded, work done, grid barrier passed, producer issued the phase's
+ * last slot] as %globaltimer nanoseconds, then the SM cycles the first
+ * consumer thread waited for weight slots and the SM cycles the producer
+ * waited for free slots; layout [cta][step][phase][7] over
+ * infernt_persistent_ctas() CTAs.  In attention phases a CTA with an item
+ * records instead: field 1 its inputs landed, 4 its partial computed, 5 its
+ * split ticket taken, 6 the merge done (when it merged).  NULL turns it off.
+ * PERSISTENT mode only. */
 INFERNT_API size_t infernt_plan_trace_entries(const infernt_plan* plan, int steps);
 INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* trace_dev);
+/* CTAs of the persistent decode kernel on the current device (one per SM). */
+INFERNT_API int infernt_persistent_ctas(void);
 
 /* ----------------------------------------- tensor parallelism ---
  * The 8B-class configuration decoded by tp_size GPUs, one process per GPU

@@ -144,6 +144,7 @@ _SIGS = {
     "infernt_plan_mode": (_I, [_P]),
     "infernt_plan_trace_entries": (_S, [_P, _I]),
     "infernt_plan_set_trace": (_I, [_P, _P]),
+    "infernt_persistent_ctas": (_I, []),
     "infernt_engine_trace_chain": (_I, [_P, _I, _I, _I, _P, _S]),
     "infernt_engine_set_mode": (_I, [_P, _I]),
     "infernt_engine_mode": (_I, [_P, ctypes.POINTER(_I)]),
@@ -210,6 +211,16 @@ def check(status, what):
 def call(name, *args):
     """Calls a C-ABI entry point and raises InferntError on a non-zero status."""
     return check(getattr(lib(), name)(*args), name)
+
+
+def _trace(cfg, fn, handle, token, position, steps):
+    """Runs a traced decode chain through `fn`; [cta][step][phase][7] int64."""
+    import numpy as np
+    nph = 5 * cfg.num_layers + 1
+    ctas = lib().infernt_persistent_ctas()
+    out = np.zeros(ctas * steps * nph * TRACE_FIELDS, dtype=np.uint64)
+    call(fn, handle, token, position, steps, out.ctypes.data, out.size)
+    return out.reshape(ctas, steps, nph, TRACE_FIELDS).astype(np.int64)
 
 
 def ptr(t):
@@ -285,15 +296,12 @@ class Engine:
 
     def trace_chain(self, token: int, position: int, steps: int):
         """Device-chained decode with the persistent kernel's phase timeline.
-        Returns an int64 array [cta (0 = first, 1 = last)][step][phase][7]:
-        %globaltimer ns of phase start, input loaded, work done, barrier
-        passed, producer issued the phase's last slot; then the SM cycles
-        the first consumer waited for slots and the producer for free ones."""
-        import numpy as np
-        nph = 5 * self.cfg.num_layers + 1
-        out = np.zeros(2 * steps * nph * TRACE_FIELDS, dtype=np.uint64)
-        call("infernt_engine_trace_chain", self._h, token, position, steps, out.ctypes.data, out.size)
-        return out.reshape(2, steps, nph, TRACE_FIELDS).astype(np.int64)
+        Returns an int64 array [cta][step][phase][7] over every CTA of the
+        launch: %globaltimer ns of phase start, input loaded, work done,
+        barrier passed, producer issued the phase's last slot; then the SM
+        cycles the CTA's first consumer waited for slots and its producer
+        for free ones."""
+        return _trace(self.cfg, "infernt_engine_trace_chain", self._h, token, position, steps)
 
     def weight_ptrs(self):
         n = 3 + 9 * self.cfg.num_layers
@@ -372,8 +380,4 @@ class TPEngine:
     def trace_chain(self, token: int, position: int, steps: int):
         """decode_chain with the persistent kernel's phase timeline (as
         Engine.trace_chain)."""
-        import numpy as np
-        nph = 5 * self.cfg.num_layers + 1
-        out = np.zeros(2 * steps * nph * TRACE_FIELDS, dtype=np.uint64)
-        call("infernt_tp_engine_trace_chain", self._h, token, position, steps, out.ctypes.data, out.size)
-        return out.reshape(2, steps, nph, TRACE_FIELDS).astype(np.int64)
+        return _trace(self.cfg, "infernt_tp_engine_trace_chain", self._h, token, position, steps)

@@ -48,6 +48,8 @@ constexpr int kProducerWarp = 4;
 constexpr int kMegaThreads = 160;  // 4 consumer warps and the producer warp
 constexpr long long kWaitCycles = 4000000000ll;  // about 2 s at the maximum SM clock
 constexpr int kResRows = 128;                    // residual rows a CTA stages per phase
+constexpr int kMergeChunk = 8;                   // attention splits merged per round of loads
+constexpr int kMergeRounds = 8;                  // lanes x rounds bound the splits of a KV head (256)
 
 template <typename WT>
 struct MegaRows {
@@ -212,11 +214,10 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// Timeline slot of (step, phase) for CTA 0 and the last CTA; -1 otherwise.
+// Timeline slot of (step, phase) for this CTA; -1 when tracing is off.
 __device__ __forceinline__ long long trace_base(const MegaParams& p, int step, int ph) {
-    if (!p.trace || (blockIdx.x != 0 && blockIdx.x != gridDim.x - 1)) return -1;
-    const long long who = blockIdx.x == 0 ? 0 : 1;
-    return ((who * p.steps + step) * p.nphases + ph) * kTraceFields;
+    if (!p.trace) return -1;
+    return (((long long)blockIdx.x * p.steps + step) * p.nphases + ph) * kTraceFields;
 }
 
 __device__ __forceinline__ void trace_mark(const MegaParams& p, long long base, int field) {
@@ -768,6 +769,8 @@ __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned cha
     if (tb >= 0) p.trace[tb + 5] = (unsigned long long)rd.waited;
 }
 
+__device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* sm, int tid);
+
 // One (KV head, split) item of decode attention inside the persistent
 // kernel: the same computation as attention_item (attention.cuh), with its
 // inputs brought in by bulk copies on the input-vector mbarrier, so the
@@ -781,7 +784,11 @@ __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned cha
 // chunk p mod (D/4), which keeps the unpadded [T][D] tile free of bank
 // conflicts; the sum order per lane is fixed, so results are deterministic.
 __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int pos, float* sm, MegaShared& sh,
-                                    int tid, uint32_t& xphase, unsigned* err) {
+                                    int tid, uint32_t& xphase, unsigned* err, unsigned long long* tr, long long tb) {
+    // timeline marks of an attention phase (thread 0, tracing on)
+    auto mark = [&](int f) {
+        if (tb >= 0) tr[tb + f] = global_ns();
+    };
     constexpr int T = kAttnBulkTile;
     constexpr int NW = kMegaConsumers / 32;
     constexpr int MAXH = (kAttnMaxGroup + NW - 1) / NW;
@@ -826,6 +833,7 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
     }
     mega_wait(&sh.xbar, xphase & 1u, &sh.abort, err);
     ++xphase;
+    mark(1);
 
     // RoPE (cuda/rope.cu:13-24 with the tabulated factors) on q and the new
     // key; append the new K/V row (cuda/kv_cache.cu:4-14)
@@ -846,9 +854,12 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
     }
     named_sync(1, kMegaConsumers);
 
+    // this warp's heads h = warp + j NW (warp-uniform validity)
+    bool hv[MAXH];
     float m_run[MAXH], l_run[MAXH], o_run[MAXH][MAXDL];
 #pragma unroll
     for (int j = 0; j < MAXH; ++j) {
+        hv[j] = warp + j * NW < G;
         m_run[j] = -INFINITY;
         l_run[j] = 0.0f;
 #pragma unroll
@@ -864,45 +875,79 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
             }
             named_sync(1, kMegaConsumers);
         }
+        // scores of key row `lane` against every head of the warp: each key
+        // chunk is read once for all of them; two partial sums per head
+        // (even / odd chunks) halve the dependent FMA chain
+        float dd[MAXH][2];
+#pragma unroll
+        for (int j = 0; j < MAXH; ++j) dd[j][0] = dd[j][1] = 0.0f;
+        if (lane < tl) {
+            const float* kr = kt + lane * D;
+            int c = cstart;
+            auto chunk = [&](int e) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * c);
+#pragma unroll
+                for (int j = 0; j < MAXH; ++j) {
+                    if (hv[j]) {
+                        const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + j * NW) * D + 4 * c);
+                        float t = dd[j][e];
+                        t = fmaf(q4.x, k4.x, t);
+                        t = fmaf(q4.y, k4.y, t);
+                        t = fmaf(q4.z, k4.z, t);
+                        t = fmaf(q4.w, k4.w, t);
+                        dd[j][e] = t;
+                    }
+                }
+                if (++c == nc) c = 0;
+            };
+            int n = 0;
+            for (; n + 2 <= nc; n += 2) {
+                chunk(0);
+                chunk(1);
+            }
+            if (n < nc) chunk(0);
+        }
+        // online softmax of each head over the tile's positions
+        float alpha[MAXH];
 #pragma unroll
         for (int j = 0; j < MAXH; ++j) {
-            const int h = warp + j * NW;
-            if (h < G) {
-                float s = -INFINITY;
-                if (lane < tl) {
-                    const float* qh = qs + h * D;
-                    const float* kr = kt + lane * D;
-                    float dot = 0.0f;
-                    int c = cstart;
-                    for (int n = 0; n < nc; ++n) {
-                        const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * c);
-                        const float4 q4 = *reinterpret_cast<const float4*>(qh + 4 * c);
-                        dot = fmaf(q4.x, k4.x, dot);
-                        dot = fmaf(q4.y, k4.y, dot);
-                        dot = fmaf(q4.z, k4.z, dot);
-                        dot = fmaf(q4.w, k4.w, dot);
-                        if (++c == nc) c = 0;
-                    }
-                    s = dot * a.scale;
-                }
+            alpha[j] = 1.0f;
+            if (hv[j]) {
+                const float s = lane < tl ? (dd[j][0] + dd[j][1]) * a.scale : -INFINITY;
                 const float m_new = fmaxf(m_run[j], warp_max(s));
-                const float alpha = expf(m_run[j] - m_new);
+                alpha[j] = expf(m_run[j] - m_new);
                 const float pe = lane < tl ? expf(s - m_new) : 0.0f;
-                ps[h * T + lane] = pe;
-                l_run[j] = l_run[j] * alpha + warp_sum(pe);
+                ps[(warp + j * NW) * T + lane] = pe;
+                l_run[j] = l_run[j] * alpha[j] + warp_sum(pe);
                 m_run[j] = m_new;
-                __syncwarp();
+            }
+        }
+        __syncwarp();
+        // P V: each value row is read once for all heads; every output
+        // column's sum runs over the positions in order
+        float acc[MAXH][MAXDL];
 #pragma unroll
-                for (int i = 0; i < MAXDL; ++i) {
-                    const int d = lane + 32 * i;
-                    if (d < D) {
-                        float acc = o_run[j][i] * alpha;
-                        for (int q = 0; q < tl; ++q) acc = fmaf(ps[h * T + q], vt[q * D + d], acc);
-                        o_run[j][i] = acc;
-                    }
+        for (int j = 0; j < MAXH; ++j)
+#pragma unroll
+            for (int i = 0; i < MAXDL; ++i) acc[j][i] = o_run[j][i] * alpha[j];
+#pragma unroll 4
+        for (int q = 0; q < tl; ++q) {
+            float vq[MAXDL];
+#pragma unroll
+            for (int i = 0; i < MAXDL; ++i) vq[i] = lane + 32 * i < D ? vt[q * D + lane + 32 * i] : 0.0f;
+#pragma unroll
+            for (int j = 0; j < MAXH; ++j) {
+                if (hv[j]) {
+                    const float pq = ps[(warp + j * NW) * T + q];
+#pragma unroll
+                    for (int i = 0; i < MAXDL; ++i) acc[j][i] = fmaf(pq, vq[i], acc[j][i]);
                 }
             }
         }
+#pragma unroll
+        for (int j = 0; j < MAXH; ++j)
+#pragma unroll
+            for (int i = 0; i < MAXDL; ++i) o_run[j][i] = acc[j][i];
         t0 += tl;
         if (t0 >= c1) break;
         // next tile: every thread's reads of the tile come before the copies
@@ -918,14 +963,14 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
         ++xphase;
     }
 
+    mark(4);
     if (active == 1) {
         // the only split: normalised output (cuda/attention.cu:30-43 after softmax)
 #pragma unroll
         for (int j = 0; j < MAXH; ++j) {
-            const int h = warp + j * NW;
-            if (h < G) {
+            if (hv[j]) {
                 const float inv = 1.0f / l_run[j];
-                float* o = a.out + ((size_t)kvh * G + h) * D;
+                float* o = a.out + ((size_t)kvh * G + warp + j * NW) * D;
 #pragma unroll
                 for (int i = 0; i < MAXDL; ++i)
                     if (lane + 32 * i < D) o[lane + 32 * i] = o_run[j][i] * inv;
@@ -937,9 +982,8 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
     // partial (m, l, o) of each head; the last split of the head merges
 #pragma unroll
     for (int j = 0; j < MAXH; ++j) {
-        const int h = warp + j * NW;
-        if (h < G) {
-            float* pp = a.part + (((size_t)kvh * a.splits + split) * G + h) * (D + 2);
+        if (hv[j]) {
+            float* pp = a.part + (((size_t)kvh * a.splits + split) * G + warp + j * NW) * (D + 2);
             if (lane == 0) {
                 pp[0] = m_run[j];
                 pp[1] = l_run[j];
@@ -957,37 +1001,107 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
         *s_last = (ticket == (unsigned)active - 1u);
     }
     named_sync(1, kMegaConsumers);
+    mark(5);
     if (*s_last) {
-        for (int h = warp; h < G; h += NW) {
-            const float* ph = a.part + ((size_t)kvh * a.splits * G + h) * (D + 2);
-            const size_t sstride = (size_t)G * (D + 2);
-            float M = -INFINITY;
-            for (int s = lane; s < active; s += 32) M = fmaxf(M, __ldcg(ph + s * sstride));
-            M = warp_max(M);
-            float L = 0.0f;
-            float acc[MAXDL];
-#pragma unroll
-            for (int i = 0; i < MAXDL; ++i) acc[i] = 0.0f;
-#pragma unroll 4
-            for (int s = 0; s < active; ++s) {
-                const float* pp = ph + s * sstride;
-                const float w = expf(__ldcg(pp) - M);
-                L = fmaf(__ldcg(pp + 1), w, L);
-#pragma unroll
-                for (int i = 0; i < MAXDL; ++i)
-                    if (lane + 32 * i < D) acc[i] = fmaf(__ldcg(pp + 2 + lane + 32 * i), w, acc[i]);
-            }
-            const float inv = 1.0f / L;
-            float* o = a.out + ((size_t)kvh * G + h) * D;
-#pragma unroll
-            for (int i = 0; i < MAXDL; ++i)
-                if (lane + 32 * i < D) o[lane + 32 * i] = acc[i] * inv;
-        }
-        if (tid == 0) a.counter[kvh] = 0u;
+        attention_merge(a, kvh, active, sm, tid);
+        mark(6);
     }
 }
 
-__device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid,
+// The flash-decoding merge of the active splits of KV head kvh by the last
+// split to finish: out = sum_s w_s o_s / sum_s w_s l_s with w_s = exp(m_s -
+// M).  This is the attention phase's critical path, so it is arranged for
+// few dependent L2 round trips: every thread owns output elements (head,
+// column) and issues the loads of its elements' partial rows for
+// kMergeChunk splits at once, the first chunk before the weights are
+// known; meanwhile each warp forms the split weights of its heads (lanes
+// over splits) into shared memory after the item's scratch.  Sums run over
+// the splits in order, so the result does not depend on timing.
+__device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* sm, int tid) {
+    constexpr int NW = kMegaConsumers / 32;
+    constexpr int MAXH = (kAttnMaxGroup + NW - 1) / NW;
+    constexpr int SC = kMergeChunk;
+    constexpr int OPT = 4;  // output elements per thread per pass
+    const int warp = tid >> 5, lane = tid & 31;
+    const int D = a.D, G = a.nq / a.nkv, S = a.splits;
+    const size_t sstride = (size_t)G * (D + 2);
+    const float* pk = a.part + (size_t)kvh * S * sstride;
+    float* wtab = sm + attn_bulk_smem_floats(G, D);  // [G][S] split weights
+    float* linv = wtab + (size_t)G * S;               // [G] 1 / sum_s w_s l_s
+    const int nout = G * D;
+
+    float ov[OPT][SC];
+    auto load_chunk = [&](int o0, int s0) {
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int e = o0 + k * kMegaConsumers;
+            const int h = e / D, d = e - h * D;
+#pragma unroll
+            for (int q = 0; q < SC; ++q)
+                ov[k][q] = (e < nout && s0 + q < active)
+                               ? __ldcg(pk + (s0 + q) * sstride + (size_t)h * (D + 2) + 2 + d)
+                               : 0.0f;
+        }
+    };
+    load_chunk(tid, 0);
+
+    // split weights of this warp's heads
+#pragma unroll
+    for (int j = 0; j < MAXH; ++j) {
+        const int h = warp + j * NW;
+        if (h >= G) continue;
+        const float* ph = pk + (size_t)h * (D + 2);
+        float mr[kMergeRounds], lr[kMergeRounds];
+#pragma unroll
+        for (int r = 0; r < kMergeRounds; ++r) {
+            const int s = lane + 32 * r;
+            mr[r] = s < active ? __ldcg(ph + s * sstride) : -INFINITY;
+            lr[r] = s < active ? __ldcg(ph + s * sstride + 1) : 0.0f;
+        }
+        float M = mr[0];
+#pragma unroll
+        for (int r = 1; r < kMergeRounds; ++r) M = fmaxf(M, mr[r]);
+        M = warp_max(M);
+        float L = 0.0f;
+#pragma unroll
+        for (int r = 0; r < kMergeRounds; ++r) {
+            const int s = lane + 32 * r;
+            if (s < active) {
+                const float w = expf(mr[r] - M);
+                wtab[h * S + s] = w;
+                L = fmaf(lr[r], w, L);
+            }
+        }
+        L = warp_sum(L);
+        if (lane == 0) linv[h] = 1.0f / L;
+    }
+    named_sync(1, kMegaConsumers);
+
+    for (int o0 = tid; o0 < nout; o0 += OPT * kMegaConsumers) {
+        float acc[OPT];
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) acc[k] = 0.0f;
+        for (int s0 = 0; s0 < active; s0 += SC) {
+            if (o0 != tid || s0 != 0) load_chunk(o0, s0);
+#pragma unroll
+            for (int k = 0; k < OPT; ++k) {
+                const int e = o0 + k * kMegaConsumers;
+                const int h = e < nout ? e / D : 0;
+#pragma unroll
+                for (int q = 0; q < SC; ++q)
+                    if (s0 + q < active) acc[k] = fmaf(ov[k][q], wtab[h * S + s0 + q], acc[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int e = o0 + k * kMegaConsumers;
+            if (e < nout) a.out[(size_t)kvh * nout + e] = acc[k] * linv[e / D];
+        }
+    }
+    if (tid == 0) a.counter[kvh] = 0u;
+}
+
+__device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, long long tb,
                                 uint32_t& xphase, int pos) {
     if (pos < 0 || pos >= p.attn.max_seq) {
         if (tid == 0 && blockIdx.x == 0) atomicOr(p.err, kErrPosition);
@@ -1009,7 +1123,7 @@ __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* 
             named_sync(1, kMegaConsumers);
         }
         first = false;
-        attention_item_bulk(a, kvh, split, pos, xs, sh, tid, xphase, p.err);
+        attention_item_bulk(a, kvh, split, pos, xs, sh, tid, xphase, p.err, p.trace, tb);
     }
 }
 
@@ -1268,7 +1382,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             // abort flag, which the producer may set at any moment): the phases
             // contain named barriers
             if (P.kind == kPhAttn) {
-                attention_phase(p, P, xs, sh, tid, xphase, pos);
+                attention_phase(p, P, xs, sh, tid, tb, xphase, pos);
             } else if (P.ns == 2) {
                 gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
             } else {

@@ -405,7 +405,8 @@ int build_mega(infernt_plan* p) {
     int x_floats = 2 * H;
     if (p->qs > x_floats) x_floats = p->qs;
     if (I > x_floats) x_floats = I;
-    const int af = attn_bulk_smem_floats(G, c.head_dim);
+    // attention scratch, then the merge's split weights [G][splits] and [G]
+    const int af = attn_bulk_smem_floats(G, c.head_dim) + G * (p->splits + 1);
     if (af > x_floats) x_floats = af;
     x_floats = (x_floats + 3) / 4 * 4;
 
@@ -511,7 +512,8 @@ int plan_create_impl(const infernt_llama_config* cfg, const void* const* weights
     p->kvs = cfg->num_key_value_heads * cfg->head_dim;
     p->mode = mode;
     const int splits = sm_count() / cfg->num_key_value_heads;
-    p->splits = splits < 1 ? 1 : splits;
+    // at most 256 splits per KV head (the persistent kernel's merge bound)
+    p->splits = splits < 1 ? 1 : (splits > 256 ? 256 : splits);
 
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t b_qkv = al(sizeof(float) * (p->qs + 2 * p->kvs));
@@ -760,7 +762,7 @@ float* infernt_plan_logits(infernt_plan* p) { return p ? p->logits : nullptr; }
 
 size_t infernt_plan_trace_entries(const infernt_plan* p, int steps) {
     if (!p || p->mode != INFERNT_MODE_PERSISTENT || steps <= 0) return 0;
-    return (size_t)2 * steps * p->mega.nphases * kTraceFields;
+    return (size_t)p->mega_ctas * steps * p->mega.nphases * kTraceFields;
 }
 
 int infernt_plan_set_trace(infernt_plan* p, unsigned long long* trace_dev) {
@@ -769,6 +771,8 @@ int infernt_plan_set_trace(infernt_plan* p, unsigned long long* trace_dev) {
     p->mega.trace = trace_dev;
     return INFERNT_OK;
 }
+
+int infernt_persistent_ctas(void) { return sm_count(); }
 
 int infernt_plan_kernels_per_step(const infernt_plan* p) {
     if (!p) return 0;
