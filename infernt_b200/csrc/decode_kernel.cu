@@ -49,7 +49,7 @@ constexpr int kMegaThreads = 160;  // 4 consumer warps and the producer warp
 constexpr long long kWaitCycles = 4000000000ll;  // about 2 s at the maximum SM clock
 constexpr int kResRows = 128;                    // residual rows a CTA stages per phase
 constexpr int kMergeChunk = 8;                   // attention splits merged per round of loads
-constexpr int kMergeRounds = 8;                  // lanes x rounds bound the splits of a KV head (256)
+constexpr int kMergeRounds = 2;                  // lanes x rounds bound the splits of a KV head (64)
 
 template <typename WT>
 struct MegaRows {
@@ -71,7 +71,6 @@ struct MegaShared {
     int res_n;     // staged rows
     float res[kResRows];
     float gpart[4][kGroupBatch][16];  // per-warp row sums of up to kGroupBatch batches
-    unsigned long long xe;            // tensor parallelism: epoch of the phase's exchange
     uint64_t xbar;                    // completion of the input-vector bulk copy
     uint64_t pbar;                   // completion of the next phase descriptor's bulk copy
 };
@@ -123,83 +122,160 @@ __device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long l
     return v;
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+// ------------------------------------------------------------ tagged words
+//
+// Activations travel between CTAs (and, with tensor parallelism, between
+// GPUs) as 8-byte words: the FP32 value in the low half, in the high half
+// the tag of the phase instance that wrote it (launch tag base + step x
+// phases + phase + 1, the same on every rank).  An aligned 8-byte store is
+// single-copy atomic, so a reader that sees the tag it expects has that
+// instance's value: consumers poll the data words themselves, and a phase
+// boundary costs one L2 round trip instead of a grid barrier followed by a
+// load.  Reuse of a buffer is safe because every phase needs the whole of
+// its predecessor's output: no CTA can overwrite a word of phase k's output
+// before every reader of it has passed phase k + 1.
+
+__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned tag) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+}
+
+__device__ __forceinline__ void st_ll(unsigned long long* a, float v, unsigned tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(a), "l"(ll_pack(v, tag)) : "memory");
+}
+
+// into another GPU's memory (tensor parallelism)
+__device__ __forceinline__ void st_ll_sys(unsigned long long* a, float v, unsigned tag) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(ll_pack(v, tag)) : "memory");
+}
+
+template <bool SYS>
+__device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long* a) {
+    ulonglong2 v;
+    if (SYS)
+        asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(a) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(a) : "memory");
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+template <bool SYS>
+__device__ __forceinline__ unsigned long long ld_ll1(const unsigned long long* a) {
+    unsigned long long v;
+    if (SYS)
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    else
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
 }
 
-// Publishes exchange epoch e to every rank (after this rank's data writes,
-// which the caller has fenced at system scope) and waits, bounded, until
-// every rank has published e.  Returns false on timeout.
-__device__ bool exchange_flags(const MegaParams& p, unsigned long long e, volatile int* abort) {
-    for (int r = 0; r < p.tp_size; ++r)
-        st_release_sys64(reinterpret_cast<unsigned long long*>(p.peers[r] + kXchFlags) + p.tp_rank, e);
-    const unsigned long long* own = reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + kXchFlags);
-    const long long t0 = clock64();
-    for (int r = 0; r < p.tp_size; ++r) {
-        while (ld_acquire_sys64(own + r) < e) {
-            if (*abort || (ld_acquire(p.err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
-                atomicOr(p.err, kErrWaitTimeout);
+__device__ __forceinline__ bool ll_is(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
+
+// Bounded re-reading of words not yet current.  On timeout (or when another
+// CTA has already timed out) the CTA is marked aborted, the error word set,
+// and the stale value returned: control flow continues without waiting.
+struct LLWait {
+    unsigned* err;
+    volatile int* abort;
+    // called once per failed polling round: checks the time budget
+    __device__ __forceinline__ bool give_up(long long t0, unsigned& spins) const {
+        if (*abort) return true;
+        if ((++spins & 63u) == 0u) {
+            if ((ld_acquire(err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
+                atomicOr(err, kErrWaitTimeout);
                 *abort = 1;
-                return false;
+                return true;
             }
         }
+        return false;
     }
-    return true;
+    template <bool SYS>
+    __device__ __forceinline__ unsigned long long one(const unsigned long long* a, unsigned long long w,
+                                                      unsigned tag) const {
+        if (ll_is(w, tag)) return w;
+        const long long t0 = clock64();
+        unsigned spins = 0;
+        do {
+            if (give_up(t0, spins)) break;
+            w = ld_ll1<SYS>(a);
+        } while (!ll_is(w, tag));
+        return w;
+    }
+    template <bool SYS>
+    __device__ __forceinline__ float2 two(const unsigned long long* a, ulonglong2 w, unsigned tag) const {
+        if (!(ll_is(w.x, tag) && ll_is(w.y, tag))) {
+            const long long t0 = clock64();
+            unsigned spins = 0;
+            do {
+                if (give_up(t0, spins)) break;
+                w = ld_ll2<SYS>(a);
+            } while (!(ll_is(w.x, tag) && ll_is(w.y, tag)));
+        }
+        return make_float2(ll_val(w.x), ll_val(w.y));
+    }
+};
+
+// Polls words w[0, n) (loaded from addr(k)) until each carries `tag`:
+// every round re-reads all stale words at once, so a round costs one round
+// trip however many words are late.
+template <int N, bool SYS, typename Addr>
+__device__ __forceinline__ void ll_poll(unsigned long long (&w)[N], int n, Addr addr, unsigned tag,
+                                        const LLWait& wt) {
+    const long long t0 = clock64();
+    unsigned spins = 0;
+    while (true) {
+        bool ok = true;
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (k < n && !ll_is(w[k], tag)) ok = false;
+        if (ok || wt.give_up(t0, spins)) return;
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (k < n && !ll_is(w[k], tag)) w[k] = ld_ll1<SYS>(addr(k));
+    }
 }
 
-// Grid barrier of the consumer warps: every CTA adds 1 (release) to a 64-bit
-// counter that only grows, and polls (acquire) until it reaches `target`
-// (the launch's base plus gridDim.x per barrier passed).  One atomic per
-// CTA, no reset and no last-arriver hop.  The named barrier orders the other
-// consumer threads' writes before thread 0's release, which is cumulative,
-// so no separate fence is needed.
-//
-// After an exchange phase (xe > 0) the barrier also crosses the GPUs: once
-// every local CTA has arrived (each fenced its writes into the peers'
-// regions at system scope first), CTA 0 publishes epoch xe to every rank,
-// waits for every rank's, and adds one more arrival; the other CTAs wait for
-// that one too (target counts it).
-__device__ __forceinline__ void grid_sync(const MegaParams& p, volatile int* abort, int tid,
-                                          unsigned long long target, unsigned long long xe = 0) {
-    named_sync(1, kMegaConsumers);
-    if (tid == 0 && !*abort) {
-        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p.bar) : "memory");
-        if (xe && blockIdx.x == 0) {
-            const long long t0 = clock64();
-            while (ld_acquire64(p.bar) < target - 1) {
-                if ((ld_acquire(p.err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
-                    atomicOr(p.err, kErrWaitTimeout);
-                    *abort = 1;
-                    break;
-                }
-            }
-            if (!*abort) {
-                __threadfence_system();
-                exchange_flags(p, xe, abort);
-            }
-            // the extra arrival is made even after a failure, so no CTA waits
-            // on it in vain
-            asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(p.bar) : "memory");
+constexpr int kLLBatch = 16;  // word pairs a thread has in flight when reading a vector
+
+// dst[0, n) = the values of the tagged words src[0, n) of phase instance
+// `tag` (src 16-byte aligned), read by the consumer threads in
+// batches of kLLBatch pairs each (one round trip per batch).  Not inlined:
+// its registers for the loads in flight do not add to its callers'.
+template <bool SYS>
+__device__ __noinline__ void ll_read_vec(const unsigned long long* src, float* dst, int n, unsigned tag, int tid,
+                                         const LLWait wt) {
+    constexpr int STEP = kMegaConsumers * 2;
+    for (int base = tid * 2; base < n; base += STEP * kLLBatch) {
+        ulonglong2 w[kLLBatch];
+#pragma unroll
+        for (int k = 0; k < kLLBatch; ++k) {
+            const int i = base + k * STEP;
+            if (i + 1 < n) w[k] = ld_ll2<SYS>(src + i);
         }
-        if (ld_acquire64(p.bar) < target) {
-            const long long t0 = clock64();
-            while (ld_acquire64(p.bar) < target) {
-                __nanosleep(20);
-                if ((ld_acquire(p.err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
-                    atomicOr(p.err, kErrWaitTimeout);
-                    *abort = 1;
-                    break;
-                }
+        // re-read the stale pairs of the batch together until all are current
+        const long long t0 = clock64();
+        unsigned spins = 0;
+        while (true) {
+            bool ok = true;
+#pragma unroll
+            for (int k = 0; k < kLLBatch; ++k) {
+                const int i = base + k * STEP;
+                if (i + 1 < n && !(ll_is(w[k].x, tag) && ll_is(w[k].y, tag))) ok = false;
             }
+            if (ok || wt.give_up(t0, spins)) break;
+#pragma unroll
+            for (int k = 0; k < kLLBatch; ++k) {
+                const int i = base + k * STEP;
+                if (i + 1 < n && !(ll_is(w[k].x, tag) && ll_is(w[k].y, tag))) w[k] = ld_ll2<SYS>(src + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kLLBatch; ++k) {
+            const int i = base + k * STEP;
+            if (i + 1 < n) *reinterpret_cast<float2*>(dst + i) = make_float2(ll_val(w[k].x), ll_val(w[k].y));
         }
     }
-    named_sync(1, kMegaConsumers);
+    if ((n & 1) && tid == 0) dst[n - 1] = ll_val(wt.one<SYS>(src + n - 1, ld_ll1<SYS>(src + n - 1), tag));
 }
 
 // Output units [u0, u1) of this CTA: [U b / P, U (b + 1) / P).
@@ -248,83 +324,93 @@ __device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4
     return acc;
 }
 
-// Input vector of a GEMV phase into shared memory (RMSNorm applied when set).
-// Residual phases also stage the residual rows of the CTA's units in sh.res,
-// so the epilogue needs no L2 round trip.
+// Input vector of a GEMV phase into shared memory (RMSNorm applied when
+// set), `ts` the tag of phase 0 of this step, `tag` this phase's.
+//
+// * Tagged input (P.x): read as it lands (phase P.x_ph's tag).
+// * Layer 0: the embedding row of the step's token (or the launch's input
+//   vector) by bulk copy; its raw values are also published as this CTA's
+//   share [K b / P, K (b + 1) / P) of the residual stream at P.xout.
+// * Tensor parallelism (P.nsum > 0): first this CTA's share of base +
+//   the ranks' partials (rank order, the same sum on every rank), published
+//   at P.xout; then the whole vector from every CTA's share.
+// Residual phases also stage the (tagged) residual rows of the CTA's units
+// in sh.res.
 __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, int u0, int u1,
-                       uint32_t& xphase, int tok) {
+                       uint32_t& xphase, int tok, unsigned ts, unsigned tag) {
     const int warp = tid >> 5, lane = tid & 31;
-    const float* src = P.x;
-    if (!src) {
-        src = p.input;
-        if (!src) {
+    const LLWait wt{p.err, &sh.abort};
+    const int K = P.K;
+    const int s0 = (int)((long long)K * blockIdx.x / gridDim.x);
+    const int s1 = (int)((long long)K * (blockIdx.x + 1) / gridDim.x);
+    const float* plain = nullptr;
+    if (!P.x && P.nsum == 0) {
+        plain = p.input;
+        if (!plain) {
             int t = tok;
             if (t < 0 || t >= p.vocab) {
                 if (tid == 0) atomicOr(p.err, kErrToken);
                 t = 0;
             }
-            src = p.emb + (size_t)t * P.K;
+            plain = p.emb + (size_t)t * K;
         }
     }
-    // the input vector (and the norm weights behind it) in one bulk copy
-    // each, issued first so the residual loads below overlap them; the
-    // vector was written by generic stores (after the grid barrier's
-    // acquire), read here through the async proxy.  A summed input (tensor
-    // parallelism) is formed by the threads instead.
-    const bool sum = P.nsum > 0;
-    const uint32_t vbytes = (uint32_t)P.K * 4u;
-    const uint32_t bytes = (sum ? 0u : vbytes) + (P.norm_w ? vbytes : 0u);
+    // constant inputs (norm weights, the embedding row) by bulk copy, issued
+    // first so the tagged reads below overlap them
+    const uint32_t vbytes = (uint32_t)K * 4u;
+    const uint32_t bytes = (plain ? vbytes : 0u) + (P.norm_w ? vbytes : 0u);
     if (tid == 0 && bytes) {
         fence_proxy_async_global();
         mbar_arrive_expect_tx(&sh.xbar, bytes);
-        if (!sum) bulk_g2s_plain(xs, src, vbytes, &sh.xbar);
-        if (P.norm_w) bulk_g2s_plain(xs + P.K, P.norm_w, vbytes, &sh.xbar);
-    }
-    if (sum) {
-        // x = src + the ranks' partials in rank order (every rank forms the
-        // same sum); this CTA also stores its share of the result for later
-        // phases' residual reads
-        const int s0 = (int)((long long)P.K * blockIdx.x / gridDim.x);
-        const int s1 = (int)((long long)P.K * (blockIdx.x + 1) / gridDim.x);
-        for (int i = tid * 4; i < P.K; i += kMegaConsumers * 4) {
-            float4 v = __ldcg(reinterpret_cast<const float4*>(src + i));
-            for (int r = 0; r < P.nsum; ++r) {
-                const float4 w = __ldcg(reinterpret_cast<const float4*>(P.xsum + (size_t)r * P.K + i));
-                v.x += w.x;
-                v.y += w.y;
-                v.z += w.z;
-                v.w += w.w;
-            }
-            *reinterpret_cast<float4*>(xs + i) = v;
-            if (P.xout) {
-                const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (i + j >= s0 && i + j < s1) P.xout[i + j] = e[j];
-            }
-        }
+        if (plain) bulk_g2s_plain(xs, plain, vbytes, &sh.xbar);
+        if (P.norm_w) bulk_g2s_plain(xs + K, P.norm_w, vbytes, &sh.xbar);
     }
     int staged = 0;
-    const int staged_base = u0;
-    if (P.epi == kEpiResidual && u1 - u0 <= kResRows) {
-        for (int i = tid; i < u1 - u0; i += kMegaConsumers) sh.res[i] = __ldcg(P.res + u0 + i);
+    if (P.res && u1 - u0 <= kResRows) {
+        const unsigned rt = ts + (unsigned)P.res_ph;
+        for (int i = tid; i < u1 - u0; i += kMegaConsumers)
+            sh.res[i] = ll_val(wt.one<false>(P.res + u0 + i, ld_ll1<false>(P.res + u0 + i), rt));
         staged = u1 - u0;
     }
     if (tid == 0) {  // one writer; read after the named barrier at the end
         sh.res_n = staged;
-        sh.res_base = staged_base;
+        sh.res_base = u0;
+    }
+    if (P.nsum > 0) {
+        // this CTA's share: base + partial 0 + partial 1 + ...
+        const unsigned bt = ts + (unsigned)P.xbase_ph, pt = ts + (unsigned)P.sum_ph;
+        const unsigned long long* parts =
+            reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + P.sum_off);
+        for (int i = s0 + tid; i < s1; i += kMegaConsumers) {
+            // the own share was stored by this CTA (current at once)
+            const float base = ll_val(wt.one<false>(P.xbase + i, ld_ll1<false>(P.xbase + i), bt));
+            unsigned long long w[kMaxTp];
+#pragma unroll
+            for (int r = 0; r < kMaxTp; ++r)
+                if (r < P.nsum) w[r] = ld_ll1<true>(parts + (size_t)r * K + i);
+            ll_poll<kMaxTp, true>(w, P.nsum, [&](int r) { return parts + (size_t)r * K + i; }, pt, wt);
+            float v = base;
+#pragma unroll
+            for (int r = 0; r < kMaxTp; ++r)
+                if (r < P.nsum) v += ll_val(w[r]);
+            st_ll(P.xout + i, v, tag);
+        }
+        ll_read_vec<false>(P.xout, xs, K, tag, tid, wt);
+    } else if (P.x) {
+        ll_read_vec<false>(P.x, xs, P.kx, ts + (unsigned)P.x_ph, tid, wt);
+        for (int i = P.kx + tid; i < K; i += kMegaConsumers) xs[i] = 0.0f;
     }
     if (bytes) {
         mega_wait(&sh.xbar, xphase & 1u, &sh.abort, p.err);
         ++xphase;
     }
+    named_sync(1, kMegaConsumers);  // every thread's tagged reads into xs
+    if (plain && P.xout)
+        for (int i = s0 + tid; i < s1; i += kMegaConsumers) st_ll(P.xout + i, xs[i], tag);
     constexpr int STRIDE = kMegaConsumers * 4;
-    if (P.x_copy && blockIdx.x == 0)
-        for (int i = tid * 4; i < P.K; i += STRIDE)
-            *reinterpret_cast<float4*>(P.x_copy + i) = *reinterpret_cast<const float4*>(xs + i);
     if (P.norm_w) {
         float ss = 0.0f;
-        for (int i = tid * 4; i < P.K; i += STRIDE) {
+        for (int i = tid * 4; i < K; i += STRIDE) {
             const float4 v = *reinterpret_cast<const float4*>(xs + i);
             ss = fmaf(v.x, v.x, ss);
             ss = fmaf(v.y, v.y, ss);
@@ -335,11 +421,11 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         if (lane == 0) sh.ss[warp] = ss;
         named_sync(1, kMegaConsumers);
         const float tot = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
-        const float rms = rsqrtf(tot / (float)P.K + P.eps);
+        const float rms = rsqrtf(tot / (float)K + P.eps);
         // each thread scales the elements it summed
-        for (int i = tid * 4; i < P.K; i += STRIDE) {
+        for (int i = tid * 4; i < K; i += STRIDE) {
             float4 v = *reinterpret_cast<const float4*>(xs + i);
-            const float4 w = *reinterpret_cast<const float4*>(xs + P.K + i);
+            const float4 w = *reinterpret_cast<const float4*>(xs + K + i);
             v.x = v.x * rms * w.x;
             v.y = v.y * rms * w.y;
             v.z = v.z * rms * w.z;
@@ -384,7 +470,7 @@ __device__ __forceinline__ float warp_reduce_scatter(const float* in, int lane) 
 // is the output index.
 template <typename WT, int NS>
 __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaShared& sh, int ub, int n, int u1,
-                                int tid, float& am_v, int& am_i) {
+                                int tid, float& am_v, int& am_i, unsigned ts, unsigned tag) {
     constexpr int BU = MegaRows<WT>::R / NS;
     for (int idx = tid; idx < n * BU; idx += kMegaConsumers) {
         const int sl = idx / BU, i = idx % BU;
@@ -394,20 +480,27 @@ __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaSha
         if (NS == 2) {
             const int u = BU + i;
             const float yu = ((sh.gpart[0][sl][u] + sh.gpart[1][sl][u]) + sh.gpart[2][sl][u]) + sh.gpart[3][sl][u];
-            P.out[row] = silu_mul(v, yu);
+            st_ll(P.out + row, silu_mul(v, yu), tag);
         } else if (P.epi == kEpiStore) {
-            P.out[row] = v;
+            st_ll(P.out + row, v, tag);
         } else if (P.epi == kEpiResidual) {
             const int ri = row - sh.res_base;
-            const float r = (ri >= 0 && ri < sh.res_n) ? sh.res[ri] : __ldcg(P.res + row);
-            P.out[row] = r + v;
+            float r;
+            if (ri >= 0 && ri < sh.res_n) {
+                r = sh.res[ri];
+            } else {
+                const LLWait wt{p.err, &sh.abort};
+                r = ll_val(wt.one<false>(P.res + row, ld_ll1<false>(P.res + row), ts + (unsigned)P.res_ph));
+            }
+            st_ll(P.out + row, r + v, tag);
         } else if (P.epi == kEpiExchange) {
             // this rank's partial of the row, into every rank's slot for it
             for (int r = 0; r < p.tp_size; ++r)
-                reinterpret_cast<float*>(p.peers[r] + P.xch_off)[(size_t)p.tp_rank * P.units + row] = v;
+                st_ll_sys(reinterpret_cast<unsigned long long*>(p.peers[r] + P.xch_off) + (size_t)p.tp_rank * P.units +
+                              row,
+                          v, tag);
         } else {
-            float* lo = P.out ? P.out : p.logits;
-            lo[row] = v;
+            p.logits[row] = v;
             const int id = P.row_base + row;
             if (argmax_better(v, id, am_v, am_i)) {
                 am_v = v;
@@ -419,7 +512,8 @@ __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaSha
 
 // Winner of the CTA -> partial; the last CTA reduces all partials in CTA
 // order, writes the token and advances the decode state.
-__device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, float am_v, int am_i) {
+__device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, float am_v, int am_i,
+                                 unsigned tag) {
     const int warp = tid >> 5, lane = tid & 31;
     // the order is total, so any reduction tree picks the same winner
 #pragma unroll
@@ -475,34 +569,58 @@ __device__ void argmax_phase_end(const MegaParams& p, MegaShared& sh, int tid, f
     }
     if (lane != 0) return;
     if (p.tp_size > 1) {
-        // this rank's winner (over its vocabulary rows) to every rank, then
-        // the winner of all ranks' (the order is total: every rank agrees)
-        const unsigned long long mine =
-            (unsigned long long)__float_as_uint(v) | ((unsigned long long)(unsigned)id << 32);
+        // this rank's winner (over its vocabulary rows) into every rank's
+        // slot for it: value bits | id << 32 | a step mark << 56 (ids below
+        // 2^24; the mark is the step's count since the plan was built, low 7
+        // bits, with the top bit set so that zeroed memory never matches);
+        // then the winner of all ranks' slots once every slot carries this
+        // step's mark (the order is total: every rank agrees)
+        const unsigned t8 = (((tag - 1u) / (unsigned)p.nphases) & 0x7fu) | 0x80u;
+        const unsigned long long mine = (unsigned long long)__float_as_uint(v) |
+                                        ((unsigned long long)((unsigned)id & 0xffffffu) << 32) |
+                                        ((unsigned long long)t8 << 56);
         for (int r = 0; r < p.tp_size; ++r)
-            reinterpret_cast<unsigned long long*>(p.peers[r] + kXchArgmax)[p.tp_rank] = mine;
-        __threadfence_system();
-        if (exchange_flags(p, sh.xe, &sh.abort)) {
-            const unsigned long long* slots =
-                reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + kXchArgmax);
-            for (int r = 0; r < p.tp_size; ++r) {
-                const unsigned long long s = __ldcg(slots + r);
-                const float rv = __uint_as_float((unsigned)(s & 0xffffffffull));
-                const int ri = (int)(unsigned)(s >> 32);
-                if (argmax_better(rv, ri, v, id)) {
-                    v = rv;
-                    id = ri;
-                }
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(
+                             reinterpret_cast<unsigned long long*>(p.peers[r] + kXchArgmax) + p.tp_rank),
+                         "l"(mine)
+                         : "memory");
+        const unsigned long long* slots = reinterpret_cast<const unsigned long long*>(p.peers[p.tp_rank] + kXchArgmax);
+        const LLWait wt{p.err, &sh.abort};
+        unsigned long long ws[kMaxTp];
+        for (int r = 0; r < p.tp_size; ++r) ws[r] = ld_ll1<true>(slots + r);
+        const long long t0 = clock64();
+        unsigned spins = 0;
+        while (true) {  // re-read the stale slots together
+            bool ok = true;
+            for (int r = 0; r < p.tp_size; ++r)
+                if ((unsigned)(ws[r] >> 56) != t8) ok = false;
+            if (ok || wt.give_up(t0, spins)) break;
+            for (int r = 0; r < p.tp_size; ++r)
+                if ((unsigned)(ws[r] >> 56) != t8) ws[r] = ld_ll1<true>(slots + r);
+        }
+        for (int r = 0; r < p.tp_size; ++r) {
+            const unsigned long long w = ws[r];
+            const float rv = __uint_as_float((unsigned)w);
+            const int ri = (int)((unsigned)(w >> 32) & 0xffffffu);
+            if (argmax_better(rv, ri, v, id)) {
+                v = rv;
+                id = ri;
             }
         }
     }
+    // the next step's (token, position) is published last, with release
+    // semantics: every CTA acquires it before the step, and with it this
+    // step's KV-cache rows and the state below
     const int step = __ldcg(p.state + 2);
+    const int pos = __ldcg(p.state + 1);
     if (p.hist) p.hist[step] = id;
     p.state[3] = id;
-    p.state[0] = id;
-    p.state[1] = __ldcg(p.state + 1) + 1;
     p.state[2] = step + 1;
     *p.am_cnt = 0u;
+    const unsigned long long nst = (unsigned long long)(unsigned)id | ((unsigned long long)(unsigned)(pos + 1) << 32);
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(reinterpret_cast<unsigned long long*>(p.state)),
+                 "l"(nst)
+                 : "memory");
 }
 
 // A consumer's view of the ring: the next slot to take, and the wait
@@ -699,7 +817,7 @@ __device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, f
 
 template <typename WT, int NS, int CB>
 __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& rd, const float* xs, MegaShared& sh,
-                          int tid, int u0, int u1) {
+                          int tid, int u0, int u1, unsigned ts, unsigned tag) {
     constexpr int R = MegaRows<WT>::R;
     constexpr int BU = R / NS;  // units per batch
     static_assert(MegaRows<WT>::PT == R, "a batch of R rows fills whole slots");
@@ -738,38 +856,48 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
         // same rows); run their epilogue before the slots are reused
         if (++bi % kGroupBatch == 0) {
             named_sync(1, kMegaConsumers);
-            combine_batches<WT, NS>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v, am_i);
+            combine_batches<WT, NS>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v, am_i, ts,
+                                    tag);
             named_sync(1, kMegaConsumers);
         }
     }
     const int rest = bi % kGroupBatch;
     if (rest) {
         named_sync(1, kMegaConsumers);
-        combine_batches<WT, NS>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i);
+        combine_batches<WT, NS>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i, ts, tag);
     }
-    if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i);
+    if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i, tag);
 }
 
 template <typename WT, int NS>
 __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned char* ring, uint64_t* full,
                            uint64_t* empty, RingPos& rp, uint32_t& xphase, float* xs, MegaShared& sh, int tid,
-                           long long tb, int tok) {
+                           long long tb, int tok, unsigned ts, unsigned tag) {
     int u0, u1;
     unit_range(P, u0, u1);
-    load_x(p, P, xs, sh, tid, u0, u1, xphase, tok);
+    load_x(p, P, xs, sh, tid, u0, u1, xphase, tok, ts, tag);
     if (tid == 0) trace_mark(p, tb, 1);
     SlotReader rd{ring, full, empty, &rp, p.ring_slots, &sh.abort, p.err, tb >= 0, 0};
     // widths that divide a slot's pieces keep their input columns in
     // registers (every thread takes the same branch: P is shared)
     switch (P.cb) {
-        case 4: gemv_body<WT, NS, 4>(p, P, rd, xs, sh, tid, u0, u1); break;
-        case 8: gemv_body<WT, NS, 8>(p, P, rd, xs, sh, tid, u0, u1); break;
-        default: gemv_body<WT, NS, 0>(p, P, rd, xs, sh, tid, u0, u1); break;
+        case 4: gemv_body<WT, NS, 4>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+        case 8: gemv_body<WT, NS, 8>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+        default: gemv_body<WT, NS, 0>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
     }
     if (tb >= 0) p.trace[tb + 5] = (unsigned long long)rd.waited;
 }
 
-__device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* sm, int tid);
+// Tagged buffers and tags of an attention phase.
+struct AttnLL {
+    const unsigned long long* qkv;  // [Nq D | Nkv D | Nkv D], written by the Q|K|V phase (tag tin)
+    unsigned long long* part;       // split partials [Nkv][splits][G][D + 2]
+    unsigned long long* out;        // [Nq D]
+    unsigned tin, tag;
+};
+
+__device__ void attention_slice_merge(const AttnArgs& a, const AttnLL& ll, int kvh, int split, int active, float* sm,
+                                      int tid, const LLWait& wt);
 
 // One (KV head, split) item of decode attention inside the persistent
 // kernel: the same computation as attention_item (attention.cuh), with its
@@ -783,8 +911,9 @@ __device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* s
 // Scores: lane p walks the D/4 float4 chunks of its key row starting at
 // chunk p mod (D/4), which keeps the unpadded [T][D] tile free of bank
 // conflicts; the sum order per lane is fixed, so results are deterministic.
-__device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int pos, float* sm, MegaShared& sh,
-                                    int tid, uint32_t& xphase, unsigned* err, unsigned long long* tr, long long tb) {
+__device__ void attention_item_bulk(const AttnArgs& a, const AttnLL& ll, int kvh, int split, int pos, float* sm,
+                                    MegaShared& sh, int tid, uint32_t& xphase, unsigned* err, unsigned long long* tr,
+                                    long long tb, const LLWait& wt) {
     // timeline marks of an attention phase (thread 0, tracing on)
     auto mark = [&](int f) {
         if (tb >= 0) tr[tb + f] = global_ns();
@@ -809,30 +938,30 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
     float* rope = ps + G * T;              // [D/2] (cos, sin)
     float* knew = rope + D;                // [D]
     float* vnew = knew + D;                // [D]
-    int* s_last = reinterpret_cast<int*>(vnew + D);
 
     const float* kbase = a.k_cache + (size_t)kvh * a.max_seq * D;
     const float* vbase = a.v_cache + (size_t)kvh * a.max_seq * D;
     const uint32_t row_bytes = (uint32_t)D * 4u;
 
-    // first round: q rows, RoPE row, new K/V rows, first K/V tile
+    // first round: the RoPE row and the first K/V tile by bulk copy, while
+    // the threads read the tagged q rows and new K/V rows as they land
     int t0 = c0, tl = min(T, c1 - c0);
     if (tid == 0) {
         fence_proxy_async_global();
-        uint32_t bytes = (uint32_t)G * row_bytes + row_bytes + 2u * (uint32_t)tl * row_bytes;
-        if (owns_new) bytes += 2u * row_bytes;
+        const uint32_t bytes = row_bytes + 2u * (uint32_t)tl * row_bytes;
         mbar_arrive_expect_tx(&sh.xbar, bytes);
-        bulk_g2s_plain(qs, a.qkv + (size_t)kvh * G * D, (uint32_t)G * row_bytes, &sh.xbar);
         bulk_g2s_plain(rope, a.rope + (size_t)pos * half, row_bytes, &sh.xbar);
-        if (owns_new) {
-            bulk_g2s_plain(knew, a.qkv + (size_t)a.nq * D + (size_t)kvh * D, row_bytes, &sh.xbar);
-            bulk_g2s_plain(vnew, a.qkv + (size_t)(a.nq + a.nkv) * D + (size_t)kvh * D, row_bytes, &sh.xbar);
-        }
         bulk_g2s_plain(kt, kbase + (size_t)t0 * D, (uint32_t)tl * row_bytes, &sh.xbar);
         bulk_g2s_plain(vt, vbase + (size_t)t0 * D, (uint32_t)tl * row_bytes, &sh.xbar);
     }
+    ll_read_vec<false>(ll.qkv + (size_t)kvh * G * D, qs, G * D, ll.tin, tid, wt);
+    if (owns_new) {
+        ll_read_vec<false>(ll.qkv + (size_t)a.nq * D + (size_t)kvh * D, knew, D, ll.tin, tid, wt);
+        ll_read_vec<false>(ll.qkv + (size_t)(a.nq + a.nkv) * D + (size_t)kvh * D, vnew, D, ll.tin, tid, wt);
+    }
     mega_wait(&sh.xbar, xphase & 1u, &sh.abort, err);
     ++xphase;
+    named_sync(1, kMegaConsumers);
     mark(1);
 
     // RoPE (cuda/rope.cu:13-24 with the tabulated factors) on q and the new
@@ -970,97 +1099,85 @@ __device__ void attention_item_bulk(const AttnArgs& a, int kvh, int split, int p
         for (int j = 0; j < MAXH; ++j) {
             if (hv[j]) {
                 const float inv = 1.0f / l_run[j];
-                float* o = a.out + ((size_t)kvh * G + warp + j * NW) * D;
+                unsigned long long* o = ll.out + ((size_t)kvh * G + warp + j * NW) * D;
 #pragma unroll
                 for (int i = 0; i < MAXDL; ++i)
-                    if (lane + 32 * i < D) o[lane + 32 * i] = o_run[j][i] * inv;
+                    if (lane + 32 * i < D) st_ll(o + lane + 32 * i, o_run[j][i] * inv, ll.tag);
             }
         }
         return;
     }
-
-    // partial (m, l, o) of each head; the last split of the head merges
+    // partial (m, l, o) of each head, tagged; every split then merges its
+    // slice of the head group's output (attention_slice_merge)
 #pragma unroll
     for (int j = 0; j < MAXH; ++j) {
         if (hv[j]) {
-            float* pp = a.part + (((size_t)kvh * a.splits + split) * G + warp + j * NW) * (D + 2);
+            unsigned long long* pp = ll.part + (((size_t)kvh * a.splits + split) * G + warp + j * NW) * (D + 2);
             if (lane == 0) {
-                pp[0] = m_run[j];
-                pp[1] = l_run[j];
+                st_ll(pp, m_run[j], ll.tag);
+                st_ll(pp + 1, l_run[j], ll.tag);
             }
 #pragma unroll
             for (int i = 0; i < MAXDL; ++i)
-                if (lane + 32 * i < D) pp[2 + lane + 32 * i] = o_run[j][i];
+                if (lane + 32 * i < D) st_ll(pp + 2 + lane + 32 * i, o_run[j][i], ll.tag);
         }
-    }
-    named_sync(1, kMegaConsumers);
-    if (tid == 0) {
-        // release: this CTA's partials (ordered by the named barrier) before
-        // the ticket; acquire: the other splits' partials before the merge
-        const unsigned ticket = atom_add_acq_rel(&a.counter[kvh], 1u);
-        *s_last = (ticket == (unsigned)active - 1u);
-    }
-    named_sync(1, kMegaConsumers);
-    mark(5);
-    if (*s_last) {
-        attention_merge(a, kvh, active, sm, tid);
-        mark(6);
     }
 }
 
-// The flash-decoding merge of the active splits of KV head kvh by the last
-// split to finish: out = sum_s w_s o_s / sum_s w_s l_s with w_s = exp(m_s -
-// M).  This is the attention phase's critical path, so it is arranged for
-// few dependent L2 round trips: every thread owns output elements (head,
-// column) and issues the loads of its elements' partial rows for
-// kMergeChunk splits at once, the first chunk before the weights are
-// known; meanwhile each warp forms the split weights of its heads (lanes
-// over splits) into shared memory after the item's scratch.  Sums run over
-// the splits in order, so the result does not depend on timing.
-__device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* sm, int tid) {
+// The flash-decoding merge of KV head kvh's active splits, shared by the
+// splits: split `split` forms output elements [G D split / active, G D
+// (split + 1) / active) of the head group, out = sum_s w_s o_s / sum_s w_s
+// l_s with w_s = exp(m_s - M), reading the tagged partials as they land (no
+// ticket, no single merging CTA).  Each thread owns an element and issues
+// the loads of its kMergeChunk splits' values before the weights are known;
+// each warp forms the weights of a head of the slice (lanes over splits)
+// in shared memory after the item's scratch.  Sums run over the splits in
+// order, so results do not depend on timing.
+__device__ void attention_slice_merge(const AttnArgs& a, const AttnLL& ll, int kvh, int split, int active, float* sm,
+                                      int tid, const LLWait& wt) {
     constexpr int NW = kMegaConsumers / 32;
-    constexpr int MAXH = (kAttnMaxGroup + NW - 1) / NW;
     constexpr int SC = kMergeChunk;
-    constexpr int OPT = 4;  // output elements per thread per pass
     const int warp = tid >> 5, lane = tid & 31;
     const int D = a.D, G = a.nq / a.nkv, S = a.splits;
+    const int nout = G * D;
+    const int e0 = (int)((long long)nout * split / active), e1 = (int)((long long)nout * (split + 1) / active);
+    const int h0 = e0 / D, h1 = (e1 - 1) / D;
     const size_t sstride = (size_t)G * (D + 2);
-    const float* pk = a.part + (size_t)kvh * S * sstride;
+    const unsigned long long* pk = ll.part + (size_t)kvh * S * sstride;
     float* wtab = sm + attn_bulk_smem_floats(G, D);  // [G][S] split weights
     float* linv = wtab + (size_t)G * S;               // [G] 1 / sum_s w_s l_s
-    const int nout = G * D;
 
-    float ov[OPT][SC];
-    auto load_chunk = [&](int o0, int s0) {
+    unsigned long long ow[SC];
+    auto issue = [&](int e, int c0) {
+        const int h = e / D, d = e - h * D;
 #pragma unroll
-        for (int k = 0; k < OPT; ++k) {
-            const int e = o0 + k * kMegaConsumers;
-            const int h = e / D, d = e - h * D;
-#pragma unroll
-            for (int q = 0; q < SC; ++q)
-                ov[k][q] = (e < nout && s0 + q < active)
-                               ? __ldcg(pk + (s0 + q) * sstride + (size_t)h * (D + 2) + 2 + d)
-                               : 0.0f;
-        }
+        for (int q = 0; q < SC; ++q)
+            if (c0 + q < active) ow[q] = ld_ll1<false>(pk + (c0 + q) * sstride + (size_t)h * (D + 2) + 2 + d);
     };
-    load_chunk(tid, 0);
+    if (e0 + tid < e1) issue(e0 + tid, 0);
 
-    // split weights of this warp's heads
-#pragma unroll
-    for (int j = 0; j < MAXH; ++j) {
-        const int h = warp + j * NW;
-        if (h >= G) continue;
-        const float* ph = pk + (size_t)h * (D + 2);
-        float mr[kMergeRounds], lr[kMergeRounds];
+    for (int h = h0 + warp; h <= h1; h += NW) {
+        const unsigned long long* ph = pk + (size_t)h * (D + 2);
+        unsigned long long mw[kMergeRounds], lw[kMergeRounds];
 #pragma unroll
         for (int r = 0; r < kMergeRounds; ++r) {
             const int s = lane + 32 * r;
-            mr[r] = s < active ? __ldcg(ph + s * sstride) : -INFINITY;
-            lr[r] = s < active ? __ldcg(ph + s * sstride + 1) : 0.0f;
+            if (s < active) {
+                mw[r] = ld_ll1<false>(ph + s * sstride);
+                lw[r] = ld_ll1<false>(ph + s * sstride + 1);
+            }
         }
-        float M = mr[0];
+        const int nr = active > lane ? (active - lane + 31) / 32 : 0;  // this lane's rounds
+        ll_poll<kMergeRounds, false>(mw, nr, [&](int r) { return ph + (lane + 32 * r) * sstride; }, ll.tag, wt);
+        ll_poll<kMergeRounds, false>(lw, nr, [&](int r) { return ph + (lane + 32 * r) * sstride + 1; }, ll.tag, wt);
+        float mr[kMergeRounds], lr[kMergeRounds];
+        float M = -INFINITY;
 #pragma unroll
-        for (int r = 1; r < kMergeRounds; ++r) M = fmaxf(M, mr[r]);
+        for (int r = 0; r < kMergeRounds; ++r) {
+            mr[r] = r < nr ? ll_val(mw[r]) : -INFINITY;
+            lr[r] = r < nr ? ll_val(lw[r]) : 0.0f;
+            M = fmaxf(M, mr[r]);
+        }
         M = warp_max(M);
         float L = 0.0f;
 #pragma unroll
@@ -1077,32 +1194,24 @@ __device__ void attention_merge(const AttnArgs& a, int kvh, int active, float* s
     }
     named_sync(1, kMegaConsumers);
 
-    for (int o0 = tid; o0 < nout; o0 += OPT * kMegaConsumers) {
-        float acc[OPT];
+    for (int e = e0 + tid; e < e1; e += kMegaConsumers) {
+        const int h = e / D, d = e - h * D;
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < active; c0 += SC) {
+            if (e != e0 + tid || c0 != 0) issue(e, c0);
+            ll_poll<SC, false>(ow, active - c0,
+                               [&](int q) { return pk + (c0 + q) * sstride + (size_t)h * (D + 2) + 2 + d; }, ll.tag,
+                               wt);
 #pragma unroll
-        for (int k = 0; k < OPT; ++k) acc[k] = 0.0f;
-        for (int s0 = 0; s0 < active; s0 += SC) {
-            if (o0 != tid || s0 != 0) load_chunk(o0, s0);
-#pragma unroll
-            for (int k = 0; k < OPT; ++k) {
-                const int e = o0 + k * kMegaConsumers;
-                const int h = e < nout ? e / D : 0;
-#pragma unroll
-                for (int q = 0; q < SC; ++q)
-                    if (s0 + q < active) acc[k] = fmaf(ov[k][q], wtab[h * S + s0 + q], acc[k]);
-            }
+            for (int q = 0; q < SC; ++q)
+                if (c0 + q < active) acc = fmaf(ll_val(ow[q]), wtab[h * S + c0 + q], acc);
         }
-#pragma unroll
-        for (int k = 0; k < OPT; ++k) {
-            const int e = o0 + k * kMegaConsumers;
-            if (e < nout) a.out[(size_t)kvh * nout + e] = acc[k] * linv[e / D];
-        }
+        st_ll(ll.out + (size_t)kvh * nout + e, acc * linv[h], ll.tag);
     }
-    if (tid == 0) a.counter[kvh] = 0u;
 }
 
 __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, long long tb,
-                                uint32_t& xphase, int pos) {
+                                uint32_t& xphase, int pos, unsigned ts, unsigned tag) {
     if (pos < 0 || pos >= p.attn.max_seq) {
         if (tid == 0 && blockIdx.x == 0) atomicOr(p.err, kErrPosition);
         return;
@@ -1110,6 +1219,8 @@ __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* 
     AttnArgs a = p.attn;
     a.k_cache = P.kc;
     a.v_cache = P.vc;
+    const AttnLL ll{p.ll_qkv, p.ll_part, p.ll_attn, ts + (unsigned)P.x_ph, tag};
+    const LLWait wt{p.err, &sh.abort};
     int chunk, active;
     attn_chunk(pos + 1, a.splits, chunk, active);
     const int items = a.nkv * a.splits;
@@ -1123,7 +1234,18 @@ __device__ void attention_phase(const MegaParams& p, const MegaPhase& P, float* 
             named_sync(1, kMegaConsumers);
         }
         first = false;
-        attention_item_bulk(a, kvh, split, pos, xs, sh, tid, xphase, p.err, p.trace, tb);
+        attention_item_bulk(a, ll, kvh, split, pos, xs, sh, tid, xphase, p.err, p.trace, tb, wt);
+    }
+    // every partial of this CTA is stored before it waits on other splits'
+    if (active > 1) {
+        for (int it = blockIdx.x; it < items; it += gridDim.x) {
+            const int kvh = it / a.splits, split = it % a.splits;
+            if (split >= active) continue;
+            named_sync(1, kMegaConsumers);
+            if (tb >= 0) p.trace[tb + 5] = global_ns();
+            attention_slice_merge(a, ll, kvh, split, active, xs, tid, wt);
+            if (tb >= 0) p.trace[tb + 6] = global_ns();
+        }
     }
 }
 
@@ -1344,16 +1466,26 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
 
     RingPos rp{0, 0u};
     uint32_t xphase = 0, pphase = 0;
-    unsigned long long xe = p.xe_base;  // exchange epochs so far
-    unsigned long long target = p.bar_base;
     int cur = 0;
     long long n = 0;  // phases started so far
     const long long total = (long long)p.steps * p.nphases;
+    const unsigned long long* stw = reinterpret_cast<const unsigned long long*>(p.state);
+    const unsigned long long st0 = ld_acquire64(stw);
+    const int pos0 = (int)(unsigned)(st0 >> 32);
     for (int step = 0; step < p.steps; ++step) {
-        // this step's token and position (written by the previous step's
-        // LM-head phase before the grid barrier)
-        const unsigned long long st = ld_acquire64(reinterpret_cast<const unsigned long long*>(p.state));
+        // this step's token and position: published (release) by the last
+        // CTA of the previous step's LM-head phase; acquiring them also makes
+        // that step's KV-cache rows visible
+        unsigned long long st = st0;
+        if (step > 0) {
+            st = ld_acquire64(stw);
+            const long long t0 = clock64();
+            unsigned spins = 0;
+            const LLWait wt{p.err, &sh.abort};
+            while ((int)(unsigned)(st >> 32) != pos0 + step && !wt.give_up(t0, spins)) st = ld_acquire64(stw);
+        }
         const int tok = (int)(unsigned)(st & 0xffffffffull), pos = (int)(unsigned)(st >> 32);
+        const unsigned ts = p.tag_base + (unsigned)step * (unsigned)p.nphases + 1u;  // tag of phase 0
         for (int ph = 0; ph < p.nphases; ++ph) {
             const long long tb = tid == 0 ? trace_base(p, step, ph) : -1;
             trace_mark(p, tb, 0);
@@ -1373,25 +1505,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
                 bulk_g2s_plain(&sP[cur ^ 1], p.phases + nph, (uint32_t)sizeof(MegaPhase), &sh.pbar);
             }
             const MegaPhase& P = sP[cur];
-            // tensor parallelism: the partial-sum phases and the LM head
-            // exchange with the other ranks, each under a new epoch
-            const bool xdata = p.tp_size > 1 && P.kind == kPhGemv && P.xch_off >= 0;
-            if (xdata || (p.tp_size > 1 && P.kind == kPhGemv && P.epi == kEpiArgmax)) ++xe;
-            if (tid == 0) sh.xe = xe;
+            const unsigned tag = ts + (unsigned)ph;
             // every consumer thread takes the same branches here (no branch on the
             // abort flag, which the producer may set at any moment): the phases
             // contain named barriers
             if (P.kind == kPhAttn) {
-                attention_phase(p, P, xs, sh, tid, tb, xphase, pos);
+                attention_phase(p, P, xs, sh, tid, tb, xphase, pos, ts, tag);
             } else if (P.ns == 2) {
-                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
+                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, ts, tag);
             } else {
-                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok);
+                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, ts, tag);
             }
             trace_mark(p, tb, 2);
-            if (xdata) __threadfence_system();  // this CTA's writes into the peers' regions
-            target += gridDim.x + (xdata ? 1 : 0);
-            grid_sync(p, &sh.abort, tid, target, xdata ? xe : 0);
             trace_mark(p, tb, 3);
             cur ^= 1;
             ++n;

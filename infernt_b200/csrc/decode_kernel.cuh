@@ -23,23 +23,31 @@ struct alignas(16) MegaPhase {
     int units;          // output rows (ns == 2: gate/up pairs)
     int K;              // input features, a multiple of 512
     int cb;             // K / 512
-    const float* x;     // input vector; NULL: the per-launch input (layer 0)
+    int kx;             // input columns written by the producing phase (<= K; the rest, down's
+                        // padding under tensor parallelism, reads as zero)
+    // activations are tagged words (decode_kernel.cu): value | phase tag << 32
+    const unsigned long long* x;  // input vector, written by phase x_ph of the step; NULL: the
+                                  // per-launch input or embedding row (layer 0), or the summed input
+    int x_ph;                     // attention phases: the Q|K|V phase
     const float* norm_w;  // RMSNorm weight or NULL
     float eps;
-    float* out;         // NULL: the per-launch logits (LM head)
-    const float* res;   // residual source (out = res + y)
-    float* x_copy;      // layer 0: the raw input row is copied here (residual stream)
+    unsigned long long* out;        // NULL: the per-launch logits (LM head, plain FP32)
+    const unsigned long long* res;  // residual rows (out = res + y), written by phase res_ph
+    int res_ph;
+    unsigned long long* xout;       // this CTA's share [K b/P, K (b+1)/P) of the input (layer 0's raw
+                                    // embedding row, or the summed input) is published here, or NULL
     int layer;          // attention phases: KV-cache layer
     float* kc;          // attention phases: the layer's K and V caches [N_kv, max_seq, D]
     float* vc;
     // tensor parallelism
-    int nsum;           // > 0: the input vector is x + the nsum partial vectors at xsum (rank order)
+    int nsum;           // > 0: x = the xout vector of shares xbase + the nsum partials (rank order)
+    const unsigned long long* xbase;  // this CTA's earlier share of the residual stream (phase xbase_ph)
+    int xbase_ph;
+    int sum_off;        // the partials [nsum][K] in this rank's exchange region, written by phase sum_ph
+    int sum_ph;
     int xch_off;        // >= 0: epilogue writes its rows to every rank's exchange region at this
                         // byte offset, slot [this rank][units]; -1: none
-    const float* xsum;  // [nsum][K] partials of the previous exchange (this rank's region)
-    float* xout;        // the summed input's rows [K b/P, K (b+1)/P) are written here (or NULL)
     int row_base;       // LM head: global index of the first local row (argmax ids)
-    int pad_;
 };
 // descriptors are bulk-copied into shared memory ahead of their phase
 static_assert(sizeof(MegaPhase) % 16 == 0, "MegaPhase must be a multiple of 16 bytes");
@@ -57,37 +65,39 @@ struct MegaParams {
     int vocab;
     AttnArgs attn;       // qkv, out, part, counter, shape, theta, scale (caches per phase)
     // scratch
-    int* state;          // {token, position, step, last token}
+    int* state;          // {token, position, step, last token}; (token, position) published with release
     unsigned* err;
-    unsigned long long* bar;       // grid-barrier arrivals (only ever grows)
-    unsigned long long bar_base;   // its value when this launch starts
+    unsigned tag_base;   // tag of this launch's first phase instance, minus 1
+    unsigned long long* ll_qkv;   // tagged Q|K|V rows, split partials and attention output
+    unsigned long long* ll_part;
+    unsigned long long* ll_attn;
     float* am_val;       // LM-head argmax partials [gridDim]
     int* am_idx;
     unsigned* am_cnt;
     int ring_slots;
     int x_floats;        // shared floats for the input vector / attention scratch
     // tensor parallelism over tp_size GPUs (tp_size 1: none): every rank's
-    // exchange region (flags at kXchFlags, argmax slots at kXchArgmax, the
-    // partial buffers at the phases' xch_off), mapped into this process
+    // exchange region (argmax slots at kXchArgmax, the partial buffers at
+    // the phases' xch_off), mapped into this process
     int tp_rank, tp_size;
     unsigned char* const* peers;   // [tp_size] region base pointers (own included)
-    unsigned long long xe_base;    // exchange epoch before this launch's first exchange    // optional phase timeline (nanoseconds, %globaltimer): for CTA 0 and the
-    // last CTA, per (step, phase): [phase start, input loaded, work done,
-    // barrier passed, producer issued the phase's last slot, SM cycles
-    // consumer warp 0 waited for full slots, SM cycles the producer waited
-    // for free slots while issuing the phase's slots]
+    // optional phase timeline (nanoseconds, %globaltimer): for every CTA,
+    // per (step, phase): [phase start, input loaded, work done, phase end,
+    // producer issued the phase's last slot, SM cycles consumer warp 0
+    // waited for full slots, SM cycles the producer waited for free slots
+    // while issuing the phase's slots]; attention phases record the item's
+    // inputs landed (1), partial computed (4), merge start and end (5, 6)
     unsigned long long* trace;
 };
 
 constexpr int kTraceFields = 7;
 
 // Exchange region layout (one per rank, cudaMalloc'd, shared by IPC):
-// flags [8] u64 (the last exchange epoch each rank has published), argmax
-// slots [8] u64 (float value bits | index << 32), then the partial buffers.
+// argmax slots [8] u64 (float value bits | index << 32 | tag << 56), then
+// the tagged partial buffers.
 constexpr int kMaxTp = 8;
-constexpr int kXchFlags = 0;
-constexpr int kXchArgmax = 256;
-constexpr int kXchData = 512;
+constexpr int kXchArgmax = 0;
+constexpr int kXchData = 256;
 
 // Rows of a consumer batch: 8 FP32 / 16 bf16 (a batch is whole 16 KB slots).
 inline int mega_batch_rows(int weight_dtype) { return weight_dtype == 1 ? 16 : 8; }

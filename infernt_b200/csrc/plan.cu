@@ -92,7 +92,8 @@ struct infernt_plan {
     void* mega_mem = nullptr;
     MegaParams mega;
     int mega_ctas = 0;
-    unsigned long long bar_epoch = 0;  // grid-barrier counter value at the next launch
+    unsigned tag_base = 0;   // phase instances run so far (tags of tagged activations)
+    void* ll_mem = nullptr;  // tagged activation buffers of the persistent kernel
     // tensor parallelism (tp_size 1: none).  cfg holds this rank's shapes:
     // its heads, its gate/up rows padded to a multiple of 512 (down's K), its
     // vocabulary rows
@@ -106,7 +107,6 @@ struct infernt_plan {
     std::vector<void*> opened;  // peers' regions mapped into this process
     unsigned char** peer_tab = nullptr;  // device copy of the region pointers
     bool peers_set = false;
-    unsigned long long xepoch = 0;  // exchange epochs published so far
 };
 
 namespace {
@@ -267,17 +267,15 @@ int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, fl
         m.logits = logits;
         m.hist = hist;
         m.steps = steps;
-        m.bar_base = p->bar_epoch;
-        // per step: one arrival per CTA and phase, plus one per all-reduce;
-        // exchange epochs: two all-reduces per layer and the argmax
-        const int L = p->cfg.num_layers;
-        const unsigned long long xch = p->tp_size > 1 ? 2ull * L : 0ull;
-        p->bar_epoch += (unsigned long long)steps * ((unsigned long long)m.nphases * p->mega_ctas + xch);
-        if (p->tp_size > 1) {
-            m.peers = p->peer_tab;
-            m.xe_base = p->xepoch;
-            p->xepoch += (unsigned long long)steps * (2ull * L + 1ull);
-        }
+        // every phase instance has its own tag (the same sequence on every
+        // rank); 32-bit tags bound a plan's lifetime
+        const unsigned long long used = (unsigned long long)steps * (unsigned long long)m.nphases;
+        INFERNT_REQUIRE((unsigned long long)p->tag_base + used < 0xffffffffull,
+                        "persistent plan: %u phase instances run, the tag space is spent; recreate the plan",
+                        p->tag_base);
+        m.tag_base = p->tag_base;
+        p->tag_base += (unsigned)used;
+        if (p->tp_size > 1) m.peers = p->peer_tab;
         INFERNT_CUDA_TRY(launch_mega(m, p->cfg.weight_dtype, p->mega_ctas, st));
         return INFERNT_OK;
     }
@@ -324,19 +322,40 @@ int build_mega(infernt_plan* p) {
     const int G = c.num_attention_heads / c.num_key_value_heads;
     const bool tp = p->tp_size > 1;
     const int T = p->tp_size;
-    // exchange buffers of the O and down partials (kept apart: a rank may
-    // write one while a slower rank still reads the other)
-    const int off_o = kXchData, off_d = kXchData + T * H * 4;
-    const float* xch_o = tp ? reinterpret_cast<const float*>(static_cast<char*>(p->xch_mem) + off_o) : nullptr;
-    const float* xch_d = tp ? reinterpret_cast<const float*>(static_cast<char*>(p->xch_mem) + off_d) : nullptr;
+    // exchange buffers of the O and down partials, tagged words [T][H]
+    const int off_o = kXchData, off_d = kXchData + T * H * 8;
+
+    // tagged activations: Q|K|V rows, split partials, attention output, the
+    // residual stream (hA: layer input / after down, hB: after O), act
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t w8 = sizeof(unsigned long long);
+    const size_t n_qkv = (size_t)p->qs + 2 * p->kvs;
+    const size_t n_part = (size_t)c.num_key_value_heads * p->splits * G * (c.head_dim + 2);
+    const size_t b_qkv = al(w8 * n_qkv), b_part = al(w8 * n_part), b_attn = al(w8 * p->qs), b_h = al(w8 * H),
+                 b_act = al(w8 * I);
+    const size_t ll_total = b_qkv + b_part + b_attn + 2 * b_h + b_act;
+    INFERNT_CUDA_TRY(cudaMalloc(&p->ll_mem, ll_total));
+    INFERNT_CUDA_TRY(cudaMemset(p->ll_mem, 0, ll_total));
+    char* lb = static_cast<char*>(p->ll_mem);
+    auto take = [&](size_t bytes) {
+        unsigned long long* r = reinterpret_cast<unsigned long long*>(lb);
+        lb += bytes;
+        return r;
+    };
+    unsigned long long* ll_qkv = take(b_qkv);
+    unsigned long long* ll_part = take(b_part);
+    unsigned long long* ll_attn = take(b_attn);
+    unsigned long long* hA = take(b_h);
+    unsigned long long* hB = take(b_h);
+    unsigned long long* ll_act = take(b_act);
 
     std::vector<MegaPhase> ph;
 
     // a GEMV phase over the matrices `mats` stacked in the row space (ns ==
-    // 2: gate, up)
+    // 2: gate, up), input x written by phase x_ph of the step
     auto gemv = [&](int epi, int ns, std::initializer_list<const void*> mats, std::initializer_list<int> rows,
-                    int units, int K, const float* x, const float* norm, float* out, const float* res,
-                    float* x_copy) -> MegaPhase& {
+                    int units, int K, const unsigned long long* x, int x_ph, const float* norm,
+                    unsigned long long* out) -> MegaPhase& {
         MegaPhase P;
         memset(&P, 0, sizeof(P));
         P.kind = kPhGemv;
@@ -349,56 +368,74 @@ int build_mega(infernt_plan* p) {
         for (int r : rows) P.seg_rows[i++] = r;
         P.units = units;
         P.K = K;
+        P.kx = K;
         P.cb = K / kPiece;
         P.x = x;
+        P.x_ph = x_ph;
         P.norm_w = norm;
         P.eps = c.rms_norm_eps;
         P.out = out;
-        P.res = res;
-        P.x_copy = x_copy;
         P.xch_off = -1;
         ph.push_back(P);
         return ph.back();
     };
-    // with tensor parallelism the input of a phase after an all-reduce is
-    // the residual stream plus every rank's partial
-    auto summed = [&](MegaPhase& P, const float* parts, float* share) {
+    // with tensor parallelism the input after an all-reduce is the sum of
+    // this CTA's share of the residual stream and every rank's partial
+    // (published at xout), then the whole of xout
+    auto summed = [&](MegaPhase& P, const unsigned long long* base, int base_ph, int off, int sum_ph,
+                      unsigned long long* xout) {
         P.nsum = T;
-        P.xsum = parts;
-        P.xout = share;
+        P.xbase = base;
+        P.xbase_ph = base_ph;
+        P.sum_off = off;
+        P.sum_ph = sum_ph;
+        P.xout = xout;
     };
     const int Iu = p->iloc;  // gate/up rows (down's K may be padded past them)
     for (int l = 0; l < L; ++l) {
         const void* const* lw = p->w.data() + 3 + 9 * l;
-        const float* qkv_in = l == 0 ? nullptr : (tp ? p->hmid : p->hidden);
+        const int q = 5 * l;       // this layer's phases: q, q+1 (attention), q+2 (O), q+3 (gate/up), q+4 (down)
+        const int dprev = q - 1;   // the previous layer's down phase
+        const float* attn_norm = static_cast<const float*>(lw[0]);
         MegaPhase& Q = gemv(kEpiStore, 1, {lw[1], lw[2], lw[3]}, {p->qs, p->kvs, p->kvs}, p->qs + 2 * p->kvs, H,
-                            qkv_in, static_cast<const float*>(lw[0]), p->qkv, nullptr, l == 0 ? p->hidden : nullptr);
-        if (tp && l > 0) summed(Q, xch_d, p->hidden);
+                            (l == 0 || tp) ? nullptr : hA, dprev, attn_norm, ll_qkv);
+        if (l == 0)
+            Q.xout = hA;  // the embedding row starts the residual stream
+        else if (tp)
+            summed(Q, hB, dprev - 1, off_d, dprev, hA);
         MegaPhase A;
         memset(&A, 0, sizeof(A));
         A.kind = kPhAttn;
         A.layer = l;
         A.kc = p->kc[l];
         A.vc = p->vc[l];
+        A.x_ph = q;
         A.xch_off = -1;
         ph.push_back(A);
         if (tp) {
-            gemv(kEpiExchange, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, nullptr, nullptr, nullptr).xch_off = off_o;
-            MegaPhase& U = gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, p->hidden,
-                                static_cast<const float*>(lw[5]), p->act, nullptr, nullptr);
-            summed(U, xch_o, p->hmid);
-            gemv(kEpiExchange, 1, {lw[8]}, {H}, H, I, p->act, nullptr, nullptr, nullptr, nullptr).xch_off = off_d;
+            gemv(kEpiExchange, 1, {lw[4]}, {H}, H, p->qs, ll_attn, q + 1, nullptr, nullptr).xch_off = off_o;
+            MegaPhase& U = gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, nullptr, 0,
+                                static_cast<const float*>(lw[5]), ll_act);
+            summed(U, hA, q, off_o, q + 2, hB);
+            MegaPhase& Dn = gemv(kEpiExchange, 1, {lw[8]}, {H}, H, I, ll_act, q + 3, nullptr, nullptr);
+            Dn.xch_off = off_d;
+            Dn.kx = Iu;  // the padding columns past this rank's gate/up rows
         } else {
-            gemv(kEpiResidual, 1, {lw[4]}, {H}, H, p->qs, p->attn, nullptr, p->hidden, p->hidden, nullptr);
-            gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, p->hidden, static_cast<const float*>(lw[5]), p->act,
-                 nullptr, nullptr);
-            gemv(kEpiResidual, 1, {lw[8]}, {H}, H, I, p->act, nullptr, p->hidden, p->hidden, nullptr);
+            MegaPhase& O = gemv(kEpiResidual, 1, {lw[4]}, {H}, H, p->qs, ll_attn, q + 1, nullptr, hB);
+            O.res = hA;
+            O.res_ph = l == 0 ? 0 : dprev;
+            gemv(kEpiSwiGLU, 2, {lw[6], lw[7]}, {Iu, Iu}, Iu, H, hB, q + 2, static_cast<const float*>(lw[5]),
+                 ll_act);
+            MegaPhase& Dn = gemv(kEpiResidual, 1, {lw[8]}, {H}, H, I, ll_act, q + 3, nullptr, hA);
+            Dn.res = hB;
+            Dn.res_ph = q + 2;
         }
     }
-    MegaPhase& LM = gemv(kEpiArgmax, 1, {p->w[2]}, {V}, V, H, tp ? p->hmid : p->hidden,
-                         static_cast<const float*>(p->w[1]), nullptr, nullptr, nullptr);
+    const int dlast = 5 * L - 1;
+    MegaPhase& LM = gemv(kEpiArgmax, 1, {p->w[2]}, {V}, V, H, tp ? nullptr : hA, dlast,
+                         static_cast<const float*>(p->w[1]), nullptr);
     LM.row_base = p->v0;
-    if (tp) summed(LM, xch_d, nullptr);
+    if (tp) summed(LM, hB, dlast - 1, off_d, dlast, hA);
 
     // input vector + the norm weights behind it (RMSNorm phases), or the
     // attention scratch, whichever is larger
@@ -422,20 +459,16 @@ int build_mega(infernt_plan* p) {
     INFERNT_REQUIRE(per_sm >= 1, "persistent decode: kernel does not fit on an SM");
     const int ctas = sm_count();
 
-    // device memory: phases | barrier | argmax partials | argmax ticket
-    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    // device memory: phases | argmax partials | argmax ticket
     const size_t b_ph = al(sizeof(MegaPhase) * ph.size());
-    const size_t b_bar = 256;
     const size_t b_am = al(sizeof(float) * ctas) + al(sizeof(int) * ctas) + 256;
-    const size_t total = b_ph + b_bar + b_am;
+    const size_t total = b_ph + b_am;
     INFERNT_CUDA_TRY(cudaMalloc(&p->mega_mem, total));
     INFERNT_CUDA_TRY(cudaMemset(p->mega_mem, 0, total));
     char* b = static_cast<char*>(p->mega_mem);
     MegaPhase* d_ph = reinterpret_cast<MegaPhase*>(b);
     INFERNT_CUDA_TRY(cudaMemcpy(d_ph, ph.data(), sizeof(MegaPhase) * ph.size(), cudaMemcpyHostToDevice));
     b += b_ph;
-    unsigned long long* d_bar = reinterpret_cast<unsigned long long*>(b);
-    b += b_bar;
     float* d_amv = reinterpret_cast<float*>(b);
     b += al(sizeof(float) * ctas);
     int* d_ami = reinterpret_cast<int*>(b);
@@ -448,10 +481,9 @@ int build_mega(infernt_plan* p) {
     m.nphases = (int)ph.size();
     m.emb = static_cast<const float*>(p->w[0]);
     m.vocab = p->vocab_global;  // embedding rows (V is this rank's LM-head rows)
-    m.attn.qkv = p->qkv;
-    m.attn.out = p->attn;
-    m.attn.part = p->attn_part;
-    m.attn.counter = p->attn_counter;
+    m.ll_qkv = ll_qkv;
+    m.ll_part = ll_part;
+    m.ll_attn = ll_attn;
     m.attn.nq = c.num_attention_heads;
     m.attn.nkv = c.num_key_value_heads;
     m.attn.D = c.head_dim;
@@ -463,7 +495,6 @@ int build_mega(infernt_plan* p) {
     m.attn.rope = p->rope;
     m.state = p->state;
     m.err = p->err;
-    m.bar = d_bar;
     m.am_val = d_amv;
     m.am_idx = d_ami;
     m.am_cnt = d_amc;
@@ -512,8 +543,8 @@ int plan_create_impl(const infernt_llama_config* cfg, const void* const* weights
     p->kvs = cfg->num_key_value_heads * cfg->head_dim;
     p->mode = mode;
     const int splits = sm_count() / cfg->num_key_value_heads;
-    // at most 256 splits per KV head (the persistent kernel's merge bound)
-    p->splits = splits < 1 ? 1 : (splits > 256 ? 256 : splits);
+    // at most 64 splits per KV head (the persistent kernel's merge bound)
+    p->splits = splits < 1 ? 1 : (splits > 64 ? 64 : splits);
 
     auto al = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t b_qkv = al(sizeof(float) * (p->qs + 2 * p->kvs));
@@ -573,7 +604,7 @@ int plan_create_impl(const infernt_llama_config* cfg, const void* const* weights
             return fail(INFERNT_ERR_UNSUPPORTED, "tensor-parallel plan: shapes not eligible for the persistent "
                                                  "kernel (K multiples of 512, 16-byte aligned, head_dim %% 4)");
         }
-        p->xch_bytes = kXchData + 2 * (size_t)p->tp_size * cfg->hidden_size * sizeof(float);
+        p->xch_bytes = kXchData + 2 * (size_t)p->tp_size * cfg->hidden_size * sizeof(unsigned long long);
         e = cudaMalloc(&p->xch_mem, p->xch_bytes);
         if (e == cudaSuccess) e = cudaMemset(p->xch_mem, 0, p->xch_bytes);
         if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&p->peer_tab), sizeof(void*) * kMaxTp);
@@ -644,6 +675,8 @@ int infernt_plan_create_tp(const infernt_llama_config* cfg, const void* const* w
     local.intermediate_size = d[3];
     local.vocab_size = d[5];
     if (int s = validate_config(&local)) return s;
+    INFERNT_REQUIRE(cfg->vocab_size <= (1 << 24), "plan_create_tp: vocabulary of %d above 2^24 ids",
+                    cfg->vocab_size);
     TpShard tp;
     tp.rank = tp_rank;
     tp.size = tp_size;
@@ -693,6 +726,7 @@ int infernt_plan_destroy(infernt_plan* p) {
     cudaFree(p->peer_tab);
     cudaFree(p->xch_mem);
     cudaFree(p->mega_mem);
+    cudaFree(p->ll_mem);
     cudaFree(p->scratch);
     delete p;
     return INFERNT_OK;
@@ -746,10 +780,6 @@ int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
     INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
     if (err) {
         cudaMemsetAsync(p->err, 0, sizeof(unsigned), st);
-        if (p->mega.bar) {  // an aborted launch leaves the barrier count short: restart it
-            cudaMemsetAsync(p->mega.bar, 0, sizeof(unsigned long long), st);
-            p->bar_epoch = 0;
-        }
         cudaStreamSynchronize(st);
         return fail(INFERNT_ERR_DEVICE,
                     "decode kernels reported error word 0x%x (1: wait timeout, 2: position, 4: token id)", err);
