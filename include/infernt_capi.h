@@ -160,6 +160,16 @@ INFERNT_API int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, co
                                                int weight_dtype, const float* x,
                                                const float* norm_w, float eps,
                                                void* workspace, void* stream);
+/* Batched projection on the tensor cores (CublasWrapper::gemm with M = batch,
+ * gemm/cublas_wrapper.cu:21-40 as called by llama_layer.cpp:18-23 for an
+ * activation batch [B, h]): for T tokens X [T][K] and row-major weights
+ * W [N][K], both bf16, partials[s][t][n] = the FP32 sum over split s's share
+ * of K of X[t][k] W[n][k]; the caller adds the `splits` partials (in order
+ * for a deterministic result).  N a multiple of 128, K a multiple of 64,
+ * 1 <= T <= 256, 1 <= splits <= K / 64, W and X 16-byte aligned.  err (or
+ * NULL): bit 0 set by the device if a wait timed out. */
+INFERNT_API int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, int T,
+                                   float* partials, int splits, unsigned* err, void* stream);
 
 /* ------------------------------------------------- the decode plan ---
  * One decoder of a LLaMA-family model over caller-owned weights and KV

@@ -132,6 +132,7 @@ _SIGS = {
     "infernt_attention_decode_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P]),
     "infernt_lm_head_workspace_bytes": (_S, []),
     "infernt_rmsnorm_lm_head_argmax": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P, _P]),
+    "infernt_bgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),
     "infernt_plan_destroy": (_I, [_P]),

@@ -1,0 +1,282 @@
+// bgemm.cu — the projections of batched decode on the 5th-generation tensor
+// cores: Y[t][n] = sum_k X[t][k] W[n][k] for T tokens (a batch of decoding
+// sequences) and row-major bf16 weights W[N][K], FP32 accumulation.
+//
+// The weights are the MMA's A operand (M = 128 output rows per tile, K-major
+// as stored) and the tokens its B operand (N = T padded to 16, K-major), so a
+// tile's accumulator is D[128 rows][T] FP32 in tensor memory.  Decode is
+// weight-bandwidth bound (2 T FLOP per weight element), so every SM must
+// stream weights: the K range of a row tile is split over `splits` CTAs, each
+// writing its partial D to part[split][t][n]; the consumer of the projection
+// adds the partials in split order (deterministic).
+//
+// Per CTA (128 threads): thread 0 of warp 0 drives TMA (tiled 2-D loads of a
+// [128 x 64] weight box and a [T x 64] token box per stage, 128-byte swizzle,
+// into a ring of kStages stages with full / empty mbarriers); thread 0 of warp
+// 1 issues tcgen05.mma (kind::f16, bf16 x bf16 -> FP32, four K = 16 steps per
+// stage) and frees each stage with tcgen05.commit; after the last stage's
+// commit all four warps read their 32 accumulator lanes with tcgen05.ld and
+// store the partial.  Every wait is bounded; on expiry the kernel sets bit 0
+// of *err and returns after its copies have landed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace infernt {
+namespace {
+
+constexpr int kBM = 128;        // weight rows per tile (MMA M)
+constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of bf16
+constexpr int kStages = 6;       // most stages (fewer for large token counts)
+constexpr int kSmemLimit = 225 * 1024;  // dynamic shared memory (the static part stays below 2 KB)
+constexpr int kThreads = 128;
+constexpr int kMaxTokens = 256;  // MMA N limit
+constexpr uint32_t kTileW = kBM * kBK * 2;  // 16 KB
+constexpr long long kWaitCycles = 2000000000ll;
+
+struct BgemmArgs {
+    float* part;      // [splits][T][N]
+    unsigned* err;    // bit 0: a wait timed out (may be NULL)
+    int N, K, T, tp, splits, stages;
+};
+
+__device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, bool& ok) {
+    if (!ok) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitCycles) {
+            ok = false;
+            return false;
+        }
+    }
+    return true;
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte swizzle:
+// rows of 128 bytes, 8-row swizzle atoms of 1024 bytes (stride byte offset),
+// descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3fffu);      // start address
+    d |= (uint64_t)1u << 16;                          // leading byte offset (unused with swizzle)
+    d |= (uint64_t)(1024u >> 4) << 32;                // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1u << 46;                          // version
+    d |= (uint64_t)2u << 61;                          // layout: 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: D FP32, A and B bf16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t bf16_idesc(int n) {
+    return (1u << 4)                      // D format F32
+           | (1u << 7)                    // A format BF16
+           | (1u << 10)                   // B format BF16
+           | ((uint32_t)(n >> 3) << 17)   // N / 8
+           | ((uint32_t)(kBM >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_addr(dst)),
+        "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ uint64_t full[kStages], empty[kStages], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // 1024-byte aligned stages: [W tile | X tile]
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t tile_x = (uint32_t)a.tp * kBK * 2;
+    const uint32_t stage_bytes = kTileW + tile_x;
+
+    const int tiles_n = a.N / kBM;
+    const int tile = blockIdx.x / a.splits, split = blockIdx.x % a.splits;
+    const int n0 = tile * kBM;
+    const int nk = a.K / kBK;
+    const int k0 = (int)((long long)nk * split / a.splits), k1 = (int)((long long)nk * (split + 1) / a.splits);
+    const int cols = a.tp < 32 ? 32 : (a.tp <= 32 ? 32 : (a.tp <= 64 ? 64 : (a.tp <= 128 ? 128 : 256)));
+    (void)tiles_n;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        mbar_fence_init();
+        s_ok = 1;
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                     "r"(cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+
+    bool ok = true;
+    if (warp == 0 && lane == 0) {
+        // producer
+        for (int i = k0; i < k1; ++i) {
+            const int j = i - k0, s = j % a.stages;
+            if (j >= a.stages && !bg_wait(&empty[s], ((j / a.stages) - 1) & 1u, ok)) break;
+            unsigned char* st = smem + (size_t)s * stage_bytes;
+            mbar_arrive_expect_tx(&full[s], stage_bytes);
+            tma_load_2d(st, &tm_w, i * kBK, n0, &full[s]);
+            tma_load_2d(st + kTileW, &tm_x, i * kBK, 0, &full[s]);
+        }
+        if (!ok) atomicExch(&s_ok, 0);
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer
+        const uint32_t idesc = bf16_idesc(a.tp);
+        for (int i = k0; i < k1; ++i) {
+            const int j = i - k0, s = j % a.stages;
+            if (!bg_wait(&full[s], (j / a.stages) & 1u, ok)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t wa = smem_addr(smem + (size_t)s * stage_bytes);
+            const uint64_t da = sw128_desc(wa), db = sw128_desc(wa + kTileW);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+                // K = 16 bf16 = 32 bytes further along the swizzled rows
+                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+                const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
+                    "l"(da + adv), "l"(db + adv), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+            }
+            // the stage is free once these MMAs have read it
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_addr(&empty[s]))
+                         : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_addr(&done))
+                     : "memory");
+        if (!ok) atomicExch(&s_ok, 0);
+    }
+    __syncwarp();
+    // epilogue: every thread waits for the accumulator, then warp w reads
+    // lanes [32 w, 32 w + 32) = output rows n0 + 32 w + lane
+    bool eok = true;
+    bg_wait(&done, 0u, eok);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int n = n0 + warp * 32 + lane;
+    float* out = a.part + (size_t)split * a.T * a.N;
+    for (int c = 0; c < a.tp; c += 16) {
+        uint32_t r[16];
+        const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(addr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+            if (c + q < a.T) out[(size_t)(c + q) * a.N + n] = __uint_as_float(r[q]);
+    }
+    if (!eok) atomicExch(&s_ok, 0);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (!s_ok) {
+        if (tid == 0 && a.err) atomicOr(a.err, 1u);
+        // copies still in flight into shared memory land before the CTA exits
+        const long long t0 = clock64();
+        while (clock64() - t0 < 20000000ll) __nanosleep(1000);
+    }
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// A [rows][K] bf16 row-major matrix as 2-D boxes of [box_rows][64].
+int make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    auto fn = encode_fn();
+    INFERNT_REQUIRE(fn, "bgemm: cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    INFERNT_REQUIRE(r == CUDA_SUCCESS, "bgemm: tensor map encoding failed (%d)", (int)r);
+    return INFERNT_OK;
+}
+
+}  // namespace
+
+int bgemm_stages(int tp) {
+    const int per = kTileW + tp * kBK * 2;
+    const int n = (kSmemLimit - 1024) / per;
+    return n < kStages ? n : kStages;
+}
+
+int bgemm_smem_bytes(int tp) { return bgemm_stages(tp) * (kTileW + tp * kBK * 2) + 1024; }
+
+// Host side of one batched projection (plan code calls this with maps it
+// built once; the C entry point builds them per call).
+int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part, int splits, unsigned* err,
+                 cudaStream_t st) {
+    INFERNT_REQUIRE(W && X && part, "bgemm: null pointer");
+    INFERNT_REQUIRE(N > 0 && N % kBM == 0, "bgemm: N = %d must be a positive multiple of %d", N, kBM);
+    INFERNT_REQUIRE(K > 0 && K % kBK == 0, "bgemm: K = %d must be a positive multiple of %d", K, kBK);
+    INFERNT_REQUIRE(T >= 1 && T <= kMaxTokens, "bgemm: T = %d outside [1, %d]", T, kMaxTokens);
+    INFERNT_REQUIRE(splits >= 1 && splits <= K / kBK, "bgemm: splits = %d outside [1, K / %d]", splits, kBK);
+    INFERNT_REQUIRE(aligned16(W) && aligned16(X), "bgemm: W and X must be 16-byte aligned");
+    const int tp = (T + 15) / 16 * 16;
+    CUtensorMap mw, mx;
+    if (int s = make_map(&mw, W, N, K, kBM)) return s;
+    if (int s = make_map(&mx, X, T, K, tp)) return s;
+    const int smem = bgemm_smem_bytes(tp);
+    static bool raised = false;
+    if (!raised) {
+        INFERNT_CUDA_TRY(cudaFuncSetAttribute(bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+        raised = true;
+    }
+    BgemmArgs args;
+    args.part = part;
+    args.err = err;
+    args.N = N;
+    args.K = K;
+    args.T = T;
+    args.tp = tp;
+    args.splits = splits;
+    args.stages = bgemm_stages(tp);
+    bgemm_kernel<<<(N / kBM) * splits, kThreads, smem, st>>>(mw, mx, args);
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
+}  // namespace infernt
+
+extern "C" int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, int T, float* partials, int splits,
+                                  unsigned* err, void* stream) {
+    return infernt::bgemm_launch(W, N, K, X, T, partials, splits, err, static_cast<cudaStream_t>(stream));
+}
