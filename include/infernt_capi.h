@@ -252,6 +252,41 @@ INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* t
 /* CTAs of the persistent decode kernel on the current device (one per SM). */
 INFERNT_API int infernt_persistent_ctas(void);
 
+/* ------------------------------------------------ batched decode ---
+ * T sequences decoding together, one token each per step (the reference's
+ * LlamaArchitecture keeps [B, h] activations, architectures/llama/
+ * llama_model.cpp:8-43, but decodes B = 1): bf16 projection weights on the
+ * tensor cores (infernt_bgemm_bf16), activations rounded to bf16 where they
+ * enter a projection, per-sequence bf16 KV caches [N_kv, max_seq, D] per
+ * layer, FP32 residual stream, norms and attention arithmetic.  Seeded
+ * synthetic weights as infernt_engine_create_seeded; hidden, heads x
+ * head_dim, intermediate and vocabulary multiples of 128, head_dim 64 or
+ * 128, query groups up to 16, 1 <= batch <= 256.  attn_splits: KV splits per
+ * (sequence, KV head) of the attention, 0 for automatic. */
+typedef struct infernt_batch_engine infernt_batch_engine;
+INFERNT_API int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch,
+                                                   uint64_t seed, float std_dev, int attn_splits,
+                                                   infernt_batch_engine** out);
+INFERNT_API int infernt_batch_engine_destroy(infernt_batch_engine* e);
+/* Rows [0, n_pos) of sequence seq's KV caches from the seeded KV streams
+ * (the values infernt_fill_kv writes), rounded to bf16. */
+INFERNT_API int infernt_batch_engine_fill_kv(infernt_batch_engine* e, int seq, uint64_t seed, int n_pos,
+                                             float std_dev);
+/* One step: tokens[t] at positions[t] for every sequence; next_tokens[t]
+ * the greedy tokens (host arrays of `batch` ints; synchronous). */
+INFERNT_API int infernt_batch_engine_step(infernt_batch_engine* e, const int* tokens,
+                                          const int* positions, int* next_tokens);
+/* `steps` chained steps on the device from (tokens, positions); tokens_out
+ * [steps][batch] (or NULL); *ms the device time of the steps (or NULL). */
+INFERNT_API int infernt_batch_engine_decode(infernt_batch_engine* e, const int* tokens,
+                                            const int* positions, int steps, int* tokens_out,
+                                            float* ms);
+/* The last step's logits [batch][vocab] (n = batch x vocab floats). */
+INFERNT_API int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, size_t n);
+/* K splits of the Q|K|V, O, gate|up, down and LM-head projections and the
+ * attention's KV splits (6 ints). */
+INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);
+
 /* ----------------------------------------- tensor parallelism ---
  * The 8B-class configuration decoded by tp_size GPUs, one process per GPU
  * (the reference has a single-GPU engine only; this extends

@@ -133,6 +133,13 @@ _SIGS = {
     "infernt_lm_head_workspace_bytes": (_S, []),
     "infernt_rmsnorm_lm_head_argmax": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _F, _P, _P]),
     "infernt_bgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
+    "infernt_batch_engine_create_seeded": (_I, [ctypes.POINTER(LlamaConfig), _I, _U64, _F, _I, ctypes.POINTER(_P)]),
+    "infernt_batch_engine_destroy": (_I, [_P]),
+    "infernt_batch_engine_fill_kv": (_I, [_P, _I, _U64, _I, _F]),
+    "infernt_batch_engine_step": (_I, [_P, _P, _P, _P]),
+    "infernt_batch_engine_decode": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_F)]),
+    "infernt_batch_engine_logits": (_I, [_P, _P, _S]),
+    "infernt_batch_engine_splits": (_I, [_P, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),
     "infernt_plan_destroy": (_I, [_P]),
@@ -316,6 +323,62 @@ class Engine:
         v = (ctypes.c_void_p * n)()
         call("infernt_engine_kv_ptrs", self._h, k, v, n)
         return [k[i] for i in range(n)], [v[i] for i in range(n)]
+
+
+class BatchEngine:
+    """T sequences decoding together on the tensor cores
+    (infernt_batch_engine_*): seeded bf16 weights, bf16 KV caches."""
+
+    def __init__(self, cfg: ModelConfig, batch: int, seed: int = 0, std: float = 0.02, attn_splits: int = 0):
+        self.cfg = cfg
+        self.T = batch
+        self._c = cfg.c()
+        h = ctypes.c_void_p()
+        call("infernt_batch_engine_create_seeded", ctypes.byref(self._c), batch, seed, std, attn_splits,
+             ctypes.byref(h))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().infernt_batch_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def fill_kv(self, seq: int, seed: int, n_pos: int, std: float = 1.0):
+        call("infernt_batch_engine_fill_kv", self._h, seq, seed, n_pos, std)
+
+    def _ints(self, xs):
+        arr = (ctypes.c_int * self.T)(*[int(x) for x in xs])
+        return arr
+
+    def step(self, tokens, positions):
+        out = (ctypes.c_int * self.T)()
+        call("infernt_batch_engine_step", self._h, self._ints(tokens), self._ints(positions), out)
+        return list(out)
+
+    def decode(self, tokens, positions, steps: int):
+        import numpy as np
+        out = np.zeros(steps * self.T, dtype=np.int32)
+        ms = ctypes.c_float()
+        call("infernt_batch_engine_decode", self._h, self._ints(tokens), self._ints(positions), steps,
+             out.ctypes.data, ctypes.byref(ms))
+        return out.reshape(steps, self.T), ms.value
+
+    def logits(self):
+        import numpy as np
+        out = np.empty((self.T, self.cfg.vocab_size), dtype=np.float32)
+        call("infernt_batch_engine_logits", self._h, out.ctypes.data, out.size)
+        return out
+
+    def splits(self):
+        out = (ctypes.c_int * 6)()
+        call("infernt_batch_engine_splits", self._h, out)
+        return list(out)
 
 
 class TPEngine:

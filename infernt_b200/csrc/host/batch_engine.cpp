@@ -1,0 +1,408 @@
+// batch_engine.cpp — batched decode of T sequences with seeded synthetic
+// weights (infernt_batch_engine_* in include/infernt_capi.h): bf16
+// projection weights (the Q|K|V and gate|up matrices stacked so each is one
+// tensor-core projection), FP32 embedding and norms, per-sequence bf16 KV
+// caches [T][N_kv][max_seq][D] per layer.  A step is a fixed sequence of
+// launches (bgemm.cu, batch.cu) captured once into a CUDA graph and
+// replayed; tokens and positions live on the device and the argmax kernel
+// advances them, so chained steps need no host round trip.  Every
+// allocation happens at creation.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../../include/infernt_capi.h"
+#include "../../../include/infernt_seed.h"
+#include "../internal.h"
+
+namespace infernt {
+int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part, int splits, unsigned* err,
+                 cudaStream_t st);
+int bt_rope_table_launch(float2* tab, int max_seq, int D, float theta, cudaStream_t st);
+int bt_embed_norm_launch(const float* emb, const int* tokens, int vocab, int T, int H, const float* norm_w, float eps,
+                         float* h, uint16_t* xb, unsigned* err, cudaStream_t st);
+int bt_resid_norm_launch(const float* part, int splits, int T, int H, float* h, const float* norm_w, float eps,
+                         uint16_t* xb, cudaStream_t st);
+int bt_qkv_finish_launch(const float* part, int splits, int T, int nq, int nkv, int D, const int* positions,
+                         const float2* rope, int max_seq, float* q, uint16_t* kc, uint16_t* vc, unsigned* err,
+                         cudaStream_t st);
+int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act, cudaStream_t st);
+int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
+                        int nkv, int D, int max_seq, int S, float* part, uint16_t* attn, cudaStream_t st);
+int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
+                      float std_dev, cudaStream_t st);
+int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st);
+}  // namespace infernt
+
+struct infernt_batch_engine {
+    infernt_llama_config cfg;
+    int T = 0, S = 1;  // sequences, attention splits
+    // weights
+    const float* emb = nullptr;
+    const float* final_norm = nullptr;
+    const void* lm = nullptr;
+    struct Layer {
+        const float *attn_norm, *ffn_norm;
+        const void *qkv, *o, *gu, *down;
+    };
+    std::vector<Layer> layers;
+    std::vector<uint16_t*> kc, vc;
+    // splits of the projections
+    int sp_qkv = 1, sp_o = 1, sp_gu = 1, sp_down = 1, sp_lm = 1;
+    // state and scratch
+    int* tokens = nullptr;
+    int* positions = nullptr;
+    unsigned* err = nullptr;
+    float* h = nullptr;
+    uint16_t* xb = nullptr;
+    uint16_t* attn = nullptr;
+    uint16_t* act = nullptr;
+    float* q = nullptr;
+    float* part = nullptr;
+    float* apart = nullptr;
+    float2* rope = nullptr;
+    std::vector<void*> bufs;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    int* hist = nullptr;  // tokens of chained steps (grown on demand)
+    size_t hist_cap = 0;
+
+    ~infernt_batch_engine() {
+        if (graph) cudaGraphExecDestroy(graph);
+        cudaFree(hist);
+        if (ev[0]) cudaEventDestroy(ev[0]);
+        if (ev[1]) cudaEventDestroy(ev[1]);
+        for (void* b : bufs) cudaFree(b);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+using infernt::fail;
+
+int alloc(infernt_batch_engine* e, size_t bytes, void** out) {
+    void* p = nullptr;
+    INFERNT_CUDA_TRY(cudaMalloc(&p, bytes));
+    e->bufs.push_back(p);
+    *out = p;
+    return INFERNT_OK;
+}
+
+// splits so that tiles x splits fills the GPU's SMs about once
+int pick_splits(int N, int K) {
+    const int tiles = N / 128, nk = K / 64;
+    int s = (infernt::sm_count() + tiles - 1) / tiles;
+    if (s > nk) s = nk;
+    return s < 1 ? 1 : s;
+}
+
+int fill_bf16(infernt_batch_engine* e, void* dst, size_t n, uint64_t seed, uint64_t stream_id, float std_dev) {
+    return infernt_fill_normal(dst, n, INFERNT_DTYPE_BF16, seed, stream_id, std_dev, e->stream);
+}
+
+int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
+    const infernt_llama_config& c = e->cfg;
+    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
+    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, T = e->T;
+    const int qs = nq * D, kvs = nkv * D, nqkv = qs + 2 * kvs;
+    INFERNT_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    void* p = nullptr;
+    // embedding (FP32) and norms
+    if (int s = alloc(e, sizeof(float) * (size_t)V * H, &p)) return s;
+    if (int s = infernt_fill_normal(p, (size_t)V * H, INFERNT_DTYPE_F32, seed, INFERNT_STREAM_EMBEDDING, std_dev,
+                                    e->stream))
+        return s;
+    e->emb = static_cast<const float*>(p);
+    float* ones = nullptr;
+    if (int s = alloc(e, sizeof(float) * H, reinterpret_cast<void**>(&ones))) return s;
+    if (int s = infernt_fill_const(ones, H, 1.0f, e->stream)) return s;
+    e->final_norm = ones;  // every norm weight is 1.0 in the seeded model
+    if (int s = alloc(e, (size_t)V * H * 2, &p)) return s;
+    if (int s = fill_bf16(e, p, (size_t)V * H, seed, INFERNT_STREAM_LM_HEAD, std_dev)) return s;
+    e->lm = p;
+    for (int l = 0; l < L; ++l) {
+        infernt_batch_engine::Layer ly;
+        ly.attn_norm = ones;
+        ly.ffn_norm = ones;
+        char* qkv = nullptr;
+        if (int s = alloc(e, (size_t)nqkv * H * 2, reinterpret_cast<void**>(&qkv))) return s;
+        if (int s = fill_bf16(e, qkv, (size_t)qs * H, seed, INFERNT_STREAM_LAYER(l, 0), std_dev)) return s;
+        if (int s = fill_bf16(e, qkv + (size_t)qs * H * 2, (size_t)kvs * H, seed, INFERNT_STREAM_LAYER(l, 1), std_dev))
+            return s;
+        if (int s = fill_bf16(e, qkv + (size_t)(qs + kvs) * H * 2, (size_t)kvs * H, seed, INFERNT_STREAM_LAYER(l, 2),
+                              std_dev))
+            return s;
+        ly.qkv = qkv;
+        if (int s = alloc(e, (size_t)H * qs * 2, &p)) return s;
+        if (int s = fill_bf16(e, p, (size_t)H * qs, seed, INFERNT_STREAM_LAYER(l, 3), std_dev)) return s;
+        ly.o = p;
+        char* gu = nullptr;
+        if (int s = alloc(e, (size_t)2 * I * H * 2, reinterpret_cast<void**>(&gu))) return s;
+        if (int s = fill_bf16(e, gu, (size_t)I * H, seed, INFERNT_STREAM_LAYER(l, 4), std_dev)) return s;
+        if (int s = fill_bf16(e, gu + (size_t)I * H * 2, (size_t)I * H, seed, INFERNT_STREAM_LAYER(l, 5), std_dev))
+            return s;
+        ly.gu = gu;
+        if (int s = alloc(e, (size_t)H * I * 2, &p)) return s;
+        if (int s = fill_bf16(e, p, (size_t)H * I, seed, INFERNT_STREAM_LAYER(l, 6), std_dev)) return s;
+        ly.down = p;
+        e->layers.push_back(ly);
+        const size_t cache = (size_t)T * nkv * c.max_seq_len * D * 2;
+        void* k = nullptr;
+        void* v = nullptr;
+        if (int s = alloc(e, cache, &k)) return s;
+        if (int s = alloc(e, cache, &v)) return s;
+        INFERNT_CUDA_TRY(cudaMemsetAsync(k, 0, cache, e->stream));
+        INFERNT_CUDA_TRY(cudaMemsetAsync(v, 0, cache, e->stream));
+        e->kc.push_back(static_cast<uint16_t*>(k));
+        e->vc.push_back(static_cast<uint16_t*>(v));
+    }
+    e->sp_qkv = pick_splits(nqkv, H);
+    e->sp_o = pick_splits(H, qs);
+    e->sp_gu = pick_splits(2 * I, H);
+    e->sp_down = pick_splits(H, I);
+    e->sp_lm = 1;  // the argmax reads whole logits
+    size_t part = 0;
+    auto need = [&](int sp, int N) {
+        const size_t b = (size_t)sp * T * N;
+        if (b > part) part = b;
+    };
+    need(e->sp_qkv, nqkv);
+    need(e->sp_o, H);
+    need(e->sp_gu, 2 * I);
+    need(e->sp_down, H);
+    need(e->sp_lm, V);
+    const int kmax = H > qs ? (H > I ? H : I) : (qs > I ? qs : I);
+    if (int s = alloc(e, sizeof(int) * T, reinterpret_cast<void**>(&e->tokens))) return s;
+    if (int s = alloc(e, sizeof(int) * T, reinterpret_cast<void**>(&e->positions))) return s;
+    if (int s = alloc(e, 256, reinterpret_cast<void**>(&e->err))) return s;
+    INFERNT_CUDA_TRY(cudaMemsetAsync(e->err, 0, 256, e->stream));
+    if (int s = alloc(e, sizeof(float) * (size_t)T * H, reinterpret_cast<void**>(&e->h))) return s;
+    if (int s = alloc(e, (size_t)T * kmax * 2, reinterpret_cast<void**>(&e->xb))) return s;
+    if (int s = alloc(e, (size_t)T * qs * 2, reinterpret_cast<void**>(&e->attn))) return s;
+    if (int s = alloc(e, (size_t)T * I * 2, reinterpret_cast<void**>(&e->act))) return s;
+    if (int s = alloc(e, sizeof(float) * (size_t)T * qs, reinterpret_cast<void**>(&e->q))) return s;
+    if (int s = alloc(e, sizeof(float) * part, reinterpret_cast<void**>(&e->part))) return s;
+    const int G = nq / nkv;
+    if (int s = alloc(e, sizeof(float) * (size_t)T * nkv * e->S * G * (D + 2), reinterpret_cast<void**>(&e->apart)))
+        return s;
+    if (int s = alloc(e, sizeof(float2) * (size_t)c.max_seq_len * (D / 2), reinterpret_cast<void**>(&e->rope)))
+        return s;
+    if (int s = infernt::bt_rope_table_launch(e->rope, c.max_seq_len, D, c.rope_theta, e->stream)) return s;
+    INFERNT_CUDA_TRY(cudaEventCreate(&e->ev[0]));
+    INFERNT_CUDA_TRY(cudaEventCreate(&e->ev[1]));
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return INFERNT_OK;
+}
+
+// One decode step of every sequence (launches only; the caller synchronises).
+int record_step(infernt_batch_engine* e, cudaStream_t st) {
+    const infernt_llama_config& c = e->cfg;
+    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
+    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, T = e->T;
+    const int qs = nq * D, nqkv = qs + 2 * nkv * D;
+    const float eps = c.rms_norm_eps;
+    using namespace infernt;
+    if (int s = bt_embed_norm_launch(e->emb, e->tokens, V, T, H, e->layers[0].attn_norm, eps, e->h, e->xb, e->err, st))
+        return s;
+    for (int l = 0; l < L; ++l) {
+        const auto& ly = e->layers[l];
+        if (int s = bgemm_launch(ly.qkv, nqkv, H, e->xb, T, e->part, e->sp_qkv, e->err, st)) return s;
+        if (int s = bt_qkv_finish_launch(e->part, e->sp_qkv, T, nq, nkv, D, e->positions, e->rope, c.max_seq_len, e->q,
+                                         e->kc[l], e->vc[l], e->err, st))
+            return s;
+        if (int s = bt_attention_launch(e->q, e->kc[l], e->vc[l], e->positions, T, nq, nkv, D, c.max_seq_len, e->S,
+                                        e->apart, e->attn, st))
+            return s;
+        if (int s = bgemm_launch(ly.o, H, qs, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
+        if (int s = bt_resid_norm_launch(e->part, e->sp_o, T, H, e->h, ly.ffn_norm, eps, e->xb, st)) return s;
+        if (int s = bgemm_launch(ly.gu, 2 * I, H, e->xb, T, e->part, e->sp_gu, e->err, st)) return s;
+        if (int s = bt_swiglu_launch(e->part, e->sp_gu, T, I, e->act, st)) return s;
+        if (int s = bgemm_launch(ly.down, H, I, e->act, T, e->part, e->sp_down, e->err, st)) return s;
+        const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
+        if (int s = bt_resid_norm_launch(e->part, e->sp_down, T, H, e->h, next_norm, eps, e->xb, st)) return s;
+    }
+    if (int s = bgemm_launch(e->lm, V, H, e->xb, T, e->part, e->sp_lm, e->err, st)) return s;
+    // the LM head runs unsplit: part[0] holds the logits
+    return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, st);
+}
+
+int ensure_graph(infernt_batch_engine* e) {
+    if (e->graph) return INFERNT_OK;
+    cudaStream_t cap = nullptr;
+    INFERNT_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    cudaError_t ce = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+    int s = ce == cudaSuccess ? record_step(e, cap) : INFERNT_ERR_CUDA;
+    cudaGraph_t g = nullptr;
+    const cudaError_t ee = cudaStreamEndCapture(cap, &g);
+    cudaStreamDestroy(cap);
+    if (ce != cudaSuccess) return infernt::cuda_fail(ce, "batch engine: stream capture");
+    if (s) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+    }
+    INFERNT_CUDA_TRY(ee);
+    const cudaError_t ie = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    INFERNT_CUDA_TRY(ie);
+    return INFERNT_OK;
+}
+
+int check_err(infernt_batch_engine* e) {
+    unsigned err = 0;
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(&err, e->err, sizeof(err), cudaMemcpyDeviceToHost, e->stream));
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if (err) {
+        cudaMemsetAsync(e->err, 0, sizeof(unsigned), e->stream);
+        cudaStreamSynchronize(e->stream);
+        return fail(INFERNT_ERR_DEVICE, "batched decode reported error word 0x%x (1: wait timeout, 2: position, "
+                                        "4: token id)", err);
+    }
+    return INFERNT_OK;
+}
+
+int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions) {
+    for (int t = 0; t < e->T; ++t) {
+        INFERNT_REQUIRE(tokens[t] >= 0 && tokens[t] < e->cfg.vocab_size, "batch engine: token %d of sequence %d",
+                        tokens[t], t);
+        INFERNT_REQUIRE(positions[t] >= 0 && positions[t] < e->cfg.max_seq_len,
+                        "batch engine: position %d of sequence %d outside [0, %d)", positions[t], t,
+                        e->cfg.max_seq_len);
+    }
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(e->tokens, tokens, sizeof(int) * e->T, cudaMemcpyHostToDevice, e->stream));
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(e->positions, positions, sizeof(int) * e->T, cudaMemcpyHostToDevice, e->stream));
+    return INFERNT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
+                                       int attn_splits, infernt_batch_engine** out) {
+    INFERNT_REQUIRE(cfg && out, "batch_engine_create_seeded: null argument");
+    *out = nullptr;
+    INFERNT_REQUIRE(cfg->weight_dtype == INFERNT_DTYPE_BF16, "batch engine: bf16 weights only");
+    INFERNT_REQUIRE(batch >= 1 && batch <= 256, "batch engine: batch %d outside [1, 256]", batch);
+    const int D = cfg->head_dim;
+    INFERNT_REQUIRE(D == 64 || D == 128, "batch engine: head_dim %d (64 or 128)", D);
+    INFERNT_REQUIRE(cfg->num_attention_heads % cfg->num_key_value_heads == 0 &&
+                        cfg->num_attention_heads / cfg->num_key_value_heads <= 16,
+                    "batch engine: query group size above 16");
+    const int qs = cfg->num_attention_heads * D, kvs = cfg->num_key_value_heads * D;
+    INFERNT_REQUIRE(cfg->hidden_size % 128 == 0 && qs % 128 == 0 && (qs + 2 * kvs) % 128 == 0 &&
+                        cfg->intermediate_size % 128 == 0 && cfg->vocab_size % 128 == 0,
+                    "batch engine: hidden, heads x head_dim, Q|K|V rows, intermediate and vocabulary must be "
+                    "multiples of 128");
+    INFERNT_REQUIRE(cfg->max_seq_len <= (1 << 20), "batch engine: max_seq_len above 2^20");
+    infernt_batch_engine* e = new (std::nothrow) infernt_batch_engine();
+    INFERNT_REQUIRE(e, "batch_engine_create_seeded: host allocation failed");
+    e->cfg = *cfg;
+    e->T = batch;
+    int S = attn_splits;
+    if (S <= 0) {
+        const int pairs = batch * cfg->num_key_value_heads;
+        S = (4 * infernt::sm_count() + pairs - 1) / pairs;
+        if (S > 64) S = 64;
+    }
+    e->S = S < 1 ? 1 : S;
+    int s = build(e, seed, std_dev);
+    if (s) {
+        delete e;
+        return s;
+    }
+    *out = e;
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_destroy(infernt_batch_engine* e) {
+    delete e;
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_fill_kv(infernt_batch_engine* e, int seq, uint64_t seed, int n_pos, float std_dev) {
+    INFERNT_REQUIRE(e && seq >= 0 && seq < e->T && n_pos >= 0 && n_pos <= e->cfg.max_seq_len,
+                    "batch_engine_fill_kv: bad arguments");
+    const uint64_t kk = infernt_stream_key(seed, INFERNT_STREAM_KV_K), vk = infernt_stream_key(seed, INFERNT_STREAM_KV_V);
+    for (int l = 0; l < e->cfg.num_layers; ++l) {
+        if (int s = infernt::bt_fill_kv_launch(e->kc[l], seq, l, e->cfg.num_key_value_heads, e->cfg.max_seq_len,
+                                               e->cfg.head_dim, n_pos, kk, std_dev, e->stream))
+            return s;
+        if (int s = infernt::bt_fill_kv_launch(e->vc[l], seq, l, e->cfg.num_key_value_heads, e->cfg.max_seq_len,
+                                               e->cfg.head_dim, n_pos, vk, std_dev, e->stream))
+            return s;
+    }
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_step(infernt_batch_engine* e, const int* tokens, const int* positions, int* next_tokens) {
+    INFERNT_REQUIRE(e && tokens && positions && next_tokens, "batch_engine_step: null argument");
+    if (int s = set_inputs(e, tokens, positions)) return s;
+    if (int s = ensure_graph(e)) return s;
+    INFERNT_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(next_tokens, e->tokens, sizeof(int) * e->T, cudaMemcpyDeviceToHost, e->stream));
+    return check_err(e);
+}
+
+int infernt_batch_engine_decode(infernt_batch_engine* e, const int* tokens, const int* positions, int steps,
+                                int* tokens_out, float* ms) {
+    INFERNT_REQUIRE(e && tokens && positions && steps > 0, "batch_engine_decode: bad arguments");
+    for (int t = 0; t < e->T; ++t)
+        INFERNT_REQUIRE((long long)positions[t] + steps <= e->cfg.max_seq_len,
+                        "batch_engine_decode: sequence %d would pass max_seq_len", t);
+    if (int s = set_inputs(e, tokens, positions)) return s;
+    if (int s = ensure_graph(e)) return s;
+    int* hist = nullptr;
+    if (tokens_out) {
+        const size_t n = (size_t)steps * e->T;
+        if (n > e->hist_cap) {
+            cudaFree(e->hist);
+            e->hist = nullptr;
+            e->hist_cap = 0;
+            INFERNT_CUDA_TRY(cudaMalloc(&e->hist, sizeof(int) * n));
+            e->hist_cap = n;
+        }
+        hist = e->hist;
+    }
+    INFERNT_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
+    for (int s = 0; s < steps; ++s) {
+        INFERNT_CUDA_TRY(cudaGraphLaunch(e->graph, e->stream));
+        if (hist)
+            INFERNT_CUDA_TRY(cudaMemcpyAsync(hist + (size_t)s * e->T, e->tokens, sizeof(int) * e->T,
+                                             cudaMemcpyDeviceToDevice, e->stream));
+    }
+    INFERNT_CUDA_TRY(cudaEventRecord(e->ev[1], e->stream));
+    if (hist)
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(tokens_out, hist, sizeof(int) * (size_t)steps * e->T, cudaMemcpyDeviceToHost,
+                                         e->stream));
+    const int s = check_err(e);
+    if (ms) cudaEventElapsedTime(ms, e->ev[0], e->ev[1]);
+    return s;
+}
+
+int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, size_t n) {
+    INFERNT_REQUIRE(e && logits_host && n == (size_t)e->T * e->cfg.vocab_size,
+                    "batch_engine_logits: need %d x %d floats", e ? e->T : 0, e ? e->cfg.vocab_size : 0);
+    INFERNT_REQUIRE(e->sp_lm == 1, "batch_engine_logits: the LM head runs split; logits are partial sums");
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    INFERNT_CUDA_TRY(cudaMemcpy(logits_host, e->part, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_splits(infernt_batch_engine* e, int* out) {
+    INFERNT_REQUIRE(e && out, "batch_engine_splits: null argument");
+    out[0] = e->sp_qkv;
+    out[1] = e->sp_o;
+    out[2] = e->sp_gu;
+    out[3] = e->sp_down;
+    out[4] = e->sp_lm;
+    out[5] = e->S;
+    return INFERNT_OK;
+}
+
+}  // extern "C"

@@ -60,6 +60,7 @@ def olib():
             build(ref=False)
         l = ctypes.CDLL(ORACLE_SO)
         l.oracle_set_threads.argtypes = [_I]
+        l.oracle_set_act_bf16.argtypes = [_I]
         l.oracle_fill_normal.argtypes = [_P, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, _F, _I]
         l.oracle_fill_normal_range.argtypes = [_P, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64,
                                                _F, _I, ctypes.c_uint64]
@@ -208,6 +209,16 @@ def gemm(A, B, M, N, K, alpha=1.0, beta=0.0, trans_a=0, trans_b=0, C=None):
     return C
 
 
+def round_bf16(a):
+    """Round FP32 values to the nearest bf16 value, ties to even (the same
+    arithmetic as infernt_round_bf16 in include/infernt_seed.h)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+    special = (a.view(np.uint32) & 0x7F800000) == 0x7F800000
+    return np.where(special, a, r).astype(np.float32)
+
+
 class LlamaOracle:
     """Seeded model + KV cache on the host; decode steps through oracle.c.
 
@@ -216,8 +227,11 @@ class LlamaOracle:
     projection matrices and lm_head to bf16 values (the bf16 variant's
     oracle)."""
 
-    def __init__(self, cfg, seed=0, std=0.02, round_bf16=False, layers=None):
+    def __init__(self, cfg, seed=0, std=0.02, round_bf16=False, layers=None, act_bf16=False):
         self.cfg = cfg
+        # the batched-decode variant: bf16 activations into the projections
+        # and bf16 KV rows (oracle_set_act_bf16)
+        self.act_bf16 = bool(act_bf16)
         c = cfg
         self.L = c.num_layers if layers is None else layers
         H, I, D = c.hidden_size, c.intermediate_size, c.head_dim
@@ -263,11 +277,12 @@ class LlamaOracle:
             for l in range(self.L):
                 for h in range(nkv):
                     base = ((l * nkv + h) << 20) * D
-                    view[l, h, :n_pos, :] = fill_normal_range(n_pos * D, seed, stream, std,
-                                                              base).reshape(n_pos, D)
+                    rows = fill_normal_range(n_pos * D, seed, stream, std, base).reshape(n_pos, D)
+                    view[l, h, :n_pos, :] = round_bf16(rows) if self.act_bf16 else rows
 
     def decode_token(self, token, position):
         logits = np.empty(self.cfg.vocab_size, dtype=np.float32)
+        olib().oracle_set_act_bf16(int(self.act_bf16))
         nxt = olib().oracle_decode_token(ctypes.byref(self._c), self._ptrs, _p(self.kv_k),
                                          _p(self.kv_v), token, position, _p(logits))
         return nxt, logits

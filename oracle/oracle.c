@@ -15,6 +15,17 @@
 static int g_threads = 1;
 
 void oracle_set_threads(int n) { g_threads = n < 1 ? 1 : (n > 256 ? 256 : n); }
+
+/* Batched-decode variant (infernt_batch_engine_*): activations rounded to
+ * bf16 where they enter a projection (normed inputs, attention output,
+ * SiLU*up) and K/V rows rounded to bf16 before they enter the cache. */
+static int g_act_bf16 = 0;
+void oracle_set_act_bf16(int on) { g_act_bf16 = on != 0; }
+
+static void round_vec(float* x, int n) {
+    if (!g_act_bf16) return;
+    for (int i = 0; i < n; ++i) x[i] = infernt_round_bf16(x[i]);
+}
 int oracle_get_threads(void) { return g_threads; }
 
 /* ------------------------------------------------------------------ */
@@ -352,11 +363,14 @@ static void layer_forward(const oracle_config* c, const float* const* lw,
     int H = c->hidden_size, D = c->head_dim, I = c->intermediate_size;
     int qs = c->num_attention_heads * D, ks = c->num_key_value_heads * D;
     oracle_rmsnorm(s->xn, h, lw[0], 1, H, c->rms_norm_eps);
+    round_vec(s->xn, H);
     gemv(lw[1], s->xn, s->q, qs, H);
     gemv(lw[2], s->xn, s->k, ks, H);
     gemv(lw[3], s->xn, s->v, ks, H);
     oracle_rope(s->q, s->k, 1, c->num_attention_heads, c->num_key_value_heads, D,
                 position, c->rope_theta);
+    round_vec(s->k, ks);
+    round_vec(s->v, ks);
     oracle_kv_cache_append(kv_k, kv_v, s->k, s->v, c->num_key_value_heads, D,
                            c->max_seq_len, position);
     int seq_len = position + 1;
@@ -366,12 +380,15 @@ static void layer_forward(const oracle_config* c, const float* const* lw,
     oracle_softmax(s->scores, s->scores, c->num_attention_heads, seq_len);
     oracle_attention_values(s->attn, s->scores, kv_v, c->num_attention_heads,
                             c->num_key_value_heads, D, seq_len, c->max_seq_len);
+    round_vec(s->attn, qs);
     gemv(lw[4], s->attn, s->o, H, qs);
     oracle_residual_add(h, h, s->o, H);
     oracle_rmsnorm(s->xn, h, lw[5], 1, H, c->rms_norm_eps);
+    round_vec(s->xn, H);
     gemv(lw[6], s->xn, s->gate, I, H);
     gemv(lw[7], s->xn, s->up, I, H);
     oracle_silu_mul(s->act, s->gate, s->up, I);
+    round_vec(s->act, I);
     gemv(lw[8], s->act, s->mlp, H, I);
     oracle_residual_add(h, h, s->mlp, H);
 }
@@ -402,6 +419,7 @@ void oracle_llama_forward(const oracle_config* c, const float* const* w,
     float* xn = malloc(sizeof(float) * c->hidden_size);
     oracle_llama_layers(c, w, kv_k, kv_v, position, input_embedding, c->num_layers, h);
     oracle_rmsnorm(xn, h, w[1], 1, c->hidden_size, c->rms_norm_eps);
+    round_vec(xn, c->hidden_size);
     gemv(w[2], xn, logits, c->vocab_size, c->hidden_size);
     free(h);
     free(xn);

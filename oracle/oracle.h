@@ -42,6 +42,9 @@ typedef struct {
 
 /* Worker threads used by the matrix-vector products (default 1). */
 void oracle_set_threads(int n);
+/* Batched-decode variant: round activations to bf16 where they enter a
+ * projection, and K/V rows before they enter the cache (default off). */
+void oracle_set_act_bf16(int on);
 int oracle_get_threads(void);
 
 /* ---- synthetic inputs (same values as the device initialiser) ---- */

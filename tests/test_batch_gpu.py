@@ -1,0 +1,88 @@
+"""Batched decode on the tensor cores (infernt_batch_engine_*) against the
+CPU oracle, sequence by sequence.
+
+The oracle runs the same seeded model with bf16-rounded weights in its
+batched-decode variant (act_bf16: activations rounded to bf16 where they
+enter a projection, K/V rows rounded to bf16), so both sides round the same
+quantities; they still differ in accumulation order (FP32 tensor-core sums
+over K splits against double sums), which can move a bf16 rounding by one
+step.  Tolerance: logits max-abs error <= 2e-3 of the largest |logit| +
+1e-4; greedy tokens identical unless the oracle's top-2 gap is below 1e-3."""
+import numpy as np
+import pytest
+
+import infernt_b200 as ib
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CFG = ib.ModelConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_attention_heads=8,
+                     num_key_value_heads=2, intermediate_size=1024, max_seq_len=256, rms_norm_eps=1e-5,
+                     rope_theta=10000.0, weight_dtype=ib.DTYPE_BF16)
+CFG_D128 = CFG.with_(hidden_size=1024, num_attention_heads=8, num_key_value_heads=4, head_dim=128,
+                     intermediate_size=1536, num_layers=1)
+
+
+def top2_gap(x):
+    s = np.sort(x)
+    return float(s[-1] - s[-2])
+
+
+def check_batch(cfg, n_pos, steps=3, seed=5, attn_splits=0):
+    T = len(n_pos)
+    eng = ib.BatchEngine(cfg, T, seed=seed, attn_splits=attn_splits)
+    orcs = []
+    for b, p in enumerate(n_pos):
+        eng.fill_kv(b, 100 + b, p)
+        o = O.LlamaOracle(cfg, seed=seed, round_bf16=True, act_bf16=True)
+        o.fill_kv(100 + b, p)
+        orcs.append(o)
+    tokens = [int(t) for t in O.prompt(T, seed, 3, cfg.vocab_size)]
+    positions = list(n_pos)
+    for step in range(steps):
+        nxt = eng.step(tokens, positions)
+        logits = eng.logits()
+        for b in range(T):
+            want_tok, want = orcs[b].decode_token(tokens[b], positions[b])
+            err = float(np.abs(logits[b] - want).max())
+            scale = float(np.abs(want).max())
+            assert err <= 2e-3 * scale + 1e-4, (step, b, err, scale)
+            if nxt[b] != want_tok:
+                assert top2_gap(want) < 1e-3, (step, b, nxt[b], want_tok)
+        tokens = nxt
+        positions = [p + 1 for p in positions]
+    eng.close()
+
+
+def test_batch_matches_oracle_mixed_contexts():
+    """Five sequences at contexts 0..130 (one or three attention splits)."""
+    check_batch(CFG, [0, 3, 40, 65, 130])
+
+
+def test_batch_single_split_and_many_splits():
+    check_batch(CFG, [7, 100], attn_splits=1)
+    check_batch(CFG, [7, 100], attn_splits=16)
+
+
+def test_batch_head_dim_128():
+    check_batch(CFG_D128, [2, 70, 129])
+
+
+def test_batch_decode_chain_equals_steps():
+    T = 4
+    eng = ib.BatchEngine(CFG, T, seed=9)
+    for b in range(T):
+        eng.fill_kv(b, 200 + b, 10 * b)
+    tokens = [5, 6, 7, 8]
+    positions = [0, 10, 20, 30]
+    chain, _ = eng.decode(tokens, positions, 4)
+    eng.close()
+    eng = ib.BatchEngine(CFG, T, seed=9)
+    for b in range(T):
+        eng.fill_kv(b, 200 + b, 10 * b)
+    toks, pos = list(tokens), list(positions)
+    for s in range(4):
+        toks = eng.step(toks, pos)
+        pos = [p + 1 for p in pos]
+        assert list(chain[s]) == toks, s
+    eng.close()
