@@ -33,18 +33,36 @@ __device__ __forceinline__ uint16_t bf16_bits(float v) {
 }
 __device__ __forceinline__ float bf16_float(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
-// sum over the splits of part[s][t][j] (in split order)
-__device__ __forceinline__ float sum_parts(const float* part, int splits, size_t stride, size_t off) {
-    float v = part[off];
-    for (int s = 1; s < splits; ++s) v += part[(size_t)s * stride + off];
+constexpr int kMaxSplits = 16;  // K splits of a batched projection (bgemm partials)
+
+// Sum over the splits of part[s][t][off .. off + 3] (in split order): every
+// split's 16 bytes are loaded first, so a thread waits one round trip, not
+// one per split.
+__device__ __forceinline__ float4 sum_parts4(const float* part, int splits, size_t stride, size_t off) {
+    float4 w[kMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s)
+        if (s < splits) w[s] = *reinterpret_cast<const float4*>(part + (size_t)s * stride + off);
+    float4 v = w[0];
+#pragma unroll
+    for (int s = 1; s < kMaxSplits; ++s)
+        if (s < splits) {
+            v.x += w[s].x;
+            v.y += w[s].y;
+            v.z += w[s].z;
+            v.w += w[s].w;
+        }
     return v;
 }
 
-// RMSNorm of the row x[0, H) (cuda/rmsnorm.cu:10-26) into bf16 xb; block-wide.
-__device__ void norm_row_bf16(const float* x, const float* w, int H, float eps, uint16_t* xb, float* red) {
+// RMSNorm (cuda/rmsnorm.cu:10-26) of a row of H = 4 x blockDim.x values,
+// thread i holding elements [4 i, 4 i + 4) in v, into bf16 xb.
+__device__ void norm_row_bf16(float4 v, const float* w, int H, float eps, uint16_t* xb, float* red) {
     const int tid = threadIdx.x, nt = blockDim.x;
-    float ss = 0.0f;
-    for (int i = tid; i < H; i += nt) ss = fmaf(x[i], x[i], ss);
+    float ss = v.x * v.x;
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
@@ -55,12 +73,17 @@ __device__ void norm_row_bf16(const float* x, const float* w, int H, float eps, 
     }
     __syncthreads();
     const float rms = red[32];
-    for (int i = tid; i < H; i += nt) xb[i] = bf16_bits(x[i] * rms * w[i]);
+    const float4 g = *reinterpret_cast<const float4*>(w + 4 * tid);
+    const uint32_t lo = (uint32_t)bf16_bits(v.x * rms * g.x) | ((uint32_t)bf16_bits(v.y * rms * g.y) << 16);
+    const uint32_t hi = (uint32_t)bf16_bits(v.z * rms * g.z) | ((uint32_t)bf16_bits(v.w * rms * g.w) << 16);
+    *reinterpret_cast<uint2*>(xb + 4 * tid) = make_uint2(lo, hi);
 }
 
-// h[t] = embedding row of tokens[t]; xb[t] = bf16(RMSNorm(h[t])).
+// h[t] = embedding row of tokens[t]; xb[t] = bf16(RMSNorm(h[t])).  H / 4 threads.
 __global__ void bt_embed_norm(const float* emb, const int* tokens, int vocab, int H, const float* norm_w, float eps,
                               float* h, uint16_t* xb, unsigned* err) {
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
     __shared__ float red[33];
     const int t = blockIdx.x;
     int tok = tokens[t];
@@ -68,22 +91,27 @@ __global__ void bt_embed_norm(const float* emb, const int* tokens, int vocab, in
         if (threadIdx.x == 0) atomicOr(err, kErrToken);
         tok = 0;
     }
-    float* ht = h + (size_t)t * H;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ht[i] = emb[(size_t)tok * H + i];
-    __syncthreads();
-    norm_row_bf16(ht, norm_w, H, eps, xb + (size_t)t * H, red);
+    const float4 v = *reinterpret_cast<const float4*>(emb + (size_t)tok * H + 4 * threadIdx.x);
+    *reinterpret_cast<float4*>(h + (size_t)t * H + 4 * threadIdx.x) = v;
+    norm_row_bf16(v, norm_w, H, eps, xb + (size_t)t * H, red);
 }
 
-// h[t] += sum of the partials; xb[t] = bf16(RMSNorm(h[t], norm_w)).
+// h[t] += sum of the partials; xb[t] = bf16(RMSNorm(h[t], norm_w)).  H / 4 threads.
 __global__ void bt_resid_norm(const float* part, int splits, int T, int H, float* h, const float* norm_w, float eps,
                               uint16_t* xb) {
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
     __shared__ float red[33];
     const int t = blockIdx.x;
-    float* ht = h + (size_t)t * H;
-    const size_t stride = (size_t)T * H;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ht[i] += sum_parts(part, splits, stride, (size_t)t * H + i);
-    __syncthreads();
-    norm_row_bf16(ht, norm_w, H, eps, xb + (size_t)t * H, red);
+    float4* hp = reinterpret_cast<float4*>(h + (size_t)t * H + 4 * threadIdx.x);
+    const float4 y = sum_parts4(part, splits, (size_t)T * H, (size_t)t * H + 4 * threadIdx.x);
+    float4 v = *hp;
+    v.x += y.x;
+    v.y += y.y;
+    v.z += y.z;
+    v.w += y.w;
+    *hp = v;
+    norm_row_bf16(v, norm_w, H, eps, xb + (size_t)t * H, red);
 }
 
 // Q|K|V of token t: q rows RoPE'd into q (FP32), K (RoPE'd) and V rows
@@ -91,6 +119,8 @@ __global__ void bt_resid_norm(const float* part, int splits, int T, int H, float
 // (cuda/rope.cu:13-34, cuda/kv_cache.cu:4-14).  Cache [T][Nkv][max_seq][D].
 __global__ void bt_qkv_finish(const float* part, int splits, int T, int nq, int nkv, int D, const int* positions,
                               const float2* rope, int max_seq, float* q, uint16_t* kc, uint16_t* vc, unsigned* err) {
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
     const int t = blockIdx.x;
     const int N = (nq + 2 * nkv) * D, half = D / 2;
     const size_t stride = (size_t)T * N, row = (size_t)t * N;
@@ -100,43 +130,56 @@ __global__ void bt_qkv_finish(const float* part, int splits, int T, int nq, int 
         return;
     }
     const float2* rp = rope + (size_t)pos * half;
-    // q and k pairs (d, d + D/2) of every head
-    for (int i = threadIdx.x; i < (nq + nkv) * half; i += blockDim.x) {
-        const int hd = i / half, d = i % half;
+    // q and k: four pairs (d .. d + 3, d + D/2 .. d + D/2 + 3) per unit
+    const int qk_units = (nq + nkv) * (half / 4);
+    for (int u = threadIdx.x; u < qk_units; u += blockDim.x) {
+        const int hd = u / (half / 4), d = (u % (half / 4)) * 4;
         const size_t j = (size_t)hd * D + d;
-        float a = sum_parts(part, splits, stride, row + j), b = sum_parts(part, splits, stride, row + j + half);
-        rope_apply(a, b, rp[d]);
+        const float4 a4 = sum_parts4(part, splits, stride, row + j), b4 = sum_parts4(part, splits, stride, row + j + half);
+        float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rope_apply(a[e], b[e], rp[d + e]);
         if (hd < nq) {
-            q[(size_t)t * nq * D + j] = a;
-            q[(size_t)t * nq * D + j + half] = b;
+            float* qd = q + (size_t)t * nq * D + j;
+            *reinterpret_cast<float4*>(qd) = make_float4(a[0], a[1], a[2], a[3]);
+            *reinterpret_cast<float4*>(qd + half) = make_float4(b[0], b[1], b[2], b[3]);
         } else {
             const int kh = hd - nq;
             uint16_t* dst = kc + (((size_t)t * nkv + kh) * max_seq + pos) * D;
-            dst[d] = bf16_bits(a);
-            dst[d + half] = bf16_bits(b);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                dst[d + e] = bf16_bits(a[e]);
+                dst[d + half + e] = bf16_bits(b[e]);
+            }
         }
     }
-    for (int i = threadIdx.x; i < nkv * D; i += blockDim.x) {
-        const int kh = i / D, d = i % D;
-        const float v = sum_parts(part, splits, stride, row + (size_t)(nq + nkv) * D + i);
-        vc[(((size_t)t * nkv + kh) * max_seq + pos) * D + d] = bf16_bits(v);
+    for (int u = threadIdx.x; u < nkv * D / 4; u += blockDim.x) {
+        const int i = 4 * u, kh = i / D, d = i % D;
+        const float4 v = sum_parts4(part, splits, stride, row + (size_t)(nq + nkv) * D + i);
+        uint16_t* dst = vc + (((size_t)t * nkv + kh) * max_seq + pos) * D + d;
+        dst[0] = bf16_bits(v.x);
+        dst[1] = bf16_bits(v.y);
+        dst[2] = bf16_bits(v.z);
+        dst[3] = bf16_bits(v.w);
     }
 }
 
 // act[t][i] = bf16(silu(gate) * up) from the partials of the stacked
 // [gate; up] projection (cuda/activation.cu:7-9).
 __global__ void bt_swiglu(const float* part, int splits, int T, int I, uint16_t* act) {
-    const int t = blockIdx.x;
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
+    const int t = blockIdx.y;
     const size_t N = (size_t)2 * I, stride = (size_t)T * N, row = (size_t)t * N;
-    for (int i = threadIdx.x; i < I; i += blockDim.x) {
-        const float g = sum_parts(part, splits, stride, row + i);
-        const float u = sum_parts(part, splits, stride, row + I + i);
-        act[(size_t)t * I + i] = bf16_bits(silu_mul(g, u));
-    }
+    const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= I) return;
+    const float4 g = sum_parts4(part, splits, stride, row + i), u = sum_parts4(part, splits, stride, row + I + i);
+    const uint32_t lo = (uint32_t)bf16_bits(silu_mul(g.x, u.x)) | ((uint32_t)bf16_bits(silu_mul(g.y, u.y)) << 16);
+    const uint32_t hi = (uint32_t)bf16_bits(silu_mul(g.z, u.z)) | ((uint32_t)bf16_bits(silu_mul(g.w, u.w)) << 16);
+    *reinterpret_cast<uint2*>(act + (size_t)t * I + i) = make_uint2(lo, hi);
 }
 
 // Positions per attention tile and the chunk of a split.
-constexpr int kBtTile = 32;
 constexpr int kBtMinChunk = 64;
 
 __device__ __forceinline__ void bt_chunk(int seq, int splits, int& chunk, int& active) {
@@ -146,24 +189,25 @@ __device__ __forceinline__ void bt_chunk(int seq, int splits, int& chunk, int& a
 }
 
 // Partial attention of (sequence t, KV head kvh, split) over its positions
-// (cuda/attention.cu:9-22, :30-42 with online softmax): G query heads,
-// D = 32 DL.  Warp w takes heads w, w + 4, ...; in the score pass lane p
-// takes position p of a 32-position tile, in the value pass lane l takes
-// columns l, l + 32, ....  The next tile's bf16 rows are loaded into
-// registers while the current tile is used.  Partials [T][Nkv][S][G][D + 2].
-template <int DL, int HW>
+// (cuda/attention.cu:9-22, :30-42 with online softmax), G query heads,
+// D = 32 DL.  Each warp takes 32 positions at a time: in the score pass lane
+// p holds position p and scores it against all G heads (q in shared memory,
+// the key row read once, 16 dimensions at a time); after the per-head online
+// softmax update the value pass gives lane l the DL columns [DL l, DL l +
+// DL) of every head.  The four warps' (m, l, o) are merged in shared memory
+// in warp order into the split's partial [T][Nkv][S][G][D + 2].
+template <int DL, int G>
 __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uint16_t* kc, const uint16_t* vc,
                                                        const int* positions, int nq, int nkv, int max_seq, int S,
                                                        float scale, float* part) {
-    constexpr int D = 32 * DL, T = kBtTile, NW = 4;
-    constexpr int CPR = D / 8;                 // 16-byte chunks per row
-    constexpr int CH = (T * CPR + 127) / 128;  // chunks per thread per tile (K or V)
-    __shared__ float qs[16 * D];
-    __shared__ float kt[T][D + 1];
-    __shared__ float vt[T][D];
-    __shared__ float ps[16][T];
+    pdl_wait();
+    pdl_launch_dependents();
+    constexpr int D = 32 * DL, NW = 4;
+    __shared__ __align__(16) float qs[G * D];
+    __shared__ __align__(16) float ps[NW][32][G];     // probabilities of the warp's 32 positions
+    __shared__ float wm[NW][G], wl[NW][G];
+    __shared__ float wo[NW][G][D];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int G = nq / nkv;
     const int item = blockIdx.x;
     const int split = item % S, kvh = (item / S) % nkv, t = item / (S * nkv);
     const int seq = positions[t] + 1;
@@ -174,98 +218,135 @@ __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uin
     const uint16_t* kb = kc + ((size_t)t * nkv + kvh) * max_seq * D;
     const uint16_t* vb = vc + ((size_t)t * nkv + kvh) * max_seq * D;
     for (int i = tid; i < G * D; i += 128) qs[i] = q[((size_t)t * nq + (size_t)kvh * G) * D + i];
+    __syncthreads();
 
-    uint4 kr[CH], vr[CH];
-    auto load = [&](int p0, int n) {
+    float m_run[G], l_run[G], o_run[G][DL];
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-            const int e = tid + c * 128, r = e / CPR, cc = e % CPR;
-            if (e < T * CPR && r < n) {
-                kr[c] = *reinterpret_cast<const uint4*>(kb + (size_t)(p0 + r) * D + cc * 8);
-                vr[c] = *reinterpret_cast<const uint4*>(vb + (size_t)(p0 + r) * D + cc * 8);
-            }
-        }
-    };
-    float m_run[HW], l_run[HW], o_run[HW][DL];
+    for (int h = 0; h < G; ++h) {
+        m_run[h] = -INFINITY;
+        l_run[h] = 0.0f;
 #pragma unroll
-    for (int j = 0; j < HW; ++j) {
-        m_run[j] = -INFINITY;
-        l_run[j] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < DL; ++i) o_run[j][i] = 0.0f;
+        for (int i = 0; i < DL; ++i) o_run[h][i] = 0.0f;
     }
-    int tl = min(T, c1 - c0);
-    load(c0, tl);
-    for (int p0 = c0; p0 < c1; p0 += T) {
-        __syncthreads();  // the previous tile's readers are done
+    for (int p0 = c0 + warp * 32; p0 < c1; p0 += NW * 32) {
+        const int n = min(32, c1 - p0);
+        const int p = p0 + lane;
+        // scores of position p against every head
+        float sc[G];
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-            const int e = tid + c * 128, r = e / CPR, cc = e % CPR;
-            if (e < T * CPR && r < tl) {
-                const uint16_t* kk = reinterpret_cast<const uint16_t*>(&kr[c]);
-                const uint16_t* vv = reinterpret_cast<const uint16_t*>(&vr[c]);
+        for (int h = 0; h < G; ++h) sc[h] = 0.0f;
+        if (lane < n) {
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)p * D);
 #pragma unroll
-                for (int x = 0; x < 8; ++x) {
-                    kt[r][cc * 8 + x] = bf16_float(kk[x]);
-                    vt[r][cc * 8 + x] = bf16_float(vv[x]);
+            for (int c = 0; c < D / 16; ++c) {
+                const uint4 k0 = kr[2 * c], k1 = kr[2 * c + 1];
+                const uint32_t kw[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                float kf[16];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    kf[2 * e] = __uint_as_float(kw[e] << 16);
+                    kf[2 * e + 1] = __uint_as_float(kw[e] & 0xffff0000u);
                 }
-            }
-        }
-        __syncthreads();
-        const int cur = tl;
-        const int nxt = p0 + T;
-        if (nxt < c1) {
-            tl = min(T, c1 - nxt);
-            load(nxt, tl);
-        }
 #pragma unroll
-        for (int j = 0; j < HW; ++j) {
-            const int h = warp + j * NW;
-            if (h < G) {
-                float s = -INFINITY;
-                if (lane < cur) {
-                    float d0 = 0.0f, d1 = 0.0f;
-                    const float* qh = qs + h * D;
-#pragma unroll 8
-                    for (int d = 0; d < D; d += 2) {
-                        d0 = fmaf(qh[d], kt[lane][d], d0);
-                        d1 = fmaf(qh[d + 1], kt[lane][d + 1], d1);
+                for (int h = 0; h < G; ++h) {
+                    const float4* qh = reinterpret_cast<const float4*>(qs + h * D + 16 * c);
+                    float acc = sc[h];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float4 qq = qh[e];
+                        acc = fmaf(qq.x, kf[4 * e], acc);
+                        acc = fmaf(qq.y, kf[4 * e + 1], acc);
+                        acc = fmaf(qq.z, kf[4 * e + 2], acc);
+                        acc = fmaf(qq.w, kf[4 * e + 3], acc);
                     }
-                    s = (d0 + d1) * scale;
+                    sc[h] = acc;
                 }
-                const float m_new = fmaxf(m_run[j], warp_max(s));
-                const float alpha = expf(m_run[j] - m_new);
-                const float pe = lane < cur ? expf(s - m_new) : 0.0f;
-                ps[h][lane] = pe;
-                l_run[j] = l_run[j] * alpha + warp_sum(pe);
-                m_run[j] = m_new;
-                __syncwarp();
-                float acc[DL];
-#pragma unroll
-                for (int i = 0; i < DL; ++i) acc[i] = o_run[j][i] * alpha;
-#pragma unroll 4
-                for (int p = 0; p < cur; ++p) {
-                    const float pp = ps[h][p];
-#pragma unroll
-                    for (int i = 0; i < DL; ++i) acc[i] = fmaf(pp, vt[p][lane + 32 * i], acc[i]);
-                }
-#pragma unroll
-                for (int i = 0; i < DL; ++i) o_run[j][i] = acc[i];
             }
+        }
+        // online softmax per head over the warp's positions
+        float alpha[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            const float s = lane < n ? sc[h] * scale : -INFINITY;
+            const float m_new = fmaxf(m_run[h], warp_max(s));
+            alpha[h] = expf(m_run[h] - m_new);
+            const float pe = lane < n ? expf(s - m_new) : 0.0f;
+            ps[warp][lane][h] = pe;
+            l_run[h] = l_run[h] * alpha[h] + warp_sum(pe);
+            m_run[h] = m_new;
+        }
+        __syncwarp();
+        // values: lane l takes columns [DL l, DL l + DL) of every head
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+#pragma unroll
+            for (int i = 0; i < DL; ++i) o_run[h][i] *= alpha[h];
+        // the sub-tile's value rows (DL bf16 columns per lane) are loaded
+        // together before they are used
+        uint32_t vw[32][DL / 2];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < n) {
+                const uint16_t* vr = vb + (size_t)(p0 + j) * D + DL * lane;
+                if (DL == 2) {
+                    vw[j][0] = *reinterpret_cast<const uint32_t*>(vr);
+                } else {
+                    const uint2 w = *reinterpret_cast<const uint2*>(vr);
+                    vw[j][0] = w.x;
+                    vw[j][(DL / 2) - 1] = w.y;
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (j < n) {
+                float vf[DL];
+#pragma unroll
+                for (int i = 0; i < DL / 2; ++i) {
+                    vf[2 * i] = __uint_as_float(vw[j][i] << 16);
+                    vf[2 * i + 1] = __uint_as_float(vw[j][i] & 0xffff0000u);
+                }
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float pj = ps[warp][j][h];
+#pragma unroll
+                    for (int i = 0; i < DL; ++i) o_run[h][i] = fmaf(pj, vf[i], o_run[h][i]);
+                }
+            }
+        }
+        __syncwarp();
+    }
+    // merge the warps' states (warp order) into the split's partial
+    if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            wm[warp][h] = m_run[h];
+            wl[warp][h] = l_run[h];
         }
     }
 #pragma unroll
-    for (int j = 0; j < HW; ++j) {
-        const int h = warp + j * NW;
-        if (h < G) {
-            float* pp = part + ((((size_t)t * nkv + kvh) * S + split) * G + h) * (D + 2);
-            if (lane == 0) {
-                pp[0] = m_run[j];
-                pp[1] = l_run[j];
-            }
+    for (int h = 0; h < G; ++h)
 #pragma unroll
-            for (int i = 0; i < DL; ++i) pp[2 + lane + 32 * i] = o_run[j][i];
+        for (int i = 0; i < DL; ++i) wo[warp][h][DL * lane + i] = o_run[h][i];
+    __syncthreads();
+    for (int e = tid; e < G * D; e += 128) {
+        const int h = e / D, d = e % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][h]);
+        float L = 0.0f, acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float f = wm[w][h] == -INFINITY ? 0.0f : expf(wm[w][h] - M);
+            L = fmaf(wl[w][h], f, L);
+            acc = fmaf(wo[w][h][d], f, acc);
         }
+        float* pp = part + ((((size_t)t * nkv + kvh) * S + split) * G + h) * (D + 2);
+        if (d == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
+        pp[2 + d] = acc;
     }
 }
 
@@ -273,6 +354,8 @@ __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uin
 // attn[t][(kvh G + h) D + d].
 __global__ void bt_attn_merge(const float* part, const int* positions, int nq, int nkv, int D, int S,
                               uint16_t* attn) {
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
     const int t = blockIdx.x / nkv, kvh = blockIdx.x % nkv;
     const int G = nq / nkv;
     int chunk, active;
@@ -296,6 +379,8 @@ __global__ void bt_attn_merge(const float* part, const int* positions, int nq, i
 // Greedy next token of sequence t (lowest index among equal maxima;
 // cuda/sampling.cu:3-40), then position + 1.
 __global__ void bt_argmax(const float* logits, int V, int* tokens, int* positions, int* hist) {
+    pdl_wait();  // the previous kernel of the step has completed
+    pdl_launch_dependents();
     __shared__ float bv[32];
     __shared__ int bi[32];
     const int t = blockIdx.x, tid = threadIdx.x;
@@ -355,6 +440,24 @@ __global__ void bt_rope_table(float2* tab, int max_seq, int D, float theta) {
         tab[i] = rope_factors((int)(i % half), D, (int)(i / half), theta);
 }
 
+// Launches k with programmatic dependent launch: it may start while the
+// previous kernel of the stream finishes; it waits (griddepcontrol.wait)
+// before it touches that kernel's outputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
 }  // namespace
 
 // ------------------------------------------------------------ host side
@@ -367,14 +470,17 @@ int bt_rope_table_launch(float2* tab, int max_seq, int D, float theta, cudaStrea
 
 int bt_embed_norm_launch(const float* emb, const int* tokens, int vocab, int T, int H, const float* norm_w, float eps,
                          float* h, uint16_t* xb, unsigned* err, cudaStream_t st) {
-    bt_embed_norm<<<T, 256, 0, st>>>(emb, tokens, vocab, H, norm_w, eps, h, xb, err);
+    INFERNT_REQUIRE(H % 128 == 0 && H / 4 <= 1024, "batched decode: hidden size %d", H);
+    INFERNT_CUDA_TRY(launch_pdl(bt_embed_norm, dim3(T), dim3(H / 4), st, emb, tokens, vocab, H, norm_w, eps, h, xb, err));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
 
 int bt_resid_norm_launch(const float* part, int splits, int T, int H, float* h, const float* norm_w, float eps,
                          uint16_t* xb, cudaStream_t st) {
-    bt_resid_norm<<<T, 256, 0, st>>>(part, splits, T, H, h, norm_w, eps, xb);
+    INFERNT_REQUIRE(H % 128 == 0 && H / 4 <= 1024 && splits <= kMaxSplits, "batched decode: hidden %d, splits %d", H,
+                    splits);
+    INFERNT_CUDA_TRY(launch_pdl(bt_resid_norm, dim3(T), dim3(H / 4), st, part, splits, T, H, h, norm_w, eps, xb));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -382,13 +488,15 @@ int bt_resid_norm_launch(const float* part, int splits, int T, int H, float* h, 
 int bt_qkv_finish_launch(const float* part, int splits, int T, int nq, int nkv, int D, const int* positions,
                          const float2* rope, int max_seq, float* q, uint16_t* kc, uint16_t* vc, unsigned* err,
                          cudaStream_t st) {
-    bt_qkv_finish<<<T, 256, 0, st>>>(part, splits, T, nq, nkv, D, positions, rope, max_seq, q, kc, vc, err);
+    INFERNT_REQUIRE(D % 8 == 0 && splits <= kMaxSplits, "batched decode: head_dim %d, splits %d", D, splits);
+    INFERNT_CUDA_TRY(launch_pdl(bt_qkv_finish, dim3(T), dim3(256), st, part, splits, T, nq, nkv, D, positions, rope, max_seq, q, kc, vc, err));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
 
 int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act, cudaStream_t st) {
-    bt_swiglu<<<T, 256, 0, st>>>(part, splits, T, I, act);
+    INFERNT_REQUIRE(I % 4 == 0 && splits <= kMaxSplits, "batched decode: intermediate %d, splits %d", I, splits);
+    INFERNT_CUDA_TRY(launch_pdl(bt_swiglu, dim3((I / 4 + 127) / 128, T), dim3(128), st, part, splits, T, I, act));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -401,25 +509,31 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
     INFERNT_REQUIRE(G >= 1 && G <= 16 && nq % nkv == 0, "batched attention: group size %d", G);
     const float scale = 1.0f / sqrtf((float)D);
     const int items = T * nkv * S;
+#define BT_ATTN(DLV, GV) \
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<DLV, GV>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv, max_seq, S, scale, part))
     if (D == 64) {
-        if (G <= 4)
-            bt_attn_partial<2, 1><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
-        else if (G <= 8)
-            bt_attn_partial<2, 2><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
-        else
-            bt_attn_partial<2, 4><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
+        switch (G) {
+            case 1: BT_ATTN(2, 1); break;
+            case 2: BT_ATTN(2, 2); break;
+            case 4: BT_ATTN(2, 4); break;
+            case 8: BT_ATTN(2, 8); break;
+            case 16: BT_ATTN(2, 16); break;
+            default: return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8, 16)", G);
+        }
     } else if (D == 128) {
-        if (G <= 4)
-            bt_attn_partial<4, 1><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
-        else if (G <= 8)
-            bt_attn_partial<4, 2><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
-        else
-            bt_attn_partial<4, 4><<<items, 128, 0, st>>>(q, kc, vc, positions, nq, nkv, max_seq, S, scale, part);
+        switch (G) {
+            case 1: BT_ATTN(4, 1); break;
+            case 2: BT_ATTN(4, 2); break;
+            case 4: BT_ATTN(4, 4); break;
+            case 8: BT_ATTN(4, 8); break;
+            default: return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8)", G);
+        }
     } else {
         return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: head_dim %d (64 or 128)", D);
     }
+#undef BT_ATTN
     INFERNT_CUDA_TRY(cudaGetLastError());
-    bt_attn_merge<<<T * nkv, 128, 0, st>>>(part, positions, nq, nkv, D, S, attn);
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, attn));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -433,7 +547,7 @@ int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq,
 }
 
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st) {
-    bt_argmax<<<T, 256, 0, st>>>(logits, V, tokens, positions, hist);
+    INFERNT_CUDA_TRY(launch_pdl(bt_argmax, dim3(T), dim3(256), st, logits, V, tokens, positions, hist));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }

@@ -17,7 +17,10 @@
 // stage) and frees each stage with tcgen05.commit; after the last stage's
 // commit all four warps read their 32 accumulator lanes with tcgen05.ld and
 // store the partial.  Every wait is bounded; on expiry the kernel sets bit 0
-// of *err and returns after its copies have landed.
+// of *err and returns after its copies have landed.  Launched with
+// programmatic dependent launch: the weight boxes of the first stages are
+// requested before the kernel waits for the previous one (griddepcontrol),
+// so the weight stream overlaps the previous kernel's tail.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -126,11 +129,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tmem_base;
 
     bool ok = true;
+    pdl_launch_dependents();
     if (warp == 0 && lane == 0) {
-        // producer
-        for (int i = k0; i < k1; ++i) {
+        // producer: the weight boxes of the first stages do not depend on the
+        // previous kernel, so they are requested before waiting for it
+        // (programmatic dependent launch); the token boxes after
+        const int first = (k1 - k0) < a.stages ? (k1 - k0) : a.stages;
+        for (int j = 0; j < first; ++j) {
+            mbar_arrive_expect_tx(&full[j], stage_bytes);
+            tma_load_2d(smem + (size_t)j * stage_bytes, &tm_w, (k0 + j) * kBK, n0, &full[j]);
+        }
+        pdl_wait();
+        for (int j = 0; j < first; ++j)
+            tma_load_2d(smem + (size_t)j * stage_bytes + kTileW, &tm_x, (k0 + j) * kBK, 0, &full[j]);
+        for (int i = k0 + first; i < k1; ++i) {
             const int j = i - k0, s = j % a.stages;
-            if (j >= a.stages && !bg_wait(&empty[s], ((j / a.stages) - 1) & 1u, ok)) break;
+            if (!bg_wait(&empty[s], ((j / a.stages) - 1) & 1u, ok)) break;
             unsigned char* st = smem + (size_t)s * stage_bytes;
             mbar_arrive_expect_tx(&full[s], stage_bytes);
             tma_load_2d(st, &tm_w, i * kBK, n0, &full[s]);
@@ -269,8 +283,19 @@ int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part,
     args.tp = tp;
     args.splits = splits;
     args.stages = bgemm_stages(tp);
-    bgemm_kernel<<<(N / kBM) * splits, kThreads, smem, st>>>(mw, mx, args);
-    INFERNT_CUDA_TRY(cudaGetLastError());
+    // programmatic dependent launch: the CTAs may start (and fetch their
+    // first weight boxes) while the previous kernel of the stream finishes
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((N / kBM) * splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    INFERNT_CUDA_TRY(cudaLaunchKernelEx(&cfg, bgemm_kernel, mw, mx, args));
     return INFERNT_OK;
 }
 

@@ -98,6 +98,7 @@ int pick_splits(int N, int K) {
     const int tiles = N / 128, nk = K / 64;
     int s = (infernt::sm_count() + tiles - 1) / tiles;
     if (s > nk) s = nk;
+    if (s > 16) s = 16;  // partial sums the finishing kernels add in one round
     return s < 1 ? 1 : s;
 }
 
