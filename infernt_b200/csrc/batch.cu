@@ -350,6 +350,266 @@ __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uin
     }
 }
 
+// ---- attention partials on the tensor cores (mma.sync m16n8k16, bf16)
+//
+// The same partial as bt_attn_partial for head groups of up to 8 query
+// heads, with the two dot products on the tensor cores.  The bf16 keys and
+// values are exact MMA operands; the FP32 queries and probabilities are
+// split into three bf16 terms x = hi + mid + lo (hi = bf16(x), mid =
+// bf16(x - hi), lo = bf16(x - hi - mid): 24 mantissa bits, as FP32) and two
+// MMAs take them: rows 0-7 of the first A operand hold the hi terms of the
+// group's heads and rows 8-15 the mid terms, rows 0-7 of the second the lo
+// terms (rows 8-15 zero), both into one accumulator, so a head's value is
+// the sum of its two accumulator rows.
+//   scores  S[16 x 8 positions] = Qsplit[16 x D] K^T      (2 D / 16 MMAs)
+//   output  O[16 x D]         += Psplit[16 x 16 pos] V     (2 D / 8 MMAs)
+// Each warp streams 32-position tiles of K and V into its own ring of
+// attn_stages<D>() shared-memory stages with 16-byte cp.async copies (rows past
+// the split's end are zero-filled), the 16-byte chunks of a row stored at
+// chunk ^ (row & 7) so that ldmatrix reads are conflict-free.  Warp w takes
+// tiles w, w + 4, ...; online softmax per warp (quad shuffles for the row
+// maxima), then the four warps' (m, l, o) are merged in warp order into the
+// split's partial [T][Nkv][S][G][D + 2] exactly as bt_attn_partial does.
+constexpr int kAttnTile = 32;
+
+template <int D>
+constexpr int attn_stages() {
+    return D == 64 ? 3 : 2;
+}
+
+template <int D>
+constexpr int attn_smem_bytes() {
+    return 4 * attn_stages<D>() * 2 * kAttnTile * D * 2;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo_elem, float hi_elem) {
+    return (uint32_t)bf16_bits(lo_elem) | ((uint32_t)bf16_bits(hi_elem) << 16);
+}
+
+// x = hi + mid + lo as bf16 pairs (elements a, b of consecutive k); every
+// difference is exact in FP32
+__device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+    const float ah = infernt_round_bf16(a), bh = infernt_round_bf16(b);
+    const float ar = a - ah, br = b - bh;
+    const float am = infernt_round_bf16(ar), bm = infernt_round_bf16(br);
+    hi = pack_bf16x2(ah, bh);
+    mid = pack_bf16x2(am, bm);
+    lo = pack_bf16x2(ar - am, br - bm);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// 16 bytes global -> shared; src_bytes 0 writes zeros (src is not read)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_t* kc, const uint16_t* vc,
+                                                   const int* positions, int nq, int nkv, int G, int max_seq, int S,
+                                                   float scale, float* part) {
+    pdl_wait();
+    pdl_launch_dependents();
+    constexpr int NW = 4, NST = attn_stages<D>();
+    constexpr int ROWB = D * 2, CH = ROWB / 16;           // bytes and 16-byte chunks per cache row
+    constexpr int TILEB = kAttnTile * ROWB;              // one K (or V) tile
+    constexpr int KC = D / 16, DB = D / 8;               // k-steps of the scores, d-blocks of the output
+    extern __shared__ __align__(128) unsigned char att_smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, tig = lane & 3;
+    const int item = blockIdx.x;
+    const int split = item % S, kvh = (item / S) % nkv, t = item / (S * nkv);
+    const int seq = positions[t] + 1;
+    int chunk, active;
+    bt_chunk(seq, S, chunk, active);
+    if (split >= active) return;
+    const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
+    const int ntiles = (c1 - c0 + kAttnTile - 1) / kAttnTile;
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(kc + ((size_t)t * nkv + kvh) * max_seq * D);
+    const unsigned char* vb = reinterpret_cast<const unsigned char*>(vc + ((size_t)t * nkv + kvh) * max_seq * D);
+    const uint32_t ring = smem_addr(att_smem) + (uint32_t)warp * NST * 2 * TILEB;
+
+    // this warp's tile i of the split -> stage i % NST (K at +0, V at +TILEB)
+    auto issue = [&](int i) {
+        const int tile = warp + NW * i;
+        if (tile < ntiles) {
+            const int p0 = c0 + tile * kAttnTile;
+            const uint32_t st = ring + (uint32_t)(i % NST) * 2 * TILEB;
+#pragma unroll
+            for (int e = 0; e < kAttnTile * CH / 32; ++e) {
+                const int idx = e * 32 + lane, row = idx / CH, ch = idx % CH;
+                const bool ok = p0 + row < c1;
+                const size_t off = (size_t)(ok ? p0 + row : c0) * ROWB + (size_t)ch * 16;
+                const uint32_t dst = st + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4));
+                cp_async16(dst, kb + off, ok ? 16u : 0u);
+                cp_async16(dst + TILEB, vb + off, ok ? 16u : 0u);
+            }
+        }
+        cp_async_commit();
+    };
+    const int my_tiles = ntiles > warp ? (ntiles - warp + NW - 1) / NW : 0;
+#pragma unroll
+    for (int i = 0; i < NST - 1; ++i) issue(i);
+
+    // query fragments: qa rows g / g + 8 = hi / mid terms of head g, ql row
+    // g = its lo terms (rows g + 8 of the second operand are zero)
+    uint32_t qa[KC][4], ql[KC][4];
+    {
+        const float* qh = q + ((size_t)t * nq + (size_t)kvh * G + g) * D;
+#pragma unroll
+        for (int k = 0; k < KC; ++k) {
+            float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+            if (g < G) {
+                const float2 lo2 = *reinterpret_cast<const float2*>(qh + 16 * k + 2 * tig);
+                const float2 hi2 = *reinterpret_cast<const float2*>(qh + 16 * k + 2 * tig + 8);
+                x0 = lo2.x;
+                x1 = lo2.y;
+                x2 = hi2.x;
+                x3 = hi2.y;
+            }
+            split3_bf16x2(x0, x1, qa[k][0], qa[k][1], ql[k][0]);
+            split3_bf16x2(x2, x3, qa[k][2], qa[k][3], ql[k][2]);
+            ql[k][1] = ql[k][3] = 0u;
+        }
+    }
+    float m_run = -INFINITY, l_run = 0.0f;
+    float acc[DB][4];
+#pragma unroll
+    for (int b = 0; b < DB; ++b) acc[b][0] = acc[b][1] = acc[b][2] = acc[b][3] = 0.0f;
+
+    for (int i = 0; i < my_tiles; ++i) {
+        issue(i + NST - 1);  // the stage it fills was read in iteration i - 1 (synced below)
+        cp_async_wait<NST - 1>();
+        __syncwarp();
+        const uint32_t kt = ring + (uint32_t)(i % NST) * 2 * TILEB, vt = kt + TILEB;
+        const int p0 = c0 + (warp + NW * i) * kAttnTile;
+        // scores
+        float sc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KC; ++k)
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const int m = lane >> 3, row = 8 * (2 * jj + (m >> 1)) + (lane & 7), ch = 2 * k + (m & 1);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kt + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4)), b0, b1, b2, b3);
+                mma_bf16_16816(sc[2 * jj], qa[k], b0, b1);
+                mma_bf16_16816(sc[2 * jj], ql[k], b0, b1);
+                mma_bf16_16816(sc[2 * jj + 1], qa[k], b2, b3);
+                mma_bf16_16816(sc[2 * jj + 1], ql[k], b2, b3);
+            }
+        // online softmax of head g over the tile (each quad holds one head)
+        float s[4][2], mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int p = p0 + 8 * j + 2 * tig + e;
+                s[j][e] = p < c1 ? (sc[j][e] + sc[j][e + 2]) * scale : -INFINITY;
+                mx = fmaxf(mx, s[j][e]);
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = expf(m_run - m_new);
+        m_run = m_new;
+        float lsum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                s[j][e] = expf(s[j][e] - m_new);
+                lsum += s[j][e];
+            }
+        l_run = l_run * alpha + lsum;
+#pragma unroll
+        for (int b = 0; b < DB; ++b)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[b][e] *= alpha;
+        // output: probabilities of 16 positions per k-step as the A operand
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            uint32_t pa[4], pl[4];
+            split3_bf16x2(s[2 * kk][0], s[2 * kk][1], pa[0], pa[1], pl[0]);
+            split3_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1], pa[2], pa[3], pl[2]);
+            pl[1] = pl[3] = 0u;
+#pragma unroll
+            for (int b2 = 0; b2 < DB / 2; ++b2) {
+                const int m = lane >> 3, row = 16 * kk + 8 * (m & 1) + (lane & 7), ch = 2 * b2 + (m >> 1);
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_trans(vt + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4)), v0, v1, v2, v3);
+                mma_bf16_16816(acc[2 * b2], pa, v0, v1);
+                mma_bf16_16816(acc[2 * b2], pl, v0, v1);
+                mma_bf16_16816(acc[2 * b2 + 1], pa, v2, v3);
+                mma_bf16_16816(acc[2 * b2 + 1], pl, v2, v3);
+            }
+        }
+        __syncwarp();  // every lane has read the stage before it is refilled
+    }
+    cp_async_wait<0>();
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    __syncthreads();  // the rings are reused for the merge
+    float* wm = reinterpret_cast<float*>(att_smem);      // [NW][8]
+    float* wl = wm + NW * 8;                              // [NW][8]
+    float* wo = wl + NW * 8;                              // [NW][8][D]
+    if (tig == 0) {
+        wm[warp * 8 + g] = m_run;
+        wl[warp * 8 + g] = l_run;
+    }
+#pragma unroll
+    for (int b = 0; b < DB; ++b) {
+        float* o = wo + ((size_t)warp * 8 + g) * D + 8 * b + 2 * tig;
+        o[0] = acc[b][0] + acc[b][2];
+        o[1] = acc[b][1] + acc[b][3];
+    }
+    __syncthreads();
+    for (int e = tid; e < G * D; e += 128) {
+        const int h = e / D, d = e % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * 8 + h]);
+        float L = 0.0f, a = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float mw = wm[w * 8 + h];
+            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+            L = fmaf(wl[w * 8 + h], f, L);
+            a = fmaf(wo[((size_t)w * 8 + h) * D + d], f, a);
+        }
+        float* pp = part + ((((size_t)t * nkv + kvh) * S + split) * G + h) * (D + 2);
+        if (d == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
+        pp[2 + d] = a;
+    }
+}
+
 // Merge of the active splits of (t, kvh) in split order; output bf16
 // attn[t][(kvh G + h) D + d].
 __global__ void bt_attn_merge(const float* part, const int* positions, int nq, int nkv, int D, int S,
@@ -444,6 +704,22 @@ __global__ void bt_rope_table(float2* tab, int max_seq, int D, float theta) {
 // previous kernel of the stream finishes; it waits (griddepcontrol.wait)
 // before it touches that kernel's outputs.
 template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_smem(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -509,6 +785,31 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
     INFERNT_REQUIRE(G >= 1 && G <= 16 && nq % nkv == 0, "batched attention: group size %d", G);
     const float scale = 1.0f / sqrtf((float)D);
     const int items = T * nkv * S;
+    if (G <= 8 && (D == 64 || D == 128)) {
+        // tensor-core partials
+        static bool raised64 = false, raised128 = false;
+        if (D == 64) {
+            if (!raised64) {
+                INFERNT_CUDA_TRY(cudaFuncSetAttribute(bt_attn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      attn_smem_bytes<64>()));
+                raised64 = true;
+            }
+            INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<64>, dim3(items), dim3(128), (size_t)attn_smem_bytes<64>(), st,
+                                             q, kc, vc, positions, nq, nkv, G, max_seq, S, scale, part));
+        } else {
+            if (!raised128) {
+                INFERNT_CUDA_TRY(cudaFuncSetAttribute(bt_attn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      attn_smem_bytes<128>()));
+                raised128 = true;
+            }
+            INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<128>, dim3(items), dim3(128), (size_t)attn_smem_bytes<128>(),
+                                             st, q, kc, vc, positions, nq, nkv, G, max_seq, S, scale, part));
+        }
+        INFERNT_CUDA_TRY(cudaGetLastError());
+        INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, attn));
+        INFERNT_CUDA_TRY(cudaGetLastError());
+        return INFERNT_OK;
+    }
 #define BT_ATTN(DLV, GV) \
     INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<DLV, GV>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv, max_seq, S, scale, part))
     if (D == 64) {

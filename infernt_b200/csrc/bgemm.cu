@@ -90,7 +90,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ uint64_t full[kStages], empty[kStages], done;
@@ -246,9 +246,20 @@ int make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) 
 
 }  // namespace
 
+// Two CTAs share an SM when at least kPairStages stages fit in half of its
+// shared memory (their weight streams and epilogues then overlap); otherwise
+// one CTA per SM with as many stages as fit.
+constexpr int kPairSmem = 112 * 1024;
+constexpr int kPairStages = 3;
+
+int bgemm_ctas_per_sm(int tp) {
+    const int per = kTileW + tp * kBK * 2;
+    return (kPairSmem - 1024) / per >= kPairStages ? 2 : 1;
+}
+
 int bgemm_stages(int tp) {
     const int per = kTileW + tp * kBK * 2;
-    const int n = (kSmemLimit - 1024) / per;
+    const int n = ((bgemm_ctas_per_sm(tp) == 2 ? kPairSmem : kSmemLimit) - 1024) / per;
     return n < kStages ? n : kStages;
 }
 

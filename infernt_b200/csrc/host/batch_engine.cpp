@@ -19,6 +19,7 @@
 #include "../internal.h"
 
 namespace infernt {
+int bgemm_ctas_per_sm(int tp);
 int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part, int splits, unsigned* err,
                  cudaStream_t st);
 int bt_rope_table_launch(float2* tab, int max_seq, int D, float theta, cudaStream_t st);
@@ -93,13 +94,26 @@ int alloc(infernt_batch_engine* e, size_t bytes, void** out) {
     return INFERNT_OK;
 }
 
-// splits so that tiles x splits fills the GPU's SMs about once
-int pick_splits(int N, int K) {
-    const int tiles = N / 128, nk = K / 64;
-    int s = (infernt::sm_count() + tiles - 1) / tiles;
-    if (s > nk) s = nk;
-    if (s > 16) s = 16;  // partial sums the finishing kernels add in one round
-    return s < 1 ? 1 : s;
+// K splits of a projection: tiles x splits CTAs of ceil(nk / splits) weight
+// stages each.  The busiest SM streams ceil(ctas / sms) CTAs' stages, and
+// every wave of resident CTAs adds a fixed cost (pipeline fill, epilogue) of
+// about two stages; the split count with the least such cost wins (ties go
+// to fewer partials).  At most 16 splits: the finishing kernels add the
+// partials in one round of loads.
+int pick_splits(int N, int K, int T) {
+    const int tiles = N / 128, nk = K / 64, sms = infernt::sm_count();
+    const int slots = sms * infernt::bgemm_ctas_per_sm((T + 15) / 16 * 16);
+    int best = 1;
+    long best_cost = -1;
+    for (int s = 1; s <= 16 && s <= nk; ++s) {
+        const long ctas = (long)tiles * s;
+        const long cost = (ctas + sms - 1) / sms * ((nk + s - 1) / s) + 2 * ((ctas + slots - 1) / slots);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
 }
 
 int fill_bf16(infernt_batch_engine* e, void* dst, size_t n, uint64_t seed, uint64_t stream_id, float std_dev) {
@@ -162,10 +176,10 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         e->kc.push_back(static_cast<uint16_t*>(k));
         e->vc.push_back(static_cast<uint16_t*>(v));
     }
-    e->sp_qkv = pick_splits(nqkv, H);
-    e->sp_o = pick_splits(H, qs);
-    e->sp_gu = pick_splits(2 * I, H);
-    e->sp_down = pick_splits(H, I);
+    e->sp_qkv = pick_splits(nqkv, H, T);
+    e->sp_o = pick_splits(H, qs, T);
+    e->sp_gu = pick_splits(2 * I, H, T);
+    e->sp_down = pick_splits(H, I, T);
     e->sp_lm = 1;  // the argmax reads whole logits
     size_t part = 0;
     auto need = [&](int sp, int N) {
