@@ -286,6 +286,28 @@ INFERNT_API int infernt_batch_engine_logits(infernt_batch_engine* e, float* logi
 /* K splits of the Q|K|V, O, gate|up, down and LM-head projections and the
  * attention's KV splits (6 ints). */
 INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);
+/* Attention work split: `splits` KV splits per (sequence, KV head), each at
+ * least min_chunk positions, and `stages` copy stages per warp (2 to 4 at
+ * head_dim 64, 2 or 3 at 128).  Results do not depend on these; the step
+ * graph is captured again at the next step. */
+INFERNT_API int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int min_chunk,
+                                                   int stages);
+
+/* Attention of T decoding sequences over bf16 caches (the batched engine's
+ * kernels; cuda/attention.cu:9-42 per sequence and query head): q [T][nq][D]
+ * FP32 (RoPE applied), caches [T][nkv][max_seq][D] bf16, sequence t
+ * attends to positions [0, positions[t]]; attn [T][nq][D] bf16 (rounded to
+ * nearest even) and, when attn_f32 is not NULL, the FP32 values.  splits
+ * KV splits per (t, KV head) of at least min_chunk positions, `stages` copy
+ * stages (2 to 4 at D = 64, 2 or 3 at 128; ignored for 16 query heads per
+ * KV head); partials holds T x nkv x splits x (nq / nkv) x (D + 2) floats.
+ * D in {64, 128}; nq / nkv from 1 to 8, or 16 at D = 64.  positions[t] in
+ * [0, max_seq) (a sequence outside is not read; its output is undefined).
+ * Device pointers; asynchronous on `stream`. */
+INFERNT_API int infernt_batch_attention(const float* q, const void* k_cache, const void* v_cache,
+                                        const int* positions, int T, int nq, int nkv, int head_dim,
+                                        int max_seq, int splits, int min_chunk, int stages,
+                                        float* partials, void* attn, float* attn_f32, void* stream);
 
 /* ----------------------------------------- tensor parallelism ---
  * The 8B-class configuration decoded by tp_size GPUs, one process per GPU

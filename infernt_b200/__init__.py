@@ -140,6 +140,8 @@ _SIGS = {
     "infernt_batch_engine_decode": (_I, [_P, _P, _P, _I, _P, ctypes.POINTER(_F)]),
     "infernt_batch_engine_logits": (_I, [_P, _P, _S]),
     "infernt_batch_engine_splits": (_I, [_P, _P]),
+    "infernt_batch_engine_set_attention": (_I, [_P, _I, _I, _I]),
+    "infernt_batch_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),
     "infernt_plan_destroy": (_I, [_P]),
@@ -379,6 +381,11 @@ class BatchEngine:
         out = (ctypes.c_int * 6)()
         call("infernt_batch_engine_splits", self._h, out)
         return list(out)
+
+    def set_attention(self, splits: int, min_chunk: int, stages: int):
+        """KV splits per (sequence, KV head), least positions per split and
+        copy stages per warp of the attention; results do not change."""
+        call("infernt_batch_engine_set_attention", self._h, splits, min_chunk, stages)
 
 
 class TPEngine:

@@ -179,12 +179,11 @@ __global__ void bt_swiglu(const float* part, int splits, int T, int I, uint16_t*
     *reinterpret_cast<uint2*>(act + (size_t)t * I + i) = make_uint2(lo, hi);
 }
 
-// Positions per attention tile and the chunk of a split.
-constexpr int kBtMinChunk = 64;
-
-__device__ __forceinline__ void bt_chunk(int seq, int splits, int& chunk, int& active) {
+// The chunk of a split: seq / splits positions, at least min_chunk; the
+// splits past the sequence's last chunk are inactive.
+__device__ __forceinline__ void bt_chunk(int seq, int splits, int min_chunk, int& chunk, int& active) {
     chunk = (seq + splits - 1) / splits;
-    if (chunk < kBtMinChunk) chunk = kBtMinChunk;
+    if (chunk < min_chunk) chunk = min_chunk;
     active = (seq + chunk - 1) / chunk;
 }
 
@@ -199,7 +198,7 @@ __device__ __forceinline__ void bt_chunk(int seq, int splits, int& chunk, int& a
 template <int DL, int G>
 __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uint16_t* kc, const uint16_t* vc,
                                                        const int* positions, int nq, int nkv, int max_seq, int S,
-                                                       float scale, float* part) {
+                                                       int min_chunk, float scale, float* part) {
     pdl_wait();
     pdl_launch_dependents();
     constexpr int D = 32 * DL, NW = 4;
@@ -212,8 +211,8 @@ __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uin
     const int split = item % S, kvh = (item / S) % nkv, t = item / (S * nkv);
     const int seq = positions[t] + 1;
     int chunk, active;
-    bt_chunk(seq, S, chunk, active);
-    if (split >= active) return;
+    bt_chunk(seq, S, min_chunk, chunk, active);
+    if (split >= active || seq > max_seq) return;  // positions past the cache are not read
     const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
     const uint16_t* kb = kc + ((size_t)t * nkv + kvh) * max_seq * D;
     const uint16_t* vb = vc + ((size_t)t * nkv + kvh) * max_seq * D;
@@ -372,29 +371,25 @@ __global__ void __launch_bounds__(128) bt_attn_partial(const float* q, const uin
 // split's partial [T][Nkv][S][G][D + 2] exactly as bt_attn_partial does.
 constexpr int kAttnTile = 32;
 
-template <int D>
-constexpr int attn_stages() {
-    return D == 64 ? 3 : 2;
-}
-
-template <int D>
+template <int D, int NST>
 constexpr int attn_smem_bytes() {
-    return 4 * attn_stages<D>() * 2 * kAttnTile * D * 2;
+    return 4 * NST * 2 * kAttnTile * D * 2;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo_elem, float hi_elem) {
-    return (uint32_t)bf16_bits(lo_elem) | ((uint32_t)bf16_bits(hi_elem) << 16);
+// bf16x2 of (a, b), each rounded to nearest even; a in the low half
+__device__ __forceinline__ uint32_t cvt_bf16x2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
 }
 
 // x = hi + mid + lo as bf16 pairs (elements a, b of consecutive k); every
 // difference is exact in FP32
 __device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
-    const float ah = infernt_round_bf16(a), bh = infernt_round_bf16(b);
-    const float ar = a - ah, br = b - bh;
-    const float am = infernt_round_bf16(ar), bm = infernt_round_bf16(br);
-    hi = pack_bf16x2(ah, bh);
-    mid = pack_bf16x2(am, bm);
-    lo = pack_bf16x2(ar - am, br - bm);
+    hi = cvt_bf16x2(a, b);
+    const float ar = a - __uint_as_float(hi << 16), br = b - __uint_as_float(hi & 0xffff0000u);
+    mid = cvt_bf16x2(ar, br);
+    lo = cvt_bf16x2(ar - __uint_as_float(mid << 16), br - __uint_as_float(mid & 0xffff0000u));
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -427,13 +422,13 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int D>
+template <int D, int NST>
 __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_t* kc, const uint16_t* vc,
                                                    const int* positions, int nq, int nkv, int G, int max_seq, int S,
-                                                   float scale, float* part) {
+                                                   int min_chunk, float scale, float* part) {
     pdl_wait();
     pdl_launch_dependents();
-    constexpr int NW = 4, NST = attn_stages<D>();
+    constexpr int NW = 4;
     constexpr int ROWB = D * 2, CH = ROWB / 16;           // bytes and 16-byte chunks per cache row
     constexpr int TILEB = kAttnTile * ROWB;              // one K (or V) tile
     constexpr int KC = D / 16, DB = D / 8;               // k-steps of the scores, d-blocks of the output
@@ -444,8 +439,8 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
     const int split = item % S, kvh = (item / S) % nkv, t = item / (S * nkv);
     const int seq = positions[t] + 1;
     int chunk, active;
-    bt_chunk(seq, S, chunk, active);
-    if (split >= active) return;
+    bt_chunk(seq, S, min_chunk, chunk, active);
+    if (split >= active || seq > max_seq) return;  // positions past the cache are not read
     const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
     const int ntiles = (c1 - c0 + kAttnTile - 1) / kAttnTile;
     const unsigned char* kb = reinterpret_cast<const unsigned char*>(kc + ((size_t)t * nkv + kvh) * max_seq * D);
@@ -506,10 +501,12 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
         __syncwarp();
         const uint32_t kt = ring + (uint32_t)(i % NST) * 2 * TILEB, vt = kt + TILEB;
         const int p0 = c0 + (warp + NW * i) * kAttnTile;
-        // scores
-        float sc[4][4];
+        // scores: hi / mid terms in sc, lo terms in sl (two shorter MMA chains)
+        float sc[4][4], sl[4][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[j][e] = sl[j][e] = 0.0f;
 #pragma unroll
         for (int k = 0; k < KC; ++k)
 #pragma unroll
@@ -518,9 +515,9 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(kt + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4)), b0, b1, b2, b3);
                 mma_bf16_16816(sc[2 * jj], qa[k], b0, b1);
-                mma_bf16_16816(sc[2 * jj], ql[k], b0, b1);
+                mma_bf16_16816(sl[2 * jj], ql[k], b0, b1);
                 mma_bf16_16816(sc[2 * jj + 1], qa[k], b2, b3);
-                mma_bf16_16816(sc[2 * jj + 1], ql[k], b2, b3);
+                mma_bf16_16816(sl[2 * jj + 1], ql[k], b2, b3);
             }
         // online softmax of head g over the tile (each quad holds one head)
         float s[4][2], mx = -INFINITY;
@@ -529,7 +526,7 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int p = p0 + 8 * j + 2 * tig + e;
-                s[j][e] = p < c1 ? (sc[j][e] + sc[j][e + 2]) * scale : -INFINITY;
+                s[j][e] = p < c1 ? ((sc[j][e] + sc[j][e + 2]) + sl[j][e]) * scale : -INFINITY;
                 mx = fmaxf(mx, s[j][e]);
             }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -611,15 +608,15 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
 }
 
 // Merge of the active splits of (t, kvh) in split order; output bf16
-// attn[t][(kvh G + h) D + d].
+// attn[t][(kvh G + h) D + d] (and the FP32 value in attn_f32 when given).
 __global__ void bt_attn_merge(const float* part, const int* positions, int nq, int nkv, int D, int S,
-                              uint16_t* attn) {
+                              int min_chunk, uint16_t* attn, float* attn_f32) {
     pdl_wait();  // the previous kernel of the step has completed
     pdl_launch_dependents();
     const int t = blockIdx.x / nkv, kvh = blockIdx.x % nkv;
     const int G = nq / nkv;
     int chunk, active;
-    bt_chunk(positions[t] + 1, S, chunk, active);
+    bt_chunk(positions[t] + 1, S, min_chunk, chunk, active);
     const float* pk = part + ((size_t)t * nkv + kvh) * S * G * (D + 2);
     for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
         const int h = e / D, d = e % D;
@@ -632,7 +629,9 @@ __global__ void bt_attn_merge(const float* part, const int* positions, int nq, i
             L = fmaf(pp[1], w, L);
             acc = fmaf(pp[2 + d], w, acc);
         }
-        attn[(size_t)t * nq * D + (size_t)kvh * G * D + e] = bf16_bits(acc / L);
+        const size_t o = (size_t)t * nq * D + (size_t)kvh * G * D + e;
+        attn[o] = bf16_bits(acc / L);
+        if (attn_f32) attn_f32[o] = acc / L;
     }
 }
 
@@ -778,63 +777,60 @@ int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act,
 }
 
 // Attention of every sequence: partials over `S` splits per (t, KV head),
-// then the merge.  D in {64, 128}, G = nq / nkv <= 16.
+// each a chunk of at least min_chunk positions, then the merge.  D in {64,
+// 128}; groups of up to 8 query heads run on the tensor cores (bt_attn_mma,
+// `stages` cp.async stages per warp), groups of 16 (D = 64) on CUDA cores
+// (bt_attn_partial).
 int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
-                        int nkv, int D, int max_seq, int S, float* part, uint16_t* attn, cudaStream_t st) {
+                        int nkv, int D, int max_seq, int S, int min_chunk, int stages, float* part, uint16_t* attn,
+                        cudaStream_t st, float* attn_f32) {
     const int G = nq / nkv;
     INFERNT_REQUIRE(G >= 1 && G <= 16 && nq % nkv == 0, "batched attention: group size %d", G);
+    INFERNT_REQUIRE(S >= 1 && min_chunk >= 1, "batched attention: splits %d, min_chunk %d", S, min_chunk);
     const float scale = 1.0f / sqrtf((float)D);
     const int items = T * nkv * S;
     if (G <= 8 && (D == 64 || D == 128)) {
-        // tensor-core partials
-        static bool raised64 = false, raised128 = false;
+        // tensor-core partials, `stages` shared-memory stages per warp
+        INFERNT_REQUIRE(stages >= 2 && stages <= (D == 64 ? 4 : 3), "batched attention: %d stages for head_dim %d",
+                        stages, D);
+#define BT_MMA(DV, NV)                                                                                               \
+    do {                                                                                                           \
+        static bool raised = false;                                                                                \
+        constexpr int smem = attn_smem_bytes<DV, NV>();                                                            \
+        if (!raised) {                                                                                             \
+            INFERNT_CUDA_TRY(                                                                                      \
+                cudaFuncSetAttribute(bt_attn_mma<DV, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));     \
+            raised = true;                                                                                         \
+        }                                                                                                          \
+        INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<DV, NV>, dim3(items), dim3(128), (size_t)smem, st, q, kc, vc, \
+                                         positions, nq, nkv, G, max_seq, S, min_chunk, scale, part));              \
+    } while (0)
         if (D == 64) {
-            if (!raised64) {
-                INFERNT_CUDA_TRY(cudaFuncSetAttribute(bt_attn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      attn_smem_bytes<64>()));
-                raised64 = true;
-            }
-            INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<64>, dim3(items), dim3(128), (size_t)attn_smem_bytes<64>(), st,
-                                             q, kc, vc, positions, nq, nkv, G, max_seq, S, scale, part));
+            if (stages == 2) BT_MMA(64, 2);
+            else if (stages == 3) BT_MMA(64, 3);
+            else BT_MMA(64, 4);
         } else {
-            if (!raised128) {
-                INFERNT_CUDA_TRY(cudaFuncSetAttribute(bt_attn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                      attn_smem_bytes<128>()));
-                raised128 = true;
-            }
-            INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<128>, dim3(items), dim3(128), (size_t)attn_smem_bytes<128>(),
-                                             st, q, kc, vc, positions, nq, nkv, G, max_seq, S, scale, part));
+            if (stages == 2) BT_MMA(128, 2);
+            else BT_MMA(128, 3);
         }
-        INFERNT_CUDA_TRY(cudaGetLastError());
-        INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, attn));
-        INFERNT_CUDA_TRY(cudaGetLastError());
-        return INFERNT_OK;
-    }
-#define BT_ATTN(DLV, GV) \
-    INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<DLV, GV>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv, max_seq, S, scale, part))
-    if (D == 64) {
-        switch (G) {
-            case 1: BT_ATTN(2, 1); break;
-            case 2: BT_ATTN(2, 2); break;
-            case 4: BT_ATTN(2, 4); break;
-            case 8: BT_ATTN(2, 8); break;
-            case 16: BT_ATTN(2, 16); break;
-            default: return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8, 16)", G);
-        }
-    } else if (D == 128) {
-        switch (G) {
-            case 1: BT_ATTN(4, 1); break;
-            case 2: BT_ATTN(4, 2); break;
-            case 4: BT_ATTN(4, 4); break;
-            case 8: BT_ATTN(4, 8); break;
-            default: return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8)", G);
-        }
+#undef BT_MMA
     } else {
-        return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: head_dim %d (64 or 128)", D);
-    }
+#define BT_ATTN(DLV, GV)                                                                                            \
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<DLV, GV>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv, \
+                                max_seq, S, min_chunk, scale, part))
+        if (D == 64 && G == 16) {
+            BT_ATTN(2, 16);
+        } else if (D == 64 || D == 128) {
+            return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8, or 16 at head_dim 64)",
+                        G);
+        } else {
+            return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: head_dim %d (64 or 128)", D);
+        }
 #undef BT_ATTN
+    }
     INFERNT_CUDA_TRY(cudaGetLastError());
-    INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, attn));
+    INFERNT_CUDA_TRY(
+        launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, min_chunk, attn, attn_f32));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -854,3 +850,15 @@ int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positi
 }
 
 }  // namespace infernt
+
+extern "C" int infernt_batch_attention(const float* q, const void* k_cache, const void* v_cache, const int* positions,
+                                       int T, int nq, int nkv, int head_dim, int max_seq, int splits, int min_chunk,
+                                       int stages, float* partials, void* attn, float* attn_f32, void* stream) {
+    INFERNT_REQUIRE(q && k_cache && v_cache && positions && partials && attn, "batch_attention: null pointer");
+    INFERNT_REQUIRE(T >= 1 && nq >= 1 && nkv >= 1 && max_seq >= 1, "batch_attention: bad sizes");
+    INFERNT_REQUIRE(infernt::aligned16(k_cache) && infernt::aligned16(v_cache) && infernt::aligned16(q),
+                    "batch_attention: q and the caches must be 16-byte aligned");
+    return infernt::bt_attention_launch(q, static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache),
+                                        positions, T, nq, nkv, head_dim, max_seq, splits, min_chunk, stages, partials,
+                                        static_cast<uint16_t*>(attn), static_cast<cudaStream_t>(stream), attn_f32);
+}

@@ -32,7 +32,8 @@ int bt_qkv_finish_launch(const float* part, int splits, int T, int nq, int nkv, 
                          cudaStream_t st);
 int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act, cudaStream_t st);
 int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
-                        int nkv, int D, int max_seq, int S, float* part, uint16_t* attn, cudaStream_t st);
+                        int nkv, int D, int max_seq, int S, int min_chunk, int stages, float* part, uint16_t* attn,
+                        cudaStream_t st, float* attn_f32 = nullptr);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
                       float std_dev, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st);
@@ -40,7 +41,8 @@ int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positi
 
 struct infernt_batch_engine {
     infernt_llama_config cfg;
-    int T = 0, S = 1;  // sequences, attention splits
+    int T = 0, S = 1;            // sequences, attention splits
+    int min_chunk = 64, stages = 3;  // attention: least positions per split, cp.async stages per warp
     // weights
     const float* emb = nullptr;
     const float* final_norm = nullptr;
@@ -231,7 +233,7 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
                                          e->kc[l], e->vc[l], e->err, st))
             return s;
         if (int s = bt_attention_launch(e->q, e->kc[l], e->vc[l], e->positions, T, nq, nkv, D, c.max_seq_len, e->S,
-                                        e->apart, e->attn, st))
+                                        e->min_chunk, e->stages, e->apart, e->attn, st))
             return s;
         if (int s = bgemm_launch(ly.o, H, qs, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
         if (int s = bt_resid_norm_launch(e->part, e->sp_o, T, H, e->h, ly.ffn_norm, eps, e->xb, st)) return s;
@@ -406,6 +408,37 @@ int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, siz
     INFERNT_REQUIRE(e->sp_lm == 1, "batch_engine_logits: the LM head runs split; logits are partial sums");
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
     INFERNT_CUDA_TRY(cudaMemcpy(logits_host, e->part, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int min_chunk, int stages) {
+    INFERNT_REQUIRE(e, "batch_engine_set_attention: null engine");
+    const int D = e->cfg.head_dim, nkv = e->cfg.num_key_value_heads, G = e->cfg.num_attention_heads / nkv;
+    INFERNT_REQUIRE(splits >= 1 && splits <= 64, "batch_engine_set_attention: splits %d outside [1, 64]", splits);
+    INFERNT_REQUIRE(min_chunk >= 1, "batch_engine_set_attention: min_chunk %d", min_chunk);
+    INFERNT_REQUIRE(stages >= 2 && stages <= (D == 64 ? 4 : 3), "batch_engine_set_attention: %d stages at head_dim %d",
+                    stages, D);
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if (splits > e->S) {
+        // the partial buffer holds [T][Nkv][S][G][D + 2]
+        for (auto it = e->bufs.begin(); it != e->bufs.end(); ++it)
+            if (*it == e->apart) {
+                e->bufs.erase(it);
+                break;
+            }
+        cudaFree(e->apart);
+        e->apart = nullptr;
+        void* p = nullptr;
+        if (int s = alloc(e, sizeof(float) * (size_t)e->T * nkv * splits * G * (D + 2), &p)) return s;
+        e->apart = static_cast<float*>(p);
+    }
+    e->S = splits;
+    e->min_chunk = min_chunk;
+    e->stages = stages;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;  // captured again at the next step
+    }
     return INFERNT_OK;
 }
 
