@@ -422,29 +422,74 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int D, int NST>
-__global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_t* kc, const uint16_t* vc,
-                                                   const int* positions, int nq, int nkv, int G, int max_seq, int S,
-                                                   int min_chunk, float scale, float* part) {
-    pdl_wait();
-    pdl_launch_dependents();
+// Arguments of the tensor-core attention.  Standalone: q [T][nq][D] FP32
+// with RoPE applied and caches already holding every position.  Fused
+// (qkv_part set): the Q|K|V projection's split partials part[s][t][(nq +
+// 2 nkv) D]; the kernel sums them in split order, applies RoPE to q and k
+// (the table rope[pos][D / 2]) and appends the bf16 K and V rows at
+// positions[t] (what bt_qkv_finish does, bit for bit).  With S == 1 the
+// kernel writes attn (and attn_f32) itself; otherwise the split partials.
+struct BtAttnArgs {
+    const float* q;
+    const float* qkv_part;
+    int qkv_splits;
+    const float2* rope;
+    uint16_t* kc;
+    uint16_t* vc;
+    const int* positions;
+    int T, nq, nkv, G, max_seq, S, min_chunk;
+    float scale;
+    float* part;
+    uint16_t* attn;
+    float* attn_f32;
+    unsigned* err;
+};
+
+template <int D>
+constexpr int attn_extra_bytes() {
+    return 8 * D * 4 + 2 * D * 2;  // q of up to 8 heads (FP32), the new K and V rows (bf16)
+}
+
+template <int D, int NST, bool FUSED>
+__global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
     constexpr int NW = 4;
     constexpr int ROWB = D * 2, CH = ROWB / 16;           // bytes and 16-byte chunks per cache row
     constexpr int TILEB = kAttnTile * ROWB;              // one K (or V) tile
     constexpr int KC = D / 16, DB = D / 8;               // k-steps of the scores, d-blocks of the output
     extern __shared__ __align__(128) unsigned char att_smem[];
+    float* qs = reinterpret_cast<float*>(att_smem + attn_smem_bytes<D, NST>());   // [8][D]
+    uint16_t* newk = reinterpret_cast<uint16_t*>(qs + 8 * D);                     // [D]
+    uint16_t* newv = newk + D;                                                      // [D]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tig = lane & 3;
+    const int S = a.S, nkv = a.nkv, nq = a.nq, G = a.G, max_seq = a.max_seq;
     const int item = blockIdx.x;
     const int split = item % S, kvh = (item / S) % nkv, t = item / (S * nkv);
-    const int seq = positions[t] + 1;
+    // positions are final before the step's first kernel, and the cache rows
+    // below them were written by kernels that have completed: the tile
+    // copies may start before the projection this kernel depends on
+    const int pos = a.positions[t];
+    if (pos < 0 || pos >= max_seq) {
+        pdl_wait();
+        pdl_launch_dependents();
+        if (FUSED && tid == 0 && a.err) atomicOr(a.err, kErrPosition);
+        return;
+    }
+    const int seq = pos + 1;
     int chunk, active;
-    bt_chunk(seq, S, min_chunk, chunk, active);
-    if (split >= active || seq > max_seq) return;  // positions past the cache are not read
+    bt_chunk(seq, S, a.min_chunk, chunk, active);
+    if (split >= active) {
+        pdl_wait();
+        pdl_launch_dependents();
+        return;
+    }
     const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
+    const bool own_row = FUSED && split == active - 1;  // this split holds position pos
     const int ntiles = (c1 - c0 + kAttnTile - 1) / kAttnTile;
-    const unsigned char* kb = reinterpret_cast<const unsigned char*>(kc + ((size_t)t * nkv + kvh) * max_seq * D);
-    const unsigned char* vb = reinterpret_cast<const unsigned char*>(vc + ((size_t)t * nkv + kvh) * max_seq * D);
+    uint16_t* kcache = a.kc + ((size_t)t * nkv + kvh) * max_seq * D;
+    uint16_t* vcache = a.vc + ((size_t)t * nkv + kvh) * max_seq * D;
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(kcache);
+    const unsigned char* vb = reinterpret_cast<const unsigned char*>(vcache);
     const uint32_t ring = smem_addr(att_smem) + (uint32_t)warp * NST * 2 * TILEB;
 
     // this warp's tile i of the split -> stage i % NST (K at +0, V at +TILEB)
@@ -467,28 +512,65 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
     };
     const int my_tiles = ntiles > warp ? (ntiles - warp + NW - 1) / NW : 0;
 #pragma unroll
-    for (int i = 0; i < NST - 1; ++i) issue(i);
+    for (int i = 0; i < NST - 1; ++i) issue(i);  // row pos of a fused step is patched in below
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // queries of the group (and the new K / V rows) into shared memory
+    if (FUSED) {
+        const int N = (nq + 2 * nkv) * D, half = D / 2;
+        const size_t stride = (size_t)a.T * N;
+        const float* pr = a.qkv_part + (size_t)t * N;
+        const float2* rp = a.rope + (size_t)pos * half;
+        auto sum = [&](int col) {
+            float v = pr[col];
+            for (int s = 1; s < a.qkv_splits; ++s) v += pr[(size_t)s * stride + col];
+            return v;
+        };
+        for (int e = tid; e < G * half; e += 128) {
+            const int h = e / half, d = e % half, col = (kvh * G + h) * D + d;
+            float x = sum(col), y = sum(col + half);
+            rope_apply(x, y, rp[d]);
+            qs[h * D + d] = x;
+            qs[h * D + d + half] = y;
+        }
+        if (own_row) {
+            for (int d = tid; d < half; d += 128) {
+                const int col = (nq + kvh) * D + d;
+                float x = sum(col), y = sum(col + half);
+                rope_apply(x, y, rp[d]);
+                newk[d] = bf16_bits(x);
+                newk[d + half] = bf16_bits(y);
+            }
+            for (int d = tid; d < D; d += 128) newv[d] = bf16_bits(sum((nq + nkv + kvh) * D + d));
+        }
+        __syncthreads();
+        if (own_row && tid < 2 * CH) {
+            // the rows for later steps (16 bytes per thread)
+            const uint16_t* src = tid < CH ? newk : newv;
+            uint16_t* dst = (tid < CH ? kcache : vcache) + (size_t)pos * D;
+            const int c = tid % CH;
+            *reinterpret_cast<uint4*>(dst + 8 * c) = *reinterpret_cast<const uint4*>(src + 8 * c);
+        }
+    } else {
+        const float* qg = a.q + ((size_t)t * nq + (size_t)kvh * G) * D;
+        for (int e = tid; e < G * D; e += 128) qs[e] = qg[e];
+        __syncthreads();
+    }
 
     // query fragments: qa rows g / g + 8 = hi / mid terms of head g, ql row
     // g = its lo terms (rows g + 8 of the second operand are zero)
     uint32_t qa[KC][4], ql[KC][4];
-    {
-        const float* qh = q + ((size_t)t * nq + (size_t)kvh * G + g) * D;
 #pragma unroll
-        for (int k = 0; k < KC; ++k) {
-            float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
-            if (g < G) {
-                const float2 lo2 = *reinterpret_cast<const float2*>(qh + 16 * k + 2 * tig);
-                const float2 hi2 = *reinterpret_cast<const float2*>(qh + 16 * k + 2 * tig + 8);
-                x0 = lo2.x;
-                x1 = lo2.y;
-                x2 = hi2.x;
-                x3 = hi2.y;
-            }
-            split3_bf16x2(x0, x1, qa[k][0], qa[k][1], ql[k][0]);
-            split3_bf16x2(x2, x3, qa[k][2], qa[k][3], ql[k][2]);
-            ql[k][1] = ql[k][3] = 0u;
+    for (int k = 0; k < KC; ++k) {
+        float2 lo2 = make_float2(0.f, 0.f), hi2 = make_float2(0.f, 0.f);
+        if (g < G) {
+            lo2 = *reinterpret_cast<const float2*>(qs + g * D + 16 * k + 2 * tig);
+            hi2 = *reinterpret_cast<const float2*>(qs + g * D + 16 * k + 2 * tig + 8);
         }
+        split3_bf16x2(lo2.x, lo2.y, qa[k][0], qa[k][1], ql[k][0]);
+        split3_bf16x2(hi2.x, hi2.y, qa[k][2], qa[k][3], ql[k][2]);
+        ql[k][1] = ql[k][3] = 0u;
     }
     float m_run = -INFINITY, l_run = 0.0f;
     float acc[DB][4];
@@ -501,6 +583,18 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
         __syncwarp();
         const uint32_t kt = ring + (uint32_t)(i % NST) * 2 * TILEB, vt = kt + TILEB;
         const int p0 = c0 + (warp + NW * i) * kAttnTile;
+        if (own_row && pos < p0 + kAttnTile) {
+            // the new row replaces what the copy read at position pos
+            if (lane < 2 * CH) {
+                const int r = pos - p0, c = lane % CH;
+                const uint32_t dst = (lane < CH ? kt : vt) + (uint32_t)(r * ROWB + ((c ^ (r & 7)) << 4));
+                const uint4 v = *reinterpret_cast<const uint4*>((lane < CH ? newk : newv) + 8 * c);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y), "r"(v.z),
+                             "r"(v.w)
+                             : "memory");
+            }
+            __syncwarp();
+        }
         // scores: hi / mid terms in sc, lo terms in sl (two shorter MMA chains)
         float sc[4][4], sl[4][4];
 #pragma unroll
@@ -520,14 +614,14 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
                 mma_bf16_16816(sl[2 * jj + 1], ql[k], b2, b3);
             }
         // online softmax of head g over the tile (each quad holds one head)
-        float s[4][2], mx = -INFINITY;
+        float sv[4][2], mx = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int p = p0 + 8 * j + 2 * tig + e;
-                s[j][e] = p < c1 ? ((sc[j][e] + sc[j][e + 2]) + sl[j][e]) * scale : -INFINITY;
-                mx = fmaxf(mx, s[j][e]);
+                sv[j][e] = p < c1 ? ((sc[j][e] + sc[j][e + 2]) + sl[j][e]) * a.scale : -INFINITY;
+                mx = fmaxf(mx, sv[j][e]);
             }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -539,8 +633,8 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-                s[j][e] = expf(s[j][e] - m_new);
-                lsum += s[j][e];
+                sv[j][e] = expf(sv[j][e] - m_new);
+                lsum += sv[j][e];
             }
         l_run = l_run * alpha + lsum;
 #pragma unroll
@@ -551,8 +645,8 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
             uint32_t pa[4], pl[4];
-            split3_bf16x2(s[2 * kk][0], s[2 * kk][1], pa[0], pa[1], pl[0]);
-            split3_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1], pa[2], pa[3], pl[2]);
+            split3_bf16x2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1], pl[0]);
+            split3_bf16x2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3], pl[2]);
             pl[1] = pl[3] = 0u;
 #pragma unroll
             for (int b2 = 0; b2 < DB / 2; ++b2) {
@@ -590,20 +684,26 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const float* q, const uint16_
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * 8 + h]);
-        float L = 0.0f, a = 0.0f;
+        float L = 0.0f, acc_o = 0.0f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
             const float mw = wm[w * 8 + h];
             const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
             L = fmaf(wl[w * 8 + h], f, L);
-            a = fmaf(wo[((size_t)w * 8 + h) * D + d], f, a);
+            acc_o = fmaf(wo[((size_t)w * 8 + h) * D + d], f, acc_o);
         }
-        float* pp = part + ((((size_t)t * nkv + kvh) * S + split) * G + h) * (D + 2);
-        if (d == 0) {
-            pp[0] = M;
-            pp[1] = L;
+        if (S == 1) {
+            const size_t o = (size_t)t * nq * D + (size_t)kvh * G * D + e;
+            a.attn[o] = bf16_bits(acc_o / L);
+            if (a.attn_f32) a.attn_f32[o] = acc_o / L;
+        } else {
+            float* pp = a.part + ((((size_t)t * nkv + kvh) * S + split) * G + h) * (D + 2);
+            if (d == 0) {
+                pp[0] = M;
+                pp[1] = L;
+            }
+            pp[2 + d] = acc_o;
         }
-        pp[2 + d] = a;
     }
 }
 
@@ -776,11 +876,50 @@ int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act,
     return INFERNT_OK;
 }
 
+namespace {
+
+template <int D, int NST, bool FUSED>
+int launch_attn_mma(const BtAttnArgs& a, int items, cudaStream_t st) {
+    static bool raised = false;
+    constexpr int smem = attn_smem_bytes<D, NST>() + attn_extra_bytes<D>();
+    if (!raised) {
+        INFERNT_CUDA_TRY(
+            cudaFuncSetAttribute(bt_attn_mma<D, NST, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        raised = true;
+    }
+    INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<D, NST, FUSED>, dim3(items), dim3(128), (size_t)smem, st, a));
+    return INFERNT_OK;
+}
+
+template <bool FUSED>
+int attn_mma_dispatch(const BtAttnArgs& a, int D, int stages, cudaStream_t st) {
+    INFERNT_REQUIRE(stages >= 2 && stages <= (D == 64 ? 4 : 3), "batched attention: %d stages for head_dim %d", stages,
+                    D);
+    const int items = a.T * a.nkv * a.S;
+    if (D == 64) {
+        if (stages == 2) return launch_attn_mma<64, 2, FUSED>(a, items, st);
+        if (stages == 3) return launch_attn_mma<64, 3, FUSED>(a, items, st);
+        return launch_attn_mma<64, 4, FUSED>(a, items, st);
+    }
+    if (stages == 2) return launch_attn_mma<128, 2, FUSED>(a, items, st);
+    return launch_attn_mma<128, 3, FUSED>(a, items, st);
+}
+
+int attn_merge(const BtAttnArgs& a, int D, cudaStream_t st) {
+    if (a.S == 1) return INFERNT_OK;  // the partial kernel wrote the output
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(a.T * a.nkv), dim3(128), st, (const float*)a.part, a.positions,
+                                a.nq, a.nkv, D, a.S, a.min_chunk, a.attn, a.attn_f32));
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
+}  // namespace
+
 // Attention of every sequence: partials over `S` splits per (t, KV head),
-// each a chunk of at least min_chunk positions, then the merge.  D in {64,
-// 128}; groups of up to 8 query heads run on the tensor cores (bt_attn_mma,
-// `stages` cp.async stages per warp), groups of 16 (D = 64) on CUDA cores
-// (bt_attn_partial).
+// each a chunk of at least min_chunk positions, then the merge (none for S =
+// 1).  D in {64, 128}; groups of up to 8 query heads run on the tensor cores
+// (bt_attn_mma, `stages` cp.async stages per warp), groups of 16 (D = 64) on
+// CUDA cores (bt_attn_partial).
 int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
                         int nkv, int D, int max_seq, int S, int min_chunk, int stages, float* part, uint16_t* attn,
                         cudaStream_t st, float* attn_f32) {
@@ -788,51 +927,76 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
     INFERNT_REQUIRE(G >= 1 && G <= 16 && nq % nkv == 0, "batched attention: group size %d", G);
     INFERNT_REQUIRE(S >= 1 && min_chunk >= 1, "batched attention: splits %d, min_chunk %d", S, min_chunk);
     const float scale = 1.0f / sqrtf((float)D);
-    const int items = T * nkv * S;
+    BtAttnArgs a = {};
+    a.q = q;
+    a.kc = const_cast<uint16_t*>(kc);
+    a.vc = const_cast<uint16_t*>(vc);
+    a.positions = positions;
+    a.T = T;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.G = G;
+    a.max_seq = max_seq;
+    a.S = S;
+    a.min_chunk = min_chunk;
+    a.scale = scale;
+    a.part = part;
+    a.attn = attn;
+    a.attn_f32 = attn_f32;
     if (G <= 8 && (D == 64 || D == 128)) {
-        // tensor-core partials, `stages` shared-memory stages per warp
-        INFERNT_REQUIRE(stages >= 2 && stages <= (D == 64 ? 4 : 3), "batched attention: %d stages for head_dim %d",
-                        stages, D);
-#define BT_MMA(DV, NV)                                                                                               \
-    do {                                                                                                           \
-        static bool raised = false;                                                                                \
-        constexpr int smem = attn_smem_bytes<DV, NV>();                                                            \
-        if (!raised) {                                                                                             \
-            INFERNT_CUDA_TRY(                                                                                      \
-                cudaFuncSetAttribute(bt_attn_mma<DV, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));     \
-            raised = true;                                                                                         \
-        }                                                                                                          \
-        INFERNT_CUDA_TRY(launch_pdl_smem(bt_attn_mma<DV, NV>, dim3(items), dim3(128), (size_t)smem, st, q, kc, vc, \
-                                         positions, nq, nkv, G, max_seq, S, min_chunk, scale, part));              \
-    } while (0)
-        if (D == 64) {
-            if (stages == 2) BT_MMA(64, 2);
-            else if (stages == 3) BT_MMA(64, 3);
-            else BT_MMA(64, 4);
-        } else {
-            if (stages == 2) BT_MMA(128, 2);
-            else BT_MMA(128, 3);
-        }
-#undef BT_MMA
-    } else {
-#define BT_ATTN(DLV, GV)                                                                                            \
-    INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<DLV, GV>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv, \
-                                max_seq, S, min_chunk, scale, part))
-        if (D == 64 && G == 16) {
-            BT_ATTN(2, 16);
-        } else if (D == 64 || D == 128) {
-            return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1, 2, 4, 8, or 16 at head_dim 64)",
-                        G);
-        } else {
-            return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: head_dim %d (64 or 128)", D);
-        }
-#undef BT_ATTN
+        if (int s = attn_mma_dispatch<false>(a, D, stages, st)) return s;
+        INFERNT_CUDA_TRY(cudaGetLastError());
+        return attn_merge(a, D, st);
     }
+    if (!(D == 64 && G == 16)) {
+        if (D == 64 || D == 128)
+            return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: group size %d (1 to 8, or 16 at head_dim 64)", G);
+        return fail(INFERNT_ERR_UNSUPPORTED, "batched attention: head_dim %d (64 or 128)", D);
+    }
+    const int items = T * nkv * S;
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_partial<2, 16>, dim3(items), dim3(128), st, q, kc, vc, positions, nq, nkv,
+                                max_seq, S, min_chunk, scale, part));
     INFERNT_CUDA_TRY(cudaGetLastError());
-    INFERNT_CUDA_TRY(
-        launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, part, positions, nq, nkv, D, S, min_chunk, attn, attn_f32));
+    a.S = S;
+    // the CUDA-core partials always write partials: merge even for one split
+    INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(T * nkv), dim3(128), st, (const float*)part, positions, nq, nkv, D,
+                                S, min_chunk, attn, attn_f32));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
+}
+
+// The batched step's attention with the Q|K|V finishing folded in (groups of
+// up to 8 query heads): q and the new K / V rows from the projection's
+// partials, RoPE, the bf16 cache append, the partials (or, for S = 1, the
+// output).
+int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
+                              const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
+                              int stages, float* part, uint16_t* attn, unsigned* err, cudaStream_t st) {
+    const int G = nq / nkv;
+    INFERNT_REQUIRE(G >= 1 && G <= 8 && nq % nkv == 0 && (D == 64 || D == 128),
+                    "fused batched attention: group size %d, head_dim %d", G, D);
+    INFERNT_REQUIRE(S >= 1 && min_chunk >= 1 && qkv_splits >= 1, "fused batched attention: splits");
+    BtAttnArgs a = {};
+    a.qkv_part = qkv_part;
+    a.qkv_splits = qkv_splits;
+    a.rope = rope;
+    a.kc = kc;
+    a.vc = vc;
+    a.positions = positions;
+    a.T = T;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.G = G;
+    a.max_seq = max_seq;
+    a.S = S;
+    a.min_chunk = min_chunk;
+    a.scale = 1.0f / sqrtf((float)D);
+    a.part = part;
+    a.attn = attn;
+    a.err = err;
+    if (int s = attn_mma_dispatch<true>(a, D, stages, st)) return s;
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return attn_merge(a, D, st);
 }
 
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,

@@ -34,6 +34,9 @@ int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act,
 int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
                         int nkv, int D, int max_seq, int S, int min_chunk, int stages, float* part, uint16_t* attn,
                         cudaStream_t st, float* attn_f32 = nullptr);
+int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
+                              const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
+                              int stages, float* part, uint16_t* attn, unsigned* err, cudaStream_t st);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
                       float std_dev, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st);
@@ -229,12 +232,20 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
     for (int l = 0; l < L; ++l) {
         const auto& ly = e->layers[l];
         if (int s = bgemm_launch(ly.qkv, nqkv, H, e->xb, T, e->part, e->sp_qkv, e->err, st)) return s;
-        if (int s = bt_qkv_finish_launch(e->part, e->sp_qkv, T, nq, nkv, D, e->positions, e->rope, c.max_seq_len, e->q,
-                                         e->kc[l], e->vc[l], e->err, st))
-            return s;
-        if (int s = bt_attention_launch(e->q, e->kc[l], e->vc[l], e->positions, T, nq, nkv, D, c.max_seq_len, e->S,
-                                        e->min_chunk, e->stages, e->apart, e->attn, st))
-            return s;
+        if (nq / nkv <= 8) {
+            // Q|K|V finishing inside the tensor-core attention
+            if (int s = bt_attention_fused_launch(e->part, e->sp_qkv, e->rope, e->kc[l], e->vc[l], e->positions, T, nq,
+                                                  nkv, D, c.max_seq_len, e->S, e->min_chunk, e->stages, e->apart,
+                                                  e->attn, e->err, st))
+                return s;
+        } else {
+            if (int s = bt_qkv_finish_launch(e->part, e->sp_qkv, T, nq, nkv, D, e->positions, e->rope, c.max_seq_len,
+                                             e->q, e->kc[l], e->vc[l], e->err, st))
+                return s;
+            if (int s = bt_attention_launch(e->q, e->kc[l], e->vc[l], e->positions, T, nq, nkv, D, c.max_seq_len, e->S,
+                                            e->min_chunk, e->stages, e->apart, e->attn, st))
+                return s;
+        }
         if (int s = bgemm_launch(ly.o, H, qs, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
         if (int s = bt_resid_norm_launch(e->part, e->sp_o, T, H, e->h, ly.ffn_norm, eps, e->xb, st)) return s;
         if (int s = bgemm_launch(ly.gu, 2 * I, H, e->xb, T, e->part, e->sp_gu, e->err, st)) return s;
@@ -322,8 +333,10 @@ int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batc
     e->T = batch;
     int S = attn_splits;
     if (S <= 0) {
-        const int pairs = batch * cfg->num_key_value_heads;
-        S = (4 * infernt::sm_count() + pairs - 1) / pairs;
+        // one split (no merge) once the (sequence, KV head) pairs fill the
+        // SMs; otherwise about two CTAs per SM
+        const int pairs = batch * cfg->num_key_value_heads, sms = infernt::sm_count();
+        S = pairs >= sms ? 1 : (2 * sms + pairs - 1) / pairs;
         if (S > 64) S = 64;
     }
     e->S = S < 1 ? 1 : S;
