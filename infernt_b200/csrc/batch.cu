@@ -428,7 +428,9 @@ __device__ __forceinline__ void cp_async_wait() {
 // 2 nkv) D]; the kernel sums them in split order, applies RoPE to q and k
 // (the table rope[pos][D / 2]) and appends the bf16 K and V rows at
 // positions[t] (what bt_qkv_finish does, bit for bit).  With S == 1 the
-// kernel writes attn (and attn_f32) itself; otherwise the split partials.
+// kernel writes attn (and attn_f32) itself; otherwise the split partials,
+// and with tickets given the last split CTA of each (t, KV head) to finish
+// merges them (in split order, as bt_attn_merge) and leaves its ticket at 0.
 struct BtAttnArgs {
     const float* q;
     const float* qkv_part;
@@ -443,6 +445,7 @@ struct BtAttnArgs {
     uint16_t* attn;
     float* attn_f32;
     unsigned* err;
+    unsigned* tickets;  // [T][nkv] zeros, or NULL (S > 1: a separate merge launch)
 };
 
 template <int D>
@@ -470,19 +473,13 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
     // copies may start before the projection this kernel depends on
     const int pos = a.positions[t];
     if (pos < 0 || pos >= max_seq) {
-        pdl_wait();
-        pdl_launch_dependents();
         if (FUSED && tid == 0 && a.err) atomicOr(a.err, kErrPosition);
         return;
     }
     const int seq = pos + 1;
     int chunk, active;
     bt_chunk(seq, S, a.min_chunk, chunk, active);
-    if (split >= active) {
-        pdl_wait();
-        pdl_launch_dependents();
-        return;
-    }
+    if (split >= active) return;
     const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
     const bool own_row = FUSED && split == active - 1;  // this split holds position pos
     const int ntiles = (c1 - c0 + kAttnTile - 1) / kAttnTile;
@@ -514,7 +511,6 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
 #pragma unroll
     for (int i = 0; i < NST - 1; ++i) issue(i);  // row pos of a fused step is patched in below
     pdl_wait();
-    pdl_launch_dependents();
 
     // queries of the group (and the new K / V rows) into shared memory
     if (FUSED) {
@@ -522,27 +518,43 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
         const size_t stride = (size_t)a.T * N;
         const float* pr = a.qkv_part + (size_t)t * N;
         const float2* rp = a.rope + (size_t)pos * half;
-        auto sum = [&](int col) {
-            float v = pr[col];
-            for (int s = 1; s < a.qkv_splits; ++s) v += pr[(size_t)s * stride + col];
-            return v;
+        // the split partials of columns col and col + half: every split's
+        // value is loaded before the in-order sums (one round trip)
+        auto sum2 = [&](int col, float& x, float& y) {
+            float wx[kMaxSplits], wy[kMaxSplits];
+#pragma unroll
+            for (int s = 0; s < kMaxSplits; ++s)
+                if (s < a.qkv_splits) {
+                    wx[s] = pr[(size_t)s * stride + col];
+                    wy[s] = pr[(size_t)s * stride + col + half];
+                }
+            x = wx[0];
+            y = wy[0];
+#pragma unroll
+            for (int s = 1; s < kMaxSplits; ++s)
+                if (s < a.qkv_splits) {
+                    x += wx[s];
+                    y += wy[s];
+                }
         };
         for (int e = tid; e < G * half; e += 128) {
-            const int h = e / half, d = e % half, col = (kvh * G + h) * D + d;
-            float x = sum(col), y = sum(col + half);
+            const int h = e / half, d = e % half;
+            float x, y;
+            sum2((kvh * G + h) * D + d, x, y);
             rope_apply(x, y, rp[d]);
             qs[h * D + d] = x;
             qs[h * D + d + half] = y;
         }
-        if (own_row) {
-            for (int d = tid; d < half; d += 128) {
-                const int col = (nq + kvh) * D + d;
-                float x = sum(col), y = sum(col + half);
-                rope_apply(x, y, rp[d]);
-                newk[d] = bf16_bits(x);
-                newk[d + half] = bf16_bits(y);
-            }
-            for (int d = tid; d < D; d += 128) newv[d] = bf16_bits(sum((nq + nkv + kvh) * D + d));
+        if (own_row && tid < half) {
+            // thread d: k pair (d, d + half) with RoPE, v elements d and d + half
+            float x, y, u, w;
+            sum2((nq + kvh) * D + tid, x, y);
+            sum2((nq + nkv + kvh) * D + tid, u, w);
+            rope_apply(x, y, rp[tid]);
+            newk[tid] = bf16_bits(x);
+            newk[tid + half] = bf16_bits(y);
+            newv[tid] = bf16_bits(u);
+            newv[tid + half] = bf16_bits(w);
         }
         __syncthreads();
         if (own_row && tid < 2 * CH) {
@@ -662,6 +674,9 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
         __syncwarp();  // every lane has read the stage before it is refilled
     }
     cp_async_wait<0>();
+    // the next kernel's CTAs may start once every CTA is past its main loop
+    // (earlier, they would hold SM slots the second wave of this grid needs)
+    pdl_launch_dependents();
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     __syncthreads();  // the rings are reused for the merge
@@ -704,6 +719,36 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
             }
             pp[2 + d] = acc_o;
         }
+    }
+    if (S == 1 || !a.tickets) return;
+    // the last split of (t, kvh) to finish merges the active splits
+    __shared__ unsigned s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        unsigned* tk = a.tickets + (size_t)t * nkv + kvh;
+        const unsigned done = atomicAdd(tk, 1u) + 1u;
+        s_last = done == (unsigned)active;
+        if (s_last) *tk = 0u;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* pk = a.part + ((size_t)t * nkv + kvh) * S * G * (D + 2);
+    for (int e = tid; e < G * D; e += 128) {
+        const int h = e / D, d = e % D;
+        float M = -INFINITY;
+        for (int sp = 0; sp < active; ++sp) M = fmaxf(M, __ldcg(pk + ((size_t)sp * G + h) * (D + 2)));
+        float L = 0.0f, acc_o = 0.0f;
+        for (int sp = 0; sp < active; ++sp) {
+            const float* pp = pk + ((size_t)sp * G + h) * (D + 2);
+            const float w = expf(__ldcg(pp) - M);
+            L = fmaf(__ldcg(pp + 1), w, L);
+            acc_o = fmaf(__ldcg(pp + 2 + d), w, acc_o);
+        }
+        const size_t o = (size_t)t * nq * D + (size_t)kvh * G * D + e;
+        a.attn[o] = bf16_bits(acc_o / L);
+        if (a.attn_f32) a.attn_f32[o] = acc_o / L;
     }
 }
 
@@ -906,7 +951,7 @@ int attn_mma_dispatch(const BtAttnArgs& a, int D, int stages, cudaStream_t st) {
 }
 
 int attn_merge(const BtAttnArgs& a, int D, cudaStream_t st) {
-    if (a.S == 1) return INFERNT_OK;  // the partial kernel wrote the output
+    if (a.S == 1 || a.tickets) return INFERNT_OK;  // the partial kernel wrote the output
     INFERNT_CUDA_TRY(launch_pdl(bt_attn_merge, dim3(a.T * a.nkv), dim3(128), st, (const float*)a.part, a.positions,
                                 a.nq, a.nkv, D, a.S, a.min_chunk, a.attn, a.attn_f32));
     INFERNT_CUDA_TRY(cudaGetLastError());
@@ -967,15 +1012,17 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
 
 // The batched step's attention with the Q|K|V finishing folded in (groups of
 // up to 8 query heads): q and the new K / V rows from the projection's
-// partials, RoPE, the bf16 cache append, the partials (or, for S = 1, the
-// output).
+// partials, RoPE, the bf16 cache append, then the output (merged in-kernel
+// by the last split with tickets [T][nkv], else by a merge launch).
 int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
                               const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
-                              int stages, float* part, uint16_t* attn, unsigned* err, cudaStream_t st) {
+                              int stages, float* part, uint16_t* attn, unsigned* err, unsigned* tickets,
+                              cudaStream_t st) {
     const int G = nq / nkv;
     INFERNT_REQUIRE(G >= 1 && G <= 8 && nq % nkv == 0 && (D == 64 || D == 128),
                     "fused batched attention: group size %d, head_dim %d", G, D);
-    INFERNT_REQUIRE(S >= 1 && min_chunk >= 1 && qkv_splits >= 1, "fused batched attention: splits");
+    INFERNT_REQUIRE(S >= 1 && min_chunk >= 1 && qkv_splits >= 1 && qkv_splits <= kMaxSplits,
+                    "fused batched attention: splits %d, Q|K|V splits %d", S, qkv_splits);
     BtAttnArgs a = {};
     a.qkv_part = qkv_part;
     a.qkv_splits = qkv_splits;
@@ -994,6 +1041,7 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
     a.part = part;
     a.attn = attn;
     a.err = err;
+    a.tickets = tickets;
     if (int s = attn_mma_dispatch<true>(a, D, stages, st)) return s;
     INFERNT_CUDA_TRY(cudaGetLastError());
     return attn_merge(a, D, st);

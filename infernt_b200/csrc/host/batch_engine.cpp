@@ -22,6 +22,7 @@ namespace infernt {
 int bgemm_ctas_per_sm(int tp);
 int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part, int splits, unsigned* err,
                  cudaStream_t st);
+int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act, cudaStream_t st);
 int bt_rope_table_launch(float2* tab, int max_seq, int D, float theta, cudaStream_t st);
 int bt_embed_norm_launch(const float* emb, const int* tokens, int vocab, int T, int H, const float* norm_w, float eps,
                          float* h, uint16_t* xb, unsigned* err, cudaStream_t st);
@@ -30,13 +31,13 @@ int bt_resid_norm_launch(const float* part, int splits, int T, int H, float* h, 
 int bt_qkv_finish_launch(const float* part, int splits, int T, int nq, int nkv, int D, const int* positions,
                          const float2* rope, int max_seq, float* q, uint16_t* kc, uint16_t* vc, unsigned* err,
                          cudaStream_t st);
-int bt_swiglu_launch(const float* part, int splits, int T, int I, uint16_t* act, cudaStream_t st);
 int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, const int* positions, int T, int nq,
                         int nkv, int D, int max_seq, int S, int min_chunk, int stages, float* part, uint16_t* attn,
                         cudaStream_t st, float* attn_f32 = nullptr);
 int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
                               const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
-                              int stages, float* part, uint16_t* attn, unsigned* err, cudaStream_t st);
+                              int stages, float* part, uint16_t* attn, unsigned* err, unsigned* tickets,
+                              cudaStream_t st);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
                       float std_dev, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st);
@@ -69,6 +70,7 @@ struct infernt_batch_engine {
     float* q = nullptr;
     float* part = nullptr;
     float* apart = nullptr;
+    unsigned* tickets = nullptr;  // [T][nkv] split tickets of the attention (zero between launches)
     float2* rope = nullptr;
     std::vector<void*> bufs;
     cudaStream_t stream = nullptr;
@@ -210,6 +212,8 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     const int G = nq / nkv;
     if (int s = alloc(e, sizeof(float) * (size_t)T * nkv * e->S * G * (D + 2), reinterpret_cast<void**>(&e->apart)))
         return s;
+    if (int s = alloc(e, sizeof(unsigned) * (size_t)T * nkv, reinterpret_cast<void**>(&e->tickets))) return s;
+    INFERNT_CUDA_TRY(cudaMemsetAsync(e->tickets, 0, sizeof(unsigned) * (size_t)T * nkv, e->stream));
     if (int s = alloc(e, sizeof(float2) * (size_t)c.max_seq_len * (D / 2), reinterpret_cast<void**>(&e->rope)))
         return s;
     if (int s = infernt::bt_rope_table_launch(e->rope, c.max_seq_len, D, c.rope_theta, e->stream)) return s;
@@ -236,7 +240,7 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
             // Q|K|V finishing inside the tensor-core attention
             if (int s = bt_attention_fused_launch(e->part, e->sp_qkv, e->rope, e->kc[l], e->vc[l], e->positions, T, nq,
                                                   nkv, D, c.max_seq_len, e->S, e->min_chunk, e->stages, e->apart,
-                                                  e->attn, e->err, st))
+                                                  e->attn, e->err, e->tickets, st))
                 return s;
         } else {
             if (int s = bt_qkv_finish_launch(e->part, e->sp_qkv, T, nq, nkv, D, e->positions, e->rope, c.max_seq_len,
