@@ -781,21 +781,35 @@ __global__ void bt_attn_merge(const float* part, const int* positions, int nq, i
 }
 
 // Greedy next token of sequence t (lowest index among equal maxima;
-// cuda/sampling.cu:3-40), then position + 1.
-__global__ void bt_argmax(const float* logits, int V, int* tokens, int* positions, int* hist) {
+// cuda/sampling.cu:3-40), then position + 1.  Grid (kArgChunks, T): CTA
+// (c, t) reduces chunk c of the vocabulary (every thread's float4 loads in
+// flight at once) to a candidate; the last chunk CTA of t to finish (split
+// ticket, left at 0) combines the candidates in chunk order.
+constexpr int kArgChunks = 8;
+
+__global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int* tokens, int* positions, int* hist,
+                                                 float* cand_v, int* cand_i, unsigned* tickets) {
     pdl_wait();  // the previous kernel of the step has completed
     pdl_launch_dependents();
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const int t = blockIdx.x, tid = threadIdx.x;
-    const float* lt = logits + (size_t)t * V;
+    __shared__ float bv[8];
+    __shared__ int bi[8];
+    const int chunk = blockIdx.x, t = blockIdx.y, tid = threadIdx.x;
+    const int n4 = V / 4;
+    const int c0 = (int)((long long)n4 * chunk / kArgChunks), c1 = (int)((long long)n4 * (chunk + 1) / kArgChunks);
+    const float4* lt = reinterpret_cast<const float4*>(logits + (size_t)t * V);
     float v = -INFINITY;
-    int id = 0;
-    for (int i = tid; i < V; i += blockDim.x)
-        if (argmax_better(lt[i], i, v, id)) {
-            v = lt[i];
-            id = i;
-        }
+    int id = 4 * c0;  // equal to the old single-pass start (index 0) once chunks combine in order
+#pragma unroll 4
+    for (int i = c0 + tid; i < c1; i += 256) {
+        const float4 x = lt[i];
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (argmax_better(xs[e], 4 * i + e, v, id)) {
+                v = xs[e];
+                id = 4 * i + e;
+            }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, v, o);
@@ -810,16 +824,32 @@ __global__ void bt_argmax(const float* logits, int V, int* tokens, int* position
         bi[tid >> 5] = id;
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int w = 1; w < (int)blockDim.x / 32; ++w)
-            if (argmax_better(bv[w], bi[w], v, id)) {
-                v = bv[w];
-                id = bi[w];
-            }
-        tokens[t] = id;
-        if (hist) hist[t] = id;
-        positions[t] += 1;
+    if (tid != 0) return;
+    for (int w = 1; w < 8; ++w)
+        if (argmax_better(bv[w], bi[w], v, id)) {
+            v = bv[w];
+            id = bi[w];
+        }
+    cand_v[(size_t)t * kArgChunks + chunk] = v;
+    cand_i[(size_t)t * kArgChunks + chunk] = id;
+    __threadfence();
+    const unsigned done = atomicAdd(tickets + t, 1u) + 1u;
+    if (done != (unsigned)kArgChunks) return;
+    tickets[t] = 0u;
+    __threadfence();
+    v = __ldcg(cand_v + (size_t)t * kArgChunks);
+    id = __ldcg(cand_i + (size_t)t * kArgChunks);
+    for (int c = 1; c < kArgChunks; ++c) {
+        const float cv = __ldcg(cand_v + (size_t)t * kArgChunks + c);
+        const int ci = __ldcg(cand_i + (size_t)t * kArgChunks + c);
+        if (argmax_better(cv, ci, v, id)) {
+            v = cv;
+            id = ci;
+        }
     }
+    tokens[t] = id;
+    if (hist) hist[t] = id;
+    positions[t] += 1;
 }
 
 // Rows [0, n_pos) of sequence `seq`'s cache of one layer, [T][Nkv][max_seq][D]
@@ -1055,8 +1085,11 @@ int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq,
     return INFERNT_OK;
 }
 
-int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st) {
-    INFERNT_CUDA_TRY(launch_pdl(bt_argmax, dim3(T), dim3(256), st, logits, V, tokens, positions, hist));
+int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
+                     int* cand_i, unsigned* tickets, cudaStream_t st) {
+    INFERNT_REQUIRE(V % 4 == 0 && V / 4 >= kArgChunks, "batched argmax: vocabulary %d", V);
+    INFERNT_CUDA_TRY(launch_pdl(bt_argmax, dim3(kArgChunks, T), dim3(256), st, logits, V, tokens, positions, hist,
+                                cand_v, cand_i, tickets));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }

@@ -40,7 +40,8 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
                               cudaStream_t st);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
                       float std_dev, cudaStream_t st);
-int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, cudaStream_t st);
+int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
+                     int* cand_i, unsigned* tickets, cudaStream_t st);
 }  // namespace infernt
 
 struct infernt_batch_engine {
@@ -70,7 +71,10 @@ struct infernt_batch_engine {
     float* q = nullptr;
     float* part = nullptr;
     float* apart = nullptr;
-    unsigned* tickets = nullptr;  // [T][nkv] split tickets of the attention (zero between launches)
+    unsigned* tickets = nullptr;     // [T][nkv] split tickets of the attention (zero between launches)
+    unsigned* am_tickets = nullptr;  // [T] chunk tickets of the argmax
+    float* cand_v = nullptr;         // [T][8] argmax candidates per vocabulary chunk
+    int* cand_i = nullptr;
     float2* rope = nullptr;
     std::vector<void*> bufs;
     cudaStream_t stream = nullptr;
@@ -214,6 +218,10 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         return s;
     if (int s = alloc(e, sizeof(unsigned) * (size_t)T * nkv, reinterpret_cast<void**>(&e->tickets))) return s;
     INFERNT_CUDA_TRY(cudaMemsetAsync(e->tickets, 0, sizeof(unsigned) * (size_t)T * nkv, e->stream));
+    if (int s = alloc(e, sizeof(unsigned) * T, reinterpret_cast<void**>(&e->am_tickets))) return s;
+    INFERNT_CUDA_TRY(cudaMemsetAsync(e->am_tickets, 0, sizeof(unsigned) * T, e->stream));
+    if (int s = alloc(e, sizeof(float) * T * 8, reinterpret_cast<void**>(&e->cand_v))) return s;
+    if (int s = alloc(e, sizeof(int) * T * 8, reinterpret_cast<void**>(&e->cand_i))) return s;
     if (int s = alloc(e, sizeof(float2) * (size_t)c.max_seq_len * (D / 2), reinterpret_cast<void**>(&e->rope)))
         return s;
     if (int s = infernt::bt_rope_table_launch(e->rope, c.max_seq_len, D, c.rope_theta, e->stream)) return s;
@@ -260,7 +268,7 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
     }
     if (int s = bgemm_launch(e->lm, V, H, e->xb, T, e->part, e->sp_lm, e->err, st)) return s;
     // the LM head runs unsplit: part[0] holds the logits
-    return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, st);
+    return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, e->cand_v, e->cand_i, e->am_tickets, st);
 }
 
 int ensure_graph(infernt_batch_engine* e) {
