@@ -33,7 +33,7 @@ __device__ __forceinline__ uint16_t bf16_bits(float v) {
 }
 __device__ __forceinline__ float bf16_float(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
-constexpr int kMaxSplits = 16;  // K splits of a batched projection (bgemm partials)
+constexpr int kMaxSplits = 8;   // K splits of a batched projection (bgemm partials)
 
 // Sum over the splits of part[s][t][off .. off + 3] (in split order): every
 // split's 16 bytes are loaded first, so a thread waits one round trip, not

@@ -109,14 +109,14 @@ int alloc(infernt_batch_engine* e, size_t bytes, void** out) {
 // stages each.  The busiest SM streams ceil(ctas / sms) CTAs' stages, and
 // every wave of resident CTAs adds a fixed cost (pipeline fill, epilogue) of
 // about two stages; the split count with the least such cost wins (ties go
-// to fewer partials).  At most 16 splits: the finishing kernels add the
-// partials in one round of loads.
+// to fewer partials).  At most 8 splits: the finishing kernels add the
+// partials in one round of loads (fewer registers than 16).
 int pick_splits(int N, int K, int T) {
     const int tiles = N / 128, nk = K / 64, sms = infernt::sm_count();
     const int slots = sms * infernt::bgemm_ctas_per_sm((T + 15) / 16 * 16);
     int best = 1;
     long best_cost = -1;
-    for (int s = 1; s <= 16 && s <= nk; ++s) {
+    for (int s = 1; s <= 8 && s <= nk; ++s) {
         const long ctas = (long)tiles * s;
         const long cost = (ctas + sms - 1) / sms * ((nk + s - 1) / s) + 2 * ((ctas + slots - 1) / slots);
         if (best_cost < 0 || cost < best_cost) {
