@@ -10,7 +10,14 @@ weights.
 Launch order on the device: `--prompt` single-step launches (the prompt),
 then one warm-up chain and one measured chain of `--steps` steps, so a
 profiler that skips `--prompt + 1` launches of the decode kernel captures
-the measured chain."""
+the measured chain.
+
+    python -m infernt_b200.profile_case --batched 64 --layers 2
+
+runs the batched engine instead (bf16, `--batched` sequences with contexts
+uniform in [512, 2048], numpy seed 1234, seeded KV rows): `--steps` timed
+steps, then one more step between cudaProfilerStart and cudaProfilerStop,
+for a profiler started with `--profile-from-start off`."""
 import argparse
 import sys
 
@@ -25,7 +32,10 @@ def main(argv=None):
     ap.add_argument("--bf16", action="store_true", help="bf16 weights (FP32 activations)")
     ap.add_argument("--shape", choices=["tinyllama", "llama3-8b"], default="tinyllama")
     ap.add_argument("--vocab", type=int, default=0, help="vocabulary size (0: the shape's own)")
+    ap.add_argument("--batched", type=int, default=0, help="sequences of a batched-engine run (0: b=1 decode)")
     args = ap.parse_args(argv)
+    if args.batched:
+        return batched(args)
     base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B.with_(max_seq_len=1024)
     cfg = base.with_(num_layers=args.layers)
     if args.vocab:
@@ -42,6 +52,35 @@ def main(argv=None):
     print("layers=%d steps=%d mode=%d: %.4f ms/step, %.0f tok/s, weights %.3f GB -> %.1f GB/s"
           % (args.layers, args.steps, eng.mode, ms / args.steps, args.steps * 1e3 / ms, wbytes / 1e9,
              wbytes / (ms / args.steps / 1e3) / 1e9))
+    eng.close()
+    return 0
+
+
+def batched(args):
+    import numpy as np
+    import torch
+    T = args.batched
+    base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B
+    cfg = base.with_(num_layers=args.layers, weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + 2 * args.steps + 8)
+    if args.vocab:
+        cfg = cfg.with_(vocab_size=args.vocab)
+    eng = ib.BatchEngine(cfg, T, seed=0)
+    ctx = np.random.default_rng(1234).integers(512, 2049, size=T)
+    for b in range(T):
+        eng.fill_kv(b, 1000 + b, int(ctx[b]))
+    tokens = [5 + b for b in range(T)]
+    pos = [int(c) for c in ctx]
+    toks, _ = eng.decode(tokens, pos, args.steps)
+    tokens, pos = [int(t) for t in toks[-1]], [p + args.steps for p in pos]
+    toks, ms = eng.decode(tokens, pos, args.steps)
+    tokens, pos = [int(t) for t in toks[-1]], [p + args.steps for p in pos]
+    print("batched T=%d layers=%d: %.4f ms/step, %.0f tok/s, splits %s"
+          % (T, args.layers, ms / args.steps, T * args.steps * 1e3 / ms, eng.splits()))
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    eng.step(tokens, pos)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
     eng.close()
     return 0
 
