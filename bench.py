@@ -527,9 +527,11 @@ def run_llama8b_tp(args):
         print(json.dumps(result), flush=True)
 
 
-def run_batched(args):
+def run_batched(args, longctx=False):
     """TinyLlama-shaped bf16 decode of 64 concurrent sequences (contexts
-    uniform in [512, 2048], seeded), data-parallel over the torchrun ranks:
+    uniform in [512, 2048], seeded), data-parallel over the torchrun ranks;
+    with longctx, the Llama-3-8B shape (bf16) with 16 sequences of 32768
+    positions each, the KV caches seeded instead of prefilled:
     rank r decodes sequences [64 r / N, 64 (r + 1) / N) with its own weight
     replica, no collective on the data path.  The projections run on the
     tensor cores (tcgen05), the KV caches are bf16.  Each sequence's first
@@ -547,14 +549,18 @@ def run_batched(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    n_seq, seed = 64, 0
-    rng = np.random.default_rng(1234)
-    ctx = rng.integers(512, 2049, size=n_seq)
+    K, W = args.steps, args.warmup
+    if longctx:
+        n_seq, seed = 16, 1
+        ctx = np.full(n_seq, 32768)
+        cfg = ib.LLAMA3_8B.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=32768 + W + K + 16)
+    else:
+        n_seq, seed = 64, 0
+        ctx = np.random.default_rng(1234).integers(512, 2049, size=n_seq)
+        cfg = ib.TINYLLAMA.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + W + K + 16)
     lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
     mine = ctx[lo:hi]
     T = hi - lo
-    K, W = args.steps, args.warmup
-    cfg = ib.TINYLLAMA.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + W + K + 16)
     eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
     for b in range(T):
         eng.fill_kv(b, 1000 + lo + b, int(mine[b]))
@@ -594,14 +600,29 @@ def run_batched(args):
     achieved = bytes_gpu * K / (ms_max / 1e3) / 1e9
     flops = 2.0 * T * cfg.weight_params
     sp = eng.splits()
+    if longctx:
+        metric = "decode tok/s (Llama-3-8B shape, bf16 weights, 16 sequences at 32768 positions)"
+        data = ("synthetic: seeded weights N(0,0.02) seed 1, norms 1.0; every sequence's 32768 KV rows "
+                "seeded (the prefill is not run); seeded first tokens")
+        workload = "llama8b-bf16-16seq-ctx32768-dp%d" % world
+    else:
+        metric = "decode tok/s (TinyLlama-1.1B shape, bf16 weights, 64 concurrent sequences)"
+        data = ("synthetic: seeded weights N(0,0.02) seed 0, norms 1.0; per-sequence contexts uniform in "
+                "[512, 2048] (numpy seed 1234) with seeded KV rows; seeded first tokens")
+        workload = "tinyllama-bf16-64seq-dp%d" % world
+    # kernels of a step: embedding + norm, per layer Q|K|V projection, the
+    # attention (with the Q|K|V finishing), O, norm, gate/up, SwiGLU, down,
+    # norm; the LM head and the argmax (groups of 16 query heads add the
+    # Q|K|V finishing and the merge per layer)
+    per_layer = 8 if cfg.num_attention_heads // cfg.num_key_value_heads <= 8 else 10
     result = {
-        "metric": "decode tok/s (TinyLlama-1.1B shape, bf16 weights, 64 concurrent sequences)",
+        "metric": metric,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms_max / K, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 weights and projection inputs, f32 accumulation, bf16 KV",
-        "data": "synthetic: seeded weights N(0,0.02) seed 0, norms 1.0; per-sequence contexts uniform in "
-                "[512, 2048] (numpy seed 1234) with seeded KV rows; seeded first tokens",
-        "config": {"workload": "tinyllama-bf16-64seq-dp%d" % world, "sequences": n_seq, "per_gpu": T,
+        "data": data,
+        "gpu_launches": K * (per_layer * cfg.num_layers + 3),
+        "config": {"workload": workload, "sequences": n_seq, "per_gpu": T,
                    "contexts_mean": round(float(np.mean(ctx)), 1), "parallelism": "dp%d" % world,
                    "splits_qkv_o_gateup_down_lm_attn": sp,
                    "l2": "no flush: %.2f GB of weights + %.2f GB of KV per GPU per step"
@@ -629,11 +650,14 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx"],
+                    default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
                          "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
                          "tensor-parallel over the torchrun ranks; batched: 64 TinyLlama-shaped bf16 "
-                         "sequences on the tensor cores, data-parallel over the torchrun ranks")
+                         "sequences on the tensor cores, data-parallel over the torchrun ranks; "
+                         "longctx: 16 8B-shaped bf16 sequences at 32768 positions, decode only, "
+                         "data-parallel over the torchrun ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -644,6 +668,8 @@ def main():
         run_llama8b_tp(args)
     elif args.workload == "batched":
         run_batched(args)
+    elif args.workload == "longctx":
+        run_batched(args, longctx=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -89,6 +89,13 @@ def test_group_sizes(nq, nkv):
     check([0, 40, 97, 300], nq, nkv, 64, 3, 64, 3)
 
 
+@pytest.mark.parametrize("splits,stages", [(1, 2), (4, 3)])
+def test_long_contexts_8b_heads(splits, stages):
+    """The long-context decode layout: 32 query heads on 8 KV heads, D = 128,
+    contexts up to the 32768-position cache."""
+    check([32767, 20000, 5], 32, 8, 128, splits, 64, stages, max_seq=32768)
+
+
 def test_peaked_scores():
     """Queries scaled by 8: scores spread over about +-60, so the softmax is
     dominated by a few positions and the running maxima change often."""
