@@ -644,20 +644,147 @@ def run_batched(args, longctx=False):
         print(json.dumps(result), flush=True)
 
 
+def prefill_flops(cfg, n, start=0):
+    """Algorithmic FLOPs of prefilling n prompt tokens at positions [start,
+    start + n): every projection (2 per weight element per token), causal
+    attention (q.k and p.v: 4 Nq D per key, token at position p reads p + 1
+    keys) and the LM head of the last token."""
+    H, L, D, I = cfg.hidden_size, cfg.num_layers, cfg.head_dim, cfg.intermediate_size
+    nq, nkv, V = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.vocab_size
+    qs = nq * D
+    proj = L * ((qs + 2 * nkv * D) * H + H * qs + 2 * I * H + H * I)
+    keys = n * start + n * (n + 1) // 2
+    return 2.0 * n * proj + 4.0 * nq * D * keys * L + 2.0 * V * H, 2.0 * n * proj, 4.0 * nq * D * keys * L
+
+
+def run_prefill(args):
+    """Prompt prefill of the long-context configuration: Llama-3-8B shape,
+    bf16 weights, 16 sequences of 32768 seeded random prompt tokens each,
+    data-parallel over the torchrun ranks (rank r prefills sequences [16 r /
+    N, 16 (r + 1) / N)).  A step is the prefill of one whole prompt through
+    the batched engine (infernt_batch_engine_prefill: chunks of 4096 tokens,
+    tensor-core projections and causal attention, every K/V row written, the
+    last token's LM head and argmax); the rank's sequences are taken in turn.
+    value: prompt tokens/s of the whole job (max over ranks of the CUDA-event
+    time); roofline: algorithmic FLOPs over the time against the measured
+    sustained bf16 tensor peak, and the dominant kernel (the gate/up
+    projection of one chunk, infernt_pgemm_bf16) timed alone."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import numpy as np
+    import infernt_b200 as ib
+    import oracle as O
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    K, W = args.steps, args.warmup
+    n_seq, n_tok, chunk, seed = 16, 32768, 4096, 1
+    cfg = ib.LLAMA3_8B.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=n_tok + 64)
+    lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
+    T = hi - lo
+    eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
+    prompts = [np.asarray(O.prompt(n_tok, 1000 + lo + b, 3, cfg.vocab_size), dtype=np.int32) for b in range(T)]
+    for i in range(W):
+        eng.prefill(i % T, prompts[i % T], chunk=chunk)
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = 0.0
+    t0 = time.perf_counter()
+    first = []
+    for i in range(K):
+        nxt, _, m = eng.prefill(i % T, prompts[i % T], chunk=chunk)
+        ms += m
+        first.append(nxt)
+    wall_s = time.perf_counter() - t0
+    clocks = sampler.stop()
+    ms_max = max_over_ranks(torch, ms, "cuda")
+    wall_max = max_over_ranks(torch, wall_s * 1e3, "cuda") / 1e3
+    value = world * K * n_tok / (ms_max / 1e3)
+    flops, f_proj, f_attn = prefill_flops(cfg, n_tok)
+    achieved = flops * K / (ms_max / 1e3) / 1e12
+    peak_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(peak_path):
+        peak, src = float(json.load(open(peak_path))["bf16_tflops_sustained"]), "measured (sustained)"
+    else:
+        peak, src = 1400.0, "fallback (sustained)"
+    # the dominant kernel alone: the gate/up projection of one 4096-token chunk
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    g = torch.Generator(device="cuda").manual_seed(3)
+    Wg = (torch.randn(2 * I, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    X = torch.randn(chunk, H, device="cuda", generator=g).to(torch.bfloat16)
+    Y = torch.empty(chunk, 2 * I, device="cuda")
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        ib.call("infernt_pgemm_bf16", Wg.data_ptr(), 2 * I, H, X.data_ptr(), chunk, Y.data_ptr(), 2 * I, None,
+                st.cuda_stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    reps = 10
+    ev[0].record(st)
+    for _ in range(reps):
+        ib.call("infernt_pgemm_bf16", Wg.data_ptr(), 2 * I, H, X.data_ptr(), chunk, Y.data_ptr(), 2 * I, None,
+                st.cuda_stream)
+    ev[1].record(st)
+    torch.cuda.synchronize()
+    gemm_ms = ev[0].elapsed_time(ev[1]) / reps
+    gemm_tflops = 2.0 * chunk * 2 * I * H / (gemm_ms / 1e3) / 1e12
+    del Wg, X, Y
+    n_chunks = (n_tok + chunk - 1) // chunk
+    per_layer = 9
+    result = {
+        "metric": "prefill tok/s (Llama-3-8B shape, bf16 weights, 32768-token prompts)",
+        "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms_max / K, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 weights, projection inputs, queries and probabilities; f32 accumulation; bf16 KV",
+        "data": "synthetic: seeded weights N(0,0.02) seed 1, norms 1.0; seeded random prompts of 32768 token ids",
+        "gpu_launches": K * (n_chunks * (per_layer * cfg.num_layers + 1) + 2),
+        "config": {"workload": "llama8b-bf16-prefill-32768-16seq-dp%d" % world, "sequences": n_seq,
+                   "per_gpu": T, "prompt_tokens": n_tok, "chunk": chunk, "parallelism": "dp%d" % world,
+                   "step": "one whole prompt", "l2": "no flush: 15 GB of weights per chunk pass"},
+        "e2e": {"value": round(world * K * n_tok / wall_max, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * n_tok + 8, "d2h_bytes_per_step": 8,
+                "api": "infernt_batch_engine_prefill (C ABI): host prompt in, next token out"},
+        "roofline": {"bound": "tensor", "kernel": "whole prefill (pgemm tcgen05 projections + pf_attn)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_source": src,
+                     "flops_per_step": flops, "projection_flops": f_proj, "attention_flops": f_attn,
+                     "dominant_kernel": {"name": "pgemm_kernel (gate/up, 4096 x 28672 x 4096)",
+                                         "ms": round(gemm_ms, 4), "achieved": round(gemm_tflops, 1),
+                                         "frac": round(gemm_tflops / float(json.load(open(peak_path))["bf16_tflops"])
+                                                       if os.path.exists(peak_path) else gemm_tflops / 1590.0, 4),
+                                         "peak": "burst bf16"}},
+        "first_tokens": first[:4],
+        "clocks": clocks,
+    }
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx"],
+    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx", "prefill"],
                     default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
                          "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
                          "tensor-parallel over the torchrun ranks; batched: 64 TinyLlama-shaped bf16 "
                          "sequences on the tensor cores, data-parallel over the torchrun ranks; "
                          "longctx: 16 8B-shaped bf16 sequences at 32768 positions, decode only, "
-                         "data-parallel over the torchrun ranks")
+                         "data-parallel over the torchrun ranks; prefill: the 32768-token prompts of "
+                         "those sequences (one prompt per step), data-parallel over the torchrun ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -670,6 +797,8 @@ def main():
         run_batched(args)
     elif args.workload == "longctx":
         run_batched(args, longctx=True)
+    elif args.workload == "prefill":
+        run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

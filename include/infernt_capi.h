@@ -170,6 +170,28 @@ INFERNT_API int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, co
  * NULL): bit 0 set by the device if a wait timed out. */
 INFERNT_API int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, int T,
                                    float* partials, int splits, unsigned* err, void* stream);
+/* Prefill projection on the tensor cores (CublasWrapper::gemm with M = the
+ * prompt tokens of a chunk, gemm/cublas_wrapper.cu:21-40; the reference
+ * instead runs M = 1 per prompt token, src/engine.cpp:124-126): Y[t][n] =
+ * the FP32 sum over k of X[t][k] W[n][k] for X [T][K] and W [N][K] bf16,
+ * one accumulation over the whole K per element; Y rows ldy floats apart
+ * (columns [0, N) written).  N a multiple of 128, K a multiple of 64,
+ * T >= 1, ldy >= N, W and X 16-byte aligned.  err as infernt_bgemm_bf16. */
+INFERNT_API int infernt_pgemm_bf16(const void* W, int N, int K, const void* X, int T, float* Y,
+                                   int ldy, unsigned* err, void* stream);
+/* Causal attention of a prompt chunk (cuda/attention.cu:9-42 and
+ * cuda/softmax.cu:13-48 per query row): q [n_tokens][nq][D] bf16 with RoPE
+ * applied, the sequence's caches [nkv][max_seq][D] bf16 holding positions
+ * [0, start_pos + n_tokens); token t (position start_pos + t) of query head
+ * h attends to positions [0, start_pos + t] of KV head h / (nq / nkv);
+ * attn [n_tokens][nq][D] bf16.  Queries and probabilities enter the tensor
+ * cores as bf16 (FP32 scores, softmax and sums), so each output is within
+ * 2^-8 of the largest |V| of its head (bf16 probabilities, bf16 output).
+ * D in {64, 128}; nq / nkv in {1, 2, 4, 8}; all pointers 16-byte aligned
+ * device memory; asynchronous on `stream`. */
+INFERNT_API int infernt_prefill_attention(const void* q, const void* k_cache, const void* v_cache,
+                                          int n_tokens, int start_pos, int nq, int nkv,
+                                          int head_dim, int max_seq, void* attn, void* stream);
 
 /* ------------------------------------------------- the decode plan ---
  * One decoder of a LLaMA-family model over caller-owned weights and KV
@@ -283,6 +305,26 @@ INFERNT_API int infernt_batch_engine_decode(infernt_batch_engine* e, const int* 
                                             float* ms);
 /* The last step's logits [batch][vocab] (n = batch x vocab floats). */
 INFERNT_API int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, size_t n);
+/* Prompt prefill of sequence seq: tokens[0, n_tokens) (host array) at
+ * positions [start_pos, start_pos + n_tokens), in chunks of `chunk` tokens
+ * (0: 4096; at most 16384) that pass through every layer at once, replacing the
+ * reference's sequential single-token forwards (src/engine.cpp:124-126,
+ * the same arithmetic per token: architectures/llama/llama_layer.cpp:11-72).
+ * The projections run as dense tensor-core GEMMs (infernt_pgemm_bf16), the
+ * attention causally over the sequence's cache (infernt_prefill_attention);
+ * the sequence's K/V rows of every prompt position are written.  Then the LM
+ * head and greedy argmax of the last prompt token: *next_token (or NULL),
+ * its logits into logits_host [vocab] (or NULL), and *ms the device time
+ * of the prefill (or NULL).  Synchronous.  The first call (and a later call
+ * with a larger chunk) allocates the prefill scratch: about chunk x (hidden
+ * x 10 + max(Q|K|V rows, 2 x intermediate) x 4 + intermediate x 2) bytes. */
+INFERNT_API int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* tokens,
+                                             int n_tokens, int start_pos, int chunk, int* next_token,
+                                             float* logits_host, float* ms);
+/* Rows [0, n_pos) of sequence seq's K and V caches of one layer into host
+ * arrays [nkv][n_pos][head_dim] of bf16 bits (uint16). */
+INFERNT_API int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, int n_pos,
+                                             void* k_host, void* v_host);
 /* K splits of the Q|K|V, O, gate|up, down and LM-head projections and the
  * attention's KV splits (6 ints). */
 INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);

@@ -142,6 +142,10 @@ _SIGS = {
     "infernt_batch_engine_splits": (_I, [_P, _P]),
     "infernt_batch_engine_set_attention": (_I, [_P, _I, _I, _I]),
     "infernt_batch_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "infernt_batch_engine_prefill": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "infernt_batch_engine_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
+    "infernt_pgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
+    "infernt_prefill_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),
     "infernt_plan_destroy": (_I, [_P]),
@@ -376,6 +380,30 @@ class BatchEngine:
         out = np.empty((self.T, self.cfg.vocab_size), dtype=np.float32)
         call("infernt_batch_engine_logits", self._h, out.ctypes.data, out.size)
         return out
+
+    def prefill(self, seq: int, tokens, start_pos: int = 0, chunk: int = 0, want_logits: bool = False):
+        """Prompt prefill of sequence `seq` (infernt_batch_engine_prefill):
+        writes its K/V rows of positions [start_pos, start_pos + len(tokens))
+        and returns (greedy next token, last token's logits or None, device ms)."""
+        import numpy as np
+        toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        nxt = ctypes.c_int()
+        ms = ctypes.c_float()
+        logits = np.empty(self.cfg.vocab_size, dtype=np.float32) if want_logits else None
+        call("infernt_batch_engine_prefill", self._h, seq, toks.ctypes.data, toks.size, start_pos, chunk,
+             ctypes.byref(nxt), None if logits is None else logits.ctypes.data, ctypes.byref(ms))
+        return nxt.value, logits, ms.value
+
+    def read_kv(self, seq: int, layer: int, n_pos: int):
+        """Rows [0, n_pos) of the sequence's K and V caches of one layer as
+        float32 arrays [nkv][n_pos][head_dim] (exact bf16 values)."""
+        import numpy as np
+        shape = (self.cfg.num_key_value_heads, n_pos, self.cfg.head_dim)
+        k = np.zeros(shape, dtype=np.uint16)
+        v = np.zeros(shape, dtype=np.uint16)
+        call("infernt_batch_engine_read_kv", self._h, seq, layer, n_pos, k.ctypes.data, v.ctypes.data)
+        widen = lambda a: (a.astype(np.uint32) << 16).view(np.float32)
+        return widen(k), widen(v)
 
     def splits(self):
         out = (ctypes.c_int * 6)()

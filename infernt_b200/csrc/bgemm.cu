@@ -215,6 +215,128 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
 }
 
+// ---------------------------------------------------------------- prefill
+// Y[t][n] = sum_k X[t][k] W[n][k] for a prompt chunk of T tokens: a dense
+// contraction (2 x 128 x 256 FLOP per pair of 16 KB weight and 32 KB token
+// boxes), so every tile keeps its whole K range in tensor memory.  One CTA
+// per (128 weight rows, tp tokens) tile, tp = 256 (fewer for a short
+// chunk); the token tile varies fastest along the grid, so the CTAs that
+// share a weight tile run in the same wave and the weights cross HBM once
+// per chunk while the chunk's token tiles stay in L2.  The same roles as
+// bgemm_kernel: one thread drives TMA into a ring of stages, one issues
+// tcgen05.mma (M = 128, N = tp, K = 16 per instruction) and frees stages with
+// tcgen05.commit, then four warps read the accumulator with tcgen05.ld and
+// store FP32 rows of Y (ldy floats apart).
+constexpr int kPStagesMax = 8;
+
+struct PgemmArgs {
+    float* y;
+    unsigned* err;
+    int N, K, T, tp, tiles_t, ldy, stages;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    pgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, PgemmArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ uint64_t full[kPStagesMax], empty[kPStagesMax], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t stage_bytes = kTileW + (uint32_t)a.tp * kBK * 2;
+    const int tile_t = blockIdx.x % a.tiles_t, tile_n = blockIdx.x / a.tiles_t;
+    const int n0 = tile_n * kBM, t0 = tile_t * a.tp;
+    const int nk = a.K / kBK;
+    const int cols = a.tp <= 32 ? 32 : (a.tp <= 64 ? 64 : (a.tp <= 128 ? 128 : 256));
+
+    if (tid == 0) {
+        for (int s = 0; s < a.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        mbar_fence_init();
+        s_ok = 1;
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                     "r"(cols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+
+    bool ok = true;
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % a.stages;
+            if (i >= a.stages && !bg_wait(&empty[s], ((i / a.stages) - 1) & 1u, ok)) break;
+            unsigned char* st = smem + (size_t)s * stage_bytes;
+            mbar_arrive_expect_tx(&full[s], stage_bytes);
+            tma_load_2d(st, &tm_w, i * kBK, n0, &full[s]);
+            tma_load_2d(st + kTileW, &tm_x, i * kBK, t0, &full[s]);
+        }
+        if (!ok) atomicExch(&s_ok, 0);
+    } else if (warp == 1 && lane == 0) {
+        const uint32_t idesc = bf16_idesc(a.tp);
+        for (int i = 0; i < nk; ++i) {
+            const int s = i % a.stages;
+            if (!bg_wait(&full[s], (i / a.stages) & 1u, ok)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t wa = smem_addr(smem + (size_t)s * stage_bytes);
+            const uint64_t da = sw128_desc(wa), db = sw128_desc(wa + kTileW);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+                const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+                const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
+                    "l"(da + adv), "l"(db + adv), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_addr(&empty[s]))
+                         : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_addr(&done))
+                     : "memory");
+        if (!ok) atomicExch(&s_ok, 0);
+    }
+    __syncwarp();
+    bool eok = true;
+    bg_wait(&done, 0u, eok);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int n = n0 + warp * 32 + lane;
+    const int tn = a.T - t0 < a.tp ? a.T - t0 : a.tp;  // tokens of this tile
+    for (int c = 0; c < tn; c += 16) {
+        uint32_t r[16];
+        const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c;
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15}, [%16];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+            : "r"(addr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float* yc = a.y + (size_t)(t0 + c) * a.ldy + n;
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+            if (c + q < tn) yc[(size_t)q * a.ldy] = __uint_as_float(r[q]);
+    }
+    if (!eok) atomicExch(&s_ok, 0);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (!s_ok) {
+        if (tid == 0 && a.err) atomicOr(a.err, 1u);
+        const long long tw = clock64();
+        while (clock64() - tw < 20000000ll) __nanosleep(1000);
+    }
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols));
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link
 // against libcuda).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -310,9 +432,54 @@ int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part,
     return INFERNT_OK;
 }
 
+// Host side of one prefill projection: Y [T][ldy] FP32 (columns [0, N)) =
+// X [T][K] bf16 times W [N][K] bf16 transposed; any T >= 1.
+int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
+                 cudaStream_t st) {
+    INFERNT_REQUIRE(W && X && Y, "pgemm: null pointer");
+    INFERNT_REQUIRE(N > 0 && N % kBM == 0, "pgemm: N = %d must be a positive multiple of %d", N, kBM);
+    INFERNT_REQUIRE(K > 0 && K % kBK == 0, "pgemm: K = %d must be a positive multiple of %d", K, kBK);
+    INFERNT_REQUIRE(T >= 1, "pgemm: T = %d", T);
+    INFERNT_REQUIRE(ldy >= N, "pgemm: ldy = %d below N = %d", ldy, N);
+    INFERNT_REQUIRE(aligned16(W) && aligned16(X), "pgemm: W and X must be 16-byte aligned");
+    const int tp = T >= kMaxTokens ? kMaxTokens : (T + 15) / 16 * 16;
+    const int tiles_t = (T + tp - 1) / tp;
+    const long long ctas = (long long)(N / kBM) * tiles_t;
+    INFERNT_REQUIRE(ctas < (1ll << 31), "pgemm: %lld tiles", ctas);
+    const int per = kTileW + tp * kBK * 2;
+    int stages = (kSmemLimit - 1024) / per;
+    if (stages > kPStagesMax) stages = kPStagesMax;
+    CUtensorMap mw, mx;
+    if (int s = make_map(&mw, W, N, K, kBM)) return s;
+    if (int s = make_map(&mx, X, T, K, tp)) return s;
+    static bool raised = false;
+    if (!raised) {
+        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+        raised = true;
+    }
+    PgemmArgs args;
+    args.y = Y;
+    args.err = err;
+    args.N = N;
+    args.K = K;
+    args.T = T;
+    args.tp = tp;
+    args.tiles_t = tiles_t;
+    args.ldy = ldy;
+    args.stages = stages;
+    pgemm_kernel<<<(unsigned)ctas, kThreads, stages * per + 1024, st>>>(mw, mx, args);
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
 }  // namespace infernt
 
 extern "C" int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, int T, float* partials, int splits,
                                   unsigned* err, void* stream) {
     return infernt::bgemm_launch(W, N, K, X, T, partials, splits, err, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int infernt_pgemm_bf16(const void* W, int N, int K, const void* X, int T, float* Y, int ldy,
+                                  unsigned* err, void* stream) {
+    return infernt::pgemm_launch(W, N, K, X, T, Y, ldy, err, static_cast<cudaStream_t>(stream));
 }

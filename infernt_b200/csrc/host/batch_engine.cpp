@@ -42,6 +42,12 @@ int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq,
                       float std_dev, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
                      int* cand_i, unsigned* tickets, cudaStream_t st);
+int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
+                 cudaStream_t st);
+int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, const float2* rope, int max_seq,
+                       uint16_t* q, uint16_t* kc, uint16_t* vc, cudaStream_t st);
+int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
+                        int D, int max_seq, uint16_t* attn, cudaStream_t st);
 }  // namespace infernt
 
 struct infernt_batch_engine {
@@ -82,6 +88,21 @@ struct infernt_batch_engine {
     cudaEvent_t ev[2] = {nullptr, nullptr};
     int* hist = nullptr;  // tokens of chained steps (grown on demand)
     size_t hist_cap = 0;
+    // prefill scratch, allocated by the first prefill call for its chunk size
+    // (grown by a later call with a larger chunk): prompt tokens [max_seq],
+    // residual stream h [C][H] FP32, projection inputs x [C][max(H, Nq D, I)]
+    // bf16 (also the attention output and SwiGLU activations), queries q
+    // [C][Nq D] bf16, projection outputs y [C][max(Q|K|V, 2 I, H)] FP32 (at
+    // least the vocabulary: the last token's logits), (token, position) of the
+    // greedy pick and its argmax ticket
+    int pf_cap = 0;
+    int* pf_tokens = nullptr;
+    float* pf_h = nullptr;
+    uint16_t* pf_x = nullptr;
+    uint16_t* pf_q = nullptr;
+    float* pf_y = nullptr;
+    int* pf_tok = nullptr;
+    unsigned* pf_ticket = nullptr;
 
     ~infernt_batch_engine() {
         if (graph) cudaGraphExecDestroy(graph);
@@ -305,6 +326,90 @@ int check_err(infernt_batch_engine* e) {
     return INFERNT_OK;
 }
 
+void release(infernt_batch_engine* e, void* p) {
+    if (!p) return;
+    for (auto it = e->bufs.begin(); it != e->bufs.end(); ++it)
+        if (*it == p) {
+            e->bufs.erase(it);
+            break;
+        }
+    cudaFree(p);
+}
+
+// Prefill scratch for chunks of up to C tokens.
+int grow_prefill(infernt_batch_engine* e, int C) {
+    if (C <= e->pf_cap) return INFERNT_OK;
+    const infernt_llama_config& c = e->cfg;
+    const int H = c.hidden_size, I = c.intermediate_size, D = c.head_dim;
+    const int qs = c.num_attention_heads * D, nqkv = qs + 2 * c.num_key_value_heads * D;
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    release(e, e->pf_h);
+    release(e, e->pf_x);
+    release(e, e->pf_q);
+    release(e, e->pf_y);
+    e->pf_h = nullptr;
+    e->pf_x = e->pf_q = nullptr;
+    e->pf_y = nullptr;
+    e->pf_cap = 0;
+    if (!e->pf_tokens) {
+        if (int s = alloc(e, sizeof(int) * (size_t)c.max_seq_len, reinterpret_cast<void**>(&e->pf_tokens))) return s;
+        if (int s = alloc(e, 256, reinterpret_cast<void**>(&e->pf_tok))) return s;
+        if (int s = alloc(e, 256, reinterpret_cast<void**>(&e->pf_ticket))) return s;
+        INFERNT_CUDA_TRY(cudaMemsetAsync(e->pf_ticket, 0, 256, e->stream));
+    }
+    const size_t kx = (size_t)(H > qs ? (H > I ? H : I) : (qs > I ? qs : I));
+    size_t ny = (size_t)(nqkv > 2 * I ? nqkv : 2 * I);
+    if ((size_t)H > ny) ny = H;
+    size_t y_floats = (size_t)C * ny;
+    if (y_floats < (size_t)c.vocab_size) y_floats = c.vocab_size;
+    if (int s = alloc(e, sizeof(float) * (size_t)C * H, reinterpret_cast<void**>(&e->pf_h))) return s;
+    if (int s = alloc(e, (size_t)C * kx * 2, reinterpret_cast<void**>(&e->pf_x))) return s;
+    if (int s = alloc(e, (size_t)C * qs * 2, reinterpret_cast<void**>(&e->pf_q))) return s;
+    if (int s = alloc(e, sizeof(float) * y_floats, reinterpret_cast<void**>(&e->pf_y))) return s;
+    e->pf_cap = C;
+    return INFERNT_OK;
+}
+
+// Prefill of sequence `seq`: prompt tokens pf_tokens[0, n) at positions
+// [start, start + n) in chunks of C, every layer per chunk; then the LM head
+// and argmax of the last token (its logits in pf_y[0, V), the greedy token
+// in pf_tok[0]).  Launches only.
+int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cudaStream_t st) {
+    const infernt_llama_config& c = e->cfg;
+    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
+    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, S = c.max_seq_len;
+    const int qs = nq * D, nqkv = qs + 2 * nkv * D;
+    const float eps = c.rms_norm_eps;
+    const size_t seq_off = (size_t)seq * nkv * S * D;
+    using namespace infernt;
+    int m = 0;
+    for (int c0 = 0; c0 < n; c0 += C) {
+        m = n - c0 < C ? n - c0 : C;
+        const int p0 = start + c0;
+        if (int s = bt_embed_norm_launch(e->emb, e->pf_tokens + c0, V, m, H, e->layers[0].attn_norm, eps, e->pf_h,
+                                         e->pf_x, e->err, st))
+            return s;
+        for (int l = 0; l < L; ++l) {
+            const auto& ly = e->layers[l];
+            uint16_t* kc = e->kc[l] + seq_off;
+            uint16_t* vc = e->vc[l] + seq_off;
+            if (int s = pgemm_launch(ly.qkv, nqkv, H, e->pf_x, m, e->pf_y, nqkv, e->err, st)) return s;
+            if (int s = pf_qkv_rope_launch(e->pf_y, m, p0, nq, nkv, D, e->rope, S, e->pf_q, kc, vc, st)) return s;
+            if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, st)) return s;
+            if (int s = pgemm_launch(ly.o, H, qs, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
+            if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, ly.ffn_norm, eps, e->pf_x, st)) return s;
+            if (int s = pgemm_launch(ly.gu, 2 * I, H, e->pf_x, m, e->pf_y, 2 * I, e->err, st)) return s;
+            if (int s = bt_swiglu_launch(e->pf_y, 1, m, I, e->pf_x, st)) return s;
+            if (int s = pgemm_launch(ly.down, H, I, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
+            const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
+            if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, next_norm, eps, e->pf_x, st)) return s;
+        }
+    }
+    // the last token's final-normed row is row m - 1 of the last chunk
+    if (int s = bgemm_launch(e->lm, V, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
+    return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket, st);
+}
+
 int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions) {
     for (int t = 0; t < e->T; ++t) {
         INFERNT_REQUIRE(tokens[t] >= 0 && tokens[t] < e->cfg.vocab_size, "batch engine: token %d of sequence %d",
@@ -463,6 +568,60 @@ int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int 
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;  // captured again at the next step
+    }
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* tokens, int n_tokens, int start_pos,
+                                 int chunk, int* next_token, float* logits_host, float* ms) {
+    INFERNT_REQUIRE(e && tokens, "batch_engine_prefill: null argument");
+    const infernt_llama_config& c = e->cfg;
+    INFERNT_REQUIRE(seq >= 0 && seq < e->T, "batch_engine_prefill: sequence %d outside [0, %d)", seq, e->T);
+    INFERNT_REQUIRE(n_tokens >= 1 && start_pos >= 0 && (long long)start_pos + n_tokens <= c.max_seq_len,
+                    "batch_engine_prefill: %d tokens at position %d pass max_seq_len %d", n_tokens, start_pos,
+                    c.max_seq_len);
+    INFERNT_REQUIRE(chunk >= 0 && chunk <= 16384, "batch_engine_prefill: chunk %d outside [0, 16384]", chunk);
+    for (int i = 0; i < n_tokens; ++i)
+        INFERNT_REQUIRE(tokens[i] >= 0 && tokens[i] < c.vocab_size, "batch_engine_prefill: token %d at index %d",
+                        tokens[i], i);
+    int C = chunk > 0 ? chunk : 4096;
+    if (C > n_tokens) C = n_tokens;
+    if (int s = grow_prefill(e, C)) return s;
+    INFERNT_CUDA_TRY(
+        cudaMemcpyAsync(e->pf_tokens, tokens, sizeof(int) * (size_t)n_tokens, cudaMemcpyHostToDevice, e->stream));
+    const int tp[2] = {0, start_pos + n_tokens - 1};  // the argmax advances the position to start + n
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(e->pf_tok, tp, sizeof(tp), cudaMemcpyHostToDevice, e->stream));
+    INFERNT_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
+    if (int s = record_prefill(e, seq, n_tokens, start_pos, C, e->stream)) return s;
+    INFERNT_CUDA_TRY(cudaEventRecord(e->ev[1], e->stream));
+    int out[2] = {0, 0};
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(out, e->pf_tok, sizeof(out), cudaMemcpyDeviceToHost, e->stream));
+    if (logits_host)
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(logits_host, e->pf_y, sizeof(float) * (size_t)c.vocab_size,
+                                         cudaMemcpyDeviceToHost, e->stream));
+    const int s = check_err(e);
+    if (s) return s;
+    if (next_token) *next_token = out[0];
+    if (ms) cudaEventElapsedTime(ms, e->ev[0], e->ev[1]);
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, int n_pos, void* k_host,
+                                 void* v_host) {
+    INFERNT_REQUIRE(e && k_host && v_host, "batch_engine_read_kv: null argument");
+    const infernt_llama_config& c = e->cfg;
+    INFERNT_REQUIRE(seq >= 0 && seq < e->T && layer >= 0 && layer < c.num_layers && n_pos >= 0 &&
+                        n_pos <= c.max_seq_len,
+                    "batch_engine_read_kv: sequence %d, layer %d, %d positions", seq, layer, n_pos);
+    const int nkv = c.num_key_value_heads, D = c.head_dim, S = c.max_seq_len;
+    const size_t row = (size_t)n_pos * D * 2;
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    for (int h = 0; h < nkv; ++h) {
+        const size_t off = ((size_t)seq * nkv + h) * S * D;
+        INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(k_host) + h * row, e->kc[layer] + off, row,
+                                    cudaMemcpyDeviceToHost));
+        INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(v_host) + h * row, e->vc[layer] + off, row,
+                                    cudaMemcpyDeviceToHost));
     }
     return INFERNT_OK;
 }
