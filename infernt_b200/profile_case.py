@@ -17,7 +17,16 @@ the measured chain.
 runs the batched engine instead (bf16, `--batched` sequences with contexts
 uniform in [512, 2048], numpy seed 1234, seeded KV rows): `--steps` timed
 steps, then one more step between cudaProfilerStart and cudaProfilerStop,
-for a profiler started with `--profile-from-start off`."""
+for a profiler started with `--profile-from-start off`.
+
+    python -m infernt_b200.profile_case --prefill 4096 --start 28672 --layers 1 --shape llama3-8b
+
+runs the batched engine's prompt prefill (bf16, one sequence): the first
+`--start` KV rows seeded, then a prompt of `--prefill` seeded tokens at
+positions [start, start + prefill) in chunks of `--chunk`, twice (a warm-up
+prefill, then the measured one).  Per chunk and layer the launch order is
+pgemm (Q|K|V), pf_qkv_rope, pf_attn, pgemm (O), bt_resid_norm, pgemm
+(gate/up), bt_swiglu, pgemm (down), bt_resid_norm."""
 import argparse
 import sys
 
@@ -33,7 +42,12 @@ def main(argv=None):
     ap.add_argument("--shape", choices=["tinyllama", "llama3-8b"], default="tinyllama")
     ap.add_argument("--vocab", type=int, default=0, help="vocabulary size (0: the shape's own)")
     ap.add_argument("--batched", type=int, default=0, help="sequences of a batched-engine run (0: b=1 decode)")
+    ap.add_argument("--prefill", type=int, default=0, help="prompt tokens of a prefill run (0: decode)")
+    ap.add_argument("--start", type=int, default=0, help="prefill: seeded KV rows before the prompt")
+    ap.add_argument("--chunk", type=int, default=4096, help="prefill: tokens per chunk")
     args = ap.parse_args(argv)
+    if args.prefill:
+        return prefill(args)
     if args.batched:
         return batched(args)
     base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B.with_(max_seq_len=1024)
@@ -81,6 +95,24 @@ def batched(args):
     eng.step(tokens, pos)
     torch.cuda.synchronize()
     torch.cuda.cudart().cudaProfilerStop()
+    eng.close()
+    return 0
+
+
+def prefill(args):
+    import oracle as O
+    base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B
+    cfg = base.with_(num_layers=args.layers, weight_dtype=ib.DTYPE_BF16, max_seq_len=args.start + args.prefill + 8)
+    if args.vocab:
+        cfg = cfg.with_(vocab_size=args.vocab)
+    eng = ib.BatchEngine(cfg, 1, seed=1)
+    if args.start:
+        eng.fill_kv(0, 77, args.start)
+    prompt = O.prompt(args.prefill, 1000, 3, cfg.vocab_size)
+    eng.prefill(0, prompt, start_pos=args.start, chunk=args.chunk)
+    nxt, _, ms = eng.prefill(0, prompt, start_pos=args.start, chunk=args.chunk)
+    print("prefill tokens=%d start=%d layers=%d chunk=%d: %.3f ms, %.0f tok/s, next token %d"
+          % (args.prefill, args.start, args.layers, args.chunk, ms, args.prefill * 1e3 / ms, nxt))
     eng.close()
     return 0
 
