@@ -527,7 +527,7 @@ def run_llama8b_tp(args):
         print(json.dumps(result), flush=True)
 
 
-def run_batched(args, longctx=False):
+def run_batched(args, longctx=False, tp=False):
     """TinyLlama-shaped bf16 decode of 64 concurrent sequences (contexts
     uniform in [512, 2048], seeded), data-parallel over the torchrun ranks;
     with longctx, the Llama-3-8B shape (bf16) with 16 sequences of 32768
@@ -537,7 +537,10 @@ def run_batched(args, longctx=False):
     tensor cores (tcgen05), the KV caches are bf16.  Each sequence's first
     `context` KV rows are seeded values (the bench times decode, not the
     prompt).  value: tokens/s of the whole job; timed with CUDA events, max
-    over ranks."""
+    over ranks.  With tp (the long-context shape only), every rank holds all
+    16 sequences and 1/N of every layer (tensor parallelism: heads, FFN rows,
+    vocabulary rows; NCCL all-reduce of the O and down sums, all-gather of
+    the argmax candidates)."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -558,10 +561,18 @@ def run_batched(args, longctx=False):
         n_seq, seed = 64, 0
         ctx = np.random.default_rng(1234).integers(512, 2049, size=n_seq)
         cfg = ib.TINYLLAMA.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + W + K + 16)
-    lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
+    if tp:
+        lo, hi = 0, n_seq
+        nid = [ib.nccl_unique_id() if rank == 0 else None]
+        if world > 1:
+            dist.broadcast_object_list(nid, src=0)
+        eng = ib.BatchEngine(cfg, n_seq, seed=seed, std=STD, rank=rank, world=world, nccl_id=nid[0])
+    else:
+        lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
     mine = ctx[lo:hi]
     T = hi - lo
-    eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
+    if not tp:
+        eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
     for b in range(T):
         eng.fill_kv(b, 1000 + lo + b, int(mine[b]))
     tokens = [int(t) for t in O.prompt(n_seq, seed, 3, cfg.vocab_size)][lo:hi]
@@ -577,6 +588,7 @@ def run_batched(args, longctx=False):
     clocks = sampler.stop()
     ms_max = max_over_ranks(torch, ms, "cuda")
     value = n_seq * K / (ms_max / 1e3)
+    shards = world if tp else 1
     # end to end through the synchronous step entry point: host token and
     # position arrays in, next tokens out, every step
     tokens = [int(t) for t in toks[-1]]
@@ -592,19 +604,19 @@ def run_batched(args, longctx=False):
     # algorithmic bytes per GPU per step: bf16 weights, the embedding rows,
     # the K/V rows read (bf16) and the rows appended
     H, L, D, nkv = cfg.hidden_size, cfg.num_layers, cfg.head_dim, cfg.num_key_value_heads
-    wbytes = 2 * cfg.weight_params + T * H * 4
+    wbytes = 2 * cfg.weight_params / shards + T * H * 4
     ctx_mean = float(np.mean(mine)) + W + K / 2.0
-    kv_bytes = L * nkv * D * 2 * 2 * T * (ctx_mean + 1)
+    kv_bytes = L * nkv * D * 2 * 2 * T * (ctx_mean + 1) / shards
     bytes_gpu = wbytes + kv_bytes
     hbm, src = peaks()
     achieved = bytes_gpu * K / (ms_max / 1e3) / 1e9
-    flops = 2.0 * T * cfg.weight_params
+    flops = 2.0 * T * cfg.weight_params / shards
     sp = eng.splits()
     if longctx:
         metric = "decode tok/s (Llama-3-8B shape, bf16 weights, 16 sequences at 32768 positions)"
         data = ("synthetic: seeded weights N(0,0.02) seed 1, norms 1.0; every sequence's 32768 KV rows "
-                "seeded (the prefill is not run); seeded first tokens")
-        workload = "llama8b-bf16-16seq-ctx32768-dp%d" % world
+                "seeded (the prefill is timed by --workload prefill); seeded first tokens")
+        workload = "llama8b-bf16-16seq-ctx32768-%s%d" % ("tp" if tp else "dp", world)
     else:
         metric = "decode tok/s (TinyLlama-1.1B shape, bf16 weights, 64 concurrent sequences)"
         data = ("synthetic: seeded weights N(0,0.02) seed 0, norms 1.0; per-sequence contexts uniform in "
@@ -615,15 +627,20 @@ def run_batched(args, longctx=False):
     # norm; the LM head and the argmax (groups of 16 query heads add the
     # Q|K|V finishing and the merge per layer)
     per_layer = 8 if cfg.num_attention_heads // cfg.num_key_value_heads <= 8 else 10
+    if tp and world > 1:
+        per_layer += 2  # the split sums before the two all-reduces (NCCL's kernels not counted)
     result = {
         "metric": metric,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms_max / K, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "parallelism_detail": ("tensor parallel: heads, FFN rows and vocabulary rows split over the ranks, NCCL "
+                               "all-reduce after O and down" if tp else "data parallel: sequences split over ranks"),
         "dtype": "bf16 weights and projection inputs, f32 accumulation, bf16 KV",
         "data": data,
-        "gpu_launches": K * (per_layer * cfg.num_layers + 3),
+        "gpu_launches": K * (per_layer * cfg.num_layers + (4 if tp and world > 1 else 3)),
         "config": {"workload": workload, "sequences": n_seq, "per_gpu": T,
-                   "contexts_mean": round(float(np.mean(ctx)), 1), "parallelism": "dp%d" % world,
+                   "contexts_mean": round(float(np.mean(ctx)), 1),
+                   "parallelism": ("tp%d" if tp else "dp%d") % world,
                    "splits_qkv_o_gateup_down_lm_attn": sp,
                    "l2": "no flush: %.2f GB of weights + %.2f GB of KV per GPU per step"
                    % (wbytes / 1e9, kv_bytes / 1e9)},
@@ -776,14 +793,16 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx", "prefill"],
+    ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx", "longctx-tp",
+                                           "prefill"],
                     default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
                          "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
                          "tensor-parallel over the torchrun ranks; batched: 64 TinyLlama-shaped bf16 "
                          "sequences on the tensor cores, data-parallel over the torchrun ranks; "
                          "longctx: 16 8B-shaped bf16 sequences at 32768 positions, decode only, "
-                         "data-parallel over the torchrun ranks; prefill: the 32768-token prompts of "
+                         "data-parallel over the torchrun ranks; longctx-tp: the same 16 sequences, "
+                         "tensor-parallel over the torchrun ranks; prefill: the 32768-token prompts of "
                          "those sequences (one prompt per step), data-parallel over the torchrun ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -797,6 +816,8 @@ def main():
         run_batched(args)
     elif args.workload == "longctx":
         run_batched(args, longctx=True)
+    elif args.workload == "longctx-tp":
+        run_batched(args, longctx=True, tp=True)
     elif args.workload == "prefill":
         run_prefill(args)
     elif args.impl == "reference":

@@ -289,6 +289,32 @@ typedef struct infernt_batch_engine infernt_batch_engine;
 INFERNT_API int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch,
                                                    uint64_t seed, float std_dev, int attn_splits,
                                                    infernt_batch_engine** out);
+/* One rank of a tensor-parallel batched decoder over `world` GPUs, one
+ * process per GPU (the reference decodes on one GPU; this splits
+ * LlamaArchitecture::forward, architectures/llama/llama_model.cpp:45-65,
+ * Megatron-style): rank r holds query heads [r Nq/world, ..), KV heads
+ * [r Nkv/world, ..) with their caches, gate/up rows and down columns
+ * [r I/world, ..), the matching O columns and LM-head vocabulary rows
+ * [V r/world, V (r+1)/world), each the window of the seeded matrices a
+ * single-GPU engine of the same seed holds.  Per layer the O and down
+ * partial sums are all-reduced over the ranks (ncclAllReduce, FP32 [batch,
+ * hidden]) and the greedy token is agreed through an all-gather of every
+ * rank's (value, id) candidates (the lowest id wins among equal values);
+ * every rank then holds the same tokens.  nccl_id: the 128-byte
+ * ncclUniqueId from infernt_nccl_unique_id on one rank, passed to all (NULL
+ * for world = 1).  All ranks create, step and destroy together; the
+ * process's libnccl.so.2 is used (the one already loaded, else the system
+ * one).  Nkv, and the per-rank Q|K|V rows, O and down K must split into
+ * tensor-core tiles (rows multiples of 128, K multiples of 64).  Prefill is
+ * single-rank only. */
+INFERNT_API int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, uint64_t seed,
+                                               float std_dev, int attn_splits, int rank, int world,
+                                               const void* nccl_id, infernt_batch_engine** out);
+/* A new ncclUniqueId (n >= 128 bytes) for infernt_batch_engine_create_tp. */
+INFERNT_API int infernt_nccl_unique_id(void* out, size_t n);
+/* This rank's vocabulary rows [*v0, *v0 + *vl) (the whole vocabulary on one
+ * rank). */
+INFERNT_API int infernt_batch_engine_vocab_range(infernt_batch_engine* e, int* v0, int* vl);
 INFERNT_API int infernt_batch_engine_destroy(infernt_batch_engine* e);
 /* Rows [0, n_pos) of sequence seq's KV caches from the seeded KV streams
  * (the values infernt_fill_kv writes), rounded to bf16. */
@@ -303,7 +329,8 @@ INFERNT_API int infernt_batch_engine_step(infernt_batch_engine* e, const int* to
 INFERNT_API int infernt_batch_engine_decode(infernt_batch_engine* e, const int* tokens,
                                             const int* positions, int steps, int* tokens_out,
                                             float* ms);
-/* The last step's logits [batch][vocab] (n = batch x vocab floats). */
+/* The last step's logits [batch][vl] of this rank's vocabulary rows
+ * (infernt_batch_engine_vocab_range; n = batch x vl floats). */
 INFERNT_API int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, size_t n);
 /* Prompt prefill of sequence seq: tokens[0, n_tokens) (host array) at
  * positions [start_pos, start_pos + n_tokens), in chunks of `chunk` tokens

@@ -143,6 +143,9 @@ _SIGS = {
     "infernt_batch_engine_set_attention": (_I, [_P, _I, _I, _I]),
     "infernt_batch_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "infernt_batch_engine_prefill": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "infernt_batch_engine_create_tp": (_I, [_P, _I, ctypes.c_uint64, _F, _I, _I, _I, _P, _P]),
+    "infernt_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
+    "infernt_batch_engine_vocab_range": (_I, [_P, _P, _P]),
     "infernt_batch_engine_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
     "infernt_pgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_prefill_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -335,14 +338,25 @@ class BatchEngine:
     """T sequences decoding together on the tensor cores
     (infernt_batch_engine_*): seeded bf16 weights, bf16 KV caches."""
 
-    def __init__(self, cfg: ModelConfig, batch: int, seed: int = 0, std: float = 0.02, attn_splits: int = 0):
+    def __init__(self, cfg: ModelConfig, batch: int, seed: int = 0, std: float = 0.02, attn_splits: int = 0,
+                 rank: int = 0, world: int = 1, nccl_id: bytes = None):
+        """world > 1: one rank of a tensor-parallel engine
+        (infernt_batch_engine_create_tp); every rank passes the same nccl_id
+        (nccl_unique_id() on one rank) and all ranks call every method in the
+        same order."""
         self.cfg = cfg
         self.T = batch
         self._c = cfg.c()
         h = ctypes.c_void_p()
-        call("infernt_batch_engine_create_seeded", ctypes.byref(self._c), batch, seed, std, attn_splits,
-             ctypes.byref(h))
+        idbuf = None
+        if nccl_id is not None:
+            idbuf = ctypes.create_string_buffer(bytes(nccl_id), len(nccl_id))
+        call("infernt_batch_engine_create_tp", ctypes.byref(self._c), batch, seed, std, attn_splits, rank, world,
+             idbuf, ctypes.byref(h))
         self._h = h
+        v0, vl = ctypes.c_int(), ctypes.c_int()
+        call("infernt_batch_engine_vocab_range", self._h, ctypes.byref(v0), ctypes.byref(vl))
+        self.vocab_range = (v0.value, v0.value + vl.value)
 
     def close(self):
         if self._h:
@@ -376,8 +390,9 @@ class BatchEngine:
         return out.reshape(steps, self.T), ms.value
 
     def logits(self):
+        """The last step's logits [T][vocabulary rows of this rank]."""
         import numpy as np
-        out = np.empty((self.T, self.cfg.vocab_size), dtype=np.float32)
+        out = np.empty((self.T, self.vocab_range[1] - self.vocab_range[0]), dtype=np.float32)
         call("infernt_batch_engine_logits", self._h, out.ctypes.data, out.size)
         return out
 
@@ -414,6 +429,13 @@ class BatchEngine:
         """KV splits per (sequence, KV head), least positions per split and
         copy stages per warp of the attention; results do not change."""
         call("infernt_batch_engine_set_attention", self._h, splits, min_chunk, stages)
+
+
+def nccl_unique_id() -> bytes:
+    """A new ncclUniqueId (128 bytes) for BatchEngine(..., world > 1)."""
+    buf = ctypes.create_string_buffer(128)
+    call("infernt_nccl_unique_id", buf, 128)
+    return buf.raw
 
 
 class TPEngine:

@@ -803,18 +803,94 @@ __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int
 }
 
 // Rows [0, n_pos) of sequence `seq`'s cache of one layer, [T][Nkv][max_seq][D]
-// bf16: element (layer, h, p, d) of the seeded KV stream (include/infernt_seed.h),
-// the values infernt_fill_kv writes in FP32, rounded to bf16.
+// bf16: element (layer, h0 + h, p, d) of the seeded KV stream of a model with
+// nkv_all KV heads (include/infernt_seed.h; h0 > 0 on a tensor-parallel rank
+// holding heads [h0, h0 + nkv)), the values infernt_fill_kv writes in FP32,
+// rounded to bf16.
 __global__ void bt_fill_kv(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos,
-                           uint64_t key, float std_dev) {
+                           uint64_t key, float std_dev, int h0, int nkv_all) {
     const size_t n = (size_t)nkv * n_pos * D;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int d = (int)(i % D);
         const int p = (int)((i / D) % n_pos);
         const int h = (int)(i / ((size_t)D * n_pos));
-        const uint64_t gi = ((((uint64_t)layer * nkv + h) << 20) + (uint64_t)p) * (uint64_t)D + d;
+        const uint64_t gi = ((((uint64_t)layer * nkv_all + h0 + h) << 20) + (uint64_t)p) * (uint64_t)D + d;
         cache[(((size_t)seq * nkv + h) * max_seq + p) * D + d] = bf16_bits(infernt_normal_std(key, gi, std_dev));
     }
+}
+
+// ---------------------------------------------------- tensor parallelism
+// y[t][n] = sum of the partials part[s][t][n] in split order: a rank's share
+// of an O or down projection before the all-reduce over the ranks.
+__global__ void tp_sum_splits(const float* part, int splits, int T, int N, float* y) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t n4 = (size_t)T * N / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x)
+        reinterpret_cast<float4*>(y)[i] = sum_parts4(part, splits, (size_t)T * N, 4 * i);
+}
+
+// Greedy pick of sequence t over this rank's vocabulary rows: logits [T][ld]
+// (rows [0, vl) valid, vocabulary ids v0 + row) -> cand[t] = (value, id).
+// The lowest id wins among equal values; NaN never wins.
+__global__ void __launch_bounds__(256) tp_argmax_local(const float* logits, int ld, int vl, int v0, int2* cand) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ float bv[8];
+    __shared__ int bi[8];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float* row = logits + (size_t)t * ld;
+    float v = -INFINITY;
+    int id = v0;
+    for (int i = tid; i < vl; i += 256) {
+        const float x = row[i];
+        if (argmax_better(x, v0 + i, v, id)) {
+            v = x;
+            id = v0 + i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, id, o);
+        if (argmax_better(ov, oi, v, id)) {
+            v = ov;
+            id = oi;
+        }
+    }
+    if ((tid & 31) == 0) {
+        bv[tid >> 5] = v;
+        bi[tid >> 5] = id;
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    for (int w = 1; w < 8; ++w)
+        if (argmax_better(bv[w], bi[w], v, id)) {
+            v = bv[w];
+            id = bi[w];
+        }
+    cand[t] = make_int2(__float_as_int(v), id);
+}
+
+// Every rank's candidates cand_all [world][T] (gathered in rank order) ->
+// the sequence's token (the same on every rank) and its next position.
+__global__ void tp_argmax_pick(const int2* cand_all, int world, int T, int* tokens, int* positions) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float v = -INFINITY;
+    int id = 0x7fffffff;
+    for (int r = 0; r < world; ++r) {
+        const int2 c = cand_all[(size_t)r * T + t];
+        if (argmax_better(__int_as_float(c.x), c.y, v, id)) {
+            v = __int_as_float(c.x);
+            id = c.y;
+        }
+    }
+    if (id == 0x7fffffff) id = 0;  // every logit NaN
+    tokens[t] = id;
+    positions[t] += 1;
 }
 
 __global__ void bt_rope_table(float2* tab, int max_seq, int D, float theta) {
@@ -1028,10 +1104,30 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
 }
 
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
-                      float std_dev, cudaStream_t st) {
+                      float std_dev, int h0, int nkv_all, cudaStream_t st) {
     if (n_pos <= 0) return INFERNT_OK;
-    bt_fill_kv<<<256, 256, 0, st>>>(cache, seq, layer, nkv, max_seq, D, n_pos, key, std_dev);
+    bt_fill_kv<<<256, 256, 0, st>>>(cache, seq, layer, nkv, max_seq, D, n_pos, key, std_dev, h0, nkv_all);
     INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
+int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, cudaStream_t st) {
+    INFERNT_REQUIRE(N % 4 == 0 && splits >= 1 && splits <= kMaxSplits, "tensor-parallel sum: N %d, splits %d", N,
+                    splits);
+    const size_t n4 = (size_t)T * N / 4;
+    const int blocks = (int)((n4 + 255) / 256 < 1184 ? (n4 + 255) / 256 : 1184);
+    INFERNT_CUDA_TRY(launch_pdl(tp_sum_splits, dim3(blocks), dim3(256), st, part, splits, T, N, y));
+    return INFERNT_OK;
+}
+
+int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, cudaStream_t st) {
+    INFERNT_CUDA_TRY(launch_pdl(tp_argmax_local, dim3(T), dim3(256), st, logits, ld, vl, v0, cand));
+    return INFERNT_OK;
+}
+
+int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, int* positions, cudaStream_t st) {
+    INFERNT_CUDA_TRY(launch_pdl(tp_argmax_pick, dim3((T + 127) / 128), dim3(128), st, cand_all, world, T, tokens,
+                                positions));
     return INFERNT_OK;
 }
 

@@ -8,6 +8,8 @@
 // advances them, so chained steps need no host round trip.  Every
 // allocation happens at creation.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstring>
@@ -39,7 +41,7 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
                               int stages, float* part, uint16_t* attn, unsigned* err, unsigned* tickets,
                               cudaStream_t st);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
-                      float std_dev, cudaStream_t st);
+                      float std_dev, int h0, int nkv_all, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
                      int* cand_i, unsigned* tickets, cudaStream_t st);
 int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
@@ -48,7 +50,47 @@ int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, co
                        uint16_t* q, uint16_t* kc, uint16_t* vc, cudaStream_t st);
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
                         int D, int max_seq, uint16_t* attn, cudaStream_t st);
+int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, cudaStream_t st);
+int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, cudaStream_t st);
+int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, int* positions, cudaStream_t st);
 }  // namespace infernt
+
+namespace {
+
+// NCCL entry points of the process's libnccl.so.2, resolved at run time: the
+// one already loaded (by the framework that set up the ranks) when there is
+// one, so that the process holds a single NCCL; the library itself does not
+// link NCCL.
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_id = nullptr;
+    decltype(&ncclCommInitRank) init = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclGetErrorString) err_str = nullptr;
+};
+
+const NcclApi* nccl_api() {
+    static NcclApi api;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+        if (h) {
+            api.get_id = reinterpret_cast<decltype(api.get_id)>(dlsym(h, "ncclGetUniqueId"));
+            api.init = reinterpret_cast<decltype(api.init)>(dlsym(h, "ncclCommInitRank"));
+            api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+            api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+            api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
+            api.err_str = reinterpret_cast<decltype(api.err_str)>(dlsym(h, "ncclGetErrorString"));
+        }
+    }
+    const bool ok = api.get_id && api.init && api.all_reduce && api.all_gather && api.destroy && api.err_str;
+    return ok ? &api : nullptr;
+}
+
+}  // namespace
 
 struct infernt_batch_engine {
     infernt_llama_config cfg;
@@ -103,9 +145,26 @@ struct infernt_batch_engine {
     float* pf_y = nullptr;
     int* pf_tok = nullptr;
     unsigned* pf_ticket = nullptr;
+    // tensor parallelism over `world` ranks (one process per GPU): this rank
+    // holds query heads [rank nq_l, ..), KV heads [rank nkv_l, ..),
+    // intermediate rows [rank il, ..) and vocabulary rows [v0, v0 + vl) of the
+    // LM head (padded with zero rows to vlp, a multiple of 128); world = 1
+    // holds everything.  comm: the NCCL communicator of the ranks; ysum
+    // [T][H] a rank's O / down sums, all-reduced in place; cand [T] and
+    // cand_all [world][T] the (value, id) argmax candidates.
+    int rank = 0, world = 1;
+    int nq_l = 0, nkv_l = 0, il = 0, v0 = 0, vl = 0, vlp = 0;
+    void* comm = nullptr;
+    float* ysum = nullptr;
+    int2* cand = nullptr;
+    int2* cand_all = nullptr;
 
     ~infernt_batch_engine() {
-        if (graph) cudaGraphExecDestroy(graph);
+        if (graph) cudaGraphExecDestroy(graph);  // before the communicator its NCCL nodes use
+        if (comm) {
+            if (stream) cudaStreamSynchronize(stream);
+            if (const NcclApi* n = nccl_api()) n->destroy(static_cast<ncclComm_t>(comm));
+        }
         cudaFree(hist);
         if (ev[0]) cudaEventDestroy(ev[0]);
         if (ev[1]) cudaEventDestroy(ev[1]);
@@ -152,12 +211,24 @@ int fill_bf16(infernt_batch_engine* e, void* dst, size_t n, uint64_t seed, uint6
     return infernt_fill_normal(dst, n, INFERNT_DTYPE_BF16, seed, stream_id, std_dev, e->stream);
 }
 
+// The rank's shard of the seeded model (the values a single-GPU engine of
+// the same seed holds, as windows of the full matrices): Q|K|V rows of its
+// query and KV heads stacked, the matching O columns, its gate and up rows
+// stacked, the matching down columns, LM-head rows [v0, v0 + vl) (zero rows
+// up to vlp); the embedding and norms whole.
 int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     const infernt_llama_config& c = e->cfg;
     const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
-    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, T = e->T;
-    const int qs = nq * D, kvs = nkv * D, nqkv = qs + 2 * kvs;
+    const int T = e->T, r = e->rank;
+    const int nq = e->nq_l, nkv = e->nkv_l, il = e->il;
+    const int qs = c.num_attention_heads * D, qsl = nq * D, kvsl = nkv * D, nqkv = qsl + 2 * kvsl;
+    const int bf = INFERNT_DTYPE_BF16;
     INFERNT_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    auto window = [&](void* dst, int rows, int cols, int ld, long long src_ld, long long row0, long long col0,
+                      uint64_t stream_id) {
+        return infernt_fill_normal_window(dst, rows, cols, ld, (uint64_t)src_ld, (uint64_t)row0, (uint64_t)col0, bf,
+                                          seed, stream_id, std_dev, e->stream);
+    };
     void* p = nullptr;
     // embedding (FP32) and norms
     if (int s = alloc(e, sizeof(float) * (size_t)V * H, &p)) return s;
@@ -169,8 +240,9 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     if (int s = alloc(e, sizeof(float) * H, reinterpret_cast<void**>(&ones))) return s;
     if (int s = infernt_fill_const(ones, H, 1.0f, e->stream)) return s;
     e->final_norm = ones;  // every norm weight is 1.0 in the seeded model
-    if (int s = alloc(e, (size_t)V * H * 2, &p)) return s;
-    if (int s = fill_bf16(e, p, (size_t)V * H, seed, INFERNT_STREAM_LM_HEAD, std_dev)) return s;
+    if (int s = alloc(e, (size_t)e->vlp * H * 2, &p)) return s;
+    INFERNT_CUDA_TRY(cudaMemsetAsync(p, 0, (size_t)e->vlp * H * 2, e->stream));
+    if (int s = window(p, e->vl, H, H, H, e->v0, 0, INFERNT_STREAM_LM_HEAD)) return s;
     e->lm = p;
     for (int l = 0; l < L; ++l) {
         infernt_batch_engine::Layer ly;
@@ -178,24 +250,24 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         ly.ffn_norm = ones;
         char* qkv = nullptr;
         if (int s = alloc(e, (size_t)nqkv * H * 2, reinterpret_cast<void**>(&qkv))) return s;
-        if (int s = fill_bf16(e, qkv, (size_t)qs * H, seed, INFERNT_STREAM_LAYER(l, 0), std_dev)) return s;
-        if (int s = fill_bf16(e, qkv + (size_t)qs * H * 2, (size_t)kvs * H, seed, INFERNT_STREAM_LAYER(l, 1), std_dev))
+        if (int s = window(qkv, qsl, H, H, H, (long long)r * qsl, 0, INFERNT_STREAM_LAYER(l, 0))) return s;
+        if (int s = window(qkv + (size_t)qsl * H * 2, kvsl, H, H, H, (long long)r * kvsl, 0, INFERNT_STREAM_LAYER(l, 1)))
             return s;
-        if (int s = fill_bf16(e, qkv + (size_t)(qs + kvs) * H * 2, (size_t)kvs * H, seed, INFERNT_STREAM_LAYER(l, 2),
-                              std_dev))
+        if (int s = window(qkv + (size_t)(qsl + kvsl) * H * 2, kvsl, H, H, H, (long long)r * kvsl, 0,
+                           INFERNT_STREAM_LAYER(l, 2)))
             return s;
         ly.qkv = qkv;
-        if (int s = alloc(e, (size_t)H * qs * 2, &p)) return s;
-        if (int s = fill_bf16(e, p, (size_t)H * qs, seed, INFERNT_STREAM_LAYER(l, 3), std_dev)) return s;
+        if (int s = alloc(e, (size_t)H * qsl * 2, &p)) return s;
+        if (int s = window(p, H, qsl, qsl, qs, 0, (long long)r * qsl, INFERNT_STREAM_LAYER(l, 3))) return s;
         ly.o = p;
         char* gu = nullptr;
-        if (int s = alloc(e, (size_t)2 * I * H * 2, reinterpret_cast<void**>(&gu))) return s;
-        if (int s = fill_bf16(e, gu, (size_t)I * H, seed, INFERNT_STREAM_LAYER(l, 4), std_dev)) return s;
-        if (int s = fill_bf16(e, gu + (size_t)I * H * 2, (size_t)I * H, seed, INFERNT_STREAM_LAYER(l, 5), std_dev))
+        if (int s = alloc(e, (size_t)2 * il * H * 2, reinterpret_cast<void**>(&gu))) return s;
+        if (int s = window(gu, il, H, H, H, (long long)r * il, 0, INFERNT_STREAM_LAYER(l, 4))) return s;
+        if (int s = window(gu + (size_t)il * H * 2, il, H, H, H, (long long)r * il, 0, INFERNT_STREAM_LAYER(l, 5)))
             return s;
         ly.gu = gu;
-        if (int s = alloc(e, (size_t)H * I * 2, &p)) return s;
-        if (int s = fill_bf16(e, p, (size_t)H * I, seed, INFERNT_STREAM_LAYER(l, 6), std_dev)) return s;
+        if (int s = alloc(e, (size_t)H * il * 2, &p)) return s;
+        if (int s = window(p, H, il, il, I, 0, (long long)r * il, INFERNT_STREAM_LAYER(l, 6))) return s;
         ly.down = p;
         e->layers.push_back(ly);
         const size_t cache = (size_t)T * nkv * c.max_seq_len * D * 2;
@@ -209,9 +281,9 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         e->vc.push_back(static_cast<uint16_t*>(v));
     }
     e->sp_qkv = pick_splits(nqkv, H, T);
-    e->sp_o = pick_splits(H, qs, T);
-    e->sp_gu = pick_splits(2 * I, H, T);
-    e->sp_down = pick_splits(H, I, T);
+    e->sp_o = pick_splits(H, qsl, T);
+    e->sp_gu = pick_splits(2 * il, H, T);
+    e->sp_down = pick_splits(H, il, T);
     e->sp_lm = 1;  // the argmax reads whole logits
     size_t part = 0;
     auto need = [&](int sp, int N) {
@@ -220,19 +292,19 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     };
     need(e->sp_qkv, nqkv);
     need(e->sp_o, H);
-    need(e->sp_gu, 2 * I);
+    need(e->sp_gu, 2 * il);
     need(e->sp_down, H);
-    need(e->sp_lm, V);
-    const int kmax = H > qs ? (H > I ? H : I) : (qs > I ? qs : I);
+    need(e->sp_lm, e->vlp);
+    const int kmax = H > qsl ? (H > il ? H : il) : (qsl > il ? qsl : il);
     if (int s = alloc(e, sizeof(int) * T, reinterpret_cast<void**>(&e->tokens))) return s;
     if (int s = alloc(e, sizeof(int) * T, reinterpret_cast<void**>(&e->positions))) return s;
     if (int s = alloc(e, 256, reinterpret_cast<void**>(&e->err))) return s;
     INFERNT_CUDA_TRY(cudaMemsetAsync(e->err, 0, 256, e->stream));
     if (int s = alloc(e, sizeof(float) * (size_t)T * H, reinterpret_cast<void**>(&e->h))) return s;
     if (int s = alloc(e, (size_t)T * kmax * 2, reinterpret_cast<void**>(&e->xb))) return s;
-    if (int s = alloc(e, (size_t)T * qs * 2, reinterpret_cast<void**>(&e->attn))) return s;
-    if (int s = alloc(e, (size_t)T * I * 2, reinterpret_cast<void**>(&e->act))) return s;
-    if (int s = alloc(e, sizeof(float) * (size_t)T * qs, reinterpret_cast<void**>(&e->q))) return s;
+    if (int s = alloc(e, (size_t)T * qsl * 2, reinterpret_cast<void**>(&e->attn))) return s;
+    if (int s = alloc(e, (size_t)T * il * 2, reinterpret_cast<void**>(&e->act))) return s;
+    if (int s = alloc(e, sizeof(float) * (size_t)T * qsl, reinterpret_cast<void**>(&e->q))) return s;
     if (int s = alloc(e, sizeof(float) * part, reinterpret_cast<void**>(&e->part))) return s;
     const int G = nq / nkv;
     if (int s = alloc(e, sizeof(float) * (size_t)T * nkv * e->S * G * (D + 2), reinterpret_cast<void**>(&e->apart)))
@@ -243,6 +315,11 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     INFERNT_CUDA_TRY(cudaMemsetAsync(e->am_tickets, 0, sizeof(unsigned) * T, e->stream));
     if (int s = alloc(e, sizeof(float) * T * 8, reinterpret_cast<void**>(&e->cand_v))) return s;
     if (int s = alloc(e, sizeof(int) * T * 8, reinterpret_cast<void**>(&e->cand_i))) return s;
+    if (e->world > 1) {
+        if (int s = alloc(e, sizeof(float) * (size_t)T * H, reinterpret_cast<void**>(&e->ysum))) return s;
+        if (int s = alloc(e, sizeof(int2) * (size_t)T, reinterpret_cast<void**>(&e->cand))) return s;
+        if (int s = alloc(e, sizeof(int2) * (size_t)T * e->world, reinterpret_cast<void**>(&e->cand_all))) return s;
+    }
     if (int s = alloc(e, sizeof(float2) * (size_t)c.max_seq_len * (D / 2), reinterpret_cast<void**>(&e->rope)))
         return s;
     if (int s = infernt::bt_rope_table_launch(e->rope, c.max_seq_len, D, c.rope_theta, e->stream)) return s;
@@ -252,12 +329,32 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     return INFERNT_OK;
 }
 
+// The sum over the ranks of y [T][H] in place (tensor parallelism).
+int all_reduce(infernt_batch_engine* e, float* y, cudaStream_t st) {
+    const NcclApi* n = nccl_api();
+    const ncclResult_t r = n->all_reduce(y, y, (size_t)e->T * e->cfg.hidden_size, ncclFloat32, ncclSum,
+                                         static_cast<ncclComm_t>(e->comm), st);
+    return r == ncclSuccess ? INFERNT_OK : fail(INFERNT_ERR_CUDA, "ncclAllReduce: %s", n->err_str(r));
+}
+
+// Residual add + RMSNorm of an O or down projection: its split partials
+// summed in order (one rank), or summed per rank and then over the ranks.
+int resid_norm(infernt_batch_engine* e, int splits, const float* norm_w, cudaStream_t st) {
+    const infernt_llama_config& c = e->cfg;
+    const int H = c.hidden_size, T = e->T;
+    using namespace infernt;
+    if (e->world == 1) return bt_resid_norm_launch(e->part, splits, T, H, e->h, norm_w, c.rms_norm_eps, e->xb, st);
+    if (int s = tp_sum_splits_launch(e->part, splits, T, H, e->ysum, st)) return s;
+    if (int s = all_reduce(e, e->ysum, st)) return s;
+    return bt_resid_norm_launch(e->ysum, 1, T, H, e->h, norm_w, c.rms_norm_eps, e->xb, st);
+}
+
 // One decode step of every sequence (launches only; the caller synchronises).
 int record_step(infernt_batch_engine* e, cudaStream_t st) {
     const infernt_llama_config& c = e->cfg;
-    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
-    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, T = e->T;
-    const int qs = nq * D, nqkv = qs + 2 * nkv * D;
+    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers;
+    const int nq = e->nq_l, nkv = e->nkv_l, il = e->il, T = e->T;
+    const int qsl = nq * D, nqkv = qsl + 2 * nkv * D;
     const float eps = c.rms_norm_eps;
     using namespace infernt;
     if (int s = bt_embed_norm_launch(e->emb, e->tokens, V, T, H, e->layers[0].attn_norm, eps, e->h, e->xb, e->err, st))
@@ -279,17 +376,25 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
                                             e->min_chunk, e->stages, e->apart, e->attn, st))
                 return s;
         }
-        if (int s = bgemm_launch(ly.o, H, qs, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
-        if (int s = bt_resid_norm_launch(e->part, e->sp_o, T, H, e->h, ly.ffn_norm, eps, e->xb, st)) return s;
-        if (int s = bgemm_launch(ly.gu, 2 * I, H, e->xb, T, e->part, e->sp_gu, e->err, st)) return s;
-        if (int s = bt_swiglu_launch(e->part, e->sp_gu, T, I, e->act, st)) return s;
-        if (int s = bgemm_launch(ly.down, H, I, e->act, T, e->part, e->sp_down, e->err, st)) return s;
+        if (int s = bgemm_launch(ly.o, H, qsl, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
+        if (int s = resid_norm(e, e->sp_o, ly.ffn_norm, st)) return s;
+        if (int s = bgemm_launch(ly.gu, 2 * il, H, e->xb, T, e->part, e->sp_gu, e->err, st)) return s;
+        if (int s = bt_swiglu_launch(e->part, e->sp_gu, T, il, e->act, st)) return s;
+        if (int s = bgemm_launch(ly.down, H, il, e->act, T, e->part, e->sp_down, e->err, st)) return s;
         const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
-        if (int s = bt_resid_norm_launch(e->part, e->sp_down, T, H, e->h, next_norm, eps, e->xb, st)) return s;
+        if (int s = resid_norm(e, e->sp_down, next_norm, st)) return s;
     }
-    if (int s = bgemm_launch(e->lm, V, H, e->xb, T, e->part, e->sp_lm, e->err, st)) return s;
-    // the LM head runs unsplit: part[0] holds the logits
-    return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, e->cand_v, e->cand_i, e->am_tickets, st);
+    if (int s = bgemm_launch(e->lm, e->vlp, H, e->xb, T, e->part, e->sp_lm, e->err, st)) return s;
+    // the LM head runs unsplit: part[0] holds the logits [T][vlp]
+    if (e->world == 1)
+        return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, e->cand_v, e->cand_i, e->am_tickets,
+                                st);
+    if (int s = tp_argmax_local_launch(e->part, T, e->vlp, e->vl, e->v0, e->cand, st)) return s;
+    const NcclApi* n = nccl_api();
+    const ncclResult_t r =
+        n->all_gather(e->cand, e->cand_all, (size_t)2 * T, ncclInt32, static_cast<ncclComm_t>(e->comm), st);
+    if (r != ncclSuccess) return fail(INFERNT_ERR_CUDA, "ncclAllGather: %s", n->err_str(r));
+    return tp_argmax_pick_launch(e->cand_all, e->world, T, e->tokens, e->positions, st);
 }
 
 int ensure_graph(infernt_batch_engine* e) {
@@ -427,12 +532,15 @@ int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions)
 
 extern "C" {
 
-int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
-                                       int attn_splits, infernt_batch_engine** out) {
-    INFERNT_REQUIRE(cfg && out, "batch_engine_create_seeded: null argument");
+int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
+                                   int attn_splits, int rank, int world, const void* nccl_id,
+                                   infernt_batch_engine** out) {
+    INFERNT_REQUIRE(cfg && out, "batch_engine_create: null argument");
     *out = nullptr;
     INFERNT_REQUIRE(cfg->weight_dtype == INFERNT_DTYPE_BF16, "batch engine: bf16 weights only");
     INFERNT_REQUIRE(batch >= 1 && batch <= 256, "batch engine: batch %d outside [1, 256]", batch);
+    INFERNT_REQUIRE(world >= 1 && world <= 64 && rank >= 0 && rank < world, "batch engine: rank %d of %d", rank, world);
+    INFERNT_REQUIRE(world == 1 || nccl_id, "batch engine: %d ranks need an NCCL unique id", world);
     const int D = cfg->head_dim;
     INFERNT_REQUIRE(D == 64 || D == 128, "batch engine: head_dim %d (64 or 128)", D);
     INFERNT_REQUIRE(cfg->num_attention_heads % cfg->num_key_value_heads == 0 &&
@@ -444,25 +552,80 @@ int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batc
                     "batch engine: hidden, heads x head_dim, Q|K|V rows, intermediate and vocabulary must be "
                     "multiples of 128");
     INFERNT_REQUIRE(cfg->max_seq_len <= (1 << 20), "batch engine: max_seq_len above 2^20");
+    // a rank's shard must keep the tensor-core tile shapes: Q|K|V and gate|up
+    // rows multiples of 128, O and down K multiples of 64
+    const int nq_l = cfg->num_attention_heads / world, nkv_l = cfg->num_key_value_heads / world;
+    const int il = cfg->intermediate_size / world;
+    INFERNT_REQUIRE(cfg->num_key_value_heads % world == 0 && (nq_l + 2 * nkv_l) * D % 128 == 0 &&
+                        nq_l * D % 64 == 0 && cfg->intermediate_size % world == 0 && il % 64 == 0,
+                    "batch engine: %d ranks do not split the KV heads, Q|K|V rows or intermediate rows into "
+                    "tensor-core tiles",
+                    world);
+    const NcclApi* nccl = nullptr;
+    if (world > 1) {
+        nccl = nccl_api();
+        INFERNT_REQUIRE(nccl, "batch engine: libnccl.so.2 is not loadable (needed for %d ranks)", world);
+    }
     infernt_batch_engine* e = new (std::nothrow) infernt_batch_engine();
-    INFERNT_REQUIRE(e, "batch_engine_create_seeded: host allocation failed");
+    INFERNT_REQUIRE(e, "batch_engine_create: host allocation failed");
     e->cfg = *cfg;
     e->T = batch;
+    e->rank = rank;
+    e->world = world;
+    e->nq_l = nq_l;
+    e->nkv_l = nkv_l;
+    e->il = il;
+    e->v0 = (int)((long long)cfg->vocab_size * rank / world);
+    e->vl = (int)((long long)cfg->vocab_size * (rank + 1) / world) - e->v0;
+    e->vlp = (e->vl + 127) / 128 * 128;
     int S = attn_splits;
     if (S <= 0) {
         // one split (no merge) once the (sequence, KV head) pairs fill the
         // SMs; otherwise about two CTAs per SM
-        const int pairs = batch * cfg->num_key_value_heads, sms = infernt::sm_count();
+        const int pairs = batch * nkv_l, sms = infernt::sm_count();
         S = pairs >= sms ? 1 : (2 * sms + pairs - 1) / pairs;
         if (S > 64) S = 64;
     }
     e->S = S < 1 ? 1 : S;
     int s = build(e, seed, std_dev);
+    if (!s && world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        ncclComm_t comm = nullptr;
+        const ncclResult_t r = nccl->init(&comm, world, id, rank);
+        if (r != ncclSuccess)
+            s = fail(INFERNT_ERR_CUDA, "ncclCommInitRank (rank %d of %d): %s", rank, world, nccl->err_str(r));
+        else
+            e->comm = comm;
+    }
     if (s) {
         delete e;
         return s;
     }
     *out = e;
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
+                                       int attn_splits, infernt_batch_engine** out) {
+    return infernt_batch_engine_create_tp(cfg, batch, seed, std_dev, attn_splits, 0, 1, nullptr, out);
+}
+
+int infernt_nccl_unique_id(void* out, size_t n) {
+    INFERNT_REQUIRE(out && n >= sizeof(ncclUniqueId), "nccl_unique_id: need %zu bytes", sizeof(ncclUniqueId));
+    const NcclApi* nccl = nccl_api();
+    INFERNT_REQUIRE(nccl, "nccl_unique_id: libnccl.so.2 is not loadable");
+    ncclUniqueId id;
+    const ncclResult_t r = nccl->get_id(&id);
+    if (r != ncclSuccess) return fail(INFERNT_ERR_CUDA, "ncclGetUniqueId: %s", nccl->err_str(r));
+    std::memcpy(out, &id, sizeof(id));
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_vocab_range(infernt_batch_engine* e, int* v0, int* vl) {
+    INFERNT_REQUIRE(e && v0 && vl, "batch_engine_vocab_range: null argument");
+    *v0 = e->v0;
+    *vl = e->vl;
     return INFERNT_OK;
 }
 
@@ -476,11 +639,11 @@ int infernt_batch_engine_fill_kv(infernt_batch_engine* e, int seq, uint64_t seed
                     "batch_engine_fill_kv: bad arguments");
     const uint64_t kk = infernt_stream_key(seed, INFERNT_STREAM_KV_K), vk = infernt_stream_key(seed, INFERNT_STREAM_KV_V);
     for (int l = 0; l < e->cfg.num_layers; ++l) {
-        if (int s = infernt::bt_fill_kv_launch(e->kc[l], seq, l, e->cfg.num_key_value_heads, e->cfg.max_seq_len,
-                                               e->cfg.head_dim, n_pos, kk, std_dev, e->stream))
+        if (int s = infernt::bt_fill_kv_launch(e->kc[l], seq, l, e->nkv_l, e->cfg.max_seq_len, e->cfg.head_dim, n_pos,
+                                               kk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream))
             return s;
-        if (int s = infernt::bt_fill_kv_launch(e->vc[l], seq, l, e->cfg.num_key_value_heads, e->cfg.max_seq_len,
-                                               e->cfg.head_dim, n_pos, vk, std_dev, e->stream))
+        if (int s = infernt::bt_fill_kv_launch(e->vc[l], seq, l, e->nkv_l, e->cfg.max_seq_len, e->cfg.head_dim, n_pos,
+                                               vk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream))
             return s;
     }
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -533,17 +696,18 @@ int infernt_batch_engine_decode(infernt_batch_engine* e, const int* tokens, cons
 }
 
 int infernt_batch_engine_logits(infernt_batch_engine* e, float* logits_host, size_t n) {
-    INFERNT_REQUIRE(e && logits_host && n == (size_t)e->T * e->cfg.vocab_size,
-                    "batch_engine_logits: need %d x %d floats", e ? e->T : 0, e ? e->cfg.vocab_size : 0);
+    INFERNT_REQUIRE(e && logits_host && n == (size_t)e->T * e->vl, "batch_engine_logits: need %d x %d floats",
+                    e ? e->T : 0, e ? e->vl : 0);
     INFERNT_REQUIRE(e->sp_lm == 1, "batch_engine_logits: the LM head runs split; logits are partial sums");
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
-    INFERNT_CUDA_TRY(cudaMemcpy(logits_host, e->part, sizeof(float) * n, cudaMemcpyDeviceToHost));
+    INFERNT_CUDA_TRY(cudaMemcpy2D(logits_host, sizeof(float) * e->vl, e->part, sizeof(float) * e->vlp,
+                                  sizeof(float) * e->vl, e->T, cudaMemcpyDeviceToHost));
     return INFERNT_OK;
 }
 
 int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int min_chunk, int stages) {
     INFERNT_REQUIRE(e, "batch_engine_set_attention: null engine");
-    const int D = e->cfg.head_dim, nkv = e->cfg.num_key_value_heads, G = e->cfg.num_attention_heads / nkv;
+    const int D = e->cfg.head_dim, nkv = e->nkv_l, G = e->nq_l / nkv;
     INFERNT_REQUIRE(splits >= 1 && splits <= 64, "batch_engine_set_attention: splits %d outside [1, 64]", splits);
     INFERNT_REQUIRE(min_chunk >= 1, "batch_engine_set_attention: min_chunk %d", min_chunk);
     INFERNT_REQUIRE(stages >= 2 && stages <= (D == 64 ? 4 : 3), "batch_engine_set_attention: %d stages at head_dim %d",
@@ -575,6 +739,7 @@ int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int 
 int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* tokens, int n_tokens, int start_pos,
                                  int chunk, int* next_token, float* logits_host, float* ms) {
     INFERNT_REQUIRE(e && tokens, "batch_engine_prefill: null argument");
+    if (e->world > 1) return fail(INFERNT_ERR_UNSUPPORTED, "batch_engine_prefill: tensor-parallel engines decode only");
     const infernt_llama_config& c = e->cfg;
     INFERNT_REQUIRE(seq >= 0 && seq < e->T, "batch_engine_prefill: sequence %d outside [0, %d)", seq, e->T);
     INFERNT_REQUIRE(n_tokens >= 1 && start_pos >= 0 && (long long)start_pos + n_tokens <= c.max_seq_len,
@@ -613,7 +778,7 @@ int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, in
     INFERNT_REQUIRE(seq >= 0 && seq < e->T && layer >= 0 && layer < c.num_layers && n_pos >= 0 &&
                         n_pos <= c.max_seq_len,
                     "batch_engine_read_kv: sequence %d, layer %d, %d positions", seq, layer, n_pos);
-    const int nkv = c.num_key_value_heads, D = c.head_dim, S = c.max_seq_len;
+    const int nkv = e->nkv_l, D = c.head_dim, S = c.max_seq_len;
     const size_t row = (size_t)n_pos * D * 2;
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
     for (int h = 0; h < nkv; ++h) {

@@ -1,0 +1,136 @@
+"""Tensor-parallel batched decode (infernt_batch_engine_create_tp) against
+the CPU oracle.
+
+Each rank is a process on its own GPU (one process per GPU, as torchrun
+starts them); rank 0 makes the NCCL unique id and a gloo process group
+hands it to the others.  Every rank must return the same greedy tokens at
+every step.  The ranks' logits slices, put together in rank order, are held
+to the batched decode's own tolerance against the oracle's batched-decode
+variant (test_batch_gpu.py): every (step, sequence) within 1e-2 of the
+largest |logit|, tokens identical unless the oracle's top-2 gap is below
+twice the error.  The shapes cover both head dims and a vocabulary whose
+rank slices need zero-padded LM-head rows (1152 over 2 ranks: 576 rows,
+padded to 640)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import infernt_b200 as ib
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CFG = ib.ModelConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_attention_heads=8,
+                     num_key_value_heads=2, intermediate_size=1024, max_seq_len=256, rms_norm_eps=1e-5,
+                     rope_theta=10000.0, weight_dtype=ib.DTYPE_BF16)
+CFG_D128 = CFG.with_(hidden_size=1024, num_attention_heads=8, num_key_value_heads=4, head_dim=128,
+                     intermediate_size=1536, num_layers=1, vocab_size=1152)
+N_POS, STEPS, SEED = [0, 40, 130], 3, 7
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, cfg, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        obj = [ib.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        T = len(N_POS)
+        eng = ib.BatchEngine(cfg, T, seed=SEED, rank=rank, world=world, nccl_id=obj[0])
+        for b, p in enumerate(N_POS):
+            eng.fill_kv(b, 100 + b, p)
+        tokens = [int(t) for t in O.prompt(T, SEED, 3, cfg.vocab_size)]
+        positions = list(N_POS)
+        toks, logits = [], []
+        for _ in range(STEPS):
+            tokens = eng.step(tokens, positions)
+            positions = [p + 1 for p in positions]
+            toks.append(tokens)
+            logits.append(eng.logits())
+        rng = eng.vocab_range
+        eng.close()
+        out[rank] = (toks, logits, rng)
+    finally:
+        dist.destroy_process_group()
+
+
+def run_tp(cfg, world):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_rank, args=(r, world, port, cfg, out)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(600)
+        codes = [p.exitcode for p in procs]
+        assert codes == [0] * world, codes
+        return dict(out)
+
+
+def top2_gap(x):
+    s = np.sort(x)
+    return float(s[-1] - s[-2])
+
+
+def check_against_oracle(cfg, world):
+    res = run_tp(cfg, world)
+    toks = [res[r][0] for r in range(world)]
+    assert all(t == toks[0] for t in toks), "ranks disagree on the greedy tokens"
+    ranges = [res[r][2] for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == cfg.vocab_size
+    assert all(ranges[r][1] == ranges[r + 1][0] for r in range(world - 1))
+    T = len(N_POS)
+    orcs = []
+    for b, p in enumerate(N_POS):
+        o = O.LlamaOracle(cfg, seed=SEED, round_bf16=True, act_bf16=True)
+        o.fill_kv(100 + b, p)
+        orcs.append(o)
+    tokens = [int(t) for t in O.prompt(T, SEED, 3, cfg.vocab_size)]
+    positions = list(N_POS)
+    for step in range(STEPS):
+        full = np.concatenate([res[r][1][step] for r in range(world)], axis=1)
+        for b in range(T):
+            want_tok, want = orcs[b].decode_token(tokens[b], positions[b])
+            err = float(np.abs(full[b] - want).max())
+            scale = float(np.abs(want).max())
+            assert err <= 1e-2 * scale, (step, b, err, scale)
+            got_tok = toks[0][step][b]
+            assert got_tok == int(np.argmax(full[b])) or full[b][got_tok] == full[b].max(), (step, b)
+            if got_tok != want_tok:
+                assert top2_gap(want) < 2 * err, (step, b, got_tok, want_tok)
+        tokens = toks[0][step]  # both sides follow the engine's tokens
+        positions = [p + 1 for p in positions]
+
+
+def _gpus():
+    import torch
+    return torch.cuda.device_count()
+
+
+def test_batch_tp1_matches_oracle():
+    """One rank through the tensor-parallel constructor: no collective."""
+    check_against_oracle(CFG, 1)
+
+
+@pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
+def test_batch_tp2_matches_oracle():
+    check_against_oracle(CFG, 2)
+
+
+@pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
+def test_batch_tp2_head_dim_128_padded_vocab():
+    check_against_oracle(CFG_D128, 2)
