@@ -5,8 +5,11 @@
 // caches [T][N_kv][max_seq][D] per layer.  A step is a fixed sequence of
 // launches (bgemm.cu, batch.cu) captured once into a CUDA graph and
 // replayed; tokens and positions live on the device and the argmax kernel
-// advances them, so chained steps need no host round trip.  Every
-// allocation happens at creation.
+// advances them, so chained steps need no host round trip.  Decode
+// allocates nothing after creation; prompt prefill (prefill.cu, pgemm in
+// bgemm.cu) allocates its chunk scratch at its first call.  With world > 1
+// the engine is one rank of a tensor-parallel decoder (NCCL all-reduce of
+// the O and down sums, all-gather of the argmax candidates).
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
