@@ -499,6 +499,43 @@ INFERNT_API int infernt_engine_decode_chain(infernt_engine* e, int token, int po
 INFERNT_API int infernt_engine_weight_ptrs(infernt_engine* e, const void** ptrs, int n);
 INFERNT_API int infernt_engine_kv_ptrs(infernt_engine* e, float** k, float** v, int n);
 
+/* ------------------------------------------------ temperature sampling ---
+ * InferenceEngine::sample_next_token(temperature) samples softmax(logits / T)
+ * on the host (src/engine.cpp:78-104, mt19937 seeded 1337).  This draws the
+ * same distribution on the GPU by the Gumbel-max method: row r's token is
+ * argmax_i (logits[r][i] / T + g_i), g_i = -ln(-ln u_i), u_i a 24-bit
+ * uniform in (0, 1) hashed from (seed, counter + r, i) — reproducible per
+ * (seed, counter), not the reference's mt19937 sequence.  T <= 0: greedy
+ * argmax.  Ties go to the lowest index; NaN never wins.  logits rows are ld
+ * floats apart (ld = 0: every row samples the same logits); out_tokens
+ * [rows] device ints; workspace: infernt_sample_workspace_bytes(rows) bytes
+ * of device memory, zeroed once before the first call (calls leave it
+ * zeroed; calls that share it must not overlap).  Asynchronous. */
+INFERNT_API size_t infernt_sample_workspace_bytes(int rows);
+INFERNT_API int infernt_sample_tokens(const float* logits, long long ld, int rows, int vocab_size,
+                                      float temperature, uint64_t seed, uint64_t counter,
+                                      int* out_tokens, void* workspace, void* stream);
+
+/* ------------------------------------------------ INFT v1 checkpoints ---
+ * The reference's CheckpointLoader (include/checkpoint_loader.h:7-14,
+ * loader/checkpoint_loader.cpp:42-161; the C++ class is in
+ * include/checkpoint_loader.h).  config.json: the keys the reference reads
+ * (with its defaults), optional head_dim and weight_dtype ("bf16" / "fp32"). */
+INFERNT_API int infernt_checkpoint_read_config(const char* config_json, infernt_llama_config* out);
+/* model.bin (magic 0x494E4654, version 1, FP32 payloads) for cfg: every
+ * tensor in its own buffer, device 0 = host memory, 1 = the current CUDA
+ * device; norms and embedding FP32, projections and lm_head in
+ * cfg->weight_dtype (bf16 rounded to nearest even).  A missing lm_head is a
+ * copy of the embedding (as the reference); a bad magic or version, a
+ * truncated file, an element count that does not match cfg or a missing
+ * tensor is INFERNT_ERR_INVALID_ARGUMENT (the reference does not check). */
+typedef struct infernt_checkpoint infernt_checkpoint;
+INFERNT_API int infernt_checkpoint_load(const char* model_bin, const infernt_llama_config* cfg, int device,
+                                        infernt_checkpoint** out);
+/* The 3 + 9 num_layers buffers in the order of infernt_plan_create. */
+INFERNT_API int infernt_checkpoint_weights(const infernt_checkpoint* ck, const void** out, int n);
+INFERNT_API int infernt_checkpoint_free(infernt_checkpoint* ck);
+
 #ifdef __cplusplus
 }
 #endif

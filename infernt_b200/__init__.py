@@ -146,6 +146,13 @@ _SIGS = {
     "infernt_batch_engine_create_tp": (_I, [_P, _I, ctypes.c_uint64, _F, _I, _I, _I, _P, _P]),
     "infernt_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "infernt_batch_engine_vocab_range": (_I, [_P, _P, _P]),
+    "infernt_sample_workspace_bytes": (_S, [_I]),
+    "infernt_sample_tokens": (_I, [_P, ctypes.c_longlong, _I, _I, _F, ctypes.c_uint64, ctypes.c_uint64, _P, _P,
+                                   _P]),
+    "infernt_checkpoint_read_config": (_I, [ctypes.c_char_p, ctypes.POINTER(LlamaConfig)]),
+    "infernt_checkpoint_load": (_I, [ctypes.c_char_p, ctypes.POINTER(LlamaConfig), _I, _P]),
+    "infernt_checkpoint_weights": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "infernt_checkpoint_free": (_I, [_P]),
     "infernt_batch_engine_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
     "infernt_pgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_prefill_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
@@ -429,6 +436,44 @@ class BatchEngine:
         """KV splits per (sequence, KV head), least positions per split and
         copy stages per warp of the attention; results do not change."""
         call("infernt_batch_engine_set_attention", self._h, splits, min_chunk, stages)
+
+
+class Checkpoint:
+    """An INFT v1 checkpoint (infernt_checkpoint_*): config.json read into a
+    ModelConfig, model.bin into one buffer per tensor on the host (device=0)
+    or the current CUDA device (device=1), projections and lm_head in
+    cfg.weight_dtype."""
+
+    @staticmethod
+    def read_config(path: str) -> "ModelConfig":
+        c = LlamaConfig()
+        call("infernt_checkpoint_read_config", path.encode(), ctypes.byref(c))
+        return ModelConfig(vocab_size=c.vocab_size, hidden_size=c.hidden_size, num_layers=c.num_layers,
+                           num_attention_heads=c.num_attention_heads, num_key_value_heads=c.num_key_value_heads,
+                           intermediate_size=c.intermediate_size, max_seq_len=c.max_seq_len, head_dim=c.head_dim,
+                           rms_norm_eps=c.rms_norm_eps, rope_theta=c.rope_theta, weight_dtype=c.weight_dtype)
+
+    def __init__(self, model_bin: str, cfg: "ModelConfig", device: int = 1):
+        self.cfg = cfg
+        self._c = cfg.c()
+        h = ctypes.c_void_p()
+        call("infernt_checkpoint_load", model_bin.encode(), ctypes.byref(self._c), device, ctypes.byref(h))
+        self._h = h
+        n = 3 + 9 * cfg.num_layers
+        arr = (_P * n)()
+        call("infernt_checkpoint_weights", self._h, arr, n)
+        self.ptrs = [arr[i] for i in range(n)]
+
+    def close(self):
+        if self._h:
+            lib().infernt_checkpoint_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def nccl_unique_id() -> bytes:

@@ -17,6 +17,7 @@
 // generated on the host and uploaded with Tensor::to (as the reference's
 // checkpoint loader does, loader/checkpoint_loader.cpp:112-114).
 #include "architecture.h"
+#include "checkpoint_loader.h"
 #include "config.h"
 #include "cublas_wrapper.h"
 #include "cuda_utils.h"
@@ -33,6 +34,8 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <stdexcept>
+#include <string>
 #include <thread>
 #include <vector>
 
@@ -286,6 +289,48 @@ float ref_engine_decode_loop(void* h, int token, int position, int steps, int* t
     cudaEventDestroy(a);
     cudaEventDestroy(b);
     return ms;
+}
+
+// The reference's CheckpointLoader on the host (Device::CPU): config.json
+// into ci [vocab, hidden, layers, q heads, kv heads, intermediate, max_seq,
+// head_dim] and cf [eps, theta]; model.bin into out[slot] (3 + 9 layers
+// caller arrays of FP32, the order of ModelWeights: embedding, final_norm,
+// lm_head, per layer attn_norm, q, k, v, o, ffn_norm, gate, up, down), each
+// of out_n[slot] floats.  Returns 0, or -1 with ref_last_error() set when
+// the reference throws.
+int ref_checkpoint_load_cpu(const char* config_json, const char* model_bin, int* ci, float* cf, int n_slots,
+                            float* const* out, const long long* out_n) {
+    try {
+        ModelConfig c = CheckpointLoader::load_config(config_json);
+        ci[0] = c.vocab_size;
+        ci[1] = c.hidden_size;
+        ci[2] = c.num_layers;
+        ci[3] = c.num_attention_heads;
+        ci[4] = c.num_key_value_heads;
+        ci[5] = c.intermediate_size;
+        ci[6] = c.max_seq_len;
+        ci[7] = c.head_dim;
+        cf[0] = c.rms_norm_eps;
+        cf[1] = c.rope_theta;
+        if (!model_bin) return 0;
+        ModelWeights w;
+        CheckpointLoader::load_weights(model_bin, c, w, Device::CPU);
+        std::vector<const Tensor*> ts = {&w.embedding, &w.final_norm, &w.lm_head};
+        for (const auto& l : w.layers)
+            for (const Tensor* x : {&l.attn_norm, &l.q_proj, &l.k_proj, &l.v_proj, &l.o_proj, &l.ffn_norm,
+                                    &l.gate_proj, &l.up_proj, &l.down_proj})
+                ts.push_back(x);
+        if ((int)ts.size() != n_slots) throw std::runtime_error("slot count mismatch");
+        for (int s = 0; s < n_slots; ++s) {
+            if (!ts[s]->is_valid() || ts[s]->num_elements() != out_n[s])
+                throw std::runtime_error("tensor " + std::to_string(s) + " missing or of another size");
+            std::memcpy(out[s], ts[s]->data_as_float(), sizeof(float) * (size_t)out_n[s]);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_err(e.what());
+        return -1;
+    }
 }
 
 }  // extern "C"
