@@ -368,6 +368,10 @@ int make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) 
 
 }  // namespace
 
+// The cuTensorMapEncodeTiled entry point for other kernels' tensor maps
+// (NULL if the driver has none).
+void* tensor_map_encoder() { return reinterpret_cast<void*>(encode_fn()); }
+
 // Two CTAs share an SM when at least kPairStages stages fit in half of its
 // shared memory (their weight streams and epilogues then overlap); otherwise
 // one CTA per SM with as many stages as fit.

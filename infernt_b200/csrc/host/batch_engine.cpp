@@ -52,7 +52,7 @@ int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, in
 int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, const float2* rope, int max_seq,
                        uint16_t* q, uint16_t* kc, uint16_t* vc, cudaStream_t st);
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
-                        int D, int max_seq, uint16_t* attn, cudaStream_t st);
+                        int D, int max_seq, uint16_t* attn, unsigned* err, int tensor_cores, cudaStream_t st);
 int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, cudaStream_t st);
 int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, cudaStream_t st);
 int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, int* positions, cudaStream_t st);
@@ -503,7 +503,7 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
             uint16_t* vc = e->vc[l] + seq_off;
             if (int s = pgemm_launch(ly.qkv, nqkv, H, e->pf_x, m, e->pf_y, nqkv, e->err, st)) return s;
             if (int s = pf_qkv_rope_launch(e->pf_y, m, p0, nq, nkv, D, e->rope, S, e->pf_q, kc, vc, st)) return s;
-            if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, st)) return s;
+            if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, e->err, 1, st)) return s;
             if (int s = pgemm_launch(ly.o, H, qs, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
             if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, ly.ffn_norm, eps, e->pf_x, st)) return s;
             if (int s = pgemm_launch(ly.gu, 2 * I, H, e->pf_x, m, e->pf_y, 2 * I, e->err, st)) return s;

@@ -17,6 +17,9 @@
 // then rounded to bf16).  Queries enter the attention's tensor cores as bf16
 // and the probabilities as bf16 (FP32 scores, softmax statistics and
 // accumulators).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <cstdint>
 
@@ -26,6 +29,8 @@
 #include "warp_mma.cuh"
 
 namespace infernt {
+
+void* tensor_map_encoder();  // bgemm.cu
 
 namespace {
 
@@ -257,6 +262,385 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
     }
 }
 
+// ------------------------------------------------ tensor-core attention
+// The same causal GQA attention for head_dim 128 on the 5th-generation
+// tensor cores, S and O in tensor memory.  One CTA of 6 warps per (KV head,
+// block of 128 / G tokens): its 128 query rows (token, head of the group)
+// are the MMA's M.  Per 128-key tile:
+//   S[128 x 128]  = Q K^T              tcgen05.mma (A = Q, B = K, both K-major)
+//   P = bf16(exp2(S scale - m))        softmax warps: tcgen05.ld of S, P into
+//                                      shared memory (128-byte swizzled K-major)
+//   O[128 x 128] += P V                tcgen05.mma (A = P, B = V MN-major:
+//                                      the cache's [key][d] rows as they are)
+// Warp 0 (one thread) drives TMA: Q once through a 4-D map of q [C][Nkv][G][D]
+// that yields the rows in (token, head) order, K and V tiles through 3-D maps
+// of the caches bounded at the chunk's last position (rows past it read as
+// zeros); two K/V stages.  Warp 1 (one thread) issues the MMAs and commits
+// them to mbarriers.  Warps 2-5 own one query row per thread (their TMEM lane
+// quarter): base-2 online softmax with the running maximum per row; when a
+// row's maximum grows after the first tile, its O row is rescaled in tensor
+// memory (tcgen05.ld / st) after the previous P V has completed.  The
+// epilogue divides O by the row sums and writes bf16 rows.  Every wait is
+// bounded; on expiry the CTA sets bit 0 of *err and returns once its copies
+// have landed.
+constexpr int kTcRows = 128;
+constexpr int kTcKeys = 128;
+constexpr uint32_t kTcBox = 16384;                     // a [128][64] bf16 box
+constexpr uint32_t kTcQ = 0, kTcStage0 = 2 * kTcBox;   // Q: 2 boxes; stage s: K (2 boxes), V (2 boxes)
+constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P: 2 boxes
+constexpr uint32_t kTcSmem = kTcP + 2 * kTcBox + 1024;
+constexpr long long kTcWait = 2000000000ll;
+
+struct PfTcArgs {
+    uint16_t* attn;  // [C][nq D]
+    unsigned* err;
+    int C, p0, nq, nkv, G, tok_per_cta;
+    float scale_log2;
+};
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, bool& ok) {
+    if (!ok) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kTcWait) {
+            ok = false;
+            return false;
+        }
+    return true;
+}
+
+// K-major operand, 128-byte swizzle: 128-byte rows, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_k_sw128(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3fffu) | (uint64_t)1u << 16 | (uint64_t)(1024u >> 4) << 32 |
+           (uint64_t)1u << 46 | (uint64_t)2u << 61;
+}
+
+// MN-major operand, 128-byte swizzle: rows of 64 MN-contiguous elements (128
+// bytes) per K index, atoms of 8 K rows 1024 bytes apart (stride byte
+// offset), the next 64 MN elements `mn_block` bytes away (leading byte offset).
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t addr, uint32_t mn_block) {
+    return (uint64_t)((addr >> 4) & 0x3fffu) | (uint64_t)((mn_block >> 4) & 0x3fffu) << 16 |
+           (uint64_t)(1024u >> 4) << 32 | (uint64_t)1u << 46 | (uint64_t)2u << 61;
+}
+
+// D FP32, A and B bf16, M = 128, N = 128; B MN-major when b_mn.
+__device__ __forceinline__ uint32_t tc_idesc(bool b_mn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(128 >> 3) << 17) |
+           ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(dst),
+        "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                       uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, "
+        "%6}], [%2];" ::"r"(dst),
+        "l"(map), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(192, 1)
+    pf_attn_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+               const __grid_constant__ CUtensorMap tm_v, const PfTcArgs a) {
+    extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
+    __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s, bar_p, bar_o;
+    __shared__ uint32_t tmem_base;
+    __shared__ int s_ok;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t base = (smem_addr(tc_smem_raw) + 1023u) & ~1023u;
+    const int C = a.C, G = a.G;
+    const int nblocks = (C + a.tok_per_cta - 1) / a.tok_per_cta;
+    const int kvh = blockIdx.x % a.nkv;
+    const int qb = nblocks - 1 - (int)(blockIdx.x / a.nkv);  // heaviest blocks first
+    const int t0 = qb * a.tok_per_cta;
+    const int t_end = min(C, t0 + a.tok_per_cta);
+    const int kend = a.p0 + t_end;
+    const int ntiles = (kend + kTcKeys - 1) / kTcKeys;
+
+    if (tid == 0) {
+        mbar_init(&full_q, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&full_k[s], 1);
+            mbar_init(&full_v[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&bar_s, 1);
+        mbar_init(&bar_p, 128);
+        mbar_init(&bar_o, 1);
+        mbar_fence_init();
+        s_ok = 1;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                     "r"(256));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_s = tmem_base, tmem_o = tmem_base + 128;
+    bool ok = true;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&full_q, 2 * kTcBox);
+            tma_4d(base + kTcQ, &tm_q, 0, 0, kvh, t0, &full_q);
+            tma_4d(base + kTcQ + kTcBox, &tm_q, 64, 0, kvh, t0, &full_q);
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i & 1;
+                if (i >= 2 && !tc_wait(&empty[s], ((i >> 1) - 1) & 1u, ok)) break;
+                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox, vb = kb + 2 * kTcBox;
+                mbar_arrive_expect_tx(&full_k[s], 2 * kTcBox);
+                tma_3d(kb, &tm_k, 0, i * kTcKeys, kvh, &full_k[s]);
+                tma_3d(kb + kTcBox, &tm_k, 64, i * kTcKeys, kvh, &full_k[s]);
+                mbar_arrive_expect_tx(&full_v[s], 2 * kTcBox);
+                tma_3d(vb, &tm_v, 0, i * kTcKeys, kvh, &full_v[s]);
+                tma_3d(vb + kTcBox, &tm_v, 64, i * kTcKeys, kvh, &full_v[s]);
+            }
+            if (!ok) atomicExch(&s_ok, 0);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id_s = tc_idesc(false), id_o = tc_idesc(true);
+            tc_wait(&full_q, 0u, ok);
+            for (int i = 0; i < ntiles && ok; ++i) {
+                const int s = i & 1;
+                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox, vb = kb + 2 * kTcBox;
+                if (!tc_wait(&full_k[s], (i >> 1) & 1u, ok)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma(tmem_s, desc_k_sw128(base + kTcQ + b * kTcBox) + 2 * kk,
+                               desc_k_sw128(kb + b * kTcBox) + 2 * kk, id_s, (b | kk) ? 1u : 0u);
+                tc_commit(&bar_s);
+                if (!tc_wait(&bar_p, i & 1u, ok)) break;
+                if (!tc_wait(&full_v[s], (i >> 1) & 1u, ok)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma(tmem_o, desc_k_sw128(base + kTcP + b * kTcBox) + 2 * kk,
+                               desc_mn_sw128(vb + (uint32_t)(b * 4 + kk) * 2048u, kTcBox), id_o,
+                               (i | b | kk) ? 1u : 0u);
+                tc_commit(&bar_o);
+                tc_commit(&empty[s]);
+            }
+            if (!ok) atomicExch(&s_ok, 0);
+        }
+    } else {
+        // softmax: thread of TMEM lane r = one query row (token t0 + r / G, head r % G)
+        const int quarter = warp & 3, r = 32 * quarter + lane;
+        const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+        const int tl = r / G, g = r % G;
+        const bool row_ok = t0 + tl < C;
+        const int pos = a.p0 + min(t0 + tl, C - 1);
+        float m_run = -INFINITY, l_run = 0.0f;
+        for (int i = 0; i < ntiles; ++i) {
+            tc_wait(&bar_s, i & 1u, ok);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            float sv[kTcKeys];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tc_ld32(tmem_s + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
+            const int k0 = i * kTcKeys;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < kTcKeys; ++j) {
+                sv[j] = k0 + j <= pos ? sv[j] * a.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sv[j]);
+            }
+            const float m_new = fmaxf(m_run, mx);
+            if (i > 0) {
+                // the previous P V has completed: O is stable and P may be rewritten
+                tc_wait(&bar_o, (i - 1) & 1u, ok);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const bool grow = m_new > m_run;
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float alpha = grow ? exp2f(m_run - m_new) : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        float o[32];
+                        tc_ld32(tmem_o + lane_off + 32 * c, o);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+                        tc_st32(tmem_o + lane_off + 32 * c, o);
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    l_run *= alpha;
+                }
+            }
+            m_run = m_new;
+            // probabilities: 16 chunks of 8 keys, bf16, into P (K-major, swizzled)
+            float ls = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                float p[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    p[e] = exp2f(sv[8 * c + e] - m_run);
+                    ls += p[e];
+                }
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) w[e] = cvt_bf16x2(p[2 * e], p[2 * e + 1]);
+                const uint32_t addr = base + kTcP + (uint32_t)(c >> 3) * kTcBox + (uint32_t)r * 128u +
+                                      ((uint32_t)((c & 7) ^ (r & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                             "r"(w[3])
+                             : "memory");
+            }
+            l_run += ls;
+            fence_proxy_async_smem();
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(&bar_p);
+        }
+        if (ok) {
+            tc_wait(&bar_o, (ntiles - 1) & 1u, ok);
+            ok = __all_sync(0xffffffffu, ok);
+        }
+        if (ok) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const float inv = 1.0f / l_run;
+            uint16_t* out = a.attn + (size_t)(t0 + tl) * a.nq * 128 + (size_t)(kvh * G + g) * 128;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float o[32];
+                tc_ld32(tmem_o + lane_off + 32 * c, o);
+                if (row_ok) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 v;
+                        v.x = cvt_bf16x2(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
+                        v.y = cvt_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
+                        v.z = cvt_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
+                        v.w = cvt_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
+                        *reinterpret_cast<uint4*>(out + 32 * c + 8 * q) = v;
+                    }
+                }
+            }
+        }
+        if (!ok) atomicExch(&s_ok, 0);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (!s_ok) {
+        if (tid == 0 && a.err) atomicOr(a.err, 1u);
+        const long long tw = clock64();
+        while (clock64() - tw < 20000000ll) __nanosleep(1000);
+    }
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(256));
+}
+
+int encode_map(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
+               const cuuint32_t* box) {
+    auto fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    INFERNT_REQUIRE(fn, "prefill attention: cuTensorMapEncodeTiled is not available");
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    INFERNT_REQUIRE(r == CUDA_SUCCESS, "prefill attention: tensor map encoding failed (%d)", (int)r);
+    return INFERNT_OK;
+}
+
+int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
+                      int max_seq, uint16_t* attn, unsigned* err, cudaStream_t st) {
+    const int G = nq / nkv, D = 128;
+    CUtensorMap mq, mk, mv;
+    {
+        const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)G, (cuuint64_t)nkv, (cuuint64_t)C};
+        const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)G * D * 2, (cuuint64_t)nq * D * 2};
+        const cuuint32_t box[4] = {64, (cuuint32_t)G, 1, (cuuint32_t)(kTcRows / G)};
+        if (int s = encode_map(&mq, 4, q, dims, strides, box)) return s;
+    }
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)(p0 + C), (cuuint64_t)nkv};
+        const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)max_seq * D * 2};
+        const cuuint32_t box[3] = {64, (cuuint32_t)kTcKeys, 1};
+        if (int s = encode_map(&mk, 3, kc, dims, strides, box)) return s;
+        if (int s = encode_map(&mv, 3, vc, dims, strides, box)) return s;
+    }
+    static bool raised = false;
+    if (!raised) {
+        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+        raised = true;
+    }
+    PfTcArgs a;
+    a.attn = attn;
+    a.err = err;
+    a.C = C;
+    a.p0 = p0;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.G = G;
+    a.tok_per_cta = kTcRows / G;
+    a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
+    const long long ctas = (long long)nkv * ((C + a.tok_per_cta - 1) / a.tok_per_cta);
+    INFERNT_REQUIRE(ctas < (1ll << 31), "prefill attention: %lld blocks", ctas);
+    pf_attn_tc<<<(unsigned)ctas, 192, kTcSmem, st>>>(mq, mk, mv, a);
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
 template <int D, int G>
 int launch_pf_attn(const PfAttnArgs& a, cudaStream_t st) {
     constexpr int smem = pf_smem_bytes<D>();
@@ -296,7 +680,7 @@ int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, co
 }
 
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
-                        int D, int max_seq, uint16_t* attn, cudaStream_t st) {
+                        int D, int max_seq, uint16_t* attn, unsigned* err, int tensor_cores, cudaStream_t st) {
     INFERNT_REQUIRE(q && kc && vc && attn, "prefill attention: null pointer");
     INFERNT_REQUIRE(C >= 1 && p0 >= 0 && (long long)p0 + C <= max_seq, "prefill attention: %d tokens at %d, max_seq %d",
                     C, p0, max_seq);
@@ -315,6 +699,8 @@ int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* v
     a.max_seq = max_seq;
     a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     const int G = nq / nkv;
+    if (D == 128 && tensor_cores && (G == 1 || G == 2 || G == 4 || G == 8))
+        return launch_pf_attn_tc(q, kc, vc, C, p0, nq, nkv, max_seq, attn, err, st);
     if (D == 64) return pf_attn_group<64>(a, G, st);
     if (D == 128) return pf_attn_group<128>(a, G, st);
     return fail(INFERNT_ERR_UNSUPPORTED, "prefill attention: head_dim %d (64 or 128)", D);
@@ -324,8 +710,9 @@ int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* v
 
 extern "C" int infernt_prefill_attention(const void* q, const void* k_cache, const void* v_cache, int n_tokens,
                                          int start_pos, int nq, int nkv, int head_dim, int max_seq, void* attn,
-                                         void* stream) {
+                                         unsigned* err, int tensor_cores, void* stream) {
     return infernt::pf_attention_launch(static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
                                         static_cast<const uint16_t*>(v_cache), n_tokens, start_pos, nq, nkv, head_dim,
-                                        max_seq, static_cast<uint16_t*>(attn), static_cast<cudaStream_t>(stream));
+                                        max_seq, static_cast<uint16_t*>(attn), err, tensor_cores,
+                                        static_cast<cudaStream_t>(stream));
 }

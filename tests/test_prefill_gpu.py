@@ -105,16 +105,24 @@ def ref_causal_attention(q, k, v, p0):
     return out
 
 
-@pytest.mark.parametrize("D,nq,nkv,C,p0", [
-    (64, 8, 1, 1, 0),         # one token, one key
-    (64, 8, 1, 100, 37),      # groups of 8 (TinyLlama), ragged blocks
-    (64, 4, 2, 130, 0),       # groups of 2, the chunk starts the sequence
-    (128, 8, 2, 65, 200),     # groups of 4 (8B shape)
-    (128, 4, 4, 33, 64),      # one query head per KV head
-    (128, 32, 8, 300, 1000),  # 8B head layout, a chunk after 1000 positions
-    (64, 32, 4, 257, 0),      # TinyLlama head layout
+@pytest.mark.parametrize("D,nq,nkv,C,p0,tc", [
+    (64, 8, 1, 1, 0, 0),         # one token, one key
+    (64, 8, 1, 100, 37, 0),      # groups of 8 (TinyLlama), ragged blocks
+    (64, 4, 2, 130, 0, 0),       # groups of 2, the chunk starts the sequence
+    (128, 8, 2, 65, 200, 0),     # groups of 4 (8B shape)
+    (128, 4, 4, 33, 64, 0),      # one query head per KV head
+    (128, 32, 8, 300, 1000, 0),  # 8B head layout, a chunk after 1000 positions
+    (64, 32, 4, 257, 0, 0),      # TinyLlama head layout
+    # the tensor-core kernel (head_dim 128)
+    (128, 8, 2, 1, 0, 1),        # one token, one key
+    (128, 8, 2, 65, 200, 1),     # groups of 4, partial last block, keys past one 128-key tile
+    (128, 4, 4, 33, 64, 1),      # one query head per KV head
+    (128, 8, 1, 100, 37, 1),     # groups of 8
+    (128, 4, 2, 130, 0, 1),      # groups of 2, the chunk starts the sequence
+    (128, 32, 8, 300, 1000, 1),  # 8B head layout, a chunk after 1000 positions
+    (128, 32, 8, 1024, 3000, 1),  # many tiles per block, diagonal tiles, rows that grow late
 ])
-def test_prefill_attention_matches_float64(D, nq, nkv, C, p0):
+def test_prefill_attention_matches_float64(D, nq, nkv, C, p0, tc):
     torch = _torch()
     S = p0 + C + 5
     g = torch.Generator(device="cuda").manual_seed(D * 7 + C + p0)
@@ -125,9 +133,11 @@ def test_prefill_attention_matches_float64(D, nq, nkv, C, p0):
     k[:, p0 + C:, :] = float("nan")
     v[:, p0 + C:, :] = float("nan")
     attn = torch.full((C, nq, D), float("nan"), dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
     ib.call("infernt_prefill_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), C, p0, nq, nkv, D, S,
-            attn.data_ptr(), _stream())
+            attn.data_ptr(), err.data_ptr(), tc, _stream())
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     want = ref_causal_attention(q.double(), k.double(), v.double(), p0)
     got = attn.double()
     assert not bool(torch.isnan(got).any())
