@@ -266,29 +266,32 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
 // The same causal GQA attention for head_dim 128 on the 5th-generation
 // tensor cores, S and O in tensor memory.  One CTA of 6 warps per (KV head,
 // block of 128 / G tokens): its 128 query rows (token, head of the group)
-// are the MMA's M.  Per 128-key tile:
-//   S[128 x 128]  = Q K^T              tcgen05.mma (A = Q, B = K, both K-major)
-//   P = bf16(exp2(S scale - m))        softmax warps: tcgen05.ld of S, P into
+// are the MMA's M.  Per 128-key tile i:
+//   S_i[128 x 128] = Q K_i^T           tcgen05.mma (A = Q, B = K, both K-major)
+//   P_i = bf16(exp2(S scale - m))      softmax warps: tcgen05.ld of S, P into
 //                                      shared memory (128-byte swizzled K-major)
-//   O[128 x 128] += P V                tcgen05.mma (A = P, B = V MN-major:
+//   O[128 x 128] += P_i V_i            tcgen05.mma (A = P, B = V MN-major:
 //                                      the cache's [key][d] rows as they are)
 // Warp 0 (one thread) drives TMA: Q once through a 4-D map of q [C][Nkv][G][D]
 // that yields the rows in (token, head) order, K and V tiles through 3-D maps
 // of the caches bounded at the chunk's last position (rows past it read as
-// zeros); two K/V stages.  Warp 1 (one thread) issues the MMAs and commits
-// them to mbarriers.  Warps 2-5 own one query row per thread (their TMEM lane
-// quarter): base-2 online softmax with the running maximum per row; when a
-// row's maximum grows after the first tile, its O row is rescaled in tensor
-// memory (tcgen05.ld / st) after the previous P V has completed.  The
-// epilogue divides O by the row sums and writes bf16 rows.  Every wait is
-// bounded; on expiry the CTA sets bit 0 of *err and returns once its copies
-// have landed.
+// zeros); two K/V stages.  Warp 1 (one thread) issues the MMAs: S_{i+1} into
+// the other of two TMEM score buffers before P_i V_i, so the tensor pipe
+// computes the next scores while the softmax warps work; P is double-buffered
+// in shared memory.  Warps 2-5 own one query row per thread (their TMEM lane
+// quarter): base-2 online softmax whose reference maximum m moves only when a
+// row's maximum exceeds it by more than 8 (probabilities stay below 2^8);
+// then the row of O is rescaled in tensor memory (tcgen05.ld / st) after the
+// previous P V has completed.  The epilogue divides O by the row sums and
+// writes bf16 rows.  Every wait is bounded; on expiry the CTA sets bit 0 of
+// *err and returns once its copies have landed.
 constexpr int kTcRows = 128;
 constexpr int kTcKeys = 128;
 constexpr uint32_t kTcBox = 16384;                     // a [128][64] bf16 box
 constexpr uint32_t kTcQ = 0, kTcStage0 = 2 * kTcBox;   // Q: 2 boxes; stage s: K (2 boxes), V (2 boxes)
-constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P: 2 boxes
-constexpr uint32_t kTcSmem = kTcP + 2 * kTcBox + 1024;
+constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P buffers b = 0, 1: 2 boxes each
+constexpr uint32_t kTcSmem = kTcP + 2 * 2 * kTcBox + 1024;
+constexpr float kTcRescale = 8.0f;                     // log2 of the largest unnormalised probability
 constexpr long long kTcWait = 2000000000ll;
 
 struct PfTcArgs {
@@ -396,7 +399,7 @@ __global__ void __launch_bounds__(192, 1)
     pf_attn_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PfTcArgs a) {
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
-    __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s, bar_p, bar_o;
+    __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s[2], bar_p[2], bar_pv[2];
     __shared__ uint32_t tmem_base;
     __shared__ int s_ok;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -416,21 +419,22 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&full_k[s], 1);
             mbar_init(&full_v[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&bar_s[s], 1);
+            mbar_init(&bar_p[s], 128);
+            mbar_init(&bar_pv[s], 1);
         }
-        mbar_init(&bar_s, 1);
-        mbar_init(&bar_p, 128);
-        mbar_init(&bar_o, 1);
         mbar_fence_init();
         s_ok = 1;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                     "r"(256));
+                     "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tmem_s = tmem_base, tmem_o = tmem_base + 128;
+    // TMEM columns: S buffers at 0 and 128, O at 256
+    const uint32_t tmem_o = tmem_base + 256;
     bool ok = true;
 
     if (warp == 0) {
@@ -454,30 +458,40 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t id_s = tc_idesc(false), id_o = tc_idesc(true);
+            // S_j = Q K_j^T into score buffer j % 2
+            auto scores = [&](int j) {
+                const int s = j & 1;
+                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox;
+                if (!tc_wait(&full_k[s], (j >> 1) & 1u, ok)) return;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma(tmem_base + 128u * (uint32_t)s, desc_k_sw128(base + kTcQ + b * kTcBox) + 2 * kk,
+                               desc_k_sw128(kb + b * kTcBox) + 2 * kk, id_s, (b | kk) ? 1u : 0u);
+                tc_commit(&bar_s[s]);
+            };
             tc_wait(&full_q, 0u, ok);
+            if (ok) scores(0);
             for (int i = 0; i < ntiles && ok; ++i) {
                 const int s = i & 1;
-                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox, vb = kb + 2 * kTcBox;
-                if (!tc_wait(&full_k[s], (i >> 1) & 1u, ok)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-                for (int b = 0; b < 2; ++b)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma(tmem_s, desc_k_sw128(base + kTcQ + b * kTcBox) + 2 * kk,
-                               desc_k_sw128(kb + b * kTcBox) + 2 * kk, id_s, (b | kk) ? 1u : 0u);
-                tc_commit(&bar_s);
-                if (!tc_wait(&bar_p, i & 1u, ok)) break;
+                // the other score buffer was read by softmax i - 1 (bar_p waited last iteration)
+                if (i + 1 < ntiles) scores(i + 1);
+                if (!ok) break;
+                if (!tc_wait(&bar_p[s], (i >> 1) & 1u, ok)) break;
                 if (!tc_wait(&full_v[s], (i >> 1) & 1u, ok)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t vb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox + 2 * kTcBox;
+                const uint32_t pb = base + kTcP + (uint32_t)s * 2 * kTcBox;
 #pragma unroll
                 for (int b = 0; b < 2; ++b)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        tc_mma(tmem_o, desc_k_sw128(base + kTcP + b * kTcBox) + 2 * kk,
+                        tc_mma(tmem_o, desc_k_sw128(pb + b * kTcBox) + 2 * kk,
                                desc_mn_sw128(vb + (uint32_t)(b * 4 + kk) * 2048u, kTcBox), id_o,
                                (i | b | kk) ? 1u : 0u);
-                tc_commit(&bar_o);
+                tc_commit(&bar_pv[s]);
                 tc_commit(&empty[s]);
             }
             if (!ok) atomicExch(&s_ok, 0);
@@ -489,15 +503,17 @@ __global__ void __launch_bounds__(192, 1)
         const int tl = r / G, g = r % G;
         const bool row_ok = t0 + tl < C;
         const int pos = a.p0 + min(t0 + tl, C - 1);
-        float m_run = -INFINITY, l_run = 0.0f;
+        float m_ref = -INFINITY, l_run = 0.0f;
         for (int i = 0; i < ntiles; ++i) {
-            tc_wait(&bar_s, i & 1u, ok);
+            const int s = i & 1;
+            tc_wait(&bar_s[s], (i >> 1) & 1u, ok);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             float sv[kTcKeys];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) tc_ld32(tmem_s + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
+            for (int c = 0; c < 4; ++c)
+                tc_ld32(tmem_base + 128u * (uint32_t)s + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
             const int k0 = i * kTcKeys;
             float mx = -INFINITY;
 #pragma unroll
@@ -505,16 +521,17 @@ __global__ void __launch_bounds__(192, 1)
                 sv[j] = k0 + j <= pos ? sv[j] * a.scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sv[j]);
             }
-            const float m_new = fmaxf(m_run, mx);
-            if (i > 0) {
-                // the previous P V has completed: O is stable and P may be rewritten
-                tc_wait(&bar_o, (i - 1) & 1u, ok);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const bool grow = m_new > m_run;
+            if (i == 0) {
+                m_ref = mx;  // every row's first tile holds key 0 <= its position: finite
+            } else {
+                const bool grow = mx > m_ref + kTcRescale;
                 if (__any_sync(0xffffffffu, grow)) {
-                    const float alpha = grow ? exp2f(m_run - m_new) : 1.0f;
+                    // O must hold P_{i-1} V_{i-1} before it is rescaled
+                    tc_wait(&bar_pv[(i - 1) & 1], ((i - 1) >> 1) & 1u, ok);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const float alpha = grow ? exp2f(m_ref - mx) : 1.0f;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         float o[32];
@@ -524,24 +541,32 @@ __global__ void __launch_bounds__(192, 1)
                         tc_st32(tmem_o + lane_off + 32 * c, o);
                     }
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                    l_run *= alpha;
+                    if (grow) {
+                        l_run *= alpha;
+                        m_ref = mx;
+                    }
                 }
             }
-            m_run = m_new;
-            // probabilities: 16 chunks of 8 keys, bf16, into P (K-major, swizzled)
+            if (i >= 2) {
+                // P buffer s was read by P_{i-2} V_{i-2}
+                tc_wait(&bar_pv[s], ((i >> 1) - 1) & 1u, ok);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+            }
             float ls = 0.0f;
+            const uint32_t pb = base + kTcP + (uint32_t)s * 2 * kTcBox;
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
                 float p[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    p[e] = exp2f(sv[8 * c + e] - m_run);
+                    p[e] = exp2f(sv[8 * c + e] - m_ref);
                     ls += p[e];
                 }
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) w[e] = cvt_bf16x2(p[2 * e], p[2 * e + 1]);
-                const uint32_t addr = base + kTcP + (uint32_t)(c >> 3) * kTcBox + (uint32_t)r * 128u +
+                const uint32_t addr = pb + (uint32_t)(c >> 3) * kTcBox + (uint32_t)r * 128u +
                                       ((uint32_t)((c & 7) ^ (r & 7)) << 4);
                 asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
                              "r"(w[3])
@@ -550,10 +575,10 @@ __global__ void __launch_bounds__(192, 1)
             l_run += ls;
             fence_proxy_async_smem();
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            mbar_arrive(&bar_p);
+            mbar_arrive(&bar_p[s]);
         }
         if (ok) {
-            tc_wait(&bar_o, (ntiles - 1) & 1u, ok);
+            tc_wait(&bar_pv[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1u, ok);
             ok = __all_sync(0xffffffffu, ok);
         }
         if (ok) {
@@ -587,7 +612,7 @@ __global__ void __launch_bounds__(192, 1)
         while (clock64() - tw < 20000000ll) __nanosleep(1000);
     }
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(256));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(512));
 }
 
 int encode_map(CUtensorMap* map, int rank, const void* base, const cuuint64_t* dims, const cuuint64_t* strides,
