@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
 
 // ------------------------------------------------ tensor-core attention
 // The same causal GQA attention for head_dim 128 on the 5th-generation
-// tensor cores, S and O in tensor memory.  One CTA of 6 warps per (KV head,
+// tensor cores, S and O in tensor memory.  One CTA of 10 warps per (KV head,
 // block of 128 / G tokens): its 128 query rows (token, head of the group)
 // are the MMA's M.  Per 128-key tile i:
 //   S_i[128 x 128] = Q K_i^T           tcgen05.mma (A = Q, B = K, both K-major)
@@ -277,20 +277,24 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
 // of the caches bounded at the chunk's last position (rows past it read as
 // zeros); two K/V stages.  Warp 1 (one thread) issues the MMAs: S_{i+1} into
 // the other of two TMEM score buffers before P_i V_i, so the tensor pipe
-// computes the next scores while the softmax warps work; P is double-buffered
-// in shared memory.  Warps 2-5 own one query row per thread (their TMEM lane
-// quarter): base-2 online softmax whose reference maximum m moves only when a
-// row's maximum exceeds it by more than 8 (probabilities stay below 2^8);
-// then the row of O is rescaled in tensor memory (tcgen05.ld / st) after the
-// previous P V has completed.  The epilogue divides O by the row sums and
+// computes the next scores while the softmax warps work; the softmax computes
+// P_i in registers while P_{i-1} V_{i-1} runs and stores it once that has
+// completed.  Warps 2-9 run the softmax, two threads per query row
+// (warps 2-5 keys and O columns 0-63, warps 6-9 64-127, each in its TMEM lane
+// quarter; the two halves' row maxima and sums meet through shared memory
+// and an mbarrier): base-2 online softmax whose reference maximum m moves
+// only when a row's maximum exceeds it by more than 8 (probabilities stay
+// below 2^8); then the row of O is rescaled in tensor memory (tcgen05.ld /
+// st) after the previous P V has completed.  Tiles wholly below a warp's
+// diagonal skip the causal mask.  The epilogue divides O by the row sums and
 // writes bf16 rows.  Every wait is bounded; on expiry the CTA sets bit 0 of
 // *err and returns once its copies have landed.
 constexpr int kTcRows = 128;
 constexpr int kTcKeys = 128;
 constexpr uint32_t kTcBox = 16384;                     // a [128][64] bf16 box
 constexpr uint32_t kTcQ = 0, kTcStage0 = 2 * kTcBox;   // Q: 2 boxes; stage s: K (2 boxes), V (2 boxes)
-constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P buffers b = 0, 1: 2 boxes each
-constexpr uint32_t kTcSmem = kTcP + 2 * 2 * kTcBox + 1024;
+constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P: 2 boxes (keys 0-63, 64-127)
+constexpr uint32_t kTcSmem = kTcP + 2 * kTcBox + 1024;
 constexpr float kTcRescale = 8.0f;                     // log2 of the largest unnormalised probability
 constexpr long long kTcWait = 2000000000ll;
 
@@ -331,6 +335,13 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t addr, uint32_t mn_blo
 __device__ __forceinline__ uint32_t tc_idesc(bool b_mn) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(128 >> 3) << 17) |
            ((uint32_t)(128 >> 4) << 24);
+}
+
+// 2^x by the MUFU instruction (flush-to-zero; 2^-inf = 0)
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -395,11 +406,13 @@ __device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int
         : "memory");
 }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     pf_attn_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PfTcArgs a) {
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
-    __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s[2], bar_p[2], bar_pv[2];
+    __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s[2], bar_p[2], bar_pv[2], bar_x[2], bar_l;
+    __shared__ float red_max[2][2][kTcRows];  // [tile parity][half][row]
+    __shared__ float red_l[2][kTcRows];
     __shared__ uint32_t tmem_base;
     __shared__ int s_ok;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -420,9 +433,11 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&full_v[s], 1);
             mbar_init(&empty[s], 1);
             mbar_init(&bar_s[s], 1);
-            mbar_init(&bar_p[s], 128);
+            mbar_init(&bar_p[s], 256);
             mbar_init(&bar_pv[s], 1);
+            mbar_init(&bar_x[s], 256);
         }
+        mbar_init(&bar_l, 256);
         mbar_fence_init();
         s_ok = 1;
     }
@@ -483,7 +498,7 @@ __global__ void __launch_bounds__(192, 1)
                 if (!tc_wait(&full_v[s], (i >> 1) & 1u, ok)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t vb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox + 2 * kTcBox;
-                const uint32_t pb = base + kTcP + (uint32_t)s * 2 * kTcBox;
+                const uint32_t pb = base + kTcP;
 #pragma unroll
                 for (int b = 0; b < 2; ++b)
 #pragma unroll
@@ -497,30 +512,44 @@ __global__ void __launch_bounds__(192, 1)
             if (!ok) atomicExch(&s_ok, 0);
         }
     } else {
-        // softmax: thread of TMEM lane r = one query row (token t0 + r / G, head r % G)
-        const int quarter = warp & 3, r = 32 * quarter + lane;
+        // softmax: the thread of TMEM lane r and half h holds keys (and O
+        // columns) [64 h, 64 h + 64) of query row r (token t0 + r / G, head r % G)
+        const int half = (warp - 2) >> 2, quarter = warp & 3, r = 32 * quarter + lane;
         const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
         const int tl = r / G, g = r % G;
         const bool row_ok = t0 + tl < C;
         const int pos = a.p0 + min(t0 + tl, C - 1);
-        float m_ref = -INFINITY, l_run = 0.0f;
+        const float sc = a.scale_log2;
+        float m_ref = -INFINITY, l_half = 0.0f;  // m_ref in base-2 units (scores x sc)
         for (int i = 0; i < ntiles; ++i) {
             const int s = i & 1;
             tc_wait(&bar_s[s], (i >> 1) & 1u, ok);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            float sv[kTcKeys];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                tc_ld32(tmem_base + 128u * (uint32_t)s + lane_off + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
-            const int k0 = i * kTcKeys;
+            float sv[64];
+            const uint32_t sb = tmem_base + 128u * (uint32_t)s + lane_off + 64u * (uint32_t)half;
+            tc_ld32(sb, *reinterpret_cast<float(*)[32]>(sv));
+            tc_ld32(sb + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+            const int k0 = i * kTcKeys + 64 * half;
             float mx = -INFINITY;
+            if (__all_sync(0xffffffffu, k0 + 63 <= pos)) {
 #pragma unroll
-            for (int j = 0; j < kTcKeys; ++j) {
-                sv[j] = k0 + j <= pos ? sv[j] * a.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sv[j]);
+                for (int j = 0; j < 64; ++j) mx = fmaxf(mx, sv[j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    sv[j] = k0 + j <= pos ? sv[j] : -INFINITY;
+                    mx = fmaxf(mx, sv[j]);
+                }
             }
+            // the row maximum over both halves
+            red_max[s][half][r] = mx;
+            mbar_arrive(&bar_x[s]);
+            tc_wait(&bar_x[s], (i >> 1) & 1u, ok);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            mx = fmaxf(red_max[s][0][r], red_max[s][1][r]) * sc;
             if (i == 0) {
                 m_ref = mx;  // every row's first tile holds key 0 <= its position: finite
             } else {
@@ -531,64 +560,66 @@ __global__ void __launch_bounds__(192, 1)
                     ok = __all_sync(0xffffffffu, ok);
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const float alpha = grow ? exp2f(m_ref - mx) : 1.0f;
+                    const float alpha = grow ? ex2_ftz(m_ref - mx) : 1.0f;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         float o[32];
-                        tc_ld32(tmem_o + lane_off + 32 * c, o);
+                        const uint32_t oa = tmem_o + lane_off + 64u * (uint32_t)half + 32u * (uint32_t)c;
+                        tc_ld32(oa, o);
 #pragma unroll
                         for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                        tc_st32(tmem_o + lane_off + 32 * c, o);
+                        tc_st32(oa, o);
                     }
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     if (grow) {
-                        l_run *= alpha;
+                        l_half *= alpha;
                         m_ref = mx;
                     }
                 }
             }
-            if (i >= 2) {
-                // P buffer s was read by P_{i-2} V_{i-2}
-                tc_wait(&bar_pv[s], ((i >> 1) - 1) & 1u, ok);
+            // probabilities of the half row, packed as bf16 pairs
+            float ls = 0.0f;
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float p0 = ex2_ftz(fmaf(sv[2 * j], sc, -m_ref)), p1 = ex2_ftz(fmaf(sv[2 * j + 1], sc, -m_ref));
+                ls += p0 + p1;
+                w[j] = cvt_bf16x2(p0, p1);
+            }
+            l_half += ls;
+            if (i >= 1) {
+                // P is read by P_{i-1} V_{i-1} until it completes
+                tc_wait(&bar_pv[(i - 1) & 1], ((i - 1) >> 1) & 1u, ok);
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
             }
-            float ls = 0.0f;
-            const uint32_t pb = base + kTcP + (uint32_t)s * 2 * kTcBox;
+            const uint32_t pb = base + kTcP + (uint32_t)half * kTcBox + (uint32_t)r * 128u;
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                float p[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    p[e] = exp2f(sv[8 * c + e] - m_ref);
-                    ls += p[e];
-                }
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) w[e] = cvt_bf16x2(p[2 * e], p[2 * e + 1]);
-                const uint32_t addr = pb + (uint32_t)(c >> 3) * kTcBox + (uint32_t)r * 128u +
-                                      ((uint32_t)((c & 7) ^ (r & 7)) << 4);
-                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-                             "r"(w[3])
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t addr = pb + ((uint32_t)(c ^ (r & 7)) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * c]), "r"(w[4 * c + 1]),
+                             "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
                              : "memory");
             }
-            l_run += ls;
             fence_proxy_async_smem();
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(&bar_p[s]);
         }
         if (ok) {
+            red_l[half][r] = l_half;
+            mbar_arrive(&bar_l);
+            tc_wait(&bar_l, 0u, ok);
             tc_wait(&bar_pv[(ntiles - 1) & 1], ((ntiles - 1) >> 1) & 1u, ok);
             ok = __all_sync(0xffffffffu, ok);
         }
         if (ok) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float inv = 1.0f / l_run;
-            uint16_t* out = a.attn + (size_t)(t0 + tl) * a.nq * 128 + (size_t)(kvh * G + g) * 128;
+            const float inv = 1.0f / (red_l[0][r] + red_l[1][r]);
+            uint16_t* out = a.attn + (size_t)(t0 + tl) * a.nq * 128 + (size_t)(kvh * G + g) * 128 + 64 * half;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 float o[32];
-                tc_ld32(tmem_o + lane_off + 32 * c, o);
+                tc_ld32(tmem_o + lane_off + 64u * (uint32_t)half + 32u * (uint32_t)c, o);
                 if (row_ok) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -661,7 +692,7 @@ int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
     a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     const long long ctas = (long long)nkv * ((C + a.tok_per_cta - 1) / a.tok_per_cta);
     INFERNT_REQUIRE(ctas < (1ll << 31), "prefill attention: %lld blocks", ctas);
-    pf_attn_tc<<<(unsigned)ctas, 192, kTcSmem, st>>>(mq, mk, mv, a);
+    pf_attn_tc<<<(unsigned)ctas, 320, kTcSmem, st>>>(mq, mk, mv, a);
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
