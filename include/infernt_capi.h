@@ -179,6 +179,13 @@ INFERNT_API int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, i
  * T >= 1, ldy >= N, W and X 16-byte aligned.  err as infernt_bgemm_bf16. */
 INFERNT_API int infernt_pgemm_bf16(const void* W, int N, int K, const void* X, int T, float* Y,
                                    int ldy, unsigned* err, void* stream);
+/* The gate/up projection of a prompt chunk with SwiGLU in its epilogue
+ * (llama_layer.cpp:61-66, cuda/activation.cu:7-9): W_gate_up [2 I][K] bf16
+ * (gate rows, then up rows), act[t][i] = bf16(silu(g) u) for the FP32 sums
+ * g = X[t] . W_gate[i], u = X[t] . W_up[i]; act rows ld_act elements apart.
+ * I a multiple of 128; otherwise as infernt_pgemm_bf16. */
+INFERNT_API int infernt_pgemm_swiglu_bf16(const void* W_gate_up, int I, int K, const void* X, int T,
+                                          void* act, int ld_act, unsigned* err, void* stream);
 /* Causal attention of a prompt chunk (cuda/attention.cu:9-42 and
  * cuda/softmax.cu:13-48 per query row): q [n_tokens][nq][D] bf16 with RoPE
  * applied, the sequence's caches [nkv][max_seq][D] bf16 holding positions

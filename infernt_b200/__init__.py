@@ -155,6 +155,7 @@ _SIGS = {
     "infernt_checkpoint_free": (_I, [_P]),
     "infernt_batch_engine_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
     "infernt_pgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
+    "infernt_pgemm_swiglu_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_prefill_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P]),
     "infernt_plan_create": (_I, [ctypes.POINTER(LlamaConfig), ctypes.POINTER(_P),
                                  ctypes.POINTER(_P), ctypes.POINTER(_P), _I, ctypes.POINTER(_P)]),

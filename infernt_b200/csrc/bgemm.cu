@@ -26,6 +26,7 @@
 
 #include <cstring>
 
+#include "../../include/infernt_seed.h"
 #include "common.cuh"
 #include "internal.h"
 
@@ -227,14 +228,26 @@ __global__ void __launch_bounds__(kThreads, 2)
 // tcgen05.mma (M = 128, N = tp, K = 16 per instruction) and frees stages with
 // tcgen05.commit, then four warps read the accumulator with tcgen05.ld and
 // store FP32 rows of Y (ldy floats apart).
+//
+// SWIGLU: W is the stacked [gate; up] matrix [2 N][K]; a tile loads the
+// gate rows [n0, n0 + 128) and the up rows [N + n0, ..) per stage into two
+// accumulators (2 tp TMEM columns) and its epilogue stores
+// act[t][n] = bf16(silu(gate) up) (cuda/activation.cu:7-9; the rounding of
+// bt_swiglu), so the FP32 gate/up rows never reach memory.
 constexpr int kPStagesMax = 8;
 
 struct PgemmArgs {
-    float* y;
+    float* y;           // FP32 output (plain)
+    uint16_t* act;      // bf16 output (SWIGLU)
     unsigned* err;
     int N, K, T, tp, tiles_t, ldy, stages;
 };
 
+__device__ __forceinline__ uint16_t pg_bf16_bits(float v) {
+    return (uint16_t)(__float_as_uint(infernt_round_bf16(v)) >> 16);
+}
+
+template <bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
     pgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, PgemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -243,11 +256,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int s_ok;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const uint32_t stage_bytes = kTileW + (uint32_t)a.tp * kBK * 2;
+    constexpr uint32_t kW = SWIGLU ? 2 * kTileW : kTileW;  // weight bytes per stage
+    const uint32_t stage_bytes = kW + (uint32_t)a.tp * kBK * 2;
     const int tile_t = blockIdx.x % a.tiles_t, tile_n = blockIdx.x / a.tiles_t;
     const int n0 = tile_n * kBM, t0 = tile_t * a.tp;
     const int nk = a.K / kBK;
-    const int cols = a.tp <= 32 ? 32 : (a.tp <= 64 ? 64 : (a.tp <= 128 ? 128 : 256));
+    const int acc_cols = a.tp <= 32 ? 32 : (a.tp <= 64 ? 64 : (a.tp <= 128 ? 128 : 256));
+    const int cols = SWIGLU ? 2 * acc_cols : acc_cols;
 
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
@@ -275,7 +290,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char* st = smem + (size_t)s * stage_bytes;
             mbar_arrive_expect_tx(&full[s], stage_bytes);
             tma_load_2d(st, &tm_w, i * kBK, n0, &full[s]);
-            tma_load_2d(st + kTileW, &tm_x, i * kBK, t0, &full[s]);
+            if (SWIGLU) tma_load_2d(st + kTileW, &tm_w, i * kBK, a.N + n0, &full[s]);
+            tma_load_2d(st + kW, &tm_x, i * kBK, t0, &full[s]);
         }
         if (!ok) atomicExch(&s_ok, 0);
     } else if (warp == 1 && lane == 0) {
@@ -285,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!bg_wait(&full[s], (i / a.stages) & 1u, ok)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t wa = smem_addr(smem + (size_t)s * stage_bytes);
-            const uint64_t da = sw128_desc(wa), db = sw128_desc(wa + kTileW);
+            const uint64_t da = sw128_desc(wa), db = sw128_desc(wa + kW), du = sw128_desc(wa + kTileW);
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk) {
                 const uint64_t adv = (uint64_t)((kk * 32) >> 4);
@@ -294,6 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                     "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem),
                     "l"(da + adv), "l"(db + adv), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+                if (SWIGLU)
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(
+                            tmem + (uint32_t)acc_cols),
+                        "l"(du + adv), "l"(db + adv), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                              smem_addr(&empty[s]))
@@ -310,20 +332,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int n = n0 + warp * 32 + lane;
     const int tn = a.T - t0 < a.tp ? a.T - t0 : a.tp;  // tokens of this tile
-    for (int c = 0; c < tn; c += 16) {
-        uint32_t r[16];
-        const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c;
+    auto ld16 = [&](uint32_t addr, uint32_t (&r)[16]) {
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
             "%14, %15}, [%16];"
             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
             : "r"(addr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        float* yc = a.y + (size_t)(t0 + c) * a.ldy + n;
+    };
+    for (int c = 0; c < tn; c += 16) {
+        uint32_t r[16];
+        const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c;
+        ld16(addr, r);
+        if (SWIGLU) {
+            uint32_t u[16];
+            ld16(addr + (uint32_t)acc_cols, u);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            uint16_t* ac = a.act + (size_t)(t0 + c) * a.ldy + n;
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-            if (c + q < tn) yc[(size_t)q * a.ldy] = __uint_as_float(r[q]);
+            for (int q = 0; q < 16; ++q)
+                if (c + q < tn)
+                    ac[(size_t)q * a.ldy] = pg_bf16_bits(silu_mul(__uint_as_float(r[q]), __uint_as_float(u[q])));
+        } else {
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            float* yc = a.y + (size_t)(t0 + c) * a.ldy + n;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (c + q < tn) yc[(size_t)q * a.ldy] = __uint_as_float(r[q]);
+        }
     }
     if (!eok) atomicExch(&s_ok, 0);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -438,9 +474,13 @@ int bgemm_launch(const void* W, int N, int K, const void* X, int T, float* part,
 
 // Host side of one prefill projection: Y [T][ldy] FP32 (columns [0, N)) =
 // X [T][K] bf16 times W [N][K] bf16 transposed; any T >= 1.
-int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
-                 cudaStream_t st) {
-    INFERNT_REQUIRE(W && X && Y, "pgemm: null pointer");
+namespace {
+
+// One prefill projection: plain (Y FP32 [T][ldy], W [N][K]) or SWIGLU (act
+// bf16 [T][ldy], W the stacked [gate; up] matrix [2 N][K]).
+int pgemm_run(bool swiglu, const void* W, int N, int K, const void* X, int T, float* Y, uint16_t* act, int ldy,
+              unsigned* err, cudaStream_t st) {
+    INFERNT_REQUIRE(W && X && (swiglu ? (const void*)act : (const void*)Y), "pgemm: null pointer");
     INFERNT_REQUIRE(N > 0 && N % kBM == 0, "pgemm: N = %d must be a positive multiple of %d", N, kBM);
     INFERNT_REQUIRE(K > 0 && K % kBK == 0, "pgemm: K = %d must be a positive multiple of %d", K, kBK);
     INFERNT_REQUIRE(T >= 1, "pgemm: T = %d", T);
@@ -450,19 +490,25 @@ int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, in
     const int tiles_t = (T + tp - 1) / tp;
     const long long ctas = (long long)(N / kBM) * tiles_t;
     INFERNT_REQUIRE(ctas < (1ll << 31), "pgemm: %lld tiles", ctas);
-    const int per = kTileW + tp * kBK * 2;
+    const int per = (swiglu ? 2 : 1) * kTileW + tp * kBK * 2;
     int stages = (kSmemLimit - 1024) / per;
     if (stages > kPStagesMax) stages = kPStagesMax;
     CUtensorMap mw, mx;
-    if (int s = make_map(&mw, W, N, K, kBM)) return s;
+    if (int s = make_map(&mw, W, swiglu ? 2 * N : N, K, kBM)) return s;
     if (int s = make_map(&mx, X, T, K, tp)) return s;
-    static bool raised = false;
-    if (!raised) {
-        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-        raised = true;
+    static bool raised[2] = {false, false};
+    if (!raised[swiglu]) {
+        if (swiglu)
+            INFERNT_CUDA_TRY(
+                cudaFuncSetAttribute(pgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+        else
+            INFERNT_CUDA_TRY(
+                cudaFuncSetAttribute(pgemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+        raised[swiglu] = true;
     }
     PgemmArgs args;
     args.y = Y;
+    args.act = act;
     args.err = err;
     args.N = N;
     args.K = K;
@@ -471,9 +517,25 @@ int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, in
     args.tiles_t = tiles_t;
     args.ldy = ldy;
     args.stages = stages;
-    pgemm_kernel<<<(unsigned)ctas, kThreads, stages * per + 1024, st>>>(mw, mx, args);
+    if (swiglu)
+        pgemm_kernel<true><<<(unsigned)ctas, kThreads, stages * per + 1024, st>>>(mw, mx, args);
+    else
+        pgemm_kernel<false><<<(unsigned)ctas, kThreads, stages * per + 1024, st>>>(mw, mx, args);
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
+}
+
+}  // namespace
+
+int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
+                 cudaStream_t st) {
+    return pgemm_run(false, W, N, K, X, T, Y, nullptr, ldy, err, st);
+}
+
+// act [T][ldy] bf16 = silu(X W_gate^T) (X W_up^T) for the stacked W_gu [2 I][K].
+int pgemm_swiglu_launch(const void* W_gu, int I, int K, const void* X, int T, uint16_t* act, int ldy, unsigned* err,
+                        cudaStream_t st) {
+    return pgemm_run(true, W_gu, I, K, X, T, nullptr, act, ldy, err, st);
 }
 
 }  // namespace infernt
@@ -486,4 +548,10 @@ extern "C" int infernt_bgemm_bf16(const void* W, int N, int K, const void* X, in
 extern "C" int infernt_pgemm_bf16(const void* W, int N, int K, const void* X, int T, float* Y, int ldy,
                                   unsigned* err, void* stream) {
     return infernt::pgemm_launch(W, N, K, X, T, Y, ldy, err, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int infernt_pgemm_swiglu_bf16(const void* W_gate_up, int I, int K, const void* X, int T, void* act,
+                                         int ld_act, unsigned* err, void* stream) {
+    return infernt::pgemm_swiglu_launch(W_gate_up, I, K, X, T, static_cast<uint16_t*>(act), ld_act, err,
+                                        static_cast<cudaStream_t>(stream));
 }

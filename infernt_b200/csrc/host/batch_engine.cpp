@@ -49,6 +49,8 @@ int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positi
                      int* cand_i, unsigned* tickets, cudaStream_t st);
 int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
                  cudaStream_t st);
+int pgemm_swiglu_launch(const void* W_gu, int I, int K, const void* X, int T, uint16_t* act, int ldy, unsigned* err,
+                        cudaStream_t st);
 int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, const float2* rope, int max_seq,
                        uint16_t* q, uint16_t* kc, uint16_t* vc, cudaStream_t st);
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
@@ -136,15 +138,16 @@ struct infernt_batch_engine {
     // prefill scratch, allocated by the first prefill call for its chunk size
     // (grown by a later call with a larger chunk): prompt tokens [max_seq],
     // residual stream h [C][H] FP32, projection inputs x [C][max(H, Nq D, I)]
-    // bf16 (also the attention output and SwiGLU activations), queries q
-    // [C][Nq D] bf16, projection outputs y [C][max(Q|K|V, 2 I, H)] FP32 (at
-    // least the vocabulary: the last token's logits), (token, position) of the
-    // greedy pick and its argmax ticket
+    // bf16 (also the attention output), queries q [C][Nq D] bf16, SwiGLU
+    // activations act [C][I] bf16, projection outputs y [C][max(Q|K|V, 2 I,
+    // H)] FP32 (at least the vocabulary: the last token's logits), (token,
+    // position) of the greedy pick and its argmax ticket
     int pf_cap = 0;
     int* pf_tokens = nullptr;
     float* pf_h = nullptr;
     uint16_t* pf_x = nullptr;
     uint16_t* pf_q = nullptr;
+    uint16_t* pf_act = nullptr;  // [C][I] bf16 SwiGLU activations (the gate/up projection's output)
     float* pf_y = nullptr;
     int* pf_tok = nullptr;
     unsigned* pf_ticket = nullptr;
@@ -454,9 +457,10 @@ int grow_prefill(infernt_batch_engine* e, int C) {
     release(e, e->pf_h);
     release(e, e->pf_x);
     release(e, e->pf_q);
+    release(e, e->pf_act);
     release(e, e->pf_y);
     e->pf_h = nullptr;
-    e->pf_x = e->pf_q = nullptr;
+    e->pf_x = e->pf_q = e->pf_act = nullptr;
     e->pf_y = nullptr;
     e->pf_cap = 0;
     if (!e->pf_tokens) {
@@ -473,6 +477,7 @@ int grow_prefill(infernt_batch_engine* e, int C) {
     if (int s = alloc(e, sizeof(float) * (size_t)C * H, reinterpret_cast<void**>(&e->pf_h))) return s;
     if (int s = alloc(e, (size_t)C * kx * 2, reinterpret_cast<void**>(&e->pf_x))) return s;
     if (int s = alloc(e, (size_t)C * qs * 2, reinterpret_cast<void**>(&e->pf_q))) return s;
+    if (int s = alloc(e, (size_t)C * I * 2, reinterpret_cast<void**>(&e->pf_act))) return s;
     if (int s = alloc(e, sizeof(float) * y_floats, reinterpret_cast<void**>(&e->pf_y))) return s;
     e->pf_cap = C;
     return INFERNT_OK;
@@ -506,9 +511,9 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
             if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, e->err, 1, st)) return s;
             if (int s = pgemm_launch(ly.o, H, qs, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
             if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, ly.ffn_norm, eps, e->pf_x, st)) return s;
-            if (int s = pgemm_launch(ly.gu, 2 * I, H, e->pf_x, m, e->pf_y, 2 * I, e->err, st)) return s;
-            if (int s = bt_swiglu_launch(e->pf_y, 1, m, I, e->pf_x, st)) return s;
-            if (int s = pgemm_launch(ly.down, H, I, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
+            // gate/up with SwiGLU in its epilogue: bf16 activations, no FP32 gate/up rows
+            if (int s = pgemm_swiglu_launch(ly.gu, I, H, e->pf_x, m, e->pf_act, I, e->err, st)) return s;
+            if (int s = pgemm_launch(ly.down, H, I, e->pf_act, m, e->pf_y, H, e->err, st)) return s;
             const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
             if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, next_norm, eps, e->pf_x, st)) return s;
         }

@@ -76,6 +76,34 @@ def test_pgemm_matches_torch(N, K, T, ldy):
         assert bool(torch.isnan(Y[:, N:]).all())
 
 
+@pytest.mark.parametrize("I,K,T", [
+    (128, 64, 1),
+    (256, 512, 300),     # two token tiles, the second ragged
+    (384, 2048, 513),
+])
+def test_pgemm_swiglu_matches_torch(I, K, T):
+    """silu(g) u rounded to bf16 against PyTorch on the same bf16 operands:
+    g and u differ from the FP32 matmul by summation order only (2e-5
+    relative), so each output is within one bf16 step (2^-7 relative) of
+    the reference value, plus 1e-6 of the largest."""
+    torch = _torch()
+    g = torch.Generator(device="cuda").manual_seed(I + K + T)
+    W = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    X = torch.randn(T, K, device="cuda", generator=g).to(torch.bfloat16)
+    act = torch.zeros(T, I, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ib.call("infernt_pgemm_swiglu_bf16", W.data_ptr(), I, K, X.data_ptr(), T, act.data_ptr(), I, err.data_ptr(),
+            _stream())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    gu = X.float() @ W.float().t()
+    gt, up = gu[:, :I], gu[:, I:]
+    want = gt / (1.0 + torch.exp(-gt)) * up
+    got = act.float()
+    tol = 2.0 ** -7 * want.abs() + 1e-6 * float(want.abs().max())
+    assert bool(((got - want).abs() <= tol).all()), float((got - want).abs().max())
+
+
 def test_pgemm_rejects_bad_shapes():
     torch = _torch()
     W = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
