@@ -248,7 +248,7 @@ __device__ __forceinline__ uint16_t pg_bf16_bits(float v) {
 }
 
 template <bool SWIGLU>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     pgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, PgemmArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     __shared__ uint64_t full[kPStagesMax], empty[kPStagesMax], done;
@@ -486,12 +486,18 @@ int pgemm_run(bool swiglu, const void* W, int N, int K, const void* X, int T, fl
     INFERNT_REQUIRE(T >= 1, "pgemm: T = %d", T);
     INFERNT_REQUIRE(ldy >= N, "pgemm: ldy = %d below N = %d", ldy, N);
     INFERNT_REQUIRE(aligned16(W) && aligned16(X), "pgemm: W and X must be 16-byte aligned");
-    const int tp = T >= kMaxTokens ? kMaxTokens : (T + 15) / 16 * 16;
+    // two CTAs per SM, two 48 KB stages each: one CTA's epilogue (tcgen05.ld
+    // and stores) and pipeline fill run under the other's MMAs; the SwiGLU
+    // variant takes 128 tokens per tile so its two accumulators fit in half
+    // of the tensor memory
+    const int tmax = swiglu ? 128 : kMaxTokens;
+    const int tp = T >= tmax ? tmax : (T + 15) / 16 * 16;
     const int tiles_t = (T + tp - 1) / tp;
     const long long ctas = (long long)(N / kBM) * tiles_t;
     INFERNT_REQUIRE(ctas < (1ll << 31), "pgemm: %lld tiles", ctas);
     const int per = (swiglu ? 2 : 1) * kTileW + tp * kBK * 2;
-    int stages = (kSmemLimit - 1024) / per;
+    int stages = (kSmemLimit / 2 - 1024 - 1024) / per;  // half of the SM per CTA (static part included)
+    if (stages < 2) stages = 2;
     if (stages > kPStagesMax) stages = kPStagesMax;
     CUtensorMap mw, mx;
     if (int s = make_map(&mw, W, swiglu ? 2 * N : N, K, kBM)) return s;
