@@ -5,6 +5,7 @@
 // into 111 kernels) plus a 4-byte device-to-host copy of the next token.
 #pragma once
 
+#include <cstdint>
 #include <memory>
 #include <string>
 #include <vector>
@@ -37,8 +38,9 @@ public:
     InferenceEngine();
     ~InferenceEngine();
 
-    // Model directory loading (INFT v1 files) is outside the decode path and
-    // not provided: these throw std::runtime_error.  Use initialize().
+    // A converted checkpoint directory (config.json, model.bin in INFT v1,
+    // tokenizer.bin), as the reference's src/engine.cpp:14-31; the weights
+    // go through CheckpointLoader (include/checkpoint_loader.h).
     void load_model(const std::string& model_dir);
     void load_model(const ModelConfig& config, const std::string& weights_path,
                     const std::string& tokenizer_path);
@@ -59,6 +61,11 @@ public:
     // sampler (src/engine.cpp:78-104): softmax at the temperature over the
     // logits and a draw from a static mt19937(1337).
     int sample_next_token(float temperature = 0.0f);
+    // Not in the reference: with `on`, sample_next_token(T > 0) draws on the
+    // GPU (infernt_sample_tokens: Gumbel-max, the same distribution,
+    // reproducible per seed and call count) instead of copying the logits to
+    // the host; off (the default) keeps the reference's host sampler.
+    void set_device_sampling(bool on, uint64_t seed = 1337);
 
     // `steps` greedy steps chained on the device from (token_id, position);
     // writes the produced tokens to tokens_out and returns the device time in ms.
@@ -87,4 +94,7 @@ private:
     Tensor tokens_dev_;
     int last_token_;
     bool is_loaded_;
+    bool device_sampling_ = false;
+    uint64_t sample_seed_ = 1337, sample_counter_ = 0;
+    Tensor sample_ws_, sample_out_;
 };

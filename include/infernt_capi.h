@@ -492,6 +492,16 @@ INFERNT_API int infernt_engine_reset(infernt_engine* e);
  * *next_token (host). */
 INFERNT_API int infernt_engine_forward_token(infernt_engine* e, int token, int position,
                                              int* next_token);
+/* InferenceEngine::load_model(model_dir) (src/engine.cpp:14-31): config.json,
+ * model.bin (INFT v1) and tokenizer.bin of a converted checkpoint;
+ * weight_dtype INFERNT_DTYPE_F32 / _BF16 overrides config.json's (negative:
+ * keep it). */
+INFERNT_API int infernt_engine_load_model(const char* model_dir, int weight_dtype, infernt_engine** out);
+/* With on != 0 the engine's sample_next_token(T > 0) draws on the GPU
+ * (infernt_sample_tokens with this seed and a per-engine call counter)
+ * instead of the reference's host mt19937 sampler (the default).  No
+ * counterpart in the reference. */
+INFERNT_API int infernt_engine_set_device_sampling(infernt_engine* e, int on, uint64_t seed);
 /* InferenceEngine::sample_next_token (src/engine.cpp:68-105). */
 INFERNT_API int infernt_engine_sample_next_token(infernt_engine* e, float temperature,
                                                  int* token);

@@ -147,6 +147,8 @@ _SIGS = {
     "infernt_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "infernt_batch_engine_vocab_range": (_I, [_P, _P, _P]),
     "infernt_sample_workspace_bytes": (_S, [_I]),
+    "infernt_engine_set_device_sampling": (_I, [_P, _I, ctypes.c_uint64]),
+    "infernt_engine_load_model": (_I, [ctypes.c_char_p, _I, _P]),
     "infernt_sample_tokens": (_I, [_P, ctypes.c_longlong, _I, _I, _F, ctypes.c_uint64, ctypes.c_uint64, _P, _P,
                                    _P]),
     "infernt_checkpoint_read_config": (_I, [ctypes.c_char_p, ctypes.POINTER(LlamaConfig)]),
@@ -300,6 +302,25 @@ class Engine:
         out = ctypes.c_int()
         call("infernt_engine_sample_next_token", self._h, temperature, ctypes.byref(out))
         return out.value
+
+    def set_device_sampling(self, on: bool = True, seed: int = 1337):
+        """Temperature sampling on the GPU (Gumbel-max) instead of the
+        reference's host sampler."""
+        call("infernt_engine_set_device_sampling", self._h, int(on), seed)
+
+    @classmethod
+    def load_model(cls, model_dir: str, weight_dtype: int = -1) -> "Engine":
+        """InferenceEngine::load_model of a converted checkpoint directory
+        (config.json, model.bin, tokenizer.bin)."""
+        cfg = Checkpoint.read_config(model_dir + "/config.json")
+        if weight_dtype >= 0:
+            cfg = cfg.with_(weight_dtype=weight_dtype)
+        e = cls.__new__(cls)
+        e.cfg = cfg
+        h = ctypes.c_void_p()
+        call("infernt_engine_load_model", model_dir.encode(), weight_dtype, ctypes.byref(h))
+        e._h = h
+        return e
 
     def logits(self):
         import numpy as np

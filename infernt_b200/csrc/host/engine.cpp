@@ -3,6 +3,8 @@
 // token-by-token prefill, greedy or temperature sampling, EOS / max_seq
 // stop, wall-clock GenerationStats.
 #include "engine.h"
+#include "checkpoint_loader.h"
+#include "infernt_capi.h"
 
 #include <cuda_runtime.h>
 
@@ -15,13 +17,26 @@
 InferenceEngine::InferenceEngine() : last_token_(0), is_loaded_(false) {}
 InferenceEngine::~InferenceEngine() = default;
 
-void InferenceEngine::load_model(const std::string&) {
-    throw std::runtime_error("InferenceEngine::load_model: checkpoint loading is not part of this engine; "
-                             "build ModelWeights and call initialize()");
+// A converted checkpoint directory (src/engine.cpp:14-31): config.json,
+// model.bin (INFT v1, host/checkpoint.cpp) and tokenizer.bin.
+void InferenceEngine::load_model(const std::string& model_dir) {
+    load_model(CheckpointLoader::load_config(model_dir + "/config.json"), model_dir + "/model.bin",
+               model_dir + "/tokenizer.bin");
 }
 
-void InferenceEngine::load_model(const ModelConfig&, const std::string&, const std::string&) {
-    load_model(std::string());
+void InferenceEngine::load_model(const ModelConfig& config, const std::string& weights_path,
+                                 const std::string& tokenizer_path) {
+    Tokenizer tok;
+    if (!tok.load(tokenizer_path)) throw std::runtime_error("Failed to load tokenizer from: " + tokenizer_path);
+    ModelWeights w;
+    CheckpointLoader::load_weights(weights_path, config, w, Device::CUDA);
+    initialize(config, std::move(w), std::move(tok));
+}
+
+void InferenceEngine::set_device_sampling(bool on, uint64_t seed) {
+    device_sampling_ = on;
+    sample_seed_ = seed;
+    sample_counter_ = 0;
 }
 
 void InferenceEngine::initialize(const ModelConfig& config, ModelWeights weights, Tokenizer tokenizer) {
@@ -48,6 +63,22 @@ int InferenceEngine::forward_token(int token_id, int position) {
 int InferenceEngine::sample_next_token(float temperature) {
     if (!is_loaded_) throw std::runtime_error("Engine model is not loaded");
     if (temperature <= 0.0f) return last_token_;
+    if (device_sampling_) {
+        // Gumbel-max on the device (sample.cu): one int crosses to the host
+        if (!sample_ws_.is_valid()) {
+            const int bytes = (int)infernt_sample_workspace_bytes(1);
+            sample_ws_ = Tensor::zeros({bytes}, DType::UINT8, Device::CUDA);
+            sample_out_ = Tensor::zeros({1}, DType::INT32, Device::CUDA);
+        }
+        const int s = infernt_sample_tokens(static_cast<const float*>(logits_.data_ptr()), 0, 1, config_.vocab_size,
+                                            temperature, sample_seed_, sample_counter_++,
+                                            static_cast<int*>(sample_out_.data_ptr()), sample_ws_.data_ptr(), nullptr);
+        if (s) throw std::runtime_error(std::string("sample_next_token: ") + infernt_last_error());
+        int tok = 0;
+        if (cudaMemcpy(&tok, sample_out_.data_ptr(), sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+            throw std::runtime_error("sample_next_token: device-to-host copy failed");
+        return tok;
+    }
     Tensor cpu = logits_.to(Device::CPU);
     const float* l = cpu.data_as_float();
     float mx = -1e30f;

@@ -2,6 +2,7 @@
 // (infernt_engine_* in include/infernt_capi.h), for ctypes / cgo / JNI
 // hosts.  The engine is built with seeded synthetic weights generated on
 // the device (include/infernt_seed.h streams; norms 1.0).
+#include "../../../include/checkpoint_loader.h"
 #include <cuda_runtime.h>
 
 #include <cstring>
@@ -157,6 +158,37 @@ int infernt_engine_forward_token(infernt_engine* e, int token, int position, int
     } catch (const std::exception& ex) {
         return infernt::fail(INFERNT_ERR_INVALID_ARGUMENT, "%s", ex.what());
     }
+    return INFERNT_OK;
+}
+
+int infernt_engine_load_model(const char* model_dir, int weight_dtype, infernt_engine** out) {
+    INFERNT_REQUIRE(model_dir && out, "engine_load_model: null argument");
+    INFERNT_REQUIRE(weight_dtype == INFERNT_DTYPE_F32 || weight_dtype == INFERNT_DTYPE_BF16 || weight_dtype < 0,
+                    "engine_load_model: weight_dtype %d", weight_dtype);
+    *out = nullptr;
+    try {
+        const std::string dir(model_dir);
+        ModelConfig mc = CheckpointLoader::load_config(dir + "/config.json");
+        if (weight_dtype >= 0) mc.weight_dtype = weight_dtype == INFERNT_DTYPE_BF16 ? DType::BF16 : DType::FP32;
+        auto* e = new infernt_engine();
+        try {
+            e->engine.load_model(mc, dir + "/model.bin", dir + "/tokenizer.bin");
+        } catch (...) {
+            delete e;
+            throw;
+        }
+        *out = e;
+        return INFERNT_OK;
+    } catch (const std::bad_alloc&) {
+        return infernt::fail(INFERNT_ERR_OUT_OF_MEMORY, "engine_load_model: host allocation failed");
+    } catch (const std::exception& ex) {
+        return infernt::fail(INFERNT_ERR_INVALID_ARGUMENT, "engine_load_model: %s", ex.what());
+    }
+}
+
+int infernt_engine_set_device_sampling(infernt_engine* e, int on, uint64_t seed) {
+    INFERNT_REQUIRE(e, "engine_set_device_sampling: null engine");
+    e->engine.set_device_sampling(on != 0, seed);
     return INFERNT_OK;
 }
 

@@ -80,3 +80,55 @@ def test_checkpoint_fp32_decodes_like_oracle(tmp_path, cuda):
 
 def test_checkpoint_bf16_option_decodes_like_oracle(tmp_path, cuda):
     run(tmp_path, cuda, bf16=True)
+
+
+def write_tokenizer(path, n):
+    """tokenizer.bin as the engine's Tokenizer::load reads it: uint32 count,
+    uint32 longest piece, then per piece float score, int32 length, bytes."""
+    import struct
+    pieces = [("t%d" % i).encode() for i in range(n)]
+    with open(path, "wb") as f:
+        f.write(struct.pack("II", n, max(len(p) for p in pieces)))
+        for i, p in enumerate(pieces):
+            f.write(struct.pack("fi", -float(i), len(p)))
+            f.write(p)
+
+
+def test_engine_load_model_and_device_sampling(tmp_path, cuda):
+    """InferenceEngine::load_model of a checkpoint directory decodes like the
+    oracle; with device sampling on, sample_next_token(T) draws from
+    softmax(logits / T) of the last step (the top token's frequency within
+    6 standard deviations of its probability over 3000 draws)."""
+    orc = O.LlamaOracle(CFG, seed=4)
+    d = str(tmp_path)
+    write_config(d + "/config.json", CFG)
+    write_inft(d + "/model.bin", oracle_tensors(orc, CFG))
+    write_tokenizer(d + "/tokenizer.bin", CFG.vocab_size)
+    eng = ib.Engine.load_model(d)
+    prompt = O.prompt(4, 4, 3, CFG.vocab_size)
+    tok = None
+    for pos in range(8):
+        t_in = int(prompt[pos]) if pos < len(prompt) else tok
+        got_tok = eng.forward_token(t_in, pos)
+        want_tok, want = orc.decode_token(t_in, pos)
+        got = eng.logits()
+        err = float(np.abs(got - want).max())
+        assert err <= 1e-3 and err / float(np.abs(want).max()) <= 1e-4, (pos, err)
+        if got_tok != want_tok:
+            s = np.sort(want)
+            assert s[-1] - s[-2] < 1e-4, pos
+        tok = got_tok
+    eng.set_device_sampling(True, seed=9)
+    T = 0.05
+    z = want.astype(np.float64) / T
+    p = np.exp(z - z.max())
+    p /= p.sum()
+    top = int(np.argmax(p))
+    n = 3000
+    draws = np.array([eng.sample_next_token(T) for _ in range(n)])
+    assert draws.min() >= 0 and draws.max() < CFG.vocab_size
+    c = int((draws == top).sum())
+    sd = np.sqrt(n * p[top] * (1 - p[top])) + 1e-9
+    assert abs(c - n * p[top]) <= 6 * sd + 1, (c, n * p[top])
+    assert eng.sample_next_token(0.0) == tok
+    eng.close()
