@@ -195,9 +195,9 @@ INFERNT_API int infernt_pgemm_swiglu_bf16(const void* W_gate_up, int I, int K, c
  * cores as bf16 (FP32 scores, softmax and sums), so each output is within
  * 2^-8 of the largest |V| of its head (bf16 probabilities, bf16 output).
  * D in {64, 128}; nq / nkv in {1, 2, 4, 8}; all pointers 16-byte aligned
- * device memory; asynchronous on `stream`.  tensor_cores != 0 at D = 128:
- * the tcgen05 kernel (S and O in tensor memory; err, or NULL, gets bit 0 if
- * one of its bounded waits ran out); otherwise mma.sync. */
+ * device memory; asynchronous on `stream`.  tensor_cores != 0: the tcgen05
+ * kernel (S and O in tensor memory; err, or NULL, gets bit 0 if one of its
+ * bounded waits ran out); 0: the mma.sync kernel. */
 INFERNT_API int infernt_prefill_attention(const void* q, const void* k_cache, const void* v_cache,
                                           int n_tokens, int start_pos, int nq, int nkv,
                                           int head_dim, int max_seq, void* attn, unsigned* err,

@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
 }
 
 // ------------------------------------------------ tensor-core attention
-// The same causal GQA attention for head_dim 128 on the 5th-generation
+// The same causal GQA attention for head_dim 64 or 128 on the 5th-generation
 // tensor cores, S and O in tensor memory.  One CTA of 10 warps per (KV head,
 // block of 128 / G tokens): its 128 query rows (token, head of the group)
 // are the MMA's M.  Per 128-key tile i:
@@ -291,10 +291,18 @@ __global__ void __launch_bounds__(256, D == 64 ? 2 : 1) pf_attn(const PfAttnArgs
 // *err and returns once its copies have landed.
 constexpr int kTcRows = 128;
 constexpr int kTcKeys = 128;
-constexpr uint32_t kTcBox = 16384;                     // a [128][64] bf16 box
-constexpr uint32_t kTcQ = 0, kTcStage0 = 2 * kTcBox;   // Q: 2 boxes; stage s: K (2 boxes), V (2 boxes)
-constexpr uint32_t kTcP = kTcStage0 + 2 * 4 * kTcBox;  // P: 2 boxes (keys 0-63, 64-127)
-constexpr uint32_t kTcSmem = kTcP + 2 * kTcBox + 1024;
+constexpr uint32_t kTcBox = 16384;  // a [128][64] bf16 box
+// Shared memory for head_dim D (D / 64 boxes per row block): Q, then two
+// stages of K and V, then P (2 boxes: keys 0-63, 64-127).
+template <int D>
+struct TcLayout {
+    static constexpr uint32_t kBoxes = D / 64;
+    static constexpr uint32_t kQ = 0;
+    static constexpr uint32_t kStage0 = kBoxes * kTcBox;
+    static constexpr uint32_t kStage = 2 * kBoxes * kTcBox;  // K boxes, then V boxes
+    static constexpr uint32_t kP = kStage0 + 2 * kStage;
+    static constexpr uint32_t kSmem = kP + 2 * kTcBox + 1024;
+};
 constexpr float kTcRescale = 8.0f;                     // log2 of the largest unnormalised probability
 constexpr long long kTcWait = 2000000000ll;
 
@@ -331,9 +339,9 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t addr, uint32_t mn_blo
            (uint64_t)(1024u >> 4) << 32 | (uint64_t)1u << 46 | (uint64_t)2u << 61;
 }
 
-// D FP32, A and B bf16, M = 128, N = 128; B MN-major when b_mn.
-__device__ __forceinline__ uint32_t tc_idesc(bool b_mn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(128 >> 3) << 17) |
+// D FP32, A and B bf16, M = 128, N = n; B MN-major when b_mn.
+__device__ __forceinline__ uint32_t tc_idesc(bool b_mn, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn ? (1u << 16) : 0u) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(128 >> 4) << 24);
 }
 
@@ -406,9 +414,14 @@ __device__ __forceinline__ void tma_4d(uint32_t dst, const CUtensorMap* map, int
         : "memory");
 }
 
+template <int D>
 __global__ void __launch_bounds__(320, 1)
     pf_attn_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PfTcArgs a) {
+    using Lay = TcLayout<D>;
+    constexpr uint32_t NB = Lay::kBoxes;
+    constexpr uint32_t kTcQ = Lay::kQ, kTcStage0 = Lay::kStage0, kTcStage = Lay::kStage, kTcP = Lay::kP;
+    constexpr int HALF = D / 2;  // O columns per softmax half
     extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
     __shared__ uint64_t full_q, full_k[2], full_v[2], empty[2], bar_s[2], bar_p[2], bar_pv[2], bar_x[2], bar_l;
     __shared__ float red_max[2][2][kTcRows];  // [tile parity][half][row]
@@ -454,33 +467,30 @@ __global__ void __launch_bounds__(320, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(&full_q, 2 * kTcBox);
-            tma_4d(base + kTcQ, &tm_q, 0, 0, kvh, t0, &full_q);
-            tma_4d(base + kTcQ + kTcBox, &tm_q, 64, 0, kvh, t0, &full_q);
+            mbar_arrive_expect_tx(&full_q, NB * kTcBox);
+            for (uint32_t b = 0; b < NB; ++b) tma_4d(base + kTcQ + b * kTcBox, &tm_q, 64 * b, 0, kvh, t0, &full_q);
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i & 1;
                 if (i >= 2 && !tc_wait(&empty[s], ((i >> 1) - 1) & 1u, ok)) break;
-                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox, vb = kb + 2 * kTcBox;
-                mbar_arrive_expect_tx(&full_k[s], 2 * kTcBox);
-                tma_3d(kb, &tm_k, 0, i * kTcKeys, kvh, &full_k[s]);
-                tma_3d(kb + kTcBox, &tm_k, 64, i * kTcKeys, kvh, &full_k[s]);
-                mbar_arrive_expect_tx(&full_v[s], 2 * kTcBox);
-                tma_3d(vb, &tm_v, 0, i * kTcKeys, kvh, &full_v[s]);
-                tma_3d(vb + kTcBox, &tm_v, 64, i * kTcKeys, kvh, &full_v[s]);
+                const uint32_t kb = base + kTcStage0 + (uint32_t)s * kTcStage, vb = kb + NB * kTcBox;
+                mbar_arrive_expect_tx(&full_k[s], NB * kTcBox);
+                for (uint32_t b = 0; b < NB; ++b) tma_3d(kb + b * kTcBox, &tm_k, 64 * b, i * kTcKeys, kvh, &full_k[s]);
+                mbar_arrive_expect_tx(&full_v[s], NB * kTcBox);
+                for (uint32_t b = 0; b < NB; ++b) tma_3d(vb + b * kTcBox, &tm_v, 64 * b, i * kTcKeys, kvh, &full_v[s]);
             }
             if (!ok) atomicExch(&s_ok, 0);
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t id_s = tc_idesc(false), id_o = tc_idesc(true);
+            const uint32_t id_s = tc_idesc(false, kTcKeys), id_o = tc_idesc(true, D);
             // S_j = Q K_j^T into score buffer j % 2
             auto scores = [&](int j) {
                 const int s = j & 1;
-                const uint32_t kb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox;
+                const uint32_t kb = base + kTcStage0 + (uint32_t)s * kTcStage;
                 if (!tc_wait(&full_k[s], (j >> 1) & 1u, ok)) return;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int b = 0; b < 2; ++b)
+                for (int b = 0; b < (int)NB; ++b)
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         tc_mma(tmem_base + 128u * (uint32_t)s, desc_k_sw128(base + kTcQ + b * kTcBox) + 2 * kk,
@@ -497,7 +507,7 @@ __global__ void __launch_bounds__(320, 1)
                 if (!tc_wait(&bar_p[s], (i >> 1) & 1u, ok)) break;
                 if (!tc_wait(&full_v[s], (i >> 1) & 1u, ok)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t vb = base + kTcStage0 + (uint32_t)s * 4 * kTcBox + 2 * kTcBox;
+                const uint32_t vb = base + kTcStage0 + (uint32_t)s * kTcStage + NB * kTcBox;
                 const uint32_t pb = base + kTcP;
 #pragma unroll
                 for (int b = 0; b < 2; ++b)
@@ -562,9 +572,9 @@ __global__ void __launch_bounds__(320, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const float alpha = grow ? ex2_ftz(m_ref - mx) : 1.0f;
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
+                    for (int c = 0; c < HALF / 32; ++c) {
                         float o[32];
-                        const uint32_t oa = tmem_o + lane_off + 64u * (uint32_t)half + 32u * (uint32_t)c;
+                        const uint32_t oa = tmem_o + lane_off + (uint32_t)(HALF * half) + 32u * (uint32_t)c;
                         tc_ld32(oa, o);
 #pragma unroll
                         for (int e = 0; e < 32; ++e) o[e] *= alpha;
@@ -615,11 +625,11 @@ __global__ void __launch_bounds__(320, 1)
         if (ok) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const float inv = 1.0f / (red_l[0][r] + red_l[1][r]);
-            uint16_t* out = a.attn + (size_t)(t0 + tl) * a.nq * 128 + (size_t)(kvh * G + g) * 128 + 64 * half;
+            uint16_t* out = a.attn + (size_t)(t0 + tl) * a.nq * D + (size_t)(kvh * G + g) * D + HALF * half;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
+            for (int c = 0; c < HALF / 32; ++c) {
                 float o[32];
-                tc_ld32(tmem_o + lane_off + 64u * (uint32_t)half + 32u * (uint32_t)c, o);
+                tc_ld32(tmem_o + lane_off + (uint32_t)(HALF * half) + 32u * (uint32_t)c, o);
                 if (row_ok) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -658,9 +668,11 @@ int encode_map(CUtensorMap* map, int rank, const void* base, const cuuint64_t* d
     return INFERNT_OK;
 }
 
+template <int D>
 int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
                       int max_seq, uint16_t* attn, unsigned* err, cudaStream_t st) {
-    const int G = nq / nkv, D = 128;
+    const int G = nq / nkv;
+    constexpr uint32_t kTcSmem = TcLayout<D>::kSmem;
     CUtensorMap mq, mk, mv;
     {
         const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)G, (cuuint64_t)nkv, (cuuint64_t)C};
@@ -677,7 +689,7 @@ int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
     }
     static bool raised = false;
     if (!raised) {
-        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
         raised = true;
     }
     PfTcArgs a;
@@ -692,7 +704,7 @@ int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
     a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     const long long ctas = (long long)nkv * ((C + a.tok_per_cta - 1) / a.tok_per_cta);
     INFERNT_REQUIRE(ctas < (1ll << 31), "prefill attention: %lld blocks", ctas);
-    pf_attn_tc<<<(unsigned)ctas, 320, kTcSmem, st>>>(mq, mk, mv, a);
+    pf_attn_tc<D><<<(unsigned)ctas, 320, kTcSmem, st>>>(mq, mk, mv, a);
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -755,8 +767,10 @@ int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* v
     a.max_seq = max_seq;
     a.scale_log2 = 1.4426950408889634f / sqrtf((float)D);
     const int G = nq / nkv;
-    if (D == 128 && tensor_cores && (G == 1 || G == 2 || G == 4 || G == 8))
-        return launch_pf_attn_tc(q, kc, vc, C, p0, nq, nkv, max_seq, attn, err, st);
+    if (tensor_cores && (G == 1 || G == 2 || G == 4 || G == 8)) {
+        if (D == 128) return launch_pf_attn_tc<128>(q, kc, vc, C, p0, nq, nkv, max_seq, attn, err, st);
+        if (D == 64) return launch_pf_attn_tc<64>(q, kc, vc, C, p0, nq, nkv, max_seq, attn, err, st);
+    }
     if (D == 64) return pf_attn_group<64>(a, G, st);
     if (D == 128) return pf_attn_group<128>(a, G, st);
     return fail(INFERNT_ERR_UNSUPPORTED, "prefill attention: head_dim %d (64 or 128)", D);

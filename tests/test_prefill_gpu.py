@@ -141,7 +141,11 @@ def ref_causal_attention(q, k, v, p0):
     (128, 4, 4, 33, 64, 0),      # one query head per KV head
     (128, 32, 8, 300, 1000, 0),  # 8B head layout, a chunk after 1000 positions
     (64, 32, 4, 257, 0, 0),      # TinyLlama head layout
-    # the tensor-core kernel (head_dim 128)
+    # the tensor-core kernel
+    (64, 8, 1, 1, 0, 1),         # head_dim 64: one token, one key
+    (64, 8, 1, 100, 37, 1),      # groups of 8 (TinyLlama), ragged blocks
+    (64, 32, 4, 257, 0, 1),      # TinyLlama head layout
+    (64, 4, 2, 700, 300, 1),     # groups of 2, several key tiles, diagonal tiles
     (128, 8, 2, 1, 0, 1),        # one token, one key
     (128, 8, 2, 65, 200, 1),     # groups of 4, partial last block, keys past one 128-key tile
     (128, 4, 4, 33, 64, 1),      # one query head per KV head
