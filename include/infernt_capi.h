@@ -362,6 +362,17 @@ INFERNT_API int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, c
  * arrays [nkv][n_pos][head_dim] of bf16 bits (uint16). */
 INFERNT_API int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, int n_pos,
                                              void* k_host, void* v_host);
+/* Token choice of the following steps (and of prefill's first token):
+ * temperature 0 greedy (the default; InferenceEngine's temperature <= 0
+ * path), otherwise a draw from softmax(logits / temperature) per sequence
+ * (src/engine.cpp:78-104 samples that distribution on the host) by
+ * Gumbel-max inside the argmax kernels: the token with the largest logit /
+ * T + g_i, g_i = -ln(-ln u_i), u_i hashed from (seed, the sequence's
+ * position, i) as infernt_sample_tokens(..., seed, counter = position)
+ * draws it.  Reproducible per seed; not the reference's mt19937 sequence.
+ * The step graph is captured again at the next step. */
+INFERNT_API int infernt_batch_engine_set_sampling(infernt_batch_engine* e, float temperature,
+                                                  uint64_t seed);
 /* K splits of the Q|K|V, O, gate|up, down and LM-head projections and the
  * attention's KV splits (6 ints). */
 INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);

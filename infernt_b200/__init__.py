@@ -146,6 +146,7 @@ _SIGS = {
     "infernt_batch_engine_create_tp": (_I, [_P, _I, ctypes.c_uint64, _F, _I, _I, _I, _P, _P]),
     "infernt_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "infernt_batch_engine_vocab_range": (_I, [_P, _P, _P]),
+    "infernt_batch_engine_set_sampling": (_I, [_P, _F, ctypes.c_uint64]),
     "infernt_sample_workspace_bytes": (_S, [_I]),
     "infernt_engine_set_device_sampling": (_I, [_P, _I, ctypes.c_uint64]),
     "infernt_engine_load_model": (_I, [ctypes.c_char_p, _I, _P]),
@@ -448,6 +449,11 @@ class BatchEngine:
         call("infernt_batch_engine_read_kv", self._h, seq, layer, n_pos, k.ctypes.data, v.ctypes.data)
         widen = lambda a: (a.astype(np.uint32) << 16).view(np.float32)
         return widen(k), widen(v)
+
+    def set_sampling(self, temperature: float, seed: int = 0):
+        """Temperature sampling (Gumbel-max in the argmax kernels) for the
+        following steps; temperature 0 is greedy."""
+        call("infernt_batch_engine_set_sampling", self._h, temperature, seed)
 
     def splits(self):
         out = (ctypes.c_int * 6)()

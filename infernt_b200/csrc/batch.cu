@@ -23,6 +23,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "internal.h"
+#include "sample.cuh"
 #include "warp_mma.cuh"
 
 namespace infernt {
@@ -738,7 +739,8 @@ __global__ void bt_attn_merge(const float* part, const int* positions, int nq, i
 constexpr int kArgChunks = 8;
 
 __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int* tokens, int* positions, int* hist,
-                                                 float* cand_v, int* cand_i, unsigned* tickets) {
+                                                 float* cand_v, int* cand_i, unsigned* tickets, float inv_t,
+                                                 uint64_t seed) {
     pdl_wait();  // the previous kernel of the step has completed
     pdl_launch_dependents();
     __shared__ float bv[8];
@@ -747,12 +749,20 @@ __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int
     const int n4 = V / 4;
     const int c0 = (int)((long long)n4 * chunk / kArgChunks), c1 = (int)((long long)n4 * (chunk + 1) / kArgChunks);
     const float4* lt = reinterpret_cast<const float4*>(logits + (size_t)t * V);
+    // temperature sampling (inv_t > 0): Gumbel scores keyed by (seed, the
+    // sequence's position), so chained steps draw fresh noise without a host
+    // counter; every chunk reads the position before the last one advances it
+    const bool sample = inv_t > 0.0f;
+    const uint64_t key = sample ? infernt_stream_key(seed, (uint64_t)positions[t]) : 0;
     float v = -INFINITY;
     int id = 4 * c0;  // equal to the old single-pass start (index 0) once chunks combine in order
 #pragma unroll 4
     for (int i = c0 + tid; i < c1; i += 256) {
         const float4 x = lt[i];
-        const float xs[4] = {x.x, x.y, x.z, x.w};
+        float xs[4] = {x.x, x.y, x.z, x.w};
+        if (sample)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) xs[e] = gumbel_score(xs[e], inv_t, key, (uint64_t)(4 * i + e));
 #pragma unroll
         for (int e = 0; e < 4; ++e)
             if (argmax_better(xs[e], 4 * i + e, v, id)) {
@@ -833,17 +843,20 @@ __global__ void tp_sum_splits(const float* part, int splits, int T, int N, float
 // Greedy pick of sequence t over this rank's vocabulary rows: logits [T][ld]
 // (rows [0, vl) valid, vocabulary ids v0 + row) -> cand[t] = (value, id).
 // The lowest id wins among equal values; NaN never wins.
-__global__ void __launch_bounds__(256) tp_argmax_local(const float* logits, int ld, int vl, int v0, int2* cand) {
+__global__ void __launch_bounds__(256) tp_argmax_local(const float* logits, int ld, int vl, int v0, int2* cand,
+                                                       const int* positions, float inv_t, uint64_t seed) {
     pdl_wait();
     pdl_launch_dependents();
     __shared__ float bv[8];
     __shared__ int bi[8];
     const int t = blockIdx.x, tid = threadIdx.x;
     const float* row = logits + (size_t)t * ld;
+    const bool sample = inv_t > 0.0f;  // Gumbel scores over global vocabulary ids, as bt_argmax
+    const uint64_t key = sample ? infernt_stream_key(seed, (uint64_t)positions[t]) : 0;
     float v = -INFINITY;
     int id = v0;
     for (int i = tid; i < vl; i += 256) {
-        const float x = row[i];
+        const float x = sample ? gumbel_score(row[i], inv_t, key, (uint64_t)(v0 + i)) : row[i];
         if (argmax_better(x, v0 + i, v, id)) {
             v = x;
             id = v0 + i;
@@ -1120,8 +1133,10 @@ int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, 
     return INFERNT_OK;
 }
 
-int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, cudaStream_t st) {
-    INFERNT_CUDA_TRY(launch_pdl(tp_argmax_local, dim3(T), dim3(256), st, logits, ld, vl, v0, cand));
+int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, const int* positions,
+                           float inv_t, uint64_t seed, cudaStream_t st) {
+    INFERNT_CUDA_TRY(
+        launch_pdl(tp_argmax_local, dim3(T), dim3(256), st, logits, ld, vl, v0, cand, positions, inv_t, seed));
     return INFERNT_OK;
 }
 
@@ -1132,10 +1147,10 @@ int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, i
 }
 
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
-                     int* cand_i, unsigned* tickets, cudaStream_t st) {
+                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st) {
     INFERNT_REQUIRE(V % 4 == 0 && V / 4 >= kArgChunks, "batched argmax: vocabulary %d", V);
     INFERNT_CUDA_TRY(launch_pdl(bt_argmax, dim3(kArgChunks, T), dim3(256), st, logits, V, tokens, positions, hist,
-                                cand_v, cand_i, tickets));
+                                cand_v, cand_i, tickets, inv_t, seed));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }

@@ -46,7 +46,7 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
                       float std_dev, int h0, int nkv_all, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
-                     int* cand_i, unsigned* tickets, cudaStream_t st);
+                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st);
 int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
                  cudaStream_t st);
 int pgemm_swiglu_launch(const void* W_gu, int I, int K, const void* X, int T, uint16_t* act, int ldy, unsigned* err,
@@ -56,7 +56,8 @@ int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, co
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
                         int D, int max_seq, uint16_t* attn, unsigned* err, int tensor_cores, cudaStream_t st);
 int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, cudaStream_t st);
-int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, cudaStream_t st);
+int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, const int* positions,
+                           float inv_t, uint64_t seed, cudaStream_t st);
 int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, int* positions, cudaStream_t st);
 }  // namespace infernt
 
@@ -164,6 +165,10 @@ struct infernt_batch_engine {
     float* ysum = nullptr;
     int2* cand = nullptr;
     int2* cand_all = nullptr;
+    // token choice: greedy (sample_inv_t = 0) or temperature sampling by
+    // Gumbel-max inside the argmax kernels, keyed by (sample_seed, position)
+    float sample_inv_t = 0.0f;
+    uint64_t sample_seed = 0;
 
     ~infernt_batch_engine() {
         if (graph) cudaGraphExecDestroy(graph);  // before the communicator its NCCL nodes use
@@ -394,8 +399,10 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
     // the LM head runs unsplit: part[0] holds the logits [T][vlp]
     if (e->world == 1)
         return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, e->cand_v, e->cand_i, e->am_tickets,
-                                st);
-    if (int s = tp_argmax_local_launch(e->part, T, e->vlp, e->vl, e->v0, e->cand, st)) return s;
+                                e->sample_inv_t, e->sample_seed, st);
+    if (int s = tp_argmax_local_launch(e->part, T, e->vlp, e->vl, e->v0, e->cand, e->positions, e->sample_inv_t,
+                                       e->sample_seed, st))
+        return s;
     const NcclApi* n = nccl_api();
     const ncclResult_t r =
         n->all_gather(e->cand, e->cand_all, (size_t)2 * T, ncclInt32, static_cast<ncclComm_t>(e->comm), st);
@@ -520,7 +527,8 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
     }
     // the last token's final-normed row is row m - 1 of the last chunk
     if (int s = bgemm_launch(e->lm, V, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
-    return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket, st);
+    return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket,
+                            e->sample_inv_t, e->sample_seed, st);
 }
 
 int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions) {
@@ -795,6 +803,20 @@ int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, in
                                     cudaMemcpyDeviceToHost));
         INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(v_host) + h * row, e->vc[layer] + off, row,
                                     cudaMemcpyDeviceToHost));
+    }
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_set_sampling(infernt_batch_engine* e, float temperature, uint64_t seed) {
+    INFERNT_REQUIRE(e, "batch_engine_set_sampling: null engine");
+    INFERNT_REQUIRE(!(temperature < 0.0f) && temperature == temperature, "batch_engine_set_sampling: temperature %g",
+                    (double)temperature);
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    e->sample_inv_t = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+    e->sample_seed = seed;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;  // captured again at the next step
     }
     return INFERNT_OK;
 }

@@ -19,6 +19,7 @@
 #include "../../include/infernt_seed.h"
 #include "common.cuh"
 #include "internal.h"
+#include "sample.cuh"
 
 namespace infernt {
 namespace {
@@ -30,11 +31,6 @@ struct SampleWs {
     unsigned* tickets;  // [rows]
     int2* cand;         // [rows][kChunks] (score bits, index)
 };
-
-__device__ __forceinline__ float uniform_open(uint64_t key, uint64_t i) {
-    const uint64_t h = infernt_splitmix64(key + i);
-    return ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-}
 
 __global__ void __launch_bounds__(kThreads) sample_gumbel(const float* logits, long long ld, int V, float inv_t,
                                                           bool greedy, uint64_t seed, uint64_t counter, int* out,
@@ -49,7 +45,7 @@ __global__ void __launch_bounds__(kThreads) sample_gumbel(const float* logits, l
     int id = 0x7fffffff;
     for (int i = i0 + tid; i < i1; i += kThreads) {
         float s = lr[i];
-        if (!greedy) s = fmaf(s, inv_t, -logf(-logf(uniform_open(key, (uint64_t)i))));
+        if (!greedy) s = gumbel_score(s, inv_t, key, (uint64_t)i);
         if (argmax_better(s, i, v, id)) {
             v = s;
             id = i;

@@ -93,3 +93,35 @@ def test_rows_with_their_own_logits(cuda):
     logits[np.arange(rows), want] = 0.0
     toks = sample(cuda, logits, rows, 0.8, ld=V)
     assert np.array_equal(toks, want)
+
+
+def test_batched_engine_sampling_matches_the_sampler(cuda):
+    """Temperature sampling fused into the batched engine's argmax
+    (infernt_batch_engine_set_sampling) draws, for every sequence and step,
+    exactly the token infernt_sample_tokens draws from the same logits row
+    with counter = the sequence's position; temperature 0 is greedy again."""
+    cfg = ib.ModelConfig(vocab_size=1024, hidden_size=512, num_layers=2, num_attention_heads=8,
+                         num_key_value_heads=2, intermediate_size=1024, max_seq_len=256,
+                         weight_dtype=ib.DTYPE_BF16)
+    eng = ib.BatchEngine(cfg, 4, seed=3)
+    positions = [0, 10, 40, 100]
+    for b, p in enumerate(positions):
+        eng.fill_kv(b, 50 + b, p)
+    tokens = [5, 6, 7, 8]
+    temp, seed = 0.8, 21
+    eng.set_sampling(temp, seed)
+    differs = 0
+    for _ in range(4):
+        nxt = eng.step(tokens, positions)
+        logits = eng.logits()
+        for b in range(4):
+            want = int(sample(cuda, logits[b], 1, temp, seed=seed, counter=positions[b])[0])
+            assert nxt[b] == want, (b, nxt[b], want)
+            differs += int(nxt[b] != int(np.argmax(logits[b])))
+        tokens, positions = nxt, [p + 1 for p in positions]
+    assert differs > 0  # at this temperature some draws are not the greedy token
+    eng.set_sampling(0.0)
+    nxt = eng.step(tokens, positions)
+    logits = eng.logits()
+    assert nxt == [int(np.argmax(logits[b])) for b in range(4)]
+    eng.close()
