@@ -502,16 +502,12 @@ int pgemm_run(bool swiglu, const void* W, int N, int K, const void* X, int T, fl
     CUtensorMap mw, mx;
     if (int s = make_map(&mw, W, swiglu ? 2 * N : N, K, kBM)) return s;
     if (int s = make_map(&mx, X, T, K, tp)) return s;
-    static bool raised[2] = {false, false};
-    if (!raised[swiglu]) {
-        if (swiglu)
-            INFERNT_CUDA_TRY(
-                cudaFuncSetAttribute(pgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-        else
-            INFERNT_CUDA_TRY(
-                cudaFuncSetAttribute(pgemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
-        raised[swiglu] = true;
-    }
+    // per launch: the attribute belongs to the current device
+    if (swiglu)
+        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pgemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
+    else
+        INFERNT_CUDA_TRY(
+            cudaFuncSetAttribute(pgemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit));
     PgemmArgs args;
     args.y = Y;
     args.act = act;

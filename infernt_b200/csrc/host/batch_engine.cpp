@@ -76,22 +76,23 @@ struct NcclApi {
     decltype(&ncclGetErrorString) err_str = nullptr;
 };
 
-const NcclApi* nccl_api() {
-    static NcclApi api;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
-        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
-        if (h) {
-            api.get_id = reinterpret_cast<decltype(api.get_id)>(dlsym(h, "ncclGetUniqueId"));
-            api.init = reinterpret_cast<decltype(api.init)>(dlsym(h, "ncclCommInitRank"));
-            api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
-            api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
-            api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
-            api.err_str = reinterpret_cast<decltype(api.err_str)>(dlsym(h, "ncclGetErrorString"));
-        }
+NcclApi load_nccl() {
+    NcclApi api;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW);
+    if (h) {
+        api.get_id = reinterpret_cast<decltype(api.get_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.init = reinterpret_cast<decltype(api.init)>(dlsym(h, "ncclCommInitRank"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+        api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.err_str = reinterpret_cast<decltype(api.err_str)>(dlsym(h, "ncclGetErrorString"));
     }
+    return api;
+}
+
+const NcclApi* nccl_api() {
+    static const NcclApi api = load_nccl();  // resolved once, thread-safe initialisation
     const bool ok = api.get_id && api.init && api.all_reduce && api.all_gather && api.destroy && api.err_str;
     return ok ? &api : nullptr;
 }

@@ -687,11 +687,8 @@ int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
         if (int s = encode_map(&mk, 3, kc, dims, strides, box)) return s;
         if (int s = encode_map(&mv, 3, vc, dims, strides, box)) return s;
     }
-    static bool raised = false;
-    if (!raised) {
-        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
-        raised = true;
-    }
+    // per launch (a driver attribute of the current device; prefill kernels run for milliseconds)
+    INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
     PfTcArgs a;
     a.attn = attn;
     a.err = err;
@@ -712,11 +709,7 @@ int launch_pf_attn_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
 template <int D, int G>
 int launch_pf_attn(const PfAttnArgs& a, cudaStream_t st) {
     constexpr int smem = pf_smem_bytes<D>();
-    static bool raised = false;
-    if (!raised) {
-        INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        raised = true;
-    }
+    INFERNT_CUDA_TRY(cudaFuncSetAttribute(pf_attn<D, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     constexpr int BQ = 16 * (kPfWarps / G);
     const long long ctas = (long long)a.nkv * ((a.C + BQ - 1) / BQ);
     INFERNT_REQUIRE(ctas < (1ll << 31), "prefill attention: %lld blocks", ctas);
