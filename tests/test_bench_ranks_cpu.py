@@ -53,3 +53,24 @@ def test_single_process_is_identity():
     import bench
     assert bench.max_over_ranks(torch, 3.5, "cpu") == 3.5
     assert bench.job_tokens_per_s(1, 100, 250.0) == pytest.approx(400.0)
+
+
+def test_prefill_flops_counts_projections_attention_and_lm_head():
+    """The prefill bench's algorithmic FLOPs: 2 per weight element per token
+    for every projection, 4 * Nq * D per (query, visible key) for the causal
+    attention of every layer, and the LM head of the last token; checked
+    against a direct count over tokens and keys."""
+    import bench
+    import infernt_b200 as ib
+    cfg = ib.ModelConfig(vocab_size=96, hidden_size=64, num_layers=3, num_attention_heads=4,
+                         num_key_value_heads=2, intermediate_size=80, max_seq_len=64)
+    for n, start in ((1, 0), (7, 0), (5, 11)):
+        total, proj, attn = bench.prefill_flops(cfg, n, start)
+        H, D, I, L = 64, 16, 80, 3
+        per_token = 0
+        for (rows, cols) in ((4 * D + 2 * 2 * D, H), (H, 4 * D), (2 * I, H), (H, I)):
+            per_token += 2 * rows * cols
+        want_proj = n * L * per_token
+        want_attn = sum(4 * 4 * D * (start + t + 1) * L for t in range(n))
+        assert proj == want_proj and attn == want_attn
+        assert total == want_proj + want_attn + 2 * 96 * H
