@@ -113,8 +113,9 @@ ModelWeights make_weights(const ModelConfig& c, uint64_t seed, float std_dev, in
     ModelWeights w;
     int qs = c.num_attention_heads * c.head_dim;
     int ks = c.num_key_value_heads * c.head_dim;
-    w.embedding = seeded({c.vocab_size, c.hidden_size}, seed, INFERNT_STREAM_EMBEDDING, std_dev,
-                         round_bf16);
+    // the embedding stays FP32 under round_bf16 (the bf16-weight variant
+    // rounds the projections and the LM head only, as the engine stores them)
+    w.embedding = seeded({c.vocab_size, c.hidden_size}, seed, INFERNT_STREAM_EMBEDDING, std_dev, 0);
     w.final_norm = ones({c.hidden_size});
     w.lm_head = seeded({c.vocab_size, c.hidden_size}, seed, INFERNT_STREAM_LM_HEAD, std_dev,
                        round_bf16);
