@@ -413,10 +413,10 @@ INFERNT_API int infernt_batch_attention(const float* q, const void* k_cache, con
  * and its KV heads' caches [Nkv/T, max_seq, D].  The O and down products are
  * all-reduced inside the persistent decode kernel: each rank writes its
  * partial rows into every rank's exchange region over NVLink (peer memory
- * mapped by CUDA IPC) and the ranks meet at a bounded system-scope flag
- * barrier; the next phase adds the partials in rank order, so every rank
- * holds bit-identical activations.  The greedy token is agreed the same
- * way.  Every rank must run the same calls in the same order.
+ * mapped by CUDA IPC) as tagged words, and the next phase polls them and
+ * adds the partials in rank order, so every rank holds bit-identical
+ * activations.  The greedy token is agreed the same way.  Every rank must
+ * run the same calls in the same order.
  *
  * infernt_tp_shard_dims: dims[6] = {Nq/T, Nkv/T, I/T, Ip, first vocabulary
  * row, vocabulary rows} of rank t.  infernt_plan_create_tp: `cfg` is the
@@ -434,6 +434,23 @@ INFERNT_API int infernt_plan_create_tp(const infernt_llama_config* cfg, const vo
                                        int tp_size, infernt_plan** out);
 INFERNT_API int infernt_plan_xchg_handle(infernt_plan* plan, void* handle_out);
 INFERNT_API int infernt_plan_set_peers(infernt_plan* plan, const void* handles);
+/* Bytes of a tensor-parallel plan's exchange region. */
+INFERNT_API int infernt_plan_xchg_bytes(const infernt_plan* plan, size_t* bytes);
+/* In place of infernt_plan_set_peers: every rank's exchange region as a
+ * device pointer this process can read and write (regions[tp_rank] must be
+ * the plan's own), for callers that map peer memory themselves (a symmetric
+ * heap, a virtual-memory mapping).  Each region holds
+ * infernt_plan_xchg_bytes bytes. */
+INFERNT_API int infernt_plan_set_peer_regions(infernt_plan* plan, void* const* regions);
+/* The own exchange region (device pointer). */
+INFERNT_API void* infernt_plan_xchg_region(infernt_plan* plan);
+/* Time budget of every wait inside the persistent decode kernel (ring
+ * slots, tagged activations, peers' partials, the step hand-off), in
+ * microseconds at the maximum SM clock; default 2 000 000 (2 s).  A wait
+ * that runs out sets the wait-timeout bit of the error word, every CTA of
+ * the launch returns, and the next synchronising call reports
+ * INFERNT_ERR_DEVICE; the plan stays usable. */
+INFERNT_API int infernt_plan_set_wait_budget(infernt_plan* plan, long long microseconds);
 
 /* One rank of a tensor-parallel decoder with seeded synthetic weights: the
  * rank's shards are windows of the matrices infernt_engine_create_seeded
@@ -455,6 +472,8 @@ INFERNT_API int infernt_tp_engine_decode_chain(infernt_tp_engine* e, int token, 
                                                int steps, int* tokens_host, float* ms);
 INFERNT_API int infernt_tp_engine_logits(infernt_tp_engine* e, float* logits_host, int n);
 INFERNT_API int infernt_tp_engine_dims(infernt_tp_engine* e, int* dims);
+/* The engine's tensor-parallel plan (owned by the engine). */
+INFERNT_API int infernt_tp_engine_plan(infernt_tp_engine* e, infernt_plan** plan);
 /* decode_chain with the phase timeline of infernt_plan_set_trace recorded into host_out
  * (infernt_plan_trace_entries entries). */
 INFERNT_API int infernt_tp_engine_trace_chain(infernt_tp_engine* e, int token, int position,

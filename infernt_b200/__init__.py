@@ -204,6 +204,11 @@ _SIGS = {
     "infernt_tp_engine_logits": (_I, [_P, _P, _I]),
     "infernt_tp_engine_dims": (_I, [_P, ctypes.POINTER(_I)]),
     "infernt_tp_engine_trace_chain": (_I, [_P, _I, _I, _I, _P, _S]),
+    "infernt_tp_engine_plan": (_I, [_P, ctypes.POINTER(_P)]),
+    "infernt_plan_xchg_bytes": (_I, [_P, ctypes.POINTER(_S)]),
+    "infernt_plan_xchg_region": (_P, [_P]),
+    "infernt_plan_set_peer_regions": (_I, [_P, ctypes.POINTER(_P)]),
+    "infernt_plan_set_wait_budget": (_I, [_P, ctypes.c_longlong]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -575,3 +580,25 @@ class TPEngine:
         """decode_chain with the persistent kernel's phase timeline (as
         Engine.trace_chain)."""
         return _trace(self.cfg, "infernt_tp_engine_trace_chain", self._h, token, position, steps)
+
+    def _plan(self):
+        p = ctypes.c_void_p()
+        call("infernt_tp_engine_plan", self._h, ctypes.byref(p))
+        return p
+
+    def xchg_region(self):
+        """(device pointer, bytes) of this rank's exchange region."""
+        p = self._plan()
+        n = ctypes.c_size_t()
+        call("infernt_plan_xchg_bytes", p, ctypes.byref(n))
+        return lib().infernt_plan_xchg_region(p), n.value
+
+    def set_peer_regions(self, regions):
+        """In place of set_peers: every rank's exchange region as a device
+        pointer of this process (own region at this rank's index)."""
+        arr = (_P * self.world)(*regions)
+        call("infernt_plan_set_peer_regions", self._plan(), arr)
+
+    def set_wait_budget(self, microseconds: int):
+        """Time budget of every wait inside the decode kernel."""
+        call("infernt_plan_set_wait_budget", self._plan(), int(microseconds))

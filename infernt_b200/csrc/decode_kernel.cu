@@ -28,8 +28,8 @@
 // Every output is reduced inside one CTA in a fixed order, so results do
 // not depend on timing and no cross-CTA merge sits on the critical path.
 //
-// Every wait (ring slots, grid barrier, bulk copies) is bounded by a clock
-// budget; on expiry the CTA sets kErrWaitTimeout in the error word, marks
+// Every wait (ring slots, tagged words, bulk copies) is bounded by a clock
+// budget (MegaParams::wait_cycles, about 2 s by default); on expiry the CTA sets kErrWaitTimeout in the error word, marks
 // itself aborted and runs the remaining control flow without waiting, so the
 // kernel always terminates and the host reports INFERNT_ERR_DEVICE.
 #include <cstring>
@@ -46,7 +46,9 @@ constexpr int kMegaSlot = 16384;
 constexpr int kMegaConsumers = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMegaThreads = 160;  // 4 consumer warps and the producer warp
-constexpr long long kWaitCycles = 4000000000ll;  // about 2 s at the maximum SM clock
+// Clock budget of every wait in this CTA (MegaParams::wait_cycles, set by
+// thread 0 before the first barrier).
+__shared__ long long s_wait_cycles;
 constexpr int kResRows = 128;                    // residual rows a CTA stages per phase
 constexpr int kMergeChunk = 8;                   // attention splits merged per round of loads
 constexpr int kMergeRounds = 2;                  // lanes x rounds bound the splits of a KV head (64)
@@ -102,7 +104,7 @@ __device__ __forceinline__ bool mega_wait(uint64_t* bar, uint32_t parity, volati
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > s_wait_cycles) {
             atomicOr(err, kErrWaitTimeout);
             *abort = 1;
             return false;
@@ -181,7 +183,7 @@ struct LLWait {
     __device__ __forceinline__ bool give_up(long long t0, unsigned& spins) const {
         if (*abort) return true;
         if ((++spins & 63u) == 0u) {
-            if ((ld_acquire(err) & kErrWaitTimeout) || clock64() - t0 > kWaitCycles) {
+            if ((ld_acquire(err) & kErrWaitTimeout) || clock64() - t0 > s_wait_cycles) {
                 atomicOr(err, kErrWaitTimeout);
                 *abort = 1;
                 return true;
@@ -1456,6 +1458,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
         sP[0] = p.phases[0];
         sP[1] = p.phases[p.nphases > 1 ? 1 : 0];
         sh.abort = 0;
+        s_wait_cycles = p.wait_cycles;
     }
     __syncthreads();
 

@@ -88,6 +88,9 @@ struct MegaParams {
     // while issuing the phase's slots]; attention phases record the item's
     // inputs landed (1), partial computed (4), merge start and end (5, 6)
     unsigned long long* trace;
+    // SM clock cycles any single wait may take before the kernel gives up
+    // (kErrWaitTimeout in the error word, every CTA returns)
+    long long wait_cycles;
 };
 
 constexpr int kTraceFields = 7;

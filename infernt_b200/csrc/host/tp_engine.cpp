@@ -221,6 +221,12 @@ int infernt_tp_engine_trace_chain(infernt_tp_engine* e, int token, int position,
     return INFERNT_OK;
 }
 
+int infernt_tp_engine_plan(infernt_tp_engine* e, infernt_plan** plan) {
+    INFERNT_REQUIRE(e && plan, "tp_engine_plan: null argument");
+    *plan = e->plan;
+    return INFERNT_OK;
+}
+
 int infernt_tp_engine_dims(infernt_tp_engine* e, int* dims) {
     INFERNT_REQUIRE(e && dims, "tp_engine_dims: null argument");
     memcpy(dims, e->dims, sizeof(e->dims));

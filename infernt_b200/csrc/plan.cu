@@ -111,6 +111,17 @@ struct infernt_plan {
 
 namespace {
 
+// SM clock cycles of `us` microseconds at the device's maximum SM clock.
+long long wait_cycles_for(long long us) {
+    int dev = 0, khz = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev) != cudaSuccess ||
+        khz <= 0) {
+        cudaGetLastError();
+        khz = 2000000;
+    }
+    return us * (long long)khz / 1000;
+}
+
 const int kInputVector = 0;  // layer 0 reads an input embedding vector
 const int kInputToken = 1;   // layer 0 reads the embedding row of state[0]
 
@@ -503,6 +514,7 @@ int build_mega(infernt_plan* p) {
     m.tp_rank = p->tp_rank;
     m.tp_size = p->tp_size;
     m.peers = p->peer_tab;  // set by infernt_plan_set_peers (tensor parallelism)
+    m.wait_cycles = wait_cycles_for(2000000);
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
@@ -715,6 +727,39 @@ int infernt_plan_set_peers(infernt_plan* p, const void* handles) {
     }
     INFERNT_CUDA_TRY(cudaMemcpy(p->peer_tab, tab.data(), sizeof(void*) * kMaxTp, cudaMemcpyHostToDevice));
     p->peers_set = true;
+    return INFERNT_OK;
+}
+
+int infernt_plan_xchg_bytes(const infernt_plan* p, size_t* bytes) {
+    INFERNT_REQUIRE(p && bytes, "plan_xchg_bytes: null argument");
+    INFERNT_REQUIRE(p->tp_size > 1 && p->xch_mem, "plan_xchg_bytes: not a tensor-parallel plan");
+    *bytes = p->xch_bytes;
+    return INFERNT_OK;
+}
+
+void* infernt_plan_xchg_region(infernt_plan* p) { return p ? p->xch_mem : nullptr; }
+
+int infernt_plan_set_peer_regions(infernt_plan* p, void* const* regions) {
+    INFERNT_REQUIRE(p && regions, "plan_set_peer_regions: null argument");
+    INFERNT_REQUIRE(p->tp_size > 1 && p->xch_mem, "plan_set_peer_regions: not a tensor-parallel plan");
+    INFERNT_REQUIRE(!p->peers_set, "plan_set_peer_regions: peers are already set");
+    INFERNT_REQUIRE(regions[p->tp_rank] == p->xch_mem, "plan_set_peer_regions: regions[%d] is not this plan's own",
+                    p->tp_rank);
+    std::vector<unsigned char*> tab(kMaxTp, nullptr);
+    for (int r = 0; r < p->tp_size; ++r) {
+        INFERNT_REQUIRE(regions[r] && aligned16(regions[r]), "plan_set_peer_regions: region %d null or unaligned", r);
+        tab[r] = static_cast<unsigned char*>(regions[r]);
+    }
+    INFERNT_CUDA_TRY(cudaMemcpy(p->peer_tab, tab.data(), sizeof(void*) * kMaxTp, cudaMemcpyHostToDevice));
+    p->peers_set = true;
+    return INFERNT_OK;
+}
+
+int infernt_plan_set_wait_budget(infernt_plan* p, long long microseconds) {
+    INFERNT_REQUIRE(p, "plan_set_wait_budget: null plan");
+    INFERNT_REQUIRE(microseconds > 0 && microseconds <= 600000000ll,
+                    "plan_set_wait_budget: %lld us outside (0, 600 s]", microseconds);
+    p->mega.wait_cycles = wait_cycles_for(microseconds);
     return INFERNT_OK;
 }
 
