@@ -4,34 +4,44 @@
 // steps): per layer the fused RMSNorm + Q/K/V projection, attention (RoPE,
 // KV append, split-KV GQA, merge), O projection + residual, RMSNorm +
 // gate/up + SiLU, down projection + residual; then RMSNorm + LM head +
-// argmax.  Phases are separated by a grid barrier among the consumer warps.
+// argmax.  Phases hand their outputs to the next phase as tagged words
+// (below), with no grid barrier.
 //
-// Warps 0-3 consume; lane 0 of warp 4 produces: it streams the CTA's share
-// of every GEMV phase's weights into a ring of 16 KB shared-memory slots with
-// 1-D bulk copies (cp.async.bulk).  A GEMV phase gives CTA b the output units
-// [U b / P, U (b + 1) / P), whose weight rows are contiguous in row-major
-// memory, so every slot is one contiguous 16 KB run of HBM (two runs where
-// it straddles a matrix or gate/up boundary): the access pattern that
-// streams fastest, and a split balanced to one row per CTA.  Weights do not
-// depend on activations, so the producer runs ahead across phase boundaries
-// and layers while the consumers wait at grid barriers or compute attention.
+// Warps 0-7 consume, as two teams of four warps; lane 0 of warp 8 produces:
+// it streams the CTA's share of every GEMV phase's weights into a ring of
+// 16 KB shared-memory slots with 1-D bulk copies (cp.async.bulk).  A GEMV
+// phase gives CTA b the output units [U b / P, U (b + 1) / P), whose weight
+// rows are contiguous in row-major memory, so every slot is one contiguous
+// 16 KB run of HBM (two runs where it straddles a matrix or gate/up
+// boundary): the access pattern that streams fastest, and a split balanced
+// to one row per CTA.  Weights do not depend on activations, so the
+// producer runs ahead across phase boundaries and layers while the
+// consumers wait for inputs or compute attention.  Warps 9-11 only complete
+// the producer's warpgroup and leave at once.
 //
-// Consumers walk the stream in 512-element pieces, each thread covering 4
-// columns of every piece, in batches of R rows (R = 8 FP32 / 16 bf16; for
-// gate/up R / 2 units, gate rows then up rows), which fill exactly K / 512
-// slots.  Each thread adds a row's pieces in column order into one
-// accumulator per row; for the usual widths the (row, column block) of every
-// piece of a batch is known at compile time and the input columns stay in
-// registers.  Row sums are reduced over the warp by a reduce-scatter (per
-// slot in that case, else once per batch), and the four warps' row sums are
-// added in warp order in the batches' epilogue.
-// Every output is reduced inside one CTA in a fixed order, so results do
-// not depend on timing and no cross-CTA merge sits on the critical path.
+// Consumers walk the stream in 512-element pieces, each thread of a team
+// covering 4 columns of every piece, in batches of R rows (R = 8 FP32 / 16
+// bf16; for gate/up R / 2 units, gate rows then up rows), which fill exactly
+// K / 512 slots.  The teams take turns: when a slot holds whole rows (K / 512
+// divides the pieces of a slot) the even slots of a phase go to team 0 and
+// the odd ones to team 1, otherwise the even batches to team 0 and the odd
+// ones to team 1; a team steps over the other's slots without waiting.  Two
+// teams keep two slots in flight per SM, so after any wait for inputs the
+// consumers drain the ring faster than HBM refills it.  Each thread adds a
+// row's pieces in column order into one accumulator per row; for the usual
+// widths the (row, column block) of every piece of a batch is known at
+// compile time and the input columns stay in registers.  Row sums are
+// reduced over the warp by a reduce-scatter (per slot in that case, else
+// once per batch), and the owning team's four warp sums are added in warp
+// order in the batches' epilogue.  Every output is reduced inside one CTA
+// in a fixed order, so results do not depend on timing and no cross-CTA
+// merge sits on the critical path.
 //
 // Every wait (ring slots, tagged words, bulk copies) is bounded by a clock
-// budget (MegaParams::wait_cycles, about 2 s by default); on expiry the CTA sets kErrWaitTimeout in the error word, marks
-// itself aborted and runs the remaining control flow without waiting, so the
-// kernel always terminates and the host reports INFERNT_ERR_DEVICE.
+// budget (MegaParams::wait_cycles, about 2 s by default); on expiry the CTA
+// sets kErrWaitTimeout in the error word, marks itself aborted and runs the
+// remaining control flow without waiting, so the kernel always terminates
+// and the host reports INFERNT_ERR_DEVICE.
 #include <cstring>
 
 #include "decode_kernel.cuh"
@@ -43,9 +53,20 @@ namespace infernt {
 namespace {
 
 constexpr int kMegaSlot = 16384;
-constexpr int kMegaConsumers = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMegaThreads = 160;  // 4 consumer warps and the producer warp
+constexpr int kMegaConsumers = 256;  // two teams of four consumer warps
+constexpr int kTeamThreads = 128;    // a team covers the 512 columns of a piece, 4 per thread
+constexpr int kTeamWarps = kTeamThreads / 32;
+constexpr int kConsumerWarps = kMegaConsumers / 32;
+constexpr int kProducerWarp = 8;     // lane 0 streams the weights; warps 9-11 leave at once
+constexpr int kMegaThreads = 384;    // three warpgroups
+// Register split (setmaxnreg): the kernel is compiled for 384 threads at
+// kLaunchRegs each; the producer's warpgroup hands registers to the two
+// consumer warpgroups.  The split must not exceed what the launch holds.
+constexpr int kLaunchRegs = 168;
+constexpr int kConsumerRegs = 232;
+constexpr int kProducerRegs = 40;
+static_assert(2 * 128 * kConsumerRegs + 128 * kProducerRegs <= kMegaThreads * kLaunchRegs,
+              "register split exceeds the launch's registers");
 // Clock budget of every wait in this CTA (MegaParams::wait_cycles, set by
 // thread 0 before the first barrier).
 __shared__ long long s_wait_cycles;
@@ -66,13 +87,13 @@ constexpr int kMaxRingSlots = 14;
 
 struct MegaShared {
     int abort;
-    float ss[4];
-    float amv[4];  // LM-head candidate of each consumer warp
-    int ami[4];
+    float ss[kConsumerWarps];
+    float amv[kConsumerWarps];  // LM-head candidate of each consumer warp
+    int ami[kConsumerWarps];
     int res_base;  // first staged residual row
     int res_n;     // staged rows
     float res[kResRows];
-    float gpart[4][kGroupBatch][16];  // per-warp row sums of up to kGroupBatch batches
+    float gpart[2][kTeamWarps][kGroupBatch][16];  // row sums per team and warp of up to kGroupBatch batches
     uint64_t xbar;                    // completion of the input-vector bulk copy
     uint64_t pbar;                   // completion of the next phase descriptor's bulk copy
 };
@@ -422,7 +443,9 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         ss = warp_sum(ss);
         if (lane == 0) sh.ss[warp] = ss;
         named_sync(1, kMegaConsumers);
-        const float tot = ((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3];
+        float tot = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) tot += sh.ss[w];
         const float rms = rsqrtf(tot / (float)K + P.eps);
         // each thread scales the elements it summed
         for (int i = tid * 4; i < K; i += STRIDE) {
@@ -464,13 +487,23 @@ __device__ __forceinline__ float warp_reduce_scatter(const float* in, int lane) 
     return a[0];
 }
 
+// Sum of the warp row sums of accumulator a of batch slot sl: the four
+// warps of team 0 in warp order, then (TWO: rows whose pieces both teams
+// summed) the four of team 1.
+template <bool TWO>
+__device__ __forceinline__ float gpart_sum(const MegaShared& sh, int sl, int a) {
+    float v = ((sh.gpart[0][0][sl][a] + sh.gpart[0][1][sl][a]) + sh.gpart[0][2][sl][a]) + sh.gpart[0][3][sl][a];
+    if (TWO) v = (((v + sh.gpart[1][0][sl][a]) + sh.gpart[1][1][sl][a]) + sh.gpart[1][2][sl][a]) + sh.gpart[1][3][sl][a];
+    return v;
+}
+
 // Epilogue of n batches whose first unit is ub (their row sums in gpart
-// slots [0, n)), units below u1: the four warps' sums added in warp order,
-// then store / residual add / SwiGLU / logits + argmax candidate.  All
-// consumer threads take part; called between named barriers.  Units of a
-// Q|K|V phase are rows of the stacked [q | k | v] output, so the stacked row
-// is the output index.
-template <typename WT, int NS>
+// slots [0, n)), units below u1: the warps' sums added in a fixed order
+// (gpart_sum), then store / residual add / SwiGLU / logits + argmax
+// candidate.  All consumer threads take part; called between named
+// barriers.  Units of a Q|K|V phase are rows of the stacked [q | k | v]
+// output, so the stacked row is the output index.
+template <typename WT, int NS, bool TWO>
 __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaShared& sh, int ub, int n, int u1,
                                 int tid, float& am_v, int& am_i, unsigned ts, unsigned tag) {
     constexpr int BU = MegaRows<WT>::R / NS;
@@ -478,10 +511,10 @@ __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaSha
         const int sl = idx / BU, i = idx % BU;
         const int row = ub + idx;
         if (row >= u1) continue;
-        const float v = ((sh.gpart[0][sl][i] + sh.gpart[1][sl][i]) + sh.gpart[2][sl][i]) + sh.gpart[3][sl][i];
+        const float v = gpart_sum<TWO>(sh, sl, i);
         if (NS == 2) {
             const int u = BU + i;
-            const float yu = ((sh.gpart[0][sl][u] + sh.gpart[1][sl][u]) + sh.gpart[2][sl][u]) + sh.gpart[3][sl][u];
+            const float yu = gpart_sum<TWO>(sh, sl, u);
             st_ll(P.out + row, silu_mul(v, yu), tag);
         } else if (P.epi == kEpiStore) {
             st_ll(P.out + row, v, tag);
@@ -655,6 +688,10 @@ struct SlotReader {
         if (lane == 0) mbar_arrive(&empty[rp->s]);
         rp->advance(slots);
     }
+    // Steps over n slots that the other team consumes (no wait, no release).
+    __device__ __forceinline__ void skip(int n) {
+        for (int i = 0; i < n; ++i) rp->advance(slots);
+    }
 };
 
 // Stream row s of a batch of nb units -> its accumulator: gate rows first,
@@ -702,44 +739,58 @@ __device__ __forceinline__ void slot_row_sums(const unsigned char* wp, const flo
 }
 
 template <typename WT, int NS, int CB>
-__device__ __forceinline__ void batch_regs(SlotReader& rd, const float4* xr, float* gp, int rows, int nb, int tid,
-                                           int lane) {
+__device__ __forceinline__ void batch_regs(SlotReader& rd, const float4* xr, float* gp, int rows, int nb, int ctid,
+                                           int lane, int par) {
     constexpr int R = MegaRows<WT>::R, BU = R / NS;
     constexpr int PT = MegaRows<WT>::PT, EB = MegaRows<WT>::EB;
     constexpr int RS = PT / CB;    // rows per slot
     constexpr int LPR = 32 / RS;   // lanes per row after the reduce-scatter
     static_assert(PT % CB == 0, "CB divides the slot");
     const int nslots = (rows + RS - 1) / RS;
+    // this team's slots of the batch: par, par + 2, ... (par = 0 or 1)
+    if (par >= nslots) {
+        rd.skip(nslots);
+        return;
+    }
     const int srow = lane / LPR;   // this lane's row within a slot after the reduction
     const bool writer = lane % LPR == 0;
+    rd.skip(par);
     float v[RS];
-    slot_row_sums<WT, CB>(rd.take(tid, EB), xr, v);
+    slot_row_sums<WT, CB>(rd.take(ctid, EB), xr, v);
     rd.release(lane);
+    int jl = par;  // the batch slot whose row sums v holds
 #pragma unroll 1
-    for (int j = 1; j < nslots; ++j) {
-        const unsigned char* wp = rd.take(tid, EB);
+    for (int j = par + 2; j < nslots; j += 2) {
+        rd.skip(1);  // the other team's slot j - 1
+        const unsigned char* wp = rd.take(ctid, EB);
         float vn[RS];
         slot_row_sums<WT, CB>(wp, xr, vn);
-        const float r = warp_reduce_scatter<RS>(v, lane);  // slot j - 1
-        const int s = (j - 1) * RS + srow;
+        const float r = warp_reduce_scatter<RS>(v, lane);  // slot jl
+        const int s = jl * RS + srow;
         if (writer && s < rows) gp[stream_row_acc<NS, BU>(s, nb)] = r;
         rd.release(lane);
 #pragma unroll
         for (int k = 0; k < RS; ++k) v[k] = vn[k];
+        jl = j;
     }
     const float r = warp_reduce_scatter<RS>(v, lane);
-    const int s = (nslots - 1) * RS + srow;
+    const int s = jl * RS + srow;
     if (writer && s < rows) gp[stream_row_acc<NS, BU>(s, nb)] = r;
+    rd.skip(nslots - 1 - jl);  // the other team's slots after this team's last
 }
 
 // A batch when K / 512 >= the pieces of a slot: a slot holds the end of one
-// row and at most the start of the next.  Both partial sums are formed
-// without branches (pieces in column order), the running row sum carries
-// over slots, and a finished row goes to its accumulator.  The input columns
-// are read from shared memory.
+// row and at most the start of the next.  The teams take alternate slots
+// (slot g of the ring belongs to team g & 1), so each forms its partial sum
+// of every row over the pieces in its own slots: both partial sums of a
+// slot are formed without branches (pieces in column order), the running
+// row sum carries over slots, and at a row's end the partial goes to its
+// accumulator; a slot of the other team contributes nothing but moves the
+// row and column bookkeeping along.  The input columns are read from
+// shared memory.
 template <typename WT, int NS>
 __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int cb, int rows, int nb, float* acc,
-                                            int tid, int lane) {
+                                            int ctid, int lane, int team) {
     constexpr int R = MegaRows<WT>::R, BU = R / NS;
     constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
     const int npieces = rows * cb;
@@ -747,16 +798,22 @@ __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int
     int s = 0;   // stream row of the slot's first piece
     float run = 0.0f;
     for (int p0 = 0; p0 < npieces; p0 += PT) {
-        const unsigned char* wp = rd.take(tid, EB);
         const int n = min(PT, npieces - p0);
         const int split = cb - q0;  // pieces of row s in this slot (>= 1)
         float pv[PT];
+        if ((rd.rp->s & 1) == team) {
+            const unsigned char* wp = rd.take(ctid, EB);
 #pragma unroll
-        for (int i = 0; i < PT; ++i) {
-            const int q = q0 + i >= cb ? q0 + i - cb : q0 + i;
-            pv[i] = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + q * kPiece));
+            for (int i = 0; i < PT; ++i) {
+                const int q = q0 + i >= cb ? q0 + i - cb : q0 + i;
+                pv[i] = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + q * kPiece));
+            }
+            rd.release(lane);
+        } else {
+#pragma unroll
+            for (int i = 0; i < PT; ++i) pv[i] = 0.0f;
+            rd.skip(1);
         }
-        rd.release(lane);
         float nxt = 0.0f;
 #pragma unroll
         for (int i = 0; i < PT; ++i) {
@@ -780,9 +837,11 @@ __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int
 // Any batch, any cb: the pieces of each slot as independent products, added
 // to a running row sum in stream order; a finished row moves to its
 // accumulator.  Pieces past the batch's end (a short last batch) are not
-// in the stream.
+// in the stream.  As in batch_split, each team sums the pieces of its own
+// slots (the other team's count as zero).
 template <typename WT, int NS>
-__device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, float* acc, int tid, int lane) {
+__device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, float* acc, int ctid, int lane,
+                              int team) {
     constexpr int R = MegaRows<WT>::R, BU = R / NS;
     constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
     const int npieces = (NS == 2 ? 2 * nb : nb) * cb;
@@ -790,18 +849,24 @@ __device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, f
     int r = 0;  // row (stream order) of the next piece
     float racc = 0.0f;
     for (int p0 = 0; p0 < npieces; p0 += PT) {
-        const unsigned char* wp = rd.take(tid, EB);
         const int n = min(PT, npieces - p0);
         float pv[PT];
-        int qi = q;
+        if ((rd.rp->s & 1) == team) {
+            const unsigned char* wp = rd.take(ctid, EB);
+            int qi = q;
 #pragma unroll
-        for (int i = 0; i < PT; ++i) {
-            // bytes past n are stale but inside the slot: read, then dropped
-            const float d = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + qi * kPiece));
-            pv[i] = i < n ? d : 0.0f;
-            if (++qi == cb) qi = 0;
+            for (int i = 0; i < PT; ++i) {
+                // bytes past n are stale but inside the slot: read, then dropped
+                const float d = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + qi * kPiece));
+                pv[i] = i < n ? d : 0.0f;
+                if (++qi == cb) qi = 0;
+            }
+            rd.release(lane);
+        } else {
+#pragma unroll
+            for (int i = 0; i < PT; ++i) pv[i] = 0.0f;
+            rd.skip(1);
         }
-        rd.release(lane);
 #pragma unroll
         for (int i = 0; i < PT; ++i) {
             if (i < n) {
@@ -820,53 +885,60 @@ __device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, f
 template <typename WT, int NS, int CB>
 __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& rd, const float* xs, MegaShared& sh,
                           int tid, int u0, int u1, unsigned ts, unsigned tag) {
-    constexpr int R = MegaRows<WT>::R;
+    constexpr int R = MegaRows<WT>::R, PT = MegaRows<WT>::PT;
     constexpr int BU = R / NS;  // units per batch
-    static_assert(MegaRows<WT>::PT == R, "a batch of R rows fills whole slots");
+    static_assert(PT == R, "a batch of R rows fills whole slots");
+    static_assert(kGroupBatch % 2 == 0, "both teams' batches of a group");
     const int warp = tid >> 5, lane = tid & 31;
-    const float* xt = xs + tid * 4;  // this thread's 4 columns of every piece
+    const int team = warp / kTeamWarps, cwarp = warp % kTeamWarps, ctid = tid % kTeamThreads;
+    const float* xt = xs + ctid * 4;  // this thread's 4 columns of every piece
     constexpr int NXR = CB > 0 ? CB : 1;
     float4 xr[NXR];
     if (CB > 0) {
 #pragma unroll
         for (int c = 0; c < NXR; ++c) xr[c] = *reinterpret_cast<const float4*>(xt + c * kPiece);
     }
-    const bool split = CB == 0 && P.cb >= MegaRows<WT>::PT;
+    const bool split = CB == 0 && P.cb >= PT;
     float am_v = -1e30f;
     int am_i = 0;
     int bi = 0;  // batches finished in this phase
     for (int ub = u0; ub < u1; ub += BU) {
         const int nb = min(BU, u1 - ub);
         const int rows = NS * nb;  // stream rows of the batch
-        float* gp = sh.gpart[warp][bi % kGroupBatch];
+        // slot g of the ring belongs to team g & 1 (the ring has an even
+        // number of slots, so a team's slot one lap earlier was its own)
         if (CB > 0) {
-            batch_regs<WT, NS, NXR>(rd, xr, gp, rows, nb, tid, lane);
+            // whole rows per slot: the owning team's warp sums, team-0 entries
+            batch_regs<WT, NS, NXR>(rd, xr, sh.gpart[0][cwarp][bi % kGroupBatch], rows, nb, ctid, lane,
+                                    (team ^ rd.rp->s) & 1);
         } else {
+            // rows across slots: both teams' partial sums of every row
+            float* gp = sh.gpart[team][cwarp][bi % kGroupBatch];
             float acc[R];
 #pragma unroll
             for (int a = 0; a < R; ++a) acc[a] = 0.0f;
             if (split)
-                batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, tid, lane);
+                batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, ctid, lane, team);
             else
-                batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, tid, lane);
+                batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, ctid, lane, team);
             // the warp's sum of each row; lane L holds row L / (32 / R)
             const float v = warp_reduce_scatter<R>(acc, lane);
             constexpr int kLanesPerRow = 32 / R;
             if (lane % kLanesPerRow == 0) gp[lane / kLanesPerRow] = v;
         }
-        // kGroupBatch batches held: every warp has summed them (all walk the
-        // same rows); run their epilogue before the slots are reused
+        // kGroupBatch batches held: both teams have summed their rows; run
+        // their epilogue before the row-sum slots are reused
         if (++bi % kGroupBatch == 0) {
             named_sync(1, kMegaConsumers);
-            combine_batches<WT, NS>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v, am_i, ts,
-                                    tag);
+            combine_batches<WT, NS, CB == 0>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v,
+                                             am_i, ts, tag);
             named_sync(1, kMegaConsumers);
         }
     }
     const int rest = bi % kGroupBatch;
     if (rest) {
         named_sync(1, kMegaConsumers);
-        combine_batches<WT, NS>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i, ts, tag);
+        combine_batches<WT, NS, CB == 0>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i, ts, tag);
     }
     if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i, tag);
 }
@@ -1450,7 +1522,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
     if (tid == 0) {
         for (int s = 0; s < slots; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kMegaConsumers / 32);
+            mbar_init(&empty[s], kTeamWarps);  // released by the owning team's warps
         }
         mbar_init(&sh.xbar, 1);
         mbar_init(&sh.pbar, 1);
@@ -1462,10 +1534,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
     }
     __syncthreads();
 
-    if (warp == kProducerWarp) {
-        if (lane == 0) produce<WT>(p, ring, full, empty, sh);
+    if (warp >= kProducerWarp) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+        if (warp == kProducerWarp && lane == 0) produce<WT>(p, ring, full, empty, sh);
         return;
     }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
 
     RingPos rp{0, 0u};
     uint32_t xphase = 0, pphase = 0;
@@ -1554,9 +1628,20 @@ int mega_static_smem(int weight_dtype) {
 }
 
 cudaError_t mega_prepare() {
-    cudaError_t e = raise_dynamic_smem_limit(reinterpret_cast<const void*>(decode_mega_kernel<float>));
-    if (e != cudaSuccess) return e;
-    return raise_dynamic_smem_limit(reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16>));
+    // the register split assumes the launch holds kLaunchRegs per thread: a
+    // build that allocated fewer could not satisfy setmaxnreg.inc, so it is
+    // refused here rather than launched
+    for (const void* k : {reinterpret_cast<const void*>(decode_mega_kernel<float>),
+                          reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16>)}) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, k);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs * kMegaThreads < 2 * 128 * kConsumerRegs + 128 * kProducerRegs)
+            return cudaErrorInvalidKernelImage;
+        e = raise_dynamic_smem_limit(k);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 int mega_occupancy(int weight_dtype, int smem_bytes) {

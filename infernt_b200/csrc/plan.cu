@@ -464,6 +464,7 @@ int build_mega(infernt_plan* p) {
     int slots = mega_max_ring_slots();
     const int budget = optin - mega_static_smem(dt) - 256;
     while (slots >= 4 && mega_smem_bytes(slots, x_floats) > budget) --slots;
+    slots &= ~1;  // the two consumer teams own alternate slots: an even ring keeps each slot with one team
     INFERNT_REQUIRE(slots >= 4, "persistent decode: shared memory budget too small");
     const int smem = mega_smem_bytes(slots, x_floats);
     const int per_sm = mega_occupancy(dt, smem);
