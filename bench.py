@@ -205,8 +205,7 @@ def run_ours(args):
     cfg = ib.TINYLLAMA
     K, W = args.steps, args.warmup
     assert PROMPT_TOKENS + W + K <= cfg.max_seq_len, "steps + warmup exceed max_seq_len"
-    import oracle as O  # the prompt generator only (seeded token ids)
-    prompt = [int(t) for t in O.prompt(PROMPT_TOKENS, SEED + rank, 3, cfg.vocab_size)]
+    prompt = ib.prompt(PROMPT_TOKENS, SEED + rank, 3, cfg.vocab_size)
 
     eng = ib.Engine(cfg, seed=SEED, std=STD)
 
@@ -305,15 +304,90 @@ def run_ours(args):
                                       "avg_launch_ms": round(k_ms, 5), "bytes_per_launch": k_bytes},
         "clocks": clocks,
     }
+    eng.close()
+    if not args.no_llama8b:
+        # the 8B-shaped tensor-parallel decode over the same ranks (the
+        # collective path), after the replicas' measurement
+        result["llama8b_tp"] = measure_llama8b_tp(torch, ib, rank, world, local)
     if world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(cfg)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
-    eng.close()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+# The first 64 greedy tokens of the Llama-3-8B-shaped decode below (seed 1,
+# 512-token seeded prompt) on one GPU: the tensor-parallel runs are checked
+# against them.
+LLAMA8B_TP1_TOKENS = None
+
+
+def measure_llama8b_tp(torch, ib, rank, world, local, steps=61, warmup=3):
+    """Llama-3-8B-shaped bf16 greedy decode, batch 1, tensor-parallel over
+    the ranks already in the process group (tp = world): seeded weights
+    (seed 1), a 512-token seeded prompt, `warmup` chained steps, then `steps`
+    chained steps timed with CUDA events on every rank, max over ranks.  The
+    O and down all-reduces and the argmax agreement run inside the
+    persistent kernel over NVLink peer memory.  Returns ms/step, tok/s, the
+    per-GPU HBM fraction, whether every rank produced the same tokens and
+    how many of the first 64 generated tokens equal the one-GPU run's."""
+    import torch.distributed as dist
+    multi = world > 1
+    prompt_len = 512
+    cfg = ib.LLAMA3_8B.with_(max_seq_len=prompt_len + warmup + steps + 8)
+    eng = ib.TPEngine(cfg, rank, world, seed=1, std=STD)
+    if multi:
+        handles = [None] * world
+        dist.all_gather_object(handles, eng.xchg_handle())
+        eng.set_peers(handles)
+        dist.barrier()
+    t = None
+    for pos, tok in enumerate(ib.prompt(prompt_len, 1, 3, cfg.vocab_size)):
+        if multi:
+            dist.barrier()  # the ranks' kernels wait on one another: launch them together
+        t = eng.forward_token(tok, pos)
+    if multi:
+        dist.barrier()
+    toks_w, _ = eng.decode_chain(t, prompt_len, warmup)
+    if multi:
+        dist.barrier()
+    torch.cuda.synchronize()
+    toks, ms = eng.decode_chain(toks_w[-1], prompt_len + warmup, steps)
+    ms_max = max_over_ranks(torch, ms, "cuda")
+    gen = [t] + toks_w + toks
+    if multi:
+        every = [None] * world
+        dist.all_gather_object(every, gen)
+        agree = all(g == every[0] for g in every)
+    else:
+        agree = True
+    ref = LLAMA8B_TP1_TOKENS
+    match = None
+    if ref is not None:
+        match = next((i for i, (a, b) in enumerate(zip(gen, ref)) if a != b), min(len(gen), len(ref)))
+    # per-GPU algorithmic bytes per step: this rank's bf16 weight shards, its
+    # KV rows read by attention (FP32), the embedding row
+    H, L, D = cfg.hidden_size, cfg.num_layers, cfg.head_dim
+    d = eng.dims
+    per_layer = (d[0] * D + 2 * d[1] * D) * H + H * d[0] * D + 2 * d[2] * H + H * d[3]
+    wbytes = 2 * (L * per_layer + d[5] * H)
+    ctx_mean = prompt_len + warmup + steps / 2.0
+    bytes_gpu = wbytes + 2 * L * d[1] * D * 4 * (ctx_mean + 1) + H * 4
+    hbm, src = peaks()
+    eng.close()
+    return {"workload": "llama3-8b-bf16-b1-tp%d" % world, "parallelism": "tp%d" % world,
+            "ms_per_step": round(ms_max / steps, 5), "tok_s": round(steps / (ms_max / 1e3), 2),
+            "steps": steps, "positions": [prompt_len + warmup, prompt_len + warmup + steps],
+            "bytes_per_gpu_per_step": bytes_gpu,
+            "hbm_frac_per_gpu": round(bytes_gpu / (ms_max / steps / 1e3) / 1e9 / hbm, 4),
+            "tokens_agree_across_ranks": agree,
+            "tokens_match_tp1": (match == 64) if match is not None else None,
+            "tokens_matching_tp1": match, "tokens": gen[:64],
+            "all_reduce": "in-kernel over NVLink peer memory (tagged words), after O and down",
+            "kernel": "decode_mega_kernel<bf16> (persistent, one launch per chain)"}
 
 
 def eng_kernels(cfg):
@@ -463,7 +537,6 @@ def run_llama8b_tp(args):
     import torch
     import torch.distributed as dist
     import infernt_b200 as ib
-    import oracle as O
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     if world > 1:
@@ -478,7 +551,7 @@ def run_llama8b_tp(args):
         dist.all_gather_object(handles, eng.xchg_handle())
         eng.set_peers(handles)
         dist.barrier()
-    prompt = [int(t) for t in O.prompt(prompt_len, seed, 3, cfg.vocab_size)]
+    prompt = ib.prompt(prompt_len, seed, 3, cfg.vocab_size)
     t = None
     for pos, tok in enumerate(prompt):
         t = eng.forward_token(tok, pos)
@@ -546,7 +619,6 @@ def run_batched(args, longctx=False, tp=False):
     import torch.distributed as dist
     import numpy as np
     import infernt_b200 as ib
-    import oracle as O
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     if world > 1:
@@ -573,14 +645,14 @@ def run_batched(args, longctx=False, tp=False):
     T = hi - lo
     if not tp:
         eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
-    tokens = [int(t) for t in O.prompt(n_seq, seed, 3, cfg.vocab_size)][lo:hi]
+    tokens = ib.prompt(n_seq, seed, 3, cfg.vocab_size)[lo:hi]
     prefill = None
     if longctx and getattr(args, "real_prefill", False) and not tp:
         # the prompts run through the engine's prefill (tensor-core chunks) and
         # each sequence decodes from the token its prompt produced
         pf_ms = 0.0
         for b in range(T):
-            prompt = O.prompt(int(mine[b]), 5000 + lo + b, 3, cfg.vocab_size)
+            prompt = ib.prompt(int(mine[b]), 5000 + lo + b, 3, cfg.vocab_size)
             nxt, _, ms_b = eng.prefill(b, prompt)
             tokens[b] = nxt
             pf_ms += ms_b
@@ -711,7 +783,6 @@ def run_prefill(args):
     import torch.distributed as dist
     import numpy as np
     import infernt_b200 as ib
-    import oracle as O
     rank, world, local = env_rank()
     torch.cuda.set_device(local)
     if world > 1:
@@ -723,7 +794,7 @@ def run_prefill(args):
     lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
     T = hi - lo
     eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
-    prompts = [np.asarray(O.prompt(n_tok, 1000 + lo + b, 3, cfg.vocab_size), dtype=np.int32) for b in range(T)]
+    prompts = [np.asarray(ib.prompt(n_tok, 1000 + lo + b, 3, cfg.vocab_size), dtype=np.int32) for b in range(T)]
     for i in range(W):
         eng.prefill(i % T, prompts[i % T], chunk=chunk)
     sampler = ClockSampler(local)
@@ -808,6 +879,92 @@ def run_prefill(args):
         print(json.dumps(result), flush=True)
 
 
+def run_profile_case(args):
+    """A run sized for profilers (one GPU), no JSON line.
+
+    Default: the TinyLlama-1.1B shape (or, with --shape llama3-8b, the
+    Llama-3-8B shape) with --layers decoder layers (the per-layer matrices
+    keep their full size; --vocab shrinks the embedding and LM head), seeded
+    N(0, 0.02) weights.  Launch order on the device: --prompt single-step
+    launches (the prompt), then one warm-up chain and one measured chain of
+    --steps steps, so a profiler that skips --prompt + 1 launches of the
+    decode kernel captures the measured chain.
+
+    --batched T: the batched engine instead (bf16, T sequences with contexts
+    uniform in [512, 2048], numpy seed 1234, seeded KV rows): --steps timed
+    steps, then one more step between cudaProfilerStart and cudaProfilerStop,
+    for a profiler started with --profile-from-start off.
+
+    --prefill N: the batched engine's prompt prefill (bf16, one sequence):
+    the first --start KV rows seeded, then a prompt of N seeded tokens at
+    positions [start, start + N) in chunks of --chunk, twice (a warm-up
+    prefill, then the measured one).  Per chunk and layer the launch order is
+    pgemm (Q|K|V), pf_qkv_rope, pf_attn, pgemm (O), bt_resid_norm, pgemm
+    (gate/up with SwiGLU), pgemm (down), bt_resid_norm."""
+    import numpy as np
+    import torch
+    import infernt_b200 as ib
+    torch.cuda.set_device(0)
+    if args.prefill:
+        base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B
+        cfg = base.with_(num_layers=args.layers, weight_dtype=ib.DTYPE_BF16,
+                         max_seq_len=args.start + args.prefill + 8)
+        if args.vocab:
+            cfg = cfg.with_(vocab_size=args.vocab)
+        eng = ib.BatchEngine(cfg, 1, seed=1)
+        if args.start:
+            eng.fill_kv(0, 77, args.start)
+        prompt = ib.prompt(args.prefill, 1000, 3, cfg.vocab_size)
+        eng.prefill(0, prompt, start_pos=args.start, chunk=args.chunk)
+        nxt, _, ms = eng.prefill(0, prompt, start_pos=args.start, chunk=args.chunk)
+        print("prefill tokens=%d start=%d layers=%d chunk=%d: %.3f ms, %.0f tok/s, next token %d"
+              % (args.prefill, args.start, args.layers, args.chunk, ms, args.prefill * 1e3 / ms, nxt))
+        eng.close()
+        return
+    if args.batched:
+        T = args.batched
+        base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B
+        cfg = base.with_(num_layers=args.layers, weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + 2 * args.steps + 8)
+        if args.vocab:
+            cfg = cfg.with_(vocab_size=args.vocab)
+        eng = ib.BatchEngine(cfg, T, seed=0)
+        ctx = np.random.default_rng(1234).integers(512, 2049, size=T)
+        for b in range(T):
+            eng.fill_kv(b, 1000 + b, int(ctx[b]))
+        tokens = [5 + b for b in range(T)]
+        pos = [int(c) for c in ctx]
+        toks, _ = eng.decode(tokens, pos, args.steps)
+        tokens, pos = [int(t) for t in toks[-1]], [p + args.steps for p in pos]
+        toks, ms = eng.decode(tokens, pos, args.steps)
+        tokens, pos = [int(t) for t in toks[-1]], [p + args.steps for p in pos]
+        print("batched T=%d layers=%d: %.4f ms/step, %.0f tok/s, splits %s"
+              % (T, args.layers, ms / args.steps, T * args.steps * 1e3 / ms, eng.splits()))
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        eng.step(tokens, pos)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        eng.close()
+        return
+    base = ib.TINYLLAMA if args.shape == "tinyllama" else ib.LLAMA3_8B.with_(max_seq_len=1024)
+    cfg = base.with_(num_layers=args.layers)
+    if args.vocab:
+        cfg = cfg.with_(vocab_size=args.vocab)
+    if args.bf16:
+        cfg = cfg.with_(weight_dtype=ib.DTYPE_BF16)
+    eng = ib.Engine(cfg, seed=0)
+    t = 5
+    for pos in range(args.prompt):
+        t = eng.forward_token(t, pos)
+    eng.decode_chain(t, args.prompt, args.steps)
+    toks, ms = eng.decode_chain(t, args.prompt, args.steps)
+    wbytes = cfg.weight_params * (2 if args.bf16 else 4)
+    print("layers=%d steps=%d mode=%d: %.4f ms/step, %.0f tok/s, weights %.3f GB -> %.1f GB/s"
+          % (args.layers, args.steps, eng.mode, ms / args.steps, args.steps * 1e3 / ms, wbytes / 1e9,
+             wbytes / (ms / args.steps / 1e3) / 1e9))
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -815,7 +972,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx", "longctx-tp",
-                                           "prefill"],
+                                           "prefill", "profile-case"],
                     default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
                          "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
@@ -824,12 +981,27 @@ def main():
                          "longctx: 16 8B-shaped bf16 sequences at 32768 positions, decode only, "
                          "data-parallel over the torchrun ranks; longctx-tp: the same 16 sequences, "
                          "tensor-parallel over the torchrun ranks; prefill: the 32768-token prompts of "
-                         "those sequences (one prompt per step), data-parallel over the torchrun ranks")
+                         "those sequences (one prompt per step), data-parallel over the torchrun ranks; "
+                         "profile-case: a run sized for profilers (see run_profile_case), no JSON line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-llama8b", action="store_true",
+                    help="decode: skip the Llama-3-8B-shaped tensor-parallel measurement")
     ap.add_argument("--real-prefill", action="store_true",
                     help="longctx: prefill every sequence's 32768-token prompt with the engine (reported "
                          "separately) instead of seeding its KV rows")
+    pc = ap.add_argument_group("profile-case")
+    pc.add_argument("--layers", type=int, default=4)
+    pc.add_argument("--prompt", type=int, default=2)
+    pc.add_argument("--bf16", action="store_true", help="bf16 weights (FP32 activations)")
+    pc.add_argument("--shape", choices=["tinyllama", "llama3-8b"], default="tinyllama")
+    pc.add_argument("--vocab", type=int, default=0, help="vocabulary size (0: the shape's own)")
+    pc.add_argument("--batched", type=int, default=0, help="sequences of a batched-engine run (0: b=1 decode)")
+    pc.add_argument("--prefill", type=int, default=0, help="prompt tokens of a prefill run (0: decode)")
+    pc.add_argument("--start", type=int, default=0, help="prefill: seeded KV rows before the prompt")
+    pc.add_argument("--chunk", type=int, default=4096, help="prefill: tokens per chunk")
     args = ap.parse_args()
+    if args.workload == "profile-case":
+        return run_profile_case(args)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.workload == "layer-ops":

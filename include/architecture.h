@@ -2,7 +2,9 @@
 // include/architecture.h:9-61.  LlamaArchitecture keeps its constructor
 // and virtual methods; underneath, forward() runs the fused B200 decode step
 // (infernt_plan_* in include/infernt_capi.h) on the stream of the
-// CublasWrapper it was built with, as one CUDA graph replay.
+// CublasWrapper it was built with: one launch of the persistent decode
+// kernel (a CUDA graph of fused kernels for shapes that kernel does not
+// take).
 #pragma once
 
 #include <vector>
@@ -59,7 +61,7 @@ public:
     int kernels_per_step() const;
 
     // The decode plan bound to these weights and this cache (created on first use).
-    infernt_plan* plan_for(const ModelWeights& weights, KVCache& kv_cache) { return bind(weights, kv_cache); }
+    infernt_plan* plan_for(const ModelWeights& weights, KVCache& kv_cache) { return bind(weights, kv_cache, true); }
 
     // INFERNT_MODE_* for the following steps (rebinds the plan).
     void set_decode_mode(int mode);
@@ -67,7 +69,9 @@ public:
     int decode_mode() const;
 
 private:
-    infernt_plan* bind(const ModelWeights& weights, KVCache& kv_cache);
+    // token_input: the plan will look tokens up in weights.embedding (else
+    // only forward(), which takes the input embedding, runs on it)
+    infernt_plan* bind(const ModelWeights& weights, KVCache& kv_cache, bool token_input);
 
     CublasWrapper& cublas_;
     ModelConfig config_;

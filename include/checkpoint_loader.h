@@ -26,10 +26,10 @@ public:
     static ModelConfig load_config(const std::string& config_path);
     // Fills `weights` (norms and embedding FP32; projections and lm_head in
     // config.weight_dtype, bf16 rounded to nearest even) on target_device.
-    // A missing lm_head is a copy of the embedding (as the reference).
-    // Throws std::runtime_error on a bad magic or version, a truncated file,
-    // a tensor whose element count does not match the config, or a missing
-    // tensor other than lm_head.
+    // A missing lm_head is a copy of the embedding, any other tensor the file
+    // lacks stays empty (both as the reference).  Throws std::runtime_error
+    // on a bad magic or version, a truncated file, or a tensor whose element
+    // count does not match the config.
     static void load_weights(const std::string& weights_path, const ModelConfig& config, ModelWeights& weights,
                              Device target_device = Device::CUDA);
 };

@@ -7,6 +7,12 @@
 
 #include <cuda_runtime.h>
 
+// The reference's handle type, declared as cuBLAS declares it (struct
+// cublasContext*), so handle() keeps its signature without a cuBLAS
+// dependency; a caller that also includes cublas_v2.h sees the same type.
+struct cublasContext;
+typedef struct cublasContext* cublasHandle_t;
+
 class CublasWrapper {
 public:
     CublasWrapper();
@@ -25,8 +31,11 @@ public:
                       bool trans_a = false, bool trans_b = false);
 
     void set_stream(cudaStream_t stream);
-    // The stream this wrapper launches on (there is no library handle).
-    cudaStream_t handle() const;
+    // The reference's accessor (include/cublas_wrapper.h:35).  No cuBLAS
+    // handle exists underneath: always nullptr.
+    cublasHandle_t handle() const;
+    // The stream this wrapper launches on.
+    cudaStream_t stream() const;
 
 private:
     cudaStream_t stream_;

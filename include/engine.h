@@ -1,8 +1,9 @@
 // engine.h — the inference engine of the reference's include/engine.h:1-66:
 // owns weights, KV cache and the architecture; all buffers are allocated in
-// initialize() (zero-allocation decode loop).  forward_token() is one CUDA
-// graph replay (embedding, 22 layers, final norm, LM head and argmax fused
-// into 111 kernels) plus a 4-byte device-to-host copy of the next token.
+// initialize() (zero-allocation decode loop).  forward_token() is one launch
+// of the persistent decode kernel (embedding, every layer, final norm, LM
+// head and argmax; a CUDA graph of fused kernels for shapes that kernel does
+// not take) plus a 4-byte device-to-host copy of the next token.
 #pragma once
 
 #include <cstdint>

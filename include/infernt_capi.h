@@ -493,6 +493,9 @@ INFERNT_API int infernt_fill_normal_window(void* dst, int rows, int cols, int ld
                                            int dtype, uint64_t seed, uint64_t stream_id,
                                            float std_dev, void* stream);
 INFERNT_API int infernt_fill_const(float* dst, size_t n, float value, void* stream);
+/* Host: n seeded token ids uniform in [lo, hi) (the prompt stream of
+ * include/infernt_seed.h; the synthetic prompts of the benchmarks). */
+INFERNT_API int infernt_fill_prompt(int* out_host, int n, uint64_t seed, int lo, int hi);
 /* KV prefill: rows [0, n_pos) of every layer's K and V cache get N(0, std) from the
  * KV streams (element (l, h, p, d) = index ((l*Nkv + h) * 2^20 + p) * D + d). */
 INFERNT_API int infernt_fill_kv(float* const* k_cache, float* const* v_cache, int num_layers,

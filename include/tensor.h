@@ -1,6 +1,8 @@
 // tensor.h — move-only owning buffer on the host or the GPU.
 // Same interface as the reference's include/tensor.h:1-80 (a drop-in: the
-// architecture, engine and KV cache signatures take these types).
+// architecture, engine and KV cache signatures take these types), plus bf16
+// accessors.  Transfers with a device end run on the legacy default stream;
+// copies that read or write host memory are complete on return.
 #pragma once
 
 #include <cstddef>
@@ -40,6 +42,9 @@ public:
     // Throw std::runtime_error unless the tensor holds FP32 (as the reference).
     float* data_as_float();
     const float* data_as_float() const;
+    // bf16 storage as raw 16-bit words; throws unless the tensor holds BF16.
+    uint16_t* data_as_bf16();
+    const uint16_t* data_as_bf16() const;
 
     int dim() const;
     int size(int d) const;

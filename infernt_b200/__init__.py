@@ -178,6 +178,7 @@ _SIGS = {
     "infernt_engine_mode": (_I, [_P, ctypes.POINTER(_I)]),
     "infernt_fill_normal": (_I, [_P, _S, _I, _U64, _U64, _F, _P]),
     "infernt_fill_const": (_I, [_P, _S, _F, _P]),
+    "infernt_fill_prompt": (_I, [_P, _I, _U64, _I, _I]),
     "infernt_fill_kv": (_I, [ctypes.POINTER(_P), ctypes.POINTER(_P), _I, _I, _I, _I, _I, _U64, _F, _P]),
     "infernt_engine_create_seeded": (_I, [ctypes.POINTER(LlamaConfig), _U64, _F, ctypes.POINTER(_P)]),
     "infernt_engine_destroy": (_I, [_P]),
@@ -254,6 +255,14 @@ def _trace(cfg, fn, handle, token, position, steps):
     out = np.zeros(ctas * steps * nph * TRACE_FIELDS, dtype=np.uint64)
     call(fn, handle, token, position, steps, out.ctypes.data, out.size)
     return out.reshape(ctas, steps, nph, TRACE_FIELDS).astype(np.int64)
+
+
+def prompt(n: int, seed: int, lo: int = 3, hi: int = 32000):
+    """n seeded token ids uniform in [lo, hi) (infernt_fill_prompt): the
+    synthetic prompts of the benchmarks."""
+    arr = (ctypes.c_int * max(int(n), 1))()
+    call("infernt_fill_prompt", arr, int(n), int(seed), int(lo), int(hi))
+    return [arr[i] for i in range(int(n))]
 
 
 def ptr(t):

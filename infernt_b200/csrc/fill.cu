@@ -110,6 +110,13 @@ int infernt_fill_const(float* dst, size_t n, float value, void* stream) {
     return INFERNT_OK;
 }
 
+int infernt_fill_prompt(int* out_host, int n, uint64_t seed, int lo, int hi) {
+    INFERNT_REQUIRE(out_host && n >= 0 && lo < hi, "fill_prompt: bad arguments");
+    const uint64_t key = infernt_stream_key(seed, INFERNT_STREAM_PROMPT);
+    for (int i = 0; i < n; ++i) out_host[i] = infernt_uniform_int(key, (uint64_t)i, lo, hi);
+    return INFERNT_OK;
+}
+
 int infernt_fill_kv(float* const* k_cache, float* const* v_cache, int num_layers, int num_kv_heads,
                     int max_seq_len, int head_dim, int n_pos, uint64_t seed, float std_dev, void* stream) {
     INFERNT_REQUIRE(k_cache && v_cache && num_layers > 0 && num_kv_heads > 0 && max_seq_len > 0 && head_dim > 0,

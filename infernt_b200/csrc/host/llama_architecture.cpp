@@ -64,7 +64,7 @@ void LlamaArchitecture::allocate_activations(const ModelConfig& config, int max_
     bound_weights_.clear();
 }
 
-infernt_plan* LlamaArchitecture::bind(const ModelWeights& w, KVCache& kv) {
+infernt_plan* LlamaArchitecture::bind(const ModelWeights& w, KVCache& kv, bool token_input) {
     const ModelConfig& c = config_;
     if (c.num_layers <= 0) throw std::runtime_error("LlamaArchitecture: allocate_activations was not called");
     if ((int)w.layers.size() != c.num_layers || (int)kv.k_cache.size() != c.num_layers ||
@@ -73,8 +73,12 @@ infernt_plan* LlamaArchitecture::bind(const ModelWeights& w, KVCache& kv) {
     const DType wd = c.weight_dtype;
     std::vector<const void*> wp;
     wp.reserve(3 + 9 * c.num_layers);
-    wp.push_back(ptr(w.embedding, "embedding", DType::FP32));
-    wp.push_back(ptr(w.final_norm, "final_norm", DType::FP32));
+    // forward() takes the input embedding and never reads the table (the
+    // reference's forward does not either): a caller may leave it empty, and
+    // the plan gets the final norm's address as a stand-in it does not read
+    const void* fnorm = ptr(w.final_norm, "final_norm", DType::FP32);
+    wp.push_back(!token_input && !w.embedding.is_valid() ? fnorm : ptr(w.embedding, "embedding", DType::FP32));
+    wp.push_back(fnorm);
     wp.push_back(ptr(w.lm_head, "lm_head", wd));
     for (const auto& lw : w.layers) {
         wp.push_back(ptr(lw.attn_norm, "attn_norm", DType::FP32));
@@ -116,7 +120,7 @@ infernt_plan* LlamaArchitecture::bind(const ModelWeights& w, KVCache& kv) {
 
 void LlamaArchitecture::forward(const Tensor& input, const ModelWeights& w, KVCache& kv, int position,
                                 Tensor& logits) {
-    infernt_plan* p = bind(w, kv);
+    infernt_plan* p = bind(w, kv, false);
     if (input.num_elements() != config_.hidden_size || logits.num_elements() != config_.vocab_size)
         throw std::runtime_error("LlamaArchitecture::forward: input or logits shape mismatch");
     check(infernt_plan_forward(p, input.data_as_float(), position, logits.data_as_float(), stream()),
@@ -125,7 +129,7 @@ void LlamaArchitecture::forward(const Tensor& input, const ModelWeights& w, KVCa
 
 void LlamaArchitecture::forward_token(int token_id, const ModelWeights& w, KVCache& kv, int position,
                                       Tensor& logits) {
-    infernt_plan* p = bind(w, kv);
+    infernt_plan* p = bind(w, kv, true);
     if (logits.num_elements() != config_.vocab_size)
         throw std::runtime_error("LlamaArchitecture::forward_token: logits shape mismatch");
     check(infernt_plan_decode(p, token_id, position, logits.data_as_float(), stream()),
@@ -134,7 +138,7 @@ void LlamaArchitecture::forward_token(int token_id, const ModelWeights& w, KVCac
 
 void LlamaArchitecture::decode_chain(int token_id, int position, int steps, const ModelWeights& w, KVCache& kv,
                                      int* tokens_dev) {
-    infernt_plan* p = bind(w, kv);
+    infernt_plan* p = bind(w, kv, true);
     check(infernt_plan_decode_chain(p, token_id, position, steps, tokens_dev, stream()),
           "LlamaArchitecture::decode_chain");
 }
@@ -146,7 +150,7 @@ int LlamaArchitecture::last_token() {
     return t;
 }
 
-cudaStream_t LlamaArchitecture::stream() const { return cublas_.handle(); }
+cudaStream_t LlamaArchitecture::stream() const { return cublas_.stream(); }
 
 int LlamaArchitecture::kernels_per_step() const {
     return plan_ ? infernt_plan_kernels_per_step(plan_) : 5 * config_.num_layers + 1;

@@ -127,7 +127,8 @@ void CublasWrapper::batched_gemm(const float* A, const float* B, float* C, int M
 }
 
 void CublasWrapper::set_stream(cudaStream_t stream) { stream_ = stream; }
-cudaStream_t CublasWrapper::handle() const { return stream_; }
+cublasHandle_t CublasWrapper::handle() const { return nullptr; }
+cudaStream_t CublasWrapper::stream() const { return stream_; }
 
 // ------------------------------------------------------------ device init --
 void cuda_init(int device_id) {

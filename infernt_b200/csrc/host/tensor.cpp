@@ -1,142 +1,203 @@
-// tensor.cpp — host/GPU buffer implementing include/tensor.h.
+// tensor.cpp — the Tensor of include/tensor.h: a move-only buffer on the
+// host or the current GPU.
+//
+// Storage: host buffers are 64-byte aligned (vector loads in host code),
+// device buffers come from cudaMalloc.  Every transfer goes through one
+// routine that picks the route from the two devices: host to host is a
+// memcpy; a transfer with a device end is issued on the legacy default
+// stream (the stream the reference's launch_* kernels use), so it is
+// ordered after every kernel launched there, and the call waits for it only
+// when a host buffer is read or written (device-to-device copies return at
+// once, like a kernel launch).  Views (reshape) share the storage without
+// owning it.
 #include "tensor.h"
 
 #include <cuda_runtime.h>
 
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <limits>
 #include <stdexcept>
 #include <string>
 
 namespace {
-void cuda_or_throw(cudaError_t e, const char* what) {
-    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+
+[[noreturn]] void fail(const std::string& what) { throw std::runtime_error("Tensor: " + what); }
+
+void check_cuda(cudaError_t e, const char* call) {
+    if (e != cudaSuccess) fail(std::string(call) + " failed (" + cudaGetErrorString(e) + ")");
 }
+
+constexpr size_t kHostAlign = 64;
+
+void* storage_alloc(Device dev, size_t bytes) {
+    if (bytes == 0) return nullptr;
+    if (dev == Device::CPU) {
+        const size_t rounded = (bytes + kHostAlign - 1) / kHostAlign * kHostAlign;
+        void* p = std::aligned_alloc(kHostAlign, rounded);
+        if (!p) fail("host allocation of " + std::to_string(bytes) + " bytes failed");
+        return p;
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail("device allocation of " + std::to_string(bytes) + " bytes failed (" + cudaGetErrorString(e) + ")");
+    }
+    return p;
+}
+
+void storage_release(Device dev, void* p) {
+    if (!p) return;
+    if (dev == Device::CPU)
+        std::free(p);
+    else
+        cudaFree(p);
+}
+
+// bytes from src (on src_dev) to dst (on dst_dev)
+void transfer(void* dst, Device dst_dev, const void* src, Device src_dev, size_t bytes) {
+    if (bytes == 0) return;
+    if (dst_dev == Device::CPU && src_dev == Device::CPU) {
+        std::memcpy(dst, src, bytes);
+        return;
+    }
+    const cudaMemcpyKind kind = dst_dev == Device::CUDA
+                                    ? (src_dev == Device::CUDA ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice)
+                                    : cudaMemcpyDeviceToHost;
+    check_cuda(cudaMemcpyAsync(dst, src, bytes, kind, cudaStreamLegacy), "cudaMemcpyAsync");
+    if (kind != cudaMemcpyDeviceToDevice) check_cuda(cudaStreamSynchronize(cudaStreamLegacy), "cudaStreamSynchronize");
+}
+
+int64_t element_count(const std::vector<int>& shape) {
+    int64_t n = 1;
+    for (size_t i = 0; i < shape.size(); ++i) {
+        if (shape[i] <= 0) fail("extent " + std::to_string(shape[i]) + " of dimension " + std::to_string(i) +
+                                " is not positive");
+        if (n > std::numeric_limits<int64_t>::max() / shape[i]) fail("element count overflows");
+        n *= shape[i];
+    }
+    return n;
+}
+
 }  // namespace
 
 size_t dtype_size(DType dtype) {
     switch (dtype) {
-        case DType::FP32: return 4;
-        case DType::FP16: return 2;
+        case DType::UINT8: return 1;
+        case DType::FP16:
         case DType::BF16: return 2;
+        case DType::FP32:
         case DType::INT32: return 4;
         case DType::INT64: return 8;
-        case DType::UINT8: return 1;
     }
     return 0;
 }
 
 const char* dtype_name(DType dtype) {
-    switch (dtype) {
-        case DType::FP32: return "FP32";
-        case DType::FP16: return "FP16";
-        case DType::BF16: return "BF16";
-        case DType::INT32: return "INT32";
-        case DType::INT64: return "INT64";
-        case DType::UINT8: return "UINT8";
-    }
-    return "UNKNOWN";
+    static const char* const names[] = {"FP32", "FP16", "BF16", "INT32", "INT64", "UINT8"};
+    const int i = static_cast<int>(dtype);
+    return i >= 0 && i < 6 ? names[i] : "?";
 }
 
-const char* device_name(Device device) { return device == Device::CPU ? "CPU" : "CUDA"; }
+const char* device_name(Device device) { return device == Device::CUDA ? "CUDA" : "CPU"; }
 
 Tensor::Tensor()
     : data_(nullptr), num_elements_(0), dtype_(DType::FP32), device_(Device::CPU), owns_data_(false) {}
 
 Tensor::Tensor(const std::vector<int>& shape, DType dtype, Device device)
-    : data_(nullptr), shape_(shape), num_elements_(1), dtype_(dtype), device_(device), owns_data_(true) {
-    for (int s : shape_) {
-        if (s <= 0) throw std::invalid_argument("Tensor dimensions must be positive");
-        num_elements_ *= s;
-    }
+    : data_(nullptr), shape_(shape), num_elements_(element_count(shape)), dtype_(dtype), device_(device),
+      owns_data_(true) {
     compute_strides();
     allocate();
 }
 
 Tensor::~Tensor() { free_memory(); }
 
-Tensor::Tensor(Tensor&& o) noexcept
-    : data_(o.data_), shape_(std::move(o.shape_)), strides_(std::move(o.strides_)),
-      num_elements_(o.num_elements_), dtype_(o.dtype_), device_(o.device_), owns_data_(o.owns_data_) {
-    o.data_ = nullptr;
-    o.num_elements_ = 0;
-    o.owns_data_ = false;
+Tensor::Tensor(Tensor&& other) noexcept
+    : data_(nullptr), num_elements_(0), dtype_(DType::FP32), device_(Device::CPU), owns_data_(false) {
+    *this = std::move(other);
 }
 
-Tensor& Tensor::operator=(Tensor&& o) noexcept {
-    if (this != &o) {
-        free_memory();
-        data_ = o.data_;
-        shape_ = std::move(o.shape_);
-        strides_ = std::move(o.strides_);
-        num_elements_ = o.num_elements_;
-        dtype_ = o.dtype_;
-        device_ = o.device_;
-        owns_data_ = o.owns_data_;
-        o.data_ = nullptr;
-        o.num_elements_ = 0;
-        o.owns_data_ = false;
-    }
+Tensor& Tensor::operator=(Tensor&& other) noexcept {
+    if (this == &other) return *this;
+    free_memory();
+    data_ = other.data_;
+    shape_.swap(other.shape_);
+    strides_.swap(other.strides_);
+    num_elements_ = other.num_elements_;
+    dtype_ = other.dtype_;
+    device_ = other.device_;
+    owns_data_ = other.owns_data_;
+    // the source keeps nothing: it is an empty, invalid tensor
+    other.data_ = nullptr;
+    other.shape_.clear();
+    other.strides_.clear();
+    other.num_elements_ = 0;
+    other.owns_data_ = false;
     return *this;
 }
 
+Tensor Tensor::empty(const std::vector<int>& shape, DType dtype, Device device) { return Tensor(shape, dtype, device); }
+
 Tensor Tensor::zeros(const std::vector<int>& shape, DType dtype, Device device) {
     Tensor t(shape, dtype, device);
-    if (device == Device::CPU)
+    if (device == Device::CUDA) {
+        // complete before return: the caller may hand the buffer to kernels
+        // on any stream
+        check_cuda(cudaMemsetAsync(t.data_, 0, t.size_bytes(), cudaStreamLegacy), "cudaMemsetAsync");
+        check_cuda(cudaStreamSynchronize(cudaStreamLegacy), "cudaStreamSynchronize");
+    } else
         std::memset(t.data_, 0, t.size_bytes());
-    else
-        cuda_or_throw(cudaMemset(t.data_, 0, t.size_bytes()), "cudaMemset");
     return t;
 }
 
-Tensor Tensor::empty(const std::vector<int>& shape, DType dtype, Device device) {
-    return Tensor(shape, dtype, device);
-}
-
-Tensor Tensor::to(Device target) const {
-    if (target == device_) throw std::runtime_error("Tensor is already on the target device");
-    Tensor r(shape_, dtype_, target);
-    cuda_or_throw(cudaMemcpy(r.data_, data_, size_bytes(),
-                             target == Device::CUDA ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost),
-                  "cudaMemcpy");
-    return r;
+Tensor Tensor::to(Device target_device) const {
+    if (target_device == device_)
+        fail(std::string("to(): the tensor already lives on ") + device_name(device_));
+    Tensor out(shape_, dtype_, target_device);
+    transfer(out.data_, target_device, data_, device_, size_bytes());
+    return out;
 }
 
 Tensor Tensor::clone() const {
-    Tensor r(shape_, dtype_, device_);
-    r.copy_from(*this);
-    return r;
+    Tensor out(shape_, dtype_, device_);
+    transfer(out.data_, device_, data_, device_, size_bytes());
+    return out;
 }
 
 void Tensor::copy_from(const Tensor& src) {
-    if (num_elements_ != src.num_elements_ || dtype_ != src.dtype_)
-        throw std::runtime_error("Tensor shape/dtype mismatch in copy_from");
-    if (device_ == Device::CPU && src.device_ == Device::CPU) {
-        std::memcpy(data_, src.data_, size_bytes());
-        return;
-    }
-    cudaMemcpyKind kind = cudaMemcpyDeviceToDevice;
-    if (device_ == Device::CUDA && src.device_ == Device::CPU) kind = cudaMemcpyHostToDevice;
-    if (device_ == Device::CPU && src.device_ == Device::CUDA) kind = cudaMemcpyDeviceToHost;
-    cuda_or_throw(cudaMemcpy(data_, src.data_, size_bytes(), kind), "cudaMemcpy");
+    if (src.dtype_ != dtype_)
+        fail(std::string("copy_from(): dtype ") + dtype_name(src.dtype_) + " into " + dtype_name(dtype_));
+    if (src.num_elements_ != num_elements_)
+        fail("copy_from(): " + std::to_string(src.num_elements_) + " elements into " + std::to_string(num_elements_));
+    transfer(data_, device_, src.data_, src.device_, size_bytes());
 }
 
 void* Tensor::data_ptr() { return data_; }
 const void* Tensor::data_ptr() const { return data_; }
 
 float* Tensor::data_as_float() {
-    if (dtype_ != DType::FP32) throw std::runtime_error("Tensor is not FP32");
+    if (dtype_ != DType::FP32) fail(std::string("data_as_float(): the tensor holds ") + dtype_name(dtype_));
     return static_cast<float*>(data_);
 }
 
-const float* Tensor::data_as_float() const {
-    if (dtype_ != DType::FP32) throw std::runtime_error("Tensor is not FP32");
-    return static_cast<const float*>(data_);
+const float* Tensor::data_as_float() const { return const_cast<Tensor*>(this)->data_as_float(); }
+
+uint16_t* Tensor::data_as_bf16() {
+    if (dtype_ != DType::BF16) fail(std::string("data_as_bf16(): the tensor holds ") + dtype_name(dtype_));
+    return static_cast<uint16_t*>(data_);
 }
 
+const uint16_t* Tensor::data_as_bf16() const { return const_cast<Tensor*>(this)->data_as_bf16(); }
+
 int Tensor::dim() const { return static_cast<int>(shape_.size()); }
-int Tensor::size(int d) const { return shape_.at(d); }
+int Tensor::size(int d) const {
+    if (d < 0 || d >= dim()) fail("size(" + std::to_string(d) + ") of a " + std::to_string(dim()) + "-d tensor");
+    return shape_[d];
+}
 const std::vector<int>& Tensor::shape() const { return shape_; }
 const std::vector<int>& Tensor::strides() const { return strides_; }
 int64_t Tensor::num_elements() const { return num_elements_; }
@@ -145,74 +206,62 @@ DType Tensor::dtype() const { return dtype_; }
 Device Tensor::device() const { return device_; }
 bool Tensor::is_cuda() const { return device_ == Device::CUDA; }
 bool Tensor::is_cpu() const { return device_ == Device::CPU; }
-bool Tensor::is_valid() const { return data_ != nullptr && num_elements_ > 0; }
+bool Tensor::is_valid() const { return data_ && num_elements_ > 0; }
 
 Tensor Tensor::reshape(const std::vector<int>& new_shape) const {
-    int64_t n = 1;
-    for (int s : new_shape) n *= s;
-    if (n != num_elements_) throw std::runtime_error("Reshape: element count mismatch");
-    Tensor r;
-    r.data_ = data_;
-    r.shape_ = new_shape;
-    r.num_elements_ = num_elements_;
-    r.dtype_ = dtype_;
-    r.device_ = device_;
-    r.owns_data_ = false;
-    r.compute_strides();
-    return r;
+    if (element_count(new_shape) != num_elements_)
+        fail("reshape(): " + std::to_string(element_count(new_shape)) + " elements from " +
+             std::to_string(num_elements_));
+    Tensor view;
+    view.data_ = data_;
+    view.shape_ = new_shape;
+    view.num_elements_ = num_elements_;
+    view.dtype_ = dtype_;
+    view.device_ = device_;
+    view.owns_data_ = false;
+    view.compute_strides();
+    return view;
 }
 
 void Tensor::print_info(const std::string& label) const {
-    if (!label.empty()) std::printf("%s: ", label.c_str());
-    std::printf("Tensor(shape=[");
-    for (int i = 0; i < dim(); ++i) std::printf(i ? ", %d" : "%d", shape_[i]);
-    std::printf("], dtype=%s, device=%s, elements=%lld, bytes=%zu)\n", dtype_name(dtype_),
-                device_name(device_), (long long)num_elements_, size_bytes());
+    std::string dims;
+    for (int i = 0; i < dim(); ++i) dims += (i ? "x" : "") + std::to_string(shape_[i]);
+    std::printf("%s%s%s %s on %s, %lld elements (%zu bytes)\n", label.c_str(), label.empty() ? "" : ": ",
+                dims.empty() ? "[]" : dims.c_str(), dtype_name(dtype_), device_name(device_),
+                static_cast<long long>(num_elements_), size_bytes());
 }
 
 void Tensor::print_data(int max_elements) const {
-    if (!is_cpu()) {
-        std::printf("[Tensor on GPU - copy to CPU to print data]\n");
+    if (device_ != Device::CPU || dtype_ != DType::FP32 || !data_) {
+        std::printf("(print_data shows FP32 host tensors; this one is %s on %s)\n", dtype_name(dtype_),
+                    device_name(device_));
         return;
     }
-    if (dtype_ != DType::FP32) {
-        std::printf("[print_data supports FP32 only]\n");
-        return;
+    const float* v = static_cast<const float*>(data_);
+    const int64_t n = num_elements_ < max_elements ? num_elements_ : (max_elements < 0 ? 0 : max_elements);
+    std::string line = "{";
+    char buf[32];
+    for (int64_t i = 0; i < n; ++i) {
+        std::snprintf(buf, sizeof(buf), "%s%g", i ? " " : "", v[i]);
+        line += buf;
     }
-    const float* d = static_cast<const float*>(data_);
-    const int n = num_elements_ < max_elements ? (int)num_elements_ : max_elements;
-    std::printf("[");
-    for (int i = 0; i < n; ++i) std::printf(i ? ", %.6f" : "%.6f", d[i]);
-    if (n < num_elements_) std::printf(", ... (%lld more)", (long long)(num_elements_ - n));
-    std::printf("]\n");
+    if (n < num_elements_) line += " +" + std::to_string(num_elements_ - n) + " more";
+    std::printf("%s}\n", line.c_str());
 }
 
-void Tensor::allocate() {
-    const size_t bytes = size_bytes();
-    if (bytes == 0) return;
-    if (device_ == Device::CPU) {
-        data_ = std::malloc(bytes);
-        if (!data_) throw std::runtime_error("CPU memory allocation failed");
-    } else {
-        cudaError_t e = cudaMalloc(&data_, bytes);
-        if (e != cudaSuccess) {
-            data_ = nullptr;
-            throw std::runtime_error(std::string("GPU memory allocation failed: ") + cudaGetErrorString(e));
-        }
-    }
-}
+void Tensor::allocate() { data_ = storage_alloc(device_, size_bytes()); }
 
 void Tensor::free_memory() {
-    if (data_ && owns_data_) {
-        if (device_ == Device::CPU)
-            std::free(data_);
-        else
-            cudaFree(data_);
-    }
+    if (owns_data_) storage_release(device_, data_);
     data_ = nullptr;
+    owns_data_ = false;
 }
 
 void Tensor::compute_strides() {
-    strides_.assign(shape_.size(), 1);
-    for (int i = (int)shape_.size() - 2; i >= 0; --i) strides_[i] = strides_[i + 1] * shape_[i + 1];
+    strides_.resize(shape_.size());
+    int stride = 1;
+    for (size_t i = shape_.size(); i-- > 0;) {
+        strides_[i] = stride;
+        stride *= shape_[i];
+    }
 }

@@ -269,6 +269,13 @@ int elementwise_grid(int n) {
     return g < 1 ? 1 : (g > cap ? cap : g);
 }
 
+// The argmax partials live in the module's own device memory (zeroed when
+// the module loads on a device), so launch_argmax allocates nothing: the
+// reference's kernels never allocate.  The last block resets the ticket, so
+// the workspace is ready for the next launch; launches that overlap on one
+// device (different streams) share it and must be ordered by the caller.
+__device__ ArgmaxWorkspace g_argmax_ws_dev;
+
 std::mutex g_ws_mu;
 ArgmaxWorkspace* g_argmax_ws[64] = {nullptr};
 
@@ -278,8 +285,7 @@ int argmax_workspace(ArgmaxWorkspace** out) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     if (!g_argmax_ws[d]) {
         void* p = nullptr;
-        INFERNT_CUDA_TRY(cudaMalloc(&p, sizeof(ArgmaxWorkspace)));
-        INFERNT_CUDA_TRY(cudaMemset(p, 0, sizeof(ArgmaxWorkspace)));
+        INFERNT_CUDA_TRY(cudaGetSymbolAddress(&p, g_argmax_ws_dev));
         g_argmax_ws[d] = static_cast<ArgmaxWorkspace*>(p);
     }
     *out = g_argmax_ws[d];

@@ -88,3 +88,12 @@ def test_model_shapes():
     per_layer = H * (2048 + 512) + 2048 * H + 3 * H * I
     assert ib.TINYLLAMA.weight_params == L * per_layer + V * H
     assert ib.LLAMA3_8B.head_dim == 128
+
+
+def test_prompt_generator_matches_oracle():
+    """The product's seeded prompt (infernt_fill_prompt, used by the
+    benchmarks) is the oracle's token for token."""
+    import infernt_b200 as ib
+    import oracle as O
+    for n, seed, hi in ((32, 0, 32000), (512, 1, 128256), (7, 99, 50)):
+        assert ib.prompt(n, seed, 3, hi) == [int(t) for t in O.prompt(n, seed, 3, hi)]
