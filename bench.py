@@ -438,12 +438,19 @@ def run_reference(args):
 
 def run_layer_ops(args):
     """Single-layer decode microbench at the TinyLlama shape (FP32): one token
-    at position 4095 with the KV cache filled with seeded N(0,1) values for
-    4095 positions; every op of the layer launched alone through the C ABI,
-    L2 flushed (a 256 MB write) before each timed launch, CUDA events around
-    the launch on its stream; median over --steps launches after --warmup.
-    Each op's algorithmic bytes (weights, inputs, outputs, K/V rows read)
-    over its time, against the measured HBM bandwidth."""
+    at position 4095 with the KV cache filled with N(0,1) values for 4095
+    positions; every op of the layer launched through its C entry point.
+
+    Each op is timed as --steps launches back to back on one stream between
+    two CUDA events (after --warmup launches), cycling through enough copies
+    of its weights / KV cache (over 256 MB per cycle, twice the L2) that every
+    launch reads them from HBM; the per-launch time is the interval over the
+    launch count, so it holds the kernel and the gap to the next launch, not
+    the host's call into the library.  Each op's algorithmic bytes (weights,
+    inputs, outputs, K/V rows read) over that time, against the measured HBM
+    bandwidth.  "cold_us" is the same op launched once after a 256 MB L2
+    flush, events around it (a spin kernel ahead keeps the host's enqueue
+    time out): launch and drain included."""
     import torch
     import infernt_b200 as ib
     torch.cuda.set_device(0)
@@ -456,59 +463,76 @@ def run_layer_ops(args):
     def randn(*shape, std=1.0):
         return torch.randn(*shape, device="cuda", generator=g) * std
 
+    def copies(nbytes):
+        return max(1, min(64, -(-(256 << 20) // max(nbytes, 1))))
+
     x, nw = randn(H), torch.ones(H, device="cuda")
-    wq, wk, wv = randn(qs, H, std=STD), randn(kvs, H, std=STD), randn(kvs, H, std=STD)
-    wo, wg, wu, wd = randn(H, qs, std=STD), randn(I, H, std=STD), randn(I, H, std=STD), randn(H, I, std=STD)
-    kc, vc = randn(Nkv, max_seq, D), randn(Nkv, max_seq, D)
     qkv, attn, act, hid, y = (torch.zeros(n, device="cuda") for n in (qs + 2 * kvs, qs, I, H, H))
     logits = randn(V)
     tok = torch.zeros(1, dtype=torch.int32, device="cuda")
     splits = torch.cuda.get_device_properties(0).multi_processor_count // Nkv
     ws = torch.zeros(ib.lib().infernt_attention_workspace_bytes(Nq, Nkv, D, splits), dtype=torch.uint8,
                      device="cuda")
+    nqkv, no, ngu, nd = (copies(b) for b in ((qs + 2 * kvs) * H * 4, H * qs * 4, 2 * I * H * 4, H * I * 4))
+    nkv = copies(2 * Nkv * max_seq * D * 4)
+    WQ = [(randn(qs, H, std=STD), randn(kvs, H, std=STD), randn(kvs, H, std=STD)) for _ in range(nqkv)]
+    WO = [randn(H, qs, std=STD) for _ in range(no)]
+    WGU = [(randn(I, H, std=STD), randn(I, H, std=STD)) for _ in range(ngu)]
+    WD = [randn(H, I, std=STD) for _ in range(nd)]
+    KV = [(randn(Nkv, max_seq, D), randn(Nkv, max_seq, D)) for _ in range(nkv)]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
     P = lambda t: t.data_ptr()  # noqa: E731
     ops = [
-        ("rmsnorm", 3 * H * 4, lambda: ib.call("infernt_rmsnorm", P(y), P(x), P(nw), 1, H, eps, sp)),
-        ("qkv_rmsnorm_gemv", (qs + 2 * kvs) * H * 4 + 2 * H * 4 + (qs + 2 * kvs) * 4,
-         lambda: ib.call("infernt_rmsnorm_gemv", P(qkv), P(wq), qs, P(wk), kvs, P(wv), kvs, H, f32, P(x), P(nw),
-                         eps, sp)),
-        ("rope", 2 * (qs + kvs) * 4, lambda: ib.call("infernt_rope", P(qkv), P(qkv) + qs * 4, 1, Nq, Nkv, D, pos,
-                                                     theta, sp)),
-        ("kv_cache_append", 4 * kvs * 4, lambda: ib.call("infernt_kv_cache_append", P(kc), P(vc), P(qkv) + qs * 4,
-                                                         P(qkv) + (qs + kvs) * 4, Nkv, D, max_seq, pos, sp)),
-        ("attention_decode", 2 * Nkv * (pos + 1) * D * 4 + (qs + 2 * kvs) * 4 + qs * 4,
-         lambda: ib.call("infernt_attention_decode", P(attn), P(qkv), P(kc), P(vc), Nq, Nkv, D, max_seq, pos, theta,
-                         splits, P(ws), sp)),
-        ("o_gemv_residual", H * qs * 4 + qs * 4 + 2 * H * 4,
-         lambda: ib.call("infernt_gemv_residual", P(hid), P(x), P(wo), H, qs, f32, P(attn), sp)),
-        ("gate_up_rmsnorm_silu", 2 * I * H * 4 + 2 * H * 4 + I * 4,
-         lambda: ib.call("infernt_rmsnorm_gate_up_silu", P(act), P(wg), P(wu), I, H, f32, P(hid), P(nw), eps, sp)),
-        ("down_gemv_residual", H * I * 4 + I * 4 + 2 * H * 4,
-         lambda: ib.call("infernt_gemv_residual", P(y), P(hid), P(wd), H, I, f32, P(act), sp)),
-        ("residual_add", 3 * H * 4, lambda: ib.call("infernt_residual_add", P(y), P(hid), P(x), H, sp)),
-        ("argmax", V * 4 + 4, lambda: ib.call("infernt_argmax", P(tok), P(logits), V, sp)),
+        ("rmsnorm", 3 * H * 4, 1, lambda i: ib.call("infernt_rmsnorm", P(y), P(x), P(nw), 1, H, eps, sp)),
+        ("qkv_rmsnorm_gemv", (qs + 2 * kvs) * H * 4 + 2 * H * 4 + (qs + 2 * kvs) * 4, nqkv,
+         lambda i: ib.call("infernt_rmsnorm_gemv", P(qkv), P(WQ[i][0]), qs, P(WQ[i][1]), kvs, P(WQ[i][2]), kvs, H,
+                           f32, P(x), P(nw), eps, sp)),
+        ("rope", 2 * (qs + kvs) * 4, 1, lambda i: ib.call("infernt_rope", P(qkv), P(qkv) + qs * 4, 1, Nq, Nkv, D,
+                                                          pos, theta, sp)),
+        ("kv_cache_append", 4 * kvs * 4, 1,
+         lambda i: ib.call("infernt_kv_cache_append", P(KV[0][0]), P(KV[0][1]), P(qkv) + qs * 4,
+                           P(qkv) + (qs + kvs) * 4, Nkv, D, max_seq, pos, sp)),
+        ("attention_decode", 2 * Nkv * (pos + 1) * D * 4 + (qs + 2 * kvs) * 4 + qs * 4, nkv,
+         lambda i: ib.call("infernt_attention_decode", P(attn), P(qkv), P(KV[i][0]), P(KV[i][1]), Nq, Nkv, D,
+                           max_seq, pos, theta, splits, P(ws), sp)),
+        ("o_gemv_residual", H * qs * 4 + qs * 4 + 2 * H * 4, no,
+         lambda i: ib.call("infernt_gemv_residual", P(hid), P(x), P(WO[i]), H, qs, f32, P(attn), sp)),
+        ("gate_up_rmsnorm_silu", 2 * I * H * 4 + 2 * H * 4 + I * 4, ngu,
+         lambda i: ib.call("infernt_rmsnorm_gate_up_silu", P(act), P(WGU[i][0]), P(WGU[i][1]), I, H, f32, P(hid),
+                           P(nw), eps, sp)),
+        ("down_gemv_residual", H * I * 4 + I * 4 + 2 * H * 4, nd,
+         lambda i: ib.call("infernt_gemv_residual", P(y), P(hid), P(WD[i]), H, I, f32, P(act), sp)),
+        ("residual_add", 3 * H * 4, 1, lambda i: ib.call("infernt_residual_add", P(y), P(hid), P(x), H, sp)),
+        ("argmax", V * 4 + 4, 1, lambda i: ib.call("infernt_argmax", P(tok), P(logits), V, sp)),
     ]
     hbm, src = peaks()
     res = {}
-    for name, nbytes, op in ops:
-        for _ in range(args.warmup):
-            op()
-        times = []
-        for _ in range(args.steps):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            op()
-            b.record(stream)
-            b.synchronize()
-            times.append(a.elapsed_time(b))
-        times.sort()
-        ms = times[len(times) // 2]
+    n = max(args.steps, 1)
+    for name, nbytes, ncopy, op in ops:
+        for i in range(args.warmup):
+            op(i % ncopy)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2000000)
+        a.record(stream)
+        for i in range(n):
+            op(i % ncopy)
+        b.record(stream)
+        b.synchronize()
+        ms = a.elapsed_time(b) / n
+        # one launch after an L2 flush, launch and drain included
+        flush.zero_()
+        c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2000000)
+        c.record(stream)
+        op(0)
+        d.record(stream)
+        d.synchronize()
         gbs = nbytes / (ms / 1e3) / 1e9
-        res[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4)}
+        res[name] = {"us": round(ms * 1e3, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / hbm, 4),
+                     "copies_cycled": ncopy, "cold_us": round(c.elapsed_time(d) * 1e3, 2)}
     total_us = sum(r["us"] for r in res.values())
     total_bytes = sum(r["bytes"] for r in res.values())
     print(json.dumps({
@@ -517,7 +541,8 @@ def run_layer_ops(args):
         "warmup": args.warmup, "dtype": "f32", "data": "synthetic: torch.randn seeded 0 (weights x0.02), "
         "KV cache N(0,1) for 4095 positions, logits N(0,1)",
         "config": {"workload": "tinyllama-layer-ops-pos4095", "position": pos, "attention_splits": splits,
-                   "l2": "flushed before every timed launch (256 MB write)"},
+                   "l2": "launches cycle through over 256 MB of weight / KV copies (HBM reads every launch); "
+                         "cold_us after a 256 MB flush"},
         "ops": res, "layer_bytes": total_bytes,
         "layer_gbs": round(total_bytes / (total_us / 1e6) / 1e9, 1),
         "peak": {"hbm_gbs": hbm, "source": src},

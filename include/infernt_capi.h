@@ -102,7 +102,12 @@ INFERNT_API int infernt_gemm_f32(const float* A, const float* B, float* C, int M
  * fp32 accumulation).  Weights are row-major [out, in] (the HF layout the
  * reference multiplies with trans_b = true, llama_layer.cpp:18-69).
  * The fast path (TMA-staged weight streaming) needs `in` % 512 == 0 and
- * 16-byte aligned rows; other shapes run a plain-load kernel.             */
+ * 16-byte aligned rows; other shapes run a plain-load kernel.
+ * These kernels and infernt_attention_decode launch with programmatic
+ * dependent launch: one may start while the previous kernel on the stream
+ * is finishing and stream its weights then, but it reads every other input
+ * and writes its outputs only after that kernel has completed.  So the
+ * weights must not be written by the kernel launched just before.       */
 enum { INFERNT_DTYPE_F32 = 0, INFERNT_DTYPE_BF16 = 1 };
 
 /* y[n] = sum_k W[n][k] * xn[k] with xn = rmsnorm(x, norm_w, eps) when norm_w != NULL

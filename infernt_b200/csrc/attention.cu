@@ -70,8 +70,10 @@ size_t attention_workspace_bytes(int nq, int nkv, int D, int splits) {
 
 // Scratch of infernt_attention_decode_noalloc: the per-KV-head tickets (up
 // to 64 heads) at a fixed place at the start, so calls of different shapes
-// find them where the previous call left them at zero; then the error word;
-// then the split partials from offset 512.  512 KiB covers every split
+// find them where the previous call left them at zero; then the kernel's
+// error word (written by the device only: the host validates the position
+// and shape before the launch, so it stays clear; it is not read back); then
+// the split partials from offset 512.  512 KiB covers every split
 // count up to the SM count for the usual LLaMA shapes (TinyLlama: 313 KB of
 // partials at 37 splits; Llama-3-8B: 300 KB at 18).  Static storage starts
 // zeroed when the module loads, which is what the tickets need; each
@@ -88,7 +90,9 @@ std::mutex g_static_mu;
 void* g_static_addr[64] = {nullptr};
 
 // Device address of the static scratch on the current device, looked up
-// once per device.
+// once per device and kept for the process: after cudaDeviceReset the
+// module reloads and the address may change, so a process that resets a
+// device must not call infernt_attention_decode_noalloc on it again.
 int attn_static_scratch(void** out) {
     const int d = current_device();
     INFERNT_REQUIRE(d >= 0 && d < 64, "attention_decode_noalloc: device ordinal %d out of range", d);
@@ -141,7 +145,7 @@ int infernt_attention_decode(float* out, const float* qkv, float* k_cache, float
     a.splits = splits;
     a.theta = theta;
     a.scale = 1.0f / sqrtf((float)head_dim);
-    INFERNT_CUDA_TRY(launch_attention_decode(a, (cudaStream_t)stream, false));
+    INFERNT_CUDA_TRY(launch_attention_decode(a, (cudaStream_t)stream, true));
     return INFERNT_OK;
 }
 
@@ -178,7 +182,7 @@ int infernt_attention_decode_noalloc(float* out, const float* qkv, float* k_cach
     a.splits = splits;
     a.theta = theta;
     a.scale = 1.0f / sqrtf((float)head_dim);
-    INFERNT_CUDA_TRY(launch_attention_decode(a, (cudaStream_t)stream, false));
+    INFERNT_CUDA_TRY(launch_attention_decode(a, (cudaStream_t)stream, true));
     return INFERNT_OK;
 }
 

@@ -267,23 +267,48 @@ __device__ void attention_item(const AttnArgs& a, int kvh, int split, int pos, f
     named_sync(1, NT);
     if (*s_last) {
         __threadfence();
-        // merge the active splits of this KV head, in split order
+        // merge the active splits of this KV head: one warp per head, the
+        // lanes load 32 splits' (m, l) at once (one round trip per 32 splits,
+        // not one per split); every output element sums w_s o_s in split
+        // order, the loads of eight splits in flight
         for (int h = warp; h < G; h += NW) {
+            const float* ph = a.part + ((size_t)kvh * a.splits * G + h) * (D + 2);
+            const size_t sstride = (size_t)G * (D + 2);
             float M = -INFINITY;
-            for (int s = 0; s < active; ++s)
-                M = fmaxf(M, __ldcg(a.part + (((size_t)kvh * a.splits + s) * G + h) * (D + 2)));
+            for (int s0 = 0; s0 < active; s0 += 32)
+                if (s0 + lane < active) M = fmaxf(M, __ldcg(ph + (size_t)(s0 + lane) * sstride));
+            M = warp_max(M);
             float L = 0.0f;
             float acc[MAXDL];
 #pragma unroll
             for (int i = 0; i < MAXDL; ++i) acc[i] = 0.0f;
-            for (int s = 0; s < active; ++s) {
-                const float* pp = a.part + (((size_t)kvh * a.splits + s) * G + h) * (D + 2);
-                const float w = expf(__ldcg(pp) - M);
-                L = fmaf(__ldcg(pp + 1), w, L);
+            for (int s0 = 0; s0 < active; s0 += 32) {
+                const int sl = s0 + lane;
+                float w = 0.0f;
+                if (sl < active) {
+                    w = expf(__ldcg(ph + (size_t)sl * sstride) - M);
+                    L = fmaf(__ldcg(ph + (size_t)sl * sstride + 1), w, L);
+                }
+                const int n = min(32, active - s0);
+                for (int k0 = 0; k0 < n; k0 += 8) {
+                    float ov[8][MAXDL];
 #pragma unroll
-                for (int i = 0; i < MAXDL; ++i)
-                    if (lane + 32 * i < D) acc[i] = fmaf(__ldcg(pp + 2 + lane + 32 * i), w, acc[i]);
+                    for (int k = 0; k < 8; ++k)
+#pragma unroll
+                        for (int i = 0; i < MAXDL; ++i)
+                            ov[k][i] = (k0 + k < n && lane + 32 * i < D)
+                                           ? __ldcg(ph + (size_t)(s0 + k0 + k) * sstride + 2 + lane + 32 * i)
+                                           : 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const float wk = __shfl_sync(0xffffffffu, w, (k0 + k) & 31);
+                        if (k0 + k < n)
+#pragma unroll
+                            for (int i = 0; i < MAXDL; ++i) acc[i] = fmaf(ov[k][i], wk, acc[i]);
+                    }
+                }
             }
+            L = warp_sum(L);
             const float inv = 1.0f / L;
             float* o = a.out + ((size_t)kvh * G + h) * D;
 #pragma unroll

@@ -1,6 +1,8 @@
 // gemv.cu — launchers and C entry points of the fused projection kernels.
 #include <cstring>
 
+#include <atomic>
+
 #include "gemv.cuh"
 #include "internal.h"
 
@@ -22,6 +24,10 @@ cudaError_t launch_one(const GemvArgs& a, bool fast, int grid, cudaStream_t stre
     }
     if (fast) {
         cfg.blockDim = dim3(kGemvThreads);
+        if (gemv_tma_smem_bytes(a.K, kGemvStagesDeep) <= kMaxDynSmem) {
+            cfg.dynamicSmemBytes = gemv_tma_smem_bytes(a.K, kGemvStagesDeep);
+            return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<WT, EPI, kGemvStagesDeep>, a);
+        }
         cfg.dynamicSmemBytes = gemv_tma_smem_bytes(a.K, kGemvStages);
         return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<WT, EPI, kGemvStages>, a);
     }
@@ -35,10 +41,12 @@ cudaError_t set_max_smem() {
     cudaError_t e =
         raise_dynamic_smem_limit(reinterpret_cast<const void*>(gemv_tma_kernel<WT, EPI, kGemvStages>));
     if (e != cudaSuccess) return e;
+    e = raise_dynamic_smem_limit(reinterpret_cast<const void*>(gemv_tma_kernel<WT, EPI, kGemvStagesDeep>));
+    if (e != cudaSuccess) return e;
     return raise_dynamic_smem_limit(reinterpret_cast<const void*>(gemv_plain_kernel<WT, EPI>));
 }
 
-bool g_prepared[64] = {false};
+std::atomic<bool> g_prepared[64] = {};  // first calls on a device may race: set once, idempotent
 
 template <typename WT>
 cudaError_t launch_dtype(const GemvArgs& a, int epi, bool fast, int grid, cudaStream_t s, bool pdl) {
@@ -87,7 +95,7 @@ int gemv_grid(const GemvArgs& a, int weight_dtype, int epi) {
 
 cudaError_t gemv_prepare() {
     const int d = current_device();
-    if (d >= 0 && d < 64 && g_prepared[d]) return cudaSuccess;
+    if (d >= 0 && d < 64 && g_prepared[d].load(std::memory_order_acquire)) return cudaSuccess;
     cudaError_t e;
     if ((e = set_max_smem<float, kEpiStore>()) != cudaSuccess) return e;
     if ((e = set_max_smem<float, kEpiResidual>()) != cudaSuccess) return e;
@@ -98,7 +106,7 @@ cudaError_t gemv_prepare() {
     if ((e = set_max_smem<__nv_bfloat16, kEpiSwiGLU>()) != cudaSuccess) return e;
     if ((e = set_max_smem<__nv_bfloat16, kEpiArgmax>()) != cudaSuccess) return e;
     if ((e = attention_prepare()) != cudaSuccess) return e;
-    if (d >= 0 && d < 64) g_prepared[d] = true;
+    if (d >= 0 && d < 64) g_prepared[d].store(true, std::memory_order_release);
     return cudaSuccess;
 }
 
@@ -162,7 +170,7 @@ int infernt_rmsnorm_gemv(float* y, const void* W0, int n0, const void* W1, int n
     a.norm_w = norm_w;
     a.eps = eps;
     a.out = y;
-    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiStore, (cudaStream_t)stream, false, nullptr));
+    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiStore, (cudaStream_t)stream, true, nullptr));
     return INFERNT_OK;
 }
 
@@ -180,7 +188,7 @@ int infernt_gemv_residual(float* out, const float* res, const void* W, int n, in
     a.x = x;
     a.out = out;
     a.res = res;
-    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiResidual, (cudaStream_t)stream, false, nullptr));
+    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiResidual, (cudaStream_t)stream, true, nullptr));
     return INFERNT_OK;
 }
 
@@ -201,7 +209,7 @@ int infernt_rmsnorm_gate_up_silu(float* out, const void* Wg, const void* Wu, int
     a.norm_w = norm_w;
     a.eps = eps;
     a.out = out;
-    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiSwiGLU, (cudaStream_t)stream, false, nullptr));
+    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiSwiGLU, (cudaStream_t)stream, true, nullptr));
     return INFERNT_OK;
 }
 
@@ -230,7 +238,7 @@ int infernt_rmsnorm_lm_head_argmax(float* logits, int* out_token, const void* W,
     a.am_out = out_token;
     a.err = &ws->err;
     INFERNT_REQUIRE(gemv_grid(a, weight_dtype, kEpiArgmax) <= kArgmaxMaxBlocks, "lm_head_argmax: grid too large");
-    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiArgmax, (cudaStream_t)stream, false, nullptr));
+    INFERNT_CUDA_TRY(launch_gemv(a, weight_dtype, kEpiArgmax, (cudaStream_t)stream, true, nullptr));
     return INFERNT_OK;
 }
 

@@ -7,12 +7,14 @@
 // one FMA, so the kernel is bound by HBM bandwidth and its job is to keep
 // enough bytes in flight on every SM.
 //
-// Fast path (in % 512 == 0, 16-byte aligned rows): one CTA per SM, one
-// producer thread streams the CTA's contiguous block of rows into a ring
-// of shared-memory slots with 1-D bulk copies (cp.async.bulk, the TMA
-// engine) and mbarrier transaction counts; four consumer warps multiply
-// the slots against the input vector held in shared memory (slot layout
-// below).  The producer starts before griddepcontrol.wait, so under programmatic
+// Fast path (in % 512 == 0, 16-byte aligned rows): one CTA per SM, four
+// producer threads (one per producer warp, taking turns slot by slot: a
+// slot takes one bulk copy per row, so one thread issuing them all would
+// cap the stream below the HBM rate) stream the CTA's contiguous block of
+// rows into a ring of shared-memory slots with 1-D bulk copies
+// (cp.async.bulk, the TMA engine) and mbarrier transaction counts; four
+// consumer warps multiply the slots against the input vector held in
+// shared memory (slot layout below).  The producer starts before griddepcontrol.wait, so under programmatic
 // dependent launch a kernel's weights stream in while the previous kernel
 // is still finishing.
 //
@@ -39,9 +41,11 @@ enum EpiKind : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiGLU = 2, kEpiArgmax
 
 constexpr int kPiece = 512;          // weight elements per piece (one float4/bf16x4 per thread)
 constexpr int kGemvConsumers = 128;  // four consumer warps
-constexpr int kGemvThreads = 160;    // plus one producer warp
+constexpr int kGemvProducers = 4;    // producer warps (lane 0 of each issues every fourth slot)
+constexpr int kGemvThreads = kGemvConsumers + 32 * kGemvProducers;
 constexpr int kSlotBytes = 16384;    // ring slot: one 512-column block of 8 FP32 / 16 bf16 rows
 constexpr int kGemvStages = 8;       // ring depth of the standalone kernels (128 KB in flight per SM)
+constexpr int kGemvStagesDeep = 12;  // when the input vector leaves room (192 KB in flight per SM)
 constexpr int kArgmaxMaxBlocks = 1024;
 constexpr int kPlainThreads = 256;
 constexpr int kMaxDynSmem = 226 * 1024;  // dynamic shared memory the launchers plan with (opt-in 227 KB
@@ -224,8 +228,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
     const int ue = (int)((long long)a.units * (blockIdx.x + 1) / gridDim.x);
     const int PPR = a.K / kPiece;
 
-    if (warp == kGemvConsumers / 32) {
-        // ---------------- producer: weights do not depend on the previous kernel
+    if (warp >= kGemvConsumers / 32) {
+        // ---------------- producers: weights do not depend on the previous
+        // kernel.  Producer k arms the slots sl = k (mod kGemvProducers);
+        // STAGES is a multiple of kGemvProducers, so every lap of a ring slot
+        // belongs to one producer.
+        static_assert(STAGES % kGemvProducers == 0, "producers divide the ring");
+        const uint32_t k = (uint32_t)(warp - kGemvConsumers / 32);
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
             uint32_t sl = 0;
@@ -233,6 +242,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
             for (int u0 = ub; u0 < ue && ok; u0 += G) {
                 const int ng = min(G, ue - u0);
                 for (int j = 0; j < PPR && ok; ++j, ++sl) {
+                    if (sl % kGemvProducers != k) continue;
                     const int s = (int)(sl % STAGES);
                     const uint32_t use = sl / STAGES;
                     if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1u, a.err)) {
@@ -248,9 +258,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_tma_kernel(const GemvArg
                                      tma_row<WT>(a, NS, q, u0 + g) + (size_t)j * PB, PB, &full[s], pol);
                 }
             }
-            if (!ok) {  // let every armed slot's copies land before the CTA can exit
+            if (!ok) {  // let every slot this producer armed land before the CTA can exit
                 const uint32_t first = sl > (uint32_t)STAGES ? sl - STAGES : 0u;
-                for (uint32_t q = first; q < sl; ++q) mbar_wait(&full[q % STAGES], (q / STAGES) & 1u, a.err);
+                for (uint32_t q = first; q < sl; ++q)
+                    if (q % kGemvProducers == k) mbar_wait(&full[q % STAGES], (q / STAGES) & 1u, a.err);
             }
         }
         return;

@@ -46,6 +46,31 @@ def test_noalloc_matches_workspace_entry_point(cuda, nq, nkv, D, pos, splits):
         assert bool(cuda.isfinite(outs["static"]).all())
 
 
+@pytest.mark.gpu
+def test_noalloc_shapes_back_to_back(cuda):
+    """Calls of different shapes in a row (4, then 8, then 2 KV heads, each
+    many splits): each finds the tickets the previous shape left at zero and
+    matches the workspace entry point."""
+    for i, (nq, nkv, D, pos, splits) in enumerate([(32, 4, 64, 700, 37), (32, 8, 128, 900, 18),
+                                                    (8, 2, 64, 333, 20)]):
+        ms = pos + 4
+        qkv = cuda.from_numpy(rnd(nq * D + 2 * nkv * D, 60 + i)).cuda()
+        kc, vc = rnd(nkv * ms * D, 70 + i), rnd(nkv * ms * D, 80 + i)
+        caches = {k: (cuda.from_numpy(kc).cuda(), cuda.from_numpy(vc).cuda()) for k in ("ws", "static")}
+        outs = {k: cuda.zeros(nq * D, device="cuda") for k in caches}
+        ws = cuda.zeros(ib.lib().infernt_attention_workspace_bytes(nq, nkv, D, splits), dtype=cuda.uint8,
+                        device="cuda")
+        kd, vd = caches["ws"]
+        ib.call("infernt_attention_decode", outs["ws"].data_ptr(), qkv.data_ptr(), kd.data_ptr(), vd.data_ptr(),
+                nq, nkv, D, ms, pos, 10000.0, splits, ws.data_ptr(), None)
+        kd, vd = caches["static"]
+        ib.call("infernt_attention_decode_noalloc", outs["static"].data_ptr(), qkv.data_ptr(), kd.data_ptr(),
+                vd.data_ptr(), nq, nkv, D, ms, pos, 10000.0, splits, None)
+        cuda.cuda.synchronize()
+        assert cuda.equal(outs["static"], outs["ws"]), (nq, nkv, D)
+        assert cuda.equal(caches["static"][0], caches["ws"][0]) and cuda.equal(caches["static"][1], caches["ws"][1])
+
+
 def test_noalloc_rejects_oversize_scratch():
     """16 q heads per KV head, D = 128, 148 splits: 9.9 MB of partials,
     above the 512 KiB static scratch; rejected before any device work."""
