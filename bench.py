@@ -320,9 +320,18 @@ def run_ours(args):
 
 
 # The first 64 greedy tokens of the Llama-3-8B-shaped decode below (seed 1,
-# 512-token seeded prompt) on one GPU: the tensor-parallel runs are checked
-# against them.
-LLAMA8B_TP1_TOKENS = None
+# 512-token seeded prompt) on one GPU (measure_llama8b_tp with world 1, one
+# B200): the tensor-parallel runs are checked against them.
+LLAMA8B_TP1_TOKENS = [
+    74325, 29784, 116036, 13841, 78160, 8054, 87554, 99912,
+    22201, 48487, 46054, 9760, 14993, 95613, 68450, 32004,
+    70506, 91286, 65530, 36762, 2697, 47189, 77848, 86374,
+    55866, 72738, 96966, 15700, 126896, 31724, 91417, 15059,
+    58308, 55092, 104689, 42894, 83670, 30557, 66623, 24200,
+    115946, 28298, 125357, 86034, 2520, 25757, 128182, 115911,
+    38943, 92207, 83477, 105780, 56659, 92537, 66869, 121544,
+    53370, 20360, 72045, 110362, 68328, 62196, 45986, 33142,
+]
 
 
 def measure_llama8b_tp(torch, ib, rank, world, local, steps=61, warmup=3):

@@ -55,18 +55,29 @@ public:
                                      const GenerationConfig& gen_config = GenerationConfig(),
                                      GenerationStats* stats = nullptr);
 
-    // One decode step at `position`: returns the greedy next token.
+    // One decode step at `position`: returns the next token, greedy, or
+    // drawn at the step temperature (set_step_temperature) inside the step.
     int forward_token(int token_id, int position);
-    // temperature <= 0: the greedy token of the last step (computed by the
-    // fused argmax; no second kernel).  Otherwise the reference's host
-    // sampler (src/engine.cpp:78-104): softmax at the temperature over the
-    // logits and a draw from a static mt19937(1337).
+    // temperature <= 0: the greedy token of the last step.  temperature > 0:
+    // a draw from softmax(logits / temperature) — on the GPU by Gumbel-max
+    // (the default): the token the step itself drew when the temperature
+    // equals the step temperature (no further kernel), else one sampling
+    // kernel over the step's logits; with set_device_sampling(false), the
+    // reference's host sampler (src/engine.cpp:78-104: softmax on the host, a
+    // draw from a static mt19937(1337)).  GPU draws are keyed by (seed, the
+    // step's position, the draw's count since the step), so every call draws
+    // afresh and runs are reproducible; they follow the distribution of the
+    // reference's draws, not its mt19937 sequence.
     int sample_next_token(float temperature = 0.0f);
-    // Not in the reference: with `on`, sample_next_token(T > 0) draws on the
-    // GPU (infernt_sample_tokens: Gumbel-max, the same distribution,
-    // reproducible per seed and call count) instead of copying the logits to
-    // the host; off (the default) keeps the reference's host sampler.
+    // Not in the reference: `on` (the default) samples on the GPU as above,
+    // off restores the reference's host sampler.
     void set_device_sampling(bool on, uint64_t seed = 1337);
+    // Not in the reference: the temperature at which forward_token draws the
+    // next token inside the decode kernel's LM-head phase (0: greedy, the
+    // default).  Needs the persistent decode kernel and device sampling;
+    // otherwise the step stays greedy and sample_next_token samples after it.
+    // generate() sets it to its temperature for the generation.
+    void set_step_temperature(float temperature);
 
     // `steps` greedy steps chained on the device from (token_id, position);
     // writes the produced tokens to tokens_out and returns the device time in ms.
@@ -95,7 +106,10 @@ private:
     Tensor tokens_dev_;
     int last_token_;
     bool is_loaded_;
-    bool device_sampling_ = false;
-    uint64_t sample_seed_ = 1337, sample_counter_ = 0;
+    bool device_sampling_ = true;
+    uint64_t sample_seed_ = 1337;
+    float step_temperature_ = 0.0f;  // temperature the last steps drew at inside the kernel (0: greedy)
+    int last_position_ = 0;
+    uint64_t draws_at_position_ = 0;  // GPU draws sample_next_token made since the last step
     Tensor sample_ws_, sample_out_;
 };

@@ -286,6 +286,16 @@ INFERNT_API int infernt_plan_kernels_per_step(const infernt_plan* plan);
  * PERSISTENT mode only. */
 INFERNT_API size_t infernt_plan_trace_entries(const infernt_plan* plan, int steps);
 INFERNT_API int infernt_plan_set_trace(infernt_plan* plan, unsigned long long* trace_dev);
+/* Token choice of the following steps: temperature <= 0 greedy (the
+ * default), otherwise the LM-head phase of the persistent decode kernel
+ * draws the token from softmax(logits / temperature) by Gumbel-max (the
+ * argmax of logit / T + g_i, g_i = -ln(-ln u_i), u_i hashed from (seed, the
+ * step's position, i)): the token infernt_sample_tokens(logits, ..., seed,
+ * counter = position) draws from the same logits.  Logits stay the raw
+ * values.  Returns INFERNT_ERR_UNSUPPORTED for T > 0 on a plan that does
+ * not run the persistent kernel.  No counterpart in the reference (its
+ * sampler runs on the host, src/engine.cpp:78-104). */
+INFERNT_API int infernt_plan_set_sampling(infernt_plan* plan, float temperature, uint64_t seed);
 /* CTAs of the persistent decode kernel on the current device (one per SM). */
 INFERNT_API int infernt_persistent_ctas(void);
 
@@ -535,11 +545,19 @@ INFERNT_API int infernt_engine_forward_token(infernt_engine* e, int token, int p
  * weight_dtype INFERNT_DTYPE_F32 / _BF16 overrides config.json's (negative:
  * keep it). */
 INFERNT_API int infernt_engine_load_model(const char* model_dir, int weight_dtype, infernt_engine** out);
-/* With on != 0 the engine's sample_next_token(T > 0) draws on the GPU
- * (infernt_sample_tokens with this seed and a per-engine call counter)
- * instead of the reference's host mt19937 sampler (the default).  No
- * counterpart in the reference. */
+/* on != 0 (the default, seed 1337): the engine's sample_next_token(T > 0)
+ * draws on the GPU by Gumbel-max as infernt_sample_tokens(..., seed, counter
+ * = position | k << 32) for its k-th draw since the last step (k = 0: the
+ * draw a step at that temperature makes inside the kernel); on == 0
+ * restores the reference's host mt19937 sampler.  No counterpart in the
+ * reference. */
 INFERNT_API int infernt_engine_set_device_sampling(infernt_engine* e, int on, uint64_t seed);
+/* InferenceEngine::set_step_temperature: following steps (forward_token,
+ * decode_chain) draw their token at this temperature inside the persistent
+ * decode kernel's LM-head phase (0: greedy).  Without the persistent kernel
+ * or with host sampling the steps stay greedy.  No counterpart in the
+ * reference. */
+INFERNT_API int infernt_engine_set_step_temperature(infernt_engine* e, float temperature);
 /* InferenceEngine::sample_next_token (src/engine.cpp:68-105). */
 INFERNT_API int infernt_engine_sample_next_token(infernt_engine* e, float temperature,
                                                  int* token);

@@ -149,6 +149,8 @@ _SIGS = {
     "infernt_batch_engine_set_sampling": (_I, [_P, _F, ctypes.c_uint64]),
     "infernt_sample_workspace_bytes": (_S, [_I]),
     "infernt_engine_set_device_sampling": (_I, [_P, _I, ctypes.c_uint64]),
+    "infernt_engine_set_step_temperature": (_I, [_P, _F]),
+    "infernt_plan_set_sampling": (_I, [_P, _F, ctypes.c_uint64]),
     "infernt_engine_load_model": (_I, [ctypes.c_char_p, _I, _P]),
     "infernt_sample_tokens": (_I, [_P, ctypes.c_longlong, _I, _I, _F, ctypes.c_uint64, ctypes.c_uint64, _P, _P,
                                    _P]),
@@ -319,9 +321,14 @@ class Engine:
         return out.value
 
     def set_device_sampling(self, on: bool = True, seed: int = 1337):
-        """Temperature sampling on the GPU (Gumbel-max) instead of the
-        reference's host sampler."""
+        """Temperature sampling on the GPU (Gumbel-max, the default) or, with
+        on=False, the reference's host sampler."""
         call("infernt_engine_set_device_sampling", self._h, int(on), seed)
+
+    def set_step_temperature(self, temperature: float):
+        """Following steps draw their token at this temperature inside the
+        decode kernel (0: greedy)."""
+        call("infernt_engine_set_step_temperature", self._h, float(temperature))
 
     @classmethod
     def load_model(cls, model_dir: str, weight_dtype: int = -1) -> "Engine":

@@ -47,6 +47,7 @@
 #include "decode_kernel.cuh"
 #include "gemv.cuh"
 #include "internal.h"
+#include "sample.cuh"
 
 namespace infernt {
 
@@ -94,6 +95,7 @@ struct MegaShared {
     int res_n;     // staged rows
     float res[kResRows];
     float gpart[2][kTeamWarps][kGroupBatch][16];  // row sums per team and warp of up to kGroupBatch batches
+    unsigned long long skey;          // Gumbel key of the step (temperature sampling)
     uint64_t xbar;                    // completion of the input-vector bulk copy
     uint64_t pbar;                   // completion of the next phase descriptor's bulk copy
 };
@@ -537,8 +539,11 @@ __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaSha
         } else {
             p.logits[row] = v;
             const int id = P.row_base + row;
-            if (argmax_better(v, id, am_v, am_i)) {
-                am_v = v;
+            // greedy: the logit; sampling: its Gumbel score (global id, so
+            // every rank of a tensor-parallel run draws the same noise)
+            const float sc = p.inv_temp > 0.0f ? gumbel_score(v, p.inv_temp, sh.skey, (uint64_t)id) : v;
+            if (argmax_better(sc, id, am_v, am_i)) {
+                am_v = sc;
                 am_i = id;
             }
         }
@@ -1562,6 +1567,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             while ((int)(unsigned)(st >> 32) != pos0 + step && !wt.give_up(t0, spins)) st = ld_acquire64(stw);
         }
         const int tok = (int)(unsigned)(st & 0xffffffffull), pos = (int)(unsigned)(st >> 32);
+        // read after the first phase's opening barrier, so no thread of the
+        // previous step still uses the old key
+        if (tid == 0) sh.skey = infernt_stream_key(p.sample_seed, (uint64_t)(unsigned)pos);
         const unsigned ts = p.tag_base + (unsigned)step * (unsigned)p.nphases + 1u;  // tag of phase 0
         for (int ph = 0; ph < p.nphases; ++ph) {
             const long long tb = tid == 0 ? trace_base(p, step, ph) : -1;

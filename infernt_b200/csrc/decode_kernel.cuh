@@ -91,6 +91,11 @@ struct MegaParams {
     // SM clock cycles any single wait may take before the kernel gives up
     // (kErrWaitTimeout in the error word, every CTA returns)
     long long wait_cycles;
+    // token choice of the LM-head phase: inv_temp 0 greedy, else a draw from
+    // softmax(logits * inv_temp) by Gumbel-max with noise keyed by
+    // (sample_seed, the step's position, the vocabulary id)
+    float inv_temp;
+    unsigned long long sample_seed;
 };
 
 constexpr int kTraceFields = 7;

@@ -33,10 +33,23 @@ void InferenceEngine::load_model(const ModelConfig& config, const std::string& w
     initialize(config, std::move(w), std::move(tok));
 }
 
+void InferenceEngine::set_step_temperature(float temperature) {
+    if (!is_loaded_) throw std::runtime_error("Engine model is not loaded");
+    infernt_plan* plan = architecture_->plan_for(weights_, kv_cache_);
+    const float t = (device_sampling_ && temperature > 0.0f) ? temperature : 0.0f;
+    if (t > 0.0f && infernt_plan_set_sampling(plan, t, sample_seed_) == INFERNT_OK) {
+        step_temperature_ = t;
+        return;
+    }
+    if (infernt_plan_set_sampling(plan, 0.0f, sample_seed_) != INFERNT_OK)
+        throw std::runtime_error(std::string("set_step_temperature: ") + infernt_last_error());
+    step_temperature_ = 0.0f;
+}
+
 void InferenceEngine::set_device_sampling(bool on, uint64_t seed) {
     device_sampling_ = on;
     sample_seed_ = seed;
-    sample_counter_ = 0;
+    if (is_loaded_ && step_temperature_ > 0.0f) set_step_temperature(on ? step_temperature_ : 0.0f);
 }
 
 void InferenceEngine::initialize(const ModelConfig& config, ModelWeights weights, Tokenizer tokenizer) {
@@ -57,23 +70,35 @@ int InferenceEngine::forward_token(int token_id, int position) {
     if (!is_loaded_) throw std::runtime_error("Engine model is not loaded");
     architecture_->forward_token(token_id, weights_, kv_cache_, position, logits_);
     last_token_ = architecture_->last_token();
+    last_position_ = position;
+    draws_at_position_ = 0;
     return last_token_;
 }
 
 int InferenceEngine::sample_next_token(float temperature) {
     if (!is_loaded_) throw std::runtime_error("Engine model is not loaded");
-    if (temperature <= 0.0f) return last_token_;
-    if (device_sampling_) {
-        // Gumbel-max on the device (sample.cu): one int crosses to the host
+    // the token the step already chose: greedy, or its first draw at this
+    // temperature (a further call at the same position draws afresh, as the
+    // reference's sampler does)
+    if (temperature <= 0.0f && step_temperature_ <= 0.0f) return last_token_;
+    if (temperature > 0.0f && temperature == step_temperature_ && draws_at_position_ == 0) {
+        draws_at_position_ = 1;
+        return last_token_;
+    }
+    if (device_sampling_ || temperature <= 0.0f) {
+        // one kernel over the step's logits (sample.cu; T <= 0 is its greedy
+        // argmax): one int crosses to the host
         if (!sample_ws_.is_valid()) {
             const int bytes = (int)infernt_sample_workspace_bytes(1);
             sample_ws_ = Tensor::zeros({bytes}, DType::UINT8, Device::CUDA);
             sample_out_ = Tensor::zeros({1}, DType::INT32, Device::CUDA);
         }
         const int s = infernt_sample_tokens(static_cast<const float*>(logits_.data_ptr()), 0, 1, config_.vocab_size,
-                                            temperature, sample_seed_, sample_counter_++,
+                                            temperature, sample_seed_,
+                                            (uint64_t)(unsigned)last_position_ | ((uint64_t)draws_at_position_ << 32),
                                             static_cast<int*>(sample_out_.data_ptr()), sample_ws_.data_ptr(), nullptr);
         if (s) throw std::runtime_error(std::string("sample_next_token: ") + infernt_last_error());
+        if (temperature > 0.0f) ++draws_at_position_;
         int tok = 0;
         if (cudaMemcpy(&tok, sample_out_.data_ptr(), sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
             throw std::runtime_error("sample_next_token: device-to-host copy failed");
@@ -132,6 +157,18 @@ std::vector<int> InferenceEngine::generate_tokens(const std::vector<int>& prompt
     if (!is_loaded_) throw std::runtime_error("Engine model is not loaded");
     std::vector<int> tokens = prompt;
     if (tokens.empty()) tokens.push_back(tokenizer_.bos_id());
+    // draw inside the decode kernel at the generation's temperature (restored
+    // to greedy afterwards)
+    set_step_temperature(gc.temperature);
+    struct Restore {
+        InferenceEngine* e;
+        ~Restore() {
+            try {
+                e->set_step_temperature(0.0f);
+            } catch (...) {
+            }
+        }
+    } restore{this};
     auto t0 = std::chrono::high_resolution_clock::now();
     kv_cache_.reset();
     for (size_t pos = 0; pos < tokens.size(); ++pos) forward_token(tokens[pos], (int)pos);

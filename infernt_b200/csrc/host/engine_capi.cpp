@@ -186,6 +186,16 @@ int infernt_engine_load_model(const char* model_dir, int weight_dtype, infernt_e
     }
 }
 
+int infernt_engine_set_step_temperature(infernt_engine* e, float temperature) {
+    INFERNT_REQUIRE(e, "engine_set_step_temperature: null engine");
+    try {
+        e->engine.set_step_temperature(temperature);
+    } catch (const std::exception& ex) {
+        return infernt::fail(INFERNT_ERR_CUDA, "engine_set_step_temperature: %s", ex.what());
+    }
+    return INFERNT_OK;
+}
+
 int infernt_engine_set_device_sampling(infernt_engine* e, int on, uint64_t seed) {
     INFERNT_REQUIRE(e, "engine_set_device_sampling: null engine");
     e->engine.set_device_sampling(on != 0, seed);

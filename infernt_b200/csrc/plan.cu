@@ -516,6 +516,8 @@ int build_mega(infernt_plan* p) {
     m.tp_size = p->tp_size;
     m.peers = p->peer_tab;  // set by infernt_plan_set_peers (tensor parallelism)
     m.wait_cycles = wait_cycles_for(2000000);
+    m.inv_temp = 0.0f;  // greedy until infernt_plan_set_sampling
+    m.sample_seed = 0;
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
@@ -761,6 +763,21 @@ int infernt_plan_set_wait_budget(infernt_plan* p, long long microseconds) {
     INFERNT_REQUIRE(microseconds > 0 && microseconds <= 600000000ll,
                     "plan_set_wait_budget: %lld us outside (0, 600 s]", microseconds);
     p->mega.wait_cycles = wait_cycles_for(microseconds);
+    return INFERNT_OK;
+}
+
+int infernt_plan_set_sampling(infernt_plan* p, float temperature, uint64_t seed) {
+    INFERNT_REQUIRE(p, "plan_set_sampling: null plan");
+    INFERNT_REQUIRE(temperature == temperature, "plan_set_sampling: temperature is NaN");
+    if (temperature <= 0.0f) {
+        p->mega.inv_temp = 0.0f;
+        return INFERNT_OK;
+    }
+    if (p->mode != INFERNT_MODE_PERSISTENT)
+        return fail(INFERNT_ERR_UNSUPPORTED, "plan_set_sampling: temperature sampling inside the step needs the "
+                                             "persistent decode kernel (this plan runs mode %d)", p->mode);
+    p->mega.inv_temp = 1.0f / temperature;
+    p->mega.sample_seed = seed;
     return INFERNT_OK;
 }
 

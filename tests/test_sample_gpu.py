@@ -125,3 +125,51 @@ def test_batched_engine_sampling_matches_the_sampler(cuda):
     logits = eng.logits()
     assert nxt == [int(np.argmax(logits[b])) for b in range(4)]
     eng.close()
+
+
+STEP_CFG = ib.ModelConfig(vocab_size=1000, hidden_size=512, num_layers=2, num_attention_heads=8,
+                          num_key_value_heads=2, intermediate_size=1536, max_seq_len=128)
+
+
+@pytest.mark.parametrize("temperature", [0.5, 1.0, 2.0])
+def test_step_sampling_inside_the_decode_kernel(cuda, temperature):
+    """With a step temperature, the persistent decode kernel's LM-head phase
+    draws the token itself (Gumbel-max over the logits it computes): the
+    token forward_token returns equals infernt_sample_tokens on the same
+    logits with (seed 1337, counter = position), and sample_next_token at
+    that temperature returns it without another kernel.  The logits are the
+    raw values; at temperature 0 the step is greedy again."""
+    eng = ib.Engine(STEP_CFG, seed=31)
+    assert eng.mode == ib.MODE_PERSISTENT
+    eng.set_step_temperature(temperature)
+    tok, drawn = 7, 0
+    for pos in range(12):
+        got = eng.forward_token(tok, pos)
+        logits = eng.logits()
+        want = int(sample(cuda, logits, 1, temperature, seed=1337, counter=pos)[0])
+        assert got == want, (pos, got, want)
+        assert eng.sample_next_token(temperature) == got
+        drawn += int(got != int(np.argmax(logits)))
+        tok = got
+    assert drawn > 0  # some steps drew a token other than the argmax
+    eng.set_step_temperature(0.0)
+    got = eng.forward_token(tok, 12)
+    assert got == int(np.argmax(eng.logits()))
+    eng.close()
+
+
+def test_sample_next_token_draws_on_the_gpu_by_default(cuda):
+    """Without a step temperature the step is greedy and sample_next_token(T)
+    draws with one kernel over the step's logits (seed 1337, counter =
+    position); sample_next_token(0) is the greedy token."""
+    eng = ib.Engine(STEP_CFG, seed=32)
+    greedy = eng.forward_token(11, 0)
+    logits = eng.logits()
+    assert greedy == int(np.argmax(logits))
+    assert eng.sample_next_token(0.0) == greedy
+    assert eng.sample_next_token(1.5) == int(sample(cuda, logits, 1, 1.5, seed=1337, counter=0)[0])
+    eng.set_step_temperature(1.5)
+    drawn = eng.forward_token(11, 0)
+    assert eng.sample_next_token(0.0) == greedy  # greedy from the same logits
+    assert drawn == int(sample(cuda, eng.logits(), 1, 1.5, seed=1337, counter=0)[0])
+    eng.close()
