@@ -390,15 +390,15 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         if (plain) bulk_g2s_plain(xs, plain, vbytes, &sh.xbar);
         if (P.norm_w) bulk_g2s_plain(xs + K, P.norm_w, vbytes, &sh.xbar);
     }
-    int staged = 0;
-    if (P.res && u1 - u0 <= kResRows) {
-        const unsigned rt = ts + (unsigned)P.res_ph;
-        for (int i = tid; i < u1 - u0; i += kMegaConsumers)
-            sh.res[i] = ll_val(wt.one<false>(P.res + u0 + i, ld_ll1<false>(P.res + u0 + i), rt));
-        staged = u1 - u0;
-    }
+    // the residual rows of the CTA's units (residual phases): loaded now,
+    // checked after the input vector, so the two reads overlap
+    static_assert(kResRows <= kMegaConsumers, "one residual row per thread");
+    const bool stage = P.res && u1 - u0 <= kResRows;
+    const bool my_res = stage && tid < u1 - u0;
+    unsigned long long res_w = 0;
+    if (my_res) res_w = ld_ll1<false>(P.res + u0 + tid);
     if (tid == 0) {  // one writer; read after the named barrier at the end
-        sh.res_n = staged;
+        sh.res_n = stage ? u1 - u0 : 0;
         sh.res_base = u0;
     }
     if (P.nsum > 0) {
@@ -425,6 +425,7 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         ll_read_vec<false>(P.x, xs, P.kx, ts + (unsigned)P.x_ph, tid, wt);
         for (int i = P.kx + tid; i < K; i += kMegaConsumers) xs[i] = 0.0f;
     }
+    if (my_res) sh.res[tid] = ll_val(wt.one<false>(P.res + u0 + tid, res_w, ts + (unsigned)P.res_ph));
     if (bytes) {
         mega_wait(&sh.xbar, xphase & 1u, &sh.abort, p.err);
         ++xphase;
