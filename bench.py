@@ -190,6 +190,39 @@ def cpu_baseline(cfg, budget_s=12.0):
                       % (n, n - 1, threads, gen_s)}
 
 
+def measure_batched_b1_exchanges(torch, ib, rank, world, pos, steps):
+    """The same 8B-shaped decode (bf16 weights, seed 1, batch 1) through the
+    batched engine: one kernel per op captured in a CUDA graph, tensor
+    parallel over the ranks, its O and down sums crossing the ranks by the
+    peer-memory exchange and then by ncclAllReduce (the NCCL baseline);
+    seeded KV rows for `pos` positions, `steps` timed steps each (CUDA
+    events, max over ranks)."""
+    import torch.distributed as dist
+    cfg = ib.LLAMA3_8B.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=pos + 2 * steps + 16)
+    nid = [ib.nccl_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(nid, src=0)
+    eng = ib.BatchEngine(cfg, 1, seed=1, std=STD, rank=rank, world=world, nccl_id=nid[0] if world > 1 else None)
+    eng.fill_kv(0, 7, pos)
+    out = {"engine": "infernt_batch_engine (bgemm tcgen05 projections, T = 1), CUDA graph per step",
+           "positions": [pos, pos + 2 * steps]}
+    tok, p = [5], [pos]
+    for mode in (["peer", "nccl"] if world > 1 else ["single"]):
+        if world > 1:
+            eng.set_tp_exchange(mode == "peer")
+            dist.barrier()
+        toks, _ = eng.decode(tok, p, 3)
+        tok, p = [int(toks[-1][0])], [p[0] + 3]
+        if world > 1:
+            dist.barrier()
+        toks, ms = eng.decode(tok, p, steps)
+        tok, p = [int(toks[-1][0])], [p[0] + steps]
+        ms_max = max_over_ranks(torch, ms, "cuda")
+        out[mode] = {"ms_per_step": round(ms_max / steps, 5), "tok_s": round(steps / (ms_max / 1e3), 2)}
+    eng.close()
+    return out
+
+
 def run_ours(args):
     import torch
     import infernt_b200 as ib
@@ -387,7 +420,9 @@ def measure_llama8b_tp(torch, ib, rank, world, local, steps=61, warmup=3):
     bytes_gpu = wbytes + 2 * L * d[1] * D * 4 * (ctx_mean + 1) + H * 4
     hbm, src = peaks()
     eng.close()
+    nccl_side = measure_batched_b1_exchanges(torch, ib, rank, world, prompt_len + warmup, steps)
     return {"workload": "llama3-8b-bf16-b1-tp%d" % world, "parallelism": "tp%d" % world,
+            "kernel_sequence_engine": nccl_side,
             "ms_per_step": round(ms_max / steps, 5), "tok_s": round(steps / (ms_max / 1e3), 2),
             "steps": steps, "positions": [prompt_len + warmup, prompt_len + warmup + steps],
             "bytes_per_gpu_per_step": bytes_gpu,
@@ -662,7 +697,7 @@ def run_batched(args, longctx=False, tp=False):
     if longctx:
         n_seq, seed = 16, 1
         ctx = np.full(n_seq, 32768)
-        cfg = ib.LLAMA3_8B.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=32768 + W + K + 16)
+        cfg = ib.LLAMA3_8B.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=32768 + W + 2 * K + 64)
     else:
         n_seq, seed = 64, 0
         ctx = np.random.default_rng(1234).integers(512, 2049, size=n_seq)
@@ -710,6 +745,22 @@ def run_batched(args, longctx=False, tp=False):
     ms_max = max_over_ranks(torch, ms, "cuda")
     value = n_seq * K / (ms_max / 1e3)
     shards = world if tp else 1
+    nccl_baseline = None
+    if tp and world > 1:
+        # the same steps with the sums crossing the ranks by ncclAllReduce
+        eng.set_tp_exchange(False)
+        tk = [int(t) for t in toks[-1]]
+        ps = [p + K for p in positions]
+        tw, _ = eng.decode(tk, ps, 2)
+        tk, ps = [int(t) for t in tw[-1]], [p + 2 for p in ps]
+        dist.barrier()
+        tn, ms_n = eng.decode(tk, ps, K)
+        ms_n = max_over_ranks(torch, ms_n, "cuda")
+        nccl_baseline = {"exchange": "ncclAllReduce after O and down", "ms_per_step": round(ms_n / K, 5),
+                         "tok_s": round(n_seq * K / (ms_n / 1e3), 1)}
+        eng.set_tp_exchange(True)
+        positions = ps
+        toks = tn
     # end to end through the synchronous step entry point: host token and
     # position arrays in, next tokens out, every step
     tokens = [int(t) for t in toks[-1]]
@@ -749,7 +800,7 @@ def run_batched(args, longctx=False, tp=False):
     # Q|K|V finishing and the merge per layer)
     per_layer = 8 if cfg.num_attention_heads // cfg.num_key_value_heads <= 8 else 10
     if tp and world > 1:
-        per_layer += 2  # the split sums before the two all-reduces (NCCL's kernels not counted)
+        per_layer += 2  # the pushes of the two sums into the ranks' regions
     result = {
         "metric": metric,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
@@ -758,7 +809,7 @@ def run_batched(args, longctx=False, tp=False):
                                "all-reduce after O and down" if tp else "data parallel: sequences split over ranks"),
         "dtype": "bf16 weights and projection inputs, f32 accumulation, bf16 KV",
         "data": data,
-        "gpu_launches": K * (per_layer * cfg.num_layers + (4 if tp and world > 1 else 3)),
+        "gpu_launches": K * (per_layer * cfg.num_layers + (5 if tp and world > 1 else 3)),
         "config": {"workload": workload, "sequences": n_seq, "per_gpu": T,
                    "contexts_mean": round(float(np.mean(ctx)), 1),
                    "parallelism": ("tp%d" if tp else "dp%d") % world,
@@ -774,6 +825,11 @@ def run_batched(args, longctx=False, tp=False):
                      "tensor_tflops": round(flops * K / (ms_max / 1e3) / 1e12, 1)},
         "clocks": clocks,
     }
+    if nccl_baseline:
+        result["nccl_baseline"] = nccl_baseline
+        result["parallelism_detail"] = ("tensor parallel: heads, FFN rows and vocabulary rows split over the ranks; "
+                                        "O and down sums pushed into every rank's region over NVLink (peer-memory "
+                                        "exchange), ncclAllReduce reported beside it")
     if prefill:
         result["prefill"] = prefill
         result["data"] = ("synthetic: seeded weights N(0,0.02) seed 1, norms 1.0; every sequence's 32768-token "

@@ -388,6 +388,16 @@ INFERNT_API int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, i
  * The step graph is captured again at the next step. */
 INFERNT_API int infernt_batch_engine_set_sampling(infernt_batch_engine* e, float temperature,
                                                   uint64_t seed);
+/* How a tensor-parallel batched engine adds the ranks' O and down sums:
+ * INFERNT_TP_EXCHANGE_PEER (the default) pushes each rank's sums into every
+ * rank's exchange region over NVLink (CUDA IPC mappings made at creation)
+ * as tagged words that the residual + RMSNorm kernel of every rank adds in
+ * rank order (no NCCL call on the data path; waits bounded, reported as
+ * INFERNT_ERR_DEVICE); INFERNT_TP_EXCHANGE_NCCL runs ncclAllReduce (the
+ * baseline).  Every rank must use the same mode.  No counterpart in the
+ * reference. */
+enum { INFERNT_TP_EXCHANGE_PEER = 1, INFERNT_TP_EXCHANGE_NCCL = 0 };
+INFERNT_API int infernt_batch_engine_set_tp_exchange(infernt_batch_engine* e, int mode);
 /* K splits of the Q|K|V, O, gate|up, down and LM-head projections and the
  * attention's KV splits (6 ints). */
 INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);

@@ -147,6 +147,7 @@ _SIGS = {
     "infernt_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "infernt_batch_engine_vocab_range": (_I, [_P, _P, _P]),
     "infernt_batch_engine_set_sampling": (_I, [_P, _F, ctypes.c_uint64]),
+    "infernt_batch_engine_set_tp_exchange": (_I, [_P, _I]),
     "infernt_sample_workspace_bytes": (_S, [_I]),
     "infernt_engine_set_device_sampling": (_I, [_P, _I, ctypes.c_uint64]),
     "infernt_engine_set_step_temperature": (_I, [_P, _F]),
@@ -475,6 +476,11 @@ class BatchEngine:
         """Temperature sampling (Gumbel-max in the argmax kernels) for the
         following steps; temperature 0 is greedy."""
         call("infernt_batch_engine_set_sampling", self._h, temperature, seed)
+
+    def set_tp_exchange(self, peer: bool):
+        """Tensor parallelism: sums cross the ranks by the peer-memory exchange
+        (True, the default) or by ncclAllReduce (False)."""
+        call("infernt_batch_engine_set_tp_exchange", self._h, 1 if peer else 0)
 
     def splits(self):
         out = (ctypes.c_int * 6)()

@@ -840,6 +840,110 @@ __global__ void tp_sum_splits(const float* part, int splits, int T, int N, float
         reinterpret_cast<float4*>(y)[i] = sum_parts4(part, splits, (size_t)T * N, 4 * i);
 }
 
+// ------------------------------------- peer-memory exchange of the sums
+// In place of an NCCL all-reduce after the O and down projections, each
+// rank pushes its sum of the split partials [T][N] into slot [rank] of every
+// rank's exchange region (CUDA IPC mappings over NVLink) as tagged words
+// (value | tag << 32, one 8-byte store each: a reader that sees the tag has
+// the value), and the residual + RMSNorm kernel of every rank adds the
+// world slots of its own region in rank order, so every rank holds the same
+// bits.  A region is two buffers [2][world][T][N] taken in turn (buffer idx &
+// 1 of the step's idx-th exchange), so a rank one exchange ahead never
+// overwrites a slot a peer still reads.  Tags: epoch x per_step + idx + 1,
+// the epoch advanced once per step on the device (bt_epoch_advance).
+
+__device__ __forceinline__ void tp_st_sys2(unsigned long long* a, unsigned long long w0, unsigned long long w1) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(a), "l"(w0), "l"(w1) : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 tp_ld_sys2(const unsigned long long* a) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(a) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long tp_pack(float v, unsigned tag) {
+    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+}
+
+__device__ __forceinline__ unsigned tp_tag(const unsigned* epoch, int per_step, int idx) {
+    return *epoch * (unsigned)per_step + (unsigned)idx + 1u;
+}
+
+__global__ void bt_epoch_advance(unsigned* epoch) {
+    pdl_wait();
+    pdl_launch_dependents();
+    ++*epoch;
+}
+
+// This rank's sum of the split partials into slot [rank] of buffer idx & 1 of
+// every rank's region (peers[r] = rank r's region, own included).
+__global__ void tp_push(const float* part, int splits, int T, int N, unsigned long long* const* peers, int rank,
+                        int world, const unsigned* epoch, int per_step, int idx) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const unsigned tag = tp_tag(epoch, per_step, idx);
+    const size_t n = (size_t)T * N;
+    const size_t base = ((size_t)(idx & 1) * world + rank) * n;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n / 4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = sum_parts4(part, splits, n, 4 * i);
+        const unsigned long long w0 = tp_pack(v.x, tag), w1 = tp_pack(v.y, tag), w2 = tp_pack(v.z, tag),
+                                 w3 = tp_pack(v.w, tag);
+        for (int r = 0; r < world; ++r) {
+            unsigned long long* d = peers[r] + base + 4 * i;
+            tp_st_sys2(d, w0, w1);
+            tp_st_sys2(d + 2, w2, w3);
+        }
+    }
+}
+
+// h[t] += the world ranks' sums (rank order) from this rank's region;
+// xb[t] = bf16(RMSNorm(h[t], norm_w)).  H / 4 threads.  Waits for the
+// peers' words at most `budget` SM cycles (then kErrWaitTimeout).
+__global__ void bt_resid_norm_tp(const unsigned long long* own, int world, int T, int H, float* h,
+                                 const float* norm_w, float eps, uint16_t* xb, const unsigned* epoch, int per_step,
+                                 int idx, unsigned* err, long long budget) {
+    pdl_wait();
+    pdl_launch_dependents();
+    __shared__ float red[33];
+    const int t = blockIdx.x;
+    const unsigned tag = tp_tag(epoch, per_step, idx);
+    const size_t n = (size_t)T * H;
+    const unsigned long long* b = own + (size_t)(idx & 1) * world * n + (size_t)t * H + 4 * threadIdx.x;
+    float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const long long t0 = clock64();
+    bool late = false;
+    for (int r = 0; r < world; ++r) {
+        const unsigned long long* a = b + (size_t)r * n;
+        ulonglong2 lo = tp_ld_sys2(a), hi = tp_ld_sys2(a + 2);
+        auto ok = [&]() {
+            return (unsigned)(lo.x >> 32) == tag && (unsigned)(lo.y >> 32) == tag && (unsigned)(hi.x >> 32) == tag &&
+                   (unsigned)(hi.y >> 32) == tag;
+        };
+        while (!ok() && !late) {
+            if (clock64() - t0 > budget) {
+                atomicOr(err, kErrWaitTimeout);
+                late = true;
+                break;
+            }
+            lo = tp_ld_sys2(a);
+            hi = tp_ld_sys2(a + 2);
+        }
+        y.x += __uint_as_float((unsigned)lo.x);
+        y.y += __uint_as_float((unsigned)lo.y);
+        y.z += __uint_as_float((unsigned)hi.x);
+        y.w += __uint_as_float((unsigned)hi.y);
+    }
+    float4* hp = reinterpret_cast<float4*>(h + (size_t)t * H + 4 * threadIdx.x);
+    float4 v = *hp;
+    v.x += y.x;
+    v.y += y.y;
+    v.z += y.z;
+    v.w += y.w;
+    *hp = v;
+    norm_row_bf16(v, norm_w, H, eps, xb + (size_t)t * H, red);
+}
+
 // Greedy pick of sequence t over this rank's vocabulary rows: logits [T][ld]
 // (rows [0, vl) valid, vocabulary ids v0 + row) -> cand[t] = (value, id).
 // The lowest id wins among equal values; NaN never wins.
@@ -1130,6 +1234,31 @@ int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, 
     const size_t n4 = (size_t)T * N / 4;
     const int blocks = (int)((n4 + 255) / 256 < 1184 ? (n4 + 255) / 256 : 1184);
     INFERNT_CUDA_TRY(launch_pdl(tp_sum_splits, dim3(blocks), dim3(256), st, part, splits, T, N, y));
+    return INFERNT_OK;
+}
+
+int bt_epoch_advance_launch(unsigned* epoch, cudaStream_t st) {
+    INFERNT_CUDA_TRY(launch_pdl(bt_epoch_advance, dim3(1), dim3(1), st, epoch));
+    return INFERNT_OK;
+}
+
+int tp_push_launch(const float* part, int splits, int T, int N, unsigned long long* const* peers, int rank, int world,
+                   const unsigned* epoch, int per_step, int idx, cudaStream_t st) {
+    INFERNT_REQUIRE(N % 4 == 0 && splits >= 1 && splits <= kMaxSplits && world >= 1,
+                    "tensor-parallel push: N %d, splits %d", N, splits);
+    const size_t n4 = (size_t)T * N / 4;
+    const int blocks = (int)((n4 + 255) / 256 < 1184 ? (n4 + 255) / 256 : 1184);
+    INFERNT_CUDA_TRY(launch_pdl(tp_push, dim3(blocks), dim3(256), st, part, splits, T, N, peers, rank, world, epoch,
+                                per_step, idx));
+    return INFERNT_OK;
+}
+
+int bt_resid_norm_tp_launch(const unsigned long long* own, int world, int T, int H, float* h, const float* norm_w,
+                            float eps, uint16_t* xb, const unsigned* epoch, int per_step, int idx, unsigned* err,
+                            long long budget, cudaStream_t st) {
+    INFERNT_REQUIRE(H % 4 == 0 && H / 4 <= 1024, "tensor-parallel residual: H %d", H);
+    INFERNT_CUDA_TRY(launch_pdl(bt_resid_norm_tp, dim3(T), dim3(H / 4), st, own, world, T, H, h, norm_w, eps, xb,
+                                epoch, per_step, idx, err, budget));
     return INFERNT_OK;
 }
 

@@ -56,6 +56,12 @@ int pf_qkv_rope_launch(const float* y, int C, int p0, int nq, int nkv, int D, co
 int pf_attention_launch(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, int C, int p0, int nq, int nkv,
                         int D, int max_seq, uint16_t* attn, unsigned* err, int tensor_cores, cudaStream_t st);
 int tp_sum_splits_launch(const float* part, int splits, int T, int N, float* y, cudaStream_t st);
+int bt_epoch_advance_launch(unsigned* epoch, cudaStream_t st);
+int tp_push_launch(const float* part, int splits, int T, int N, unsigned long long* const* peers, int rank, int world,
+                   const unsigned* epoch, int per_step, int idx, cudaStream_t st);
+int bt_resid_norm_tp_launch(const unsigned long long* own, int world, int T, int H, float* h, const float* norm_w,
+                            float eps, uint16_t* xb, const unsigned* epoch, int per_step, int idx, unsigned* err,
+                            long long budget, cudaStream_t st);
 int tp_argmax_local_launch(const float* logits, int T, int ld, int vl, int v0, int2* cand, const int* positions,
                            float inv_t, uint64_t seed, cudaStream_t st);
 int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, int* positions, cudaStream_t st);
@@ -166,6 +172,18 @@ struct infernt_batch_engine {
     float* ysum = nullptr;
     int2* cand = nullptr;
     int2* cand_all = nullptr;
+    // the sums after O and down cross the ranks by the peer-memory exchange
+    // (tp_peer, the default: tp_push into every rank's region over NVLink,
+    // bt_resid_norm_tp adds them) or by ncclAllReduce (the baseline).  xch:
+    // this rank's region [2][world][T][H] tagged words; peer_tab [world]:
+    // every rank's region mapped here (CUDA IPC); epoch: step counter of the
+    // exchange tags
+    bool tp_peer = true;
+    unsigned long long* xch = nullptr;
+    unsigned long long** peer_tab = nullptr;
+    std::vector<void*> opened;
+    unsigned* epoch = nullptr;
+    long long wait_cycles = 4000000000ll;  // about 2 s at the maximum SM clock
     // token choice: greedy (sample_inv_t = 0) or temperature sampling by
     // Gumbel-max inside the argmax kernels, keyed by (sample_seed, position)
     float sample_inv_t = 0.0f;
@@ -173,8 +191,9 @@ struct infernt_batch_engine {
 
     ~infernt_batch_engine() {
         if (graph) cudaGraphExecDestroy(graph);  // before the communicator its NCCL nodes use
+        if (stream) cudaStreamSynchronize(stream);
+        for (void* p : opened) cudaIpcCloseMemHandle(p);
         if (comm) {
-            if (stream) cudaStreamSynchronize(stream);
             if (const NcclApi* n = nccl_api()) n->destroy(static_cast<ncclComm_t>(comm));
         }
         cudaFree(hist);
@@ -328,6 +347,12 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
     if (int s = alloc(e, sizeof(float) * T * 8, reinterpret_cast<void**>(&e->cand_v))) return s;
     if (int s = alloc(e, sizeof(int) * T * 8, reinterpret_cast<void**>(&e->cand_i))) return s;
     if (e->world > 1) {
+        const size_t xb_bytes = sizeof(unsigned long long) * 2 * (size_t)e->world * T * H;
+        if (int s = alloc(e, xb_bytes, reinterpret_cast<void**>(&e->xch))) return s;
+        INFERNT_CUDA_TRY(cudaMemsetAsync(e->xch, 0, xb_bytes, e->stream));
+        if (int s = alloc(e, 256, reinterpret_cast<void**>(&e->epoch))) return s;
+        INFERNT_CUDA_TRY(cudaMemsetAsync(e->epoch, 0, 256, e->stream));
+        if (int s = alloc(e, sizeof(void*) * (size_t)e->world, reinterpret_cast<void**>(&e->peer_tab))) return s;
         if (int s = alloc(e, sizeof(float) * (size_t)T * H, reinterpret_cast<void**>(&e->ysum))) return s;
         if (int s = alloc(e, sizeof(int2) * (size_t)T, reinterpret_cast<void**>(&e->cand))) return s;
         if (int s = alloc(e, sizeof(int2) * (size_t)T * e->world, reinterpret_cast<void**>(&e->cand_all))) return s;
@@ -349,13 +374,21 @@ int all_reduce(infernt_batch_engine* e, float* y, cudaStream_t st) {
     return r == ncclSuccess ? INFERNT_OK : fail(INFERNT_ERR_CUDA, "ncclAllReduce: %s", n->err_str(r));
 }
 
-// Residual add + RMSNorm of an O or down projection: its split partials
-// summed in order (one rank), or summed per rank and then over the ranks.
-int resid_norm(infernt_batch_engine* e, int splits, const float* norm_w, cudaStream_t st) {
+// Residual add + RMSNorm of an O or down projection (the step's idx-th
+// exchange): its split partials summed in order (one rank), or summed per
+// rank and then over the ranks (peer-memory exchange, or NCCL).
+int resid_norm(infernt_batch_engine* e, int splits, const float* norm_w, int idx, cudaStream_t st) {
     const infernt_llama_config& c = e->cfg;
     const int H = c.hidden_size, T = e->T;
     using namespace infernt;
     if (e->world == 1) return bt_resid_norm_launch(e->part, splits, T, H, e->h, norm_w, c.rms_norm_eps, e->xb, st);
+    if (e->tp_peer) {
+        const int per_step = 2 * c.num_layers;
+        if (int s = tp_push_launch(e->part, splits, T, H, e->peer_tab, e->rank, e->world, e->epoch, per_step, idx, st))
+            return s;
+        return bt_resid_norm_tp_launch(e->xch, e->world, T, H, e->h, norm_w, c.rms_norm_eps, e->xb, e->epoch, per_step,
+                                       idx, e->err, e->wait_cycles, st);
+    }
     if (int s = tp_sum_splits_launch(e->part, splits, T, H, e->ysum, st)) return s;
     if (int s = all_reduce(e, e->ysum, st)) return s;
     return bt_resid_norm_launch(e->ysum, 1, T, H, e->h, norm_w, c.rms_norm_eps, e->xb, st);
@@ -369,6 +402,8 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
     const int qsl = nq * D, nqkv = qsl + 2 * nkv * D;
     const float eps = c.rms_norm_eps;
     using namespace infernt;
+    if (e->world > 1 && e->tp_peer)
+        if (int s = bt_epoch_advance_launch(e->epoch, st)) return s;
     if (int s = bt_embed_norm_launch(e->emb, e->tokens, V, T, H, e->layers[0].attn_norm, eps, e->h, e->xb, e->err, st))
         return s;
     for (int l = 0; l < L; ++l) {
@@ -389,12 +424,12 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
                 return s;
         }
         if (int s = bgemm_launch(ly.o, H, qsl, e->attn, T, e->part, e->sp_o, e->err, st)) return s;
-        if (int s = resid_norm(e, e->sp_o, ly.ffn_norm, st)) return s;
+        if (int s = resid_norm(e, e->sp_o, ly.ffn_norm, 2 * l, st)) return s;
         if (int s = bgemm_launch(ly.gu, 2 * il, H, e->xb, T, e->part, e->sp_gu, e->err, st)) return s;
         if (int s = bt_swiglu_launch(e->part, e->sp_gu, T, il, e->act, st)) return s;
         if (int s = bgemm_launch(ly.down, H, il, e->act, T, e->part, e->sp_down, e->err, st)) return s;
         const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
-        if (int s = resid_norm(e, e->sp_down, next_norm, st)) return s;
+        if (int s = resid_norm(e, e->sp_down, next_norm, 2 * l + 1, st)) return s;
     }
     if (int s = bgemm_launch(e->lm, e->vlp, H, e->xb, T, e->part, e->sp_lm, e->err, st)) return s;
     // the LM head runs unsplit: part[0] holds the logits [T][vlp]
@@ -429,6 +464,36 @@ int ensure_graph(infernt_batch_engine* e) {
     const cudaError_t ie = cudaGraphInstantiate(&e->graph, g, 0);
     cudaGraphDestroy(g);
     INFERNT_CUDA_TRY(ie);
+    return INFERNT_OK;
+}
+
+// Every rank's exchange region mapped into this process: the CUDA IPC
+// handles gathered over the ranks' NCCL communicator at creation.
+int map_peers(infernt_batch_engine* e, const NcclApi* nccl) {
+    const int W = e->world;
+    cudaIpcMemHandle_t h;
+    INFERNT_CUDA_TRY(cudaIpcGetMemHandle(&h, e->xch));
+    char* d_h = nullptr;
+    if (int s = alloc(e, sizeof(h) * (size_t)(W + 1), reinterpret_cast<void**>(&d_h))) return s;
+    INFERNT_CUDA_TRY(cudaMemcpy(d_h, &h, sizeof(h), cudaMemcpyHostToDevice));
+    const ncclResult_t r = nccl->all_gather(d_h, d_h + sizeof(h), sizeof(h), ncclUint8,
+                                            static_cast<ncclComm_t>(e->comm), e->stream);
+    if (r != ncclSuccess) return fail(INFERNT_ERR_CUDA, "ncclAllGather (exchange handles): %s", nccl->err_str(r));
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    std::vector<cudaIpcMemHandle_t> all(W);
+    INFERNT_CUDA_TRY(cudaMemcpy(all.data(), d_h + sizeof(h), sizeof(h) * (size_t)W, cudaMemcpyDeviceToHost));
+    std::vector<unsigned long long*> tab(W, nullptr);
+    for (int q = 0; q < W; ++q) {
+        if (q == e->rank) {
+            tab[q] = e->xch;
+            continue;
+        }
+        void* ptr = nullptr;
+        INFERNT_CUDA_TRY(cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess));
+        e->opened.push_back(ptr);
+        tab[q] = static_cast<unsigned long long*>(ptr);
+    }
+    INFERNT_CUDA_TRY(cudaMemcpy(e->peer_tab, tab.data(), sizeof(void*) * (size_t)W, cudaMemcpyHostToDevice));
     return INFERNT_OK;
 }
 
@@ -614,6 +679,7 @@ int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, u
             s = fail(INFERNT_ERR_CUDA, "ncclCommInitRank (rank %d of %d): %s", rank, world, nccl->err_str(r));
         else
             e->comm = comm;
+        if (!s) s = map_peers(e, nccl);
     }
     if (s) {
         delete e;
@@ -815,6 +881,19 @@ int infernt_batch_engine_set_sampling(infernt_batch_engine* e, float temperature
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
     e->sample_inv_t = temperature > 0.0f ? 1.0f / temperature : 0.0f;
     e->sample_seed = seed;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;  // captured again at the next step
+    }
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_set_tp_exchange(infernt_batch_engine* e, int mode) {
+    INFERNT_REQUIRE(e, "batch_engine_set_tp_exchange: null engine");
+    INFERNT_REQUIRE(mode == INFERNT_TP_EXCHANGE_PEER || mode == INFERNT_TP_EXCHANGE_NCCL,
+                    "batch_engine_set_tp_exchange: mode %d", mode);
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    e->tp_peer = mode == INFERNT_TP_EXCHANGE_PEER;
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;  // captured again at the next step

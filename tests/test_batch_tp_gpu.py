@@ -10,7 +10,9 @@ variant (test_batch_gpu.py): every (step, sequence) within 1e-2 of the
 largest |logit|, tokens identical unless the oracle's top-2 gap is below
 twice the error.  The shapes cover both head dims and a vocabulary whose
 rank slices need zero-padded LM-head rows (1152 over 2 ranks: 576 rows,
-padded to 640)."""
+padded to 640).  The ranks' O and down sums cross by the peer-memory
+exchange (the default; every rank adds them in rank order) and by
+ncclAllReduce (the baseline); both are held to the same tolerance."""
 import os
 import socket
 
@@ -36,7 +38,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, cfg, out):
+def _rank(rank, world, port, cfg, out, peer=True):
     import datetime
     import torch
     import torch.distributed as dist
@@ -48,6 +50,8 @@ def _rank(rank, world, port, cfg, out):
         dist.broadcast_object_list(obj, src=0)
         T = len(N_POS)
         eng = ib.BatchEngine(cfg, T, seed=SEED, rank=rank, world=world, nccl_id=obj[0])
+        if world > 1:
+            eng.set_tp_exchange(peer)
         for b, p in enumerate(N_POS):
             eng.fill_kv(b, 100 + b, p)
         tokens = [int(t) for t in O.prompt(T, SEED, 3, cfg.vocab_size)]
@@ -65,13 +69,13 @@ def _rank(rank, world, port, cfg, out):
         dist.destroy_process_group()
 
 
-def run_tp(cfg, world):
+def run_tp(cfg, world, peer=True):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         out = mgr.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_rank, args=(r, world, port, cfg, out)) for r in range(world)]
+        procs = [ctx.Process(target=_rank, args=(r, world, port, cfg, out, peer)) for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
@@ -86,8 +90,8 @@ def top2_gap(x):
     return float(s[-1] - s[-2])
 
 
-def check_against_oracle(cfg, world):
-    res = run_tp(cfg, world)
+def check_against_oracle(cfg, world, peer=True):
+    res = run_tp(cfg, world, peer)
     toks = [res[r][0] for r in range(world)]
     assert all(t == toks[0] for t in toks), "ranks disagree on the greedy tokens"
     ranges = [res[r][2] for r in range(world)]
@@ -127,8 +131,9 @@ def test_batch_tp1_matches_oracle():
 
 
 @pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
-def test_batch_tp2_matches_oracle():
-    check_against_oracle(CFG, 2)
+@pytest.mark.parametrize("peer", [True, False], ids=["peer-exchange", "nccl"])
+def test_batch_tp2_matches_oracle(peer):
+    check_against_oracle(CFG, 2, peer)
 
 
 @pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
