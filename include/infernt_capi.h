@@ -408,6 +408,127 @@ INFERNT_API int infernt_batch_engine_splits(infernt_batch_engine* e, int* out);
 INFERNT_API int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int min_chunk,
                                                    int stages);
 
+/* ------------------------------------------ paged KV, continuous batching ---
+ * Not in the reference (its README lists paged KV and continuous batching as
+ * future work; it keeps one KVCache [N_kv, max_seq, D] per layer for one
+ * sequence, include/kv_cache.h:7-15).
+ *
+ * A batched engine whose caches are pools of pages: per layer K and V pools
+ * [num_pages][N_kv][page_size][head_dim] bf16, and a block table [batch]
+ * [max_pages] (max_pages = ceil(max_seq_len / page_size)): position p of
+ * sequence t lives in page table[t][p / page_size] at row p % page_size.
+ * Slots whose position is -1 in a step are empty (not read, not written,
+ * their position stays -1).  Everything else as infernt_batch_engine_create_
+ * seeded, with query groups of at most 8 heads.  Prefill runs on contiguous
+ * staging caches ([N_kv][max_seq_len][head_dim] per layer, allocated by the
+ * first prefill) and copies the written rows into the pages. */
+INFERNT_API int infernt_batch_engine_create_paged(const infernt_llama_config* cfg, int batch, int page_size,
+                                                  int num_pages, uint64_t seed, float std_dev,
+                                                  int attn_splits, infernt_batch_engine** out);
+/* Pages of sequence seq: pages[0, n_pages) for its positions [0, n_pages x
+ * page_size); the rest of its row is cleared.  Each in [0, num_pages); the
+ * caller keeps live sequences' pages disjoint.  A step, prefill or fill_kv
+ * needs pages for every position it touches (checked on the host). */
+INFERNT_API int infernt_batch_engine_set_pages(infernt_batch_engine* e, int seq, const int* pages,
+                                               int n_pages);
+/* page_size, num_pages and max_pages per sequence (all 0: contiguous). */
+INFERNT_API int infernt_batch_engine_paging(infernt_batch_engine* e, int* page_size, int* num_pages,
+                                            int* max_pages);
+/* Per-sequence sampling salts (`batch` values, e.g. request ids; NULL: none):
+ * temperature draws of sequence t are keyed by (infernt_stream_key(seed,
+ * salts[t]), position), so sequences at one position draw independently. */
+INFERNT_API int infernt_batch_engine_set_salts(infernt_batch_engine* e, const uint64_t* salts);
+
+/* Iteration-level scheduler over `slots` sequence slots and a pool of
+ * num_pages pages of page_size positions (host logic, no GPU).  Requests
+ * (prompt, max_new_tokens, eos) queue first-come first-served; a request is
+ * admitted when a slot is free and the pool holds pages for its known tokens
+ * plus the next position; each admitted request is prefilled once, then
+ * takes one position per step in the batched decode beside the others.  A
+ * running request that needs a page when the pool is empty preempts the
+ * most recently admitted request (its pages are freed; it goes back to the
+ * head of the queue and is prefilled again later with its prompt and the
+ * tokens generated so far: recomputation).  A request finishes after
+ * max_new_tokens tokens, or at the eos token (included). */
+typedef struct infernt_scheduler infernt_scheduler;
+typedef struct infernt_sched_plan {
+    int n_prefill;              /* requests to prefill this step */
+    const int* prefill_slot;    /* [n_prefill] their slots */
+    const int* prefill_offset;  /* [n_prefill] start of each one's tokens in prefill_tokens */
+    const int* prefill_len;     /* [n_prefill] tokens to prefill (positions [0, len)) */
+    const int* prefill_tokens;
+    int n_decode;               /* slots in this step's batched decode */
+    const int* tokens;          /* [slots] token per slot (0 where empty) */
+    const int* positions;       /* [slots] position per slot, -1: not decoding this step */
+    int n_changed;              /* slots whose pages changed since the last plan */
+    const int* changed_slot;    /* [n_changed] */
+    const int* pages;           /* [slots][max_pages] page table, -1 past a slot's pages */
+    const int* n_pages;         /* [slots] pages per slot */
+    int max_pages;
+    int n_preempted;            /* requests this plan preempted */
+} infernt_sched_plan;
+typedef struct infernt_sched_stats {
+    int waiting, running, finished, free_pages;
+    long long steps, preemptions, prefill_tokens, decode_tokens;
+} infernt_sched_stats;
+enum {
+    INFERNT_REQUEST_WAITING = 0,
+    INFERNT_REQUEST_RUNNING = 1,
+    INFERNT_REQUEST_FINISHED = 2,
+    INFERNT_REQUEST_CANCELLED = 3
+};
+INFERNT_API int infernt_scheduler_create(int slots, int page_size, int num_pages, int max_seq_len,
+                                         infernt_scheduler** out);
+INFERNT_API int infernt_scheduler_destroy(infernt_scheduler* s);
+/* Queue a request: prompt[0, n) with 1 <= n, max_new_tokens >= 1, n +
+ * max_new_tokens <= max_seq_len and pages for them within the pool; eos < 0
+ * for none.  *id: the request's id (increasing from 1). */
+INFERNT_API int infernt_scheduler_submit(infernt_scheduler* s, const int* prompt, int n, int max_new_tokens,
+                                         int eos, int64_t* id);
+/* Drop a waiting or running request (its pages and slot are freed). */
+INFERNT_API int infernt_scheduler_cancel(infernt_scheduler* s, int64_t id);
+/* The next step's work: preemptions, page growth and admissions applied.
+ * The arrays stay valid until the next plan or commit. */
+INFERNT_API int infernt_scheduler_plan(infernt_scheduler* s, infernt_sched_plan* plan);
+/* The step's results: prefill_next [n_prefill] the token after each prefill,
+ * decode_next [slots] the token after each decoding slot (others ignored). */
+INFERNT_API int infernt_scheduler_commit(infernt_scheduler* s, const int* prefill_next, const int* decode_next);
+/* Request id: *state (INFERNT_REQUEST_*), *n generated tokens so far, the
+ * first min(cap, *n) of them into tokens (may be NULL when cap is 0),
+ * *preemptions how often it was preempted (or NULL). */
+INFERNT_API int infernt_scheduler_result(infernt_scheduler* s, int64_t id, int* tokens, int cap, int* n,
+                                         int* state, int* preemptions);
+/* Forget a finished or cancelled request's record. */
+INFERNT_API int infernt_scheduler_release(infernt_scheduler* s, int64_t id);
+INFERNT_API int infernt_scheduler_stats(infernt_scheduler* s, infernt_sched_stats* out);
+
+/* Continuous-batching server: the scheduler above driving a paged batched
+ * engine of `slots` sequences (seeded weights as infernt_batch_engine_create_
+ * paged).  A step: the plan's page tables into the engine, each admitted
+ * request's prefill, one batched decode step of the running requests, the
+ * results into the scheduler. */
+typedef struct infernt_server infernt_server;
+INFERNT_API int infernt_server_create_seeded(const infernt_llama_config* cfg, int slots, int page_size,
+                                             int num_pages, uint64_t seed, float std_dev,
+                                             infernt_server** out);
+INFERNT_API int infernt_server_destroy(infernt_server* srv);
+INFERNT_API int infernt_server_submit(infernt_server* srv, const int* prompt, int n, int max_new_tokens,
+                                      int eos, int64_t* id);
+/* One step; *n_finished (or NULL) the requests it finished. */
+INFERNT_API int infernt_server_step(infernt_server* srv, int* n_finished);
+/* Steps until no request waits or runs; *ms (or NULL) the host time. */
+INFERNT_API int infernt_server_run(infernt_server* srv, double* ms);
+INFERNT_API int infernt_server_result(infernt_server* srv, int64_t id, int* tokens, int cap, int* n, int* state,
+                                      int* preemptions);
+INFERNT_API int infernt_server_stats(infernt_server* srv, infernt_sched_stats* out);
+/* Temperature sampling of the following steps (0: greedy), keyed per
+ * request: draws of request r at position p use (infernt_stream_key(seed,
+ * r), p). */
+INFERNT_API int infernt_server_set_sampling(infernt_server* srv, float temperature, uint64_t seed);
+/* The server's engine (logits of the last decode step, attention settings);
+ * owned by the server. */
+INFERNT_API int infernt_server_engine(infernt_server* srv, infernt_batch_engine** out);
+
 /* Attention of T decoding sequences over bf16 caches (the batched engine's
  * kernels; cuda/attention.cu:9-42 per sequence and query head): q [T][nq][D]
  * FP32 (RoPE applied), caches [T][nkv][max_seq][D] bf16, sequence t

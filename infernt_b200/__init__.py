@@ -160,6 +160,28 @@ _SIGS = {
     "infernt_checkpoint_weights": (_I, [_P, ctypes.POINTER(_P), _I]),
     "infernt_checkpoint_free": (_I, [_P]),
     "infernt_batch_engine_read_kv": (_I, [_P, _I, _I, _I, _P, _P]),
+    "infernt_batch_engine_create_paged": (_I, [_P, _I, _I, _I, _U64, _F, _I, _P]),
+    "infernt_batch_engine_set_pages": (_I, [_P, _I, _P, _I]),
+    "infernt_batch_engine_paging": (_I, [_P, _P, _P, _P]),
+    "infernt_batch_engine_set_salts": (_I, [_P, _P]),
+    "infernt_scheduler_create": (_I, [_I, _I, _I, _I, _P]),
+    "infernt_scheduler_destroy": (_I, [_P]),
+    "infernt_scheduler_submit": (_I, [_P, _P, _I, _I, _I, _P]),
+    "infernt_scheduler_cancel": (_I, [_P, ctypes.c_int64]),
+    "infernt_scheduler_plan": (_I, [_P, _P]),
+    "infernt_scheduler_commit": (_I, [_P, _P, _P]),
+    "infernt_scheduler_result": (_I, [_P, ctypes.c_int64, _P, _I, _P, _P, _P]),
+    "infernt_scheduler_release": (_I, [_P, ctypes.c_int64]),
+    "infernt_scheduler_stats": (_I, [_P, _P]),
+    "infernt_server_create_seeded": (_I, [_P, _I, _I, _I, _U64, _F, _P]),
+    "infernt_server_destroy": (_I, [_P]),
+    "infernt_server_submit": (_I, [_P, _P, _I, _I, _I, _P]),
+    "infernt_server_step": (_I, [_P, _P]),
+    "infernt_server_run": (_I, [_P, _P]),
+    "infernt_server_result": (_I, [_P, ctypes.c_int64, _P, _I, _P, _P, _P]),
+    "infernt_server_stats": (_I, [_P, _P]),
+    "infernt_server_set_sampling": (_I, [_P, _F, _U64]),
+    "infernt_server_engine": (_I, [_P, _P]),
     "infernt_pgemm_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_pgemm_swiglu_bf16": (_I, [_P, _I, _I, _P, _I, _P, _I, _P, _P]),
     "infernt_prefill_attention": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _P, _I, _P]),
@@ -391,28 +413,39 @@ class BatchEngine:
     (infernt_batch_engine_*): seeded bf16 weights, bf16 KV caches."""
 
     def __init__(self, cfg: ModelConfig, batch: int, seed: int = 0, std: float = 0.02, attn_splits: int = 0,
-                 rank: int = 0, world: int = 1, nccl_id: bytes = None):
+                 rank: int = 0, world: int = 1, nccl_id: bytes = None, pages=None, _handle=None):
         """world > 1: one rank of a tensor-parallel engine
         (infernt_batch_engine_create_tp); every rank passes the same nccl_id
         (nccl_unique_id() on one rank) and all ranks call every method in the
-        same order."""
+        same order.  pages=(page_size, num_pages): paged KV caches
+        (infernt_batch_engine_create_paged; set_pages gives each sequence its
+        pages)."""
         self.cfg = cfg
         self.T = batch
         self._c = cfg.c()
-        h = ctypes.c_void_p()
-        idbuf = None
-        if nccl_id is not None:
-            idbuf = ctypes.create_string_buffer(bytes(nccl_id), len(nccl_id))
-        call("infernt_batch_engine_create_tp", ctypes.byref(self._c), batch, seed, std, attn_splits, rank, world,
-             idbuf, ctypes.byref(h))
-        self._h = h
+        self._owned = _handle is None
+        if _handle is not None:
+            self._h = _handle
+        else:
+            h = ctypes.c_void_p()
+            if pages is not None:
+                call("infernt_batch_engine_create_paged", ctypes.byref(self._c), batch, pages[0], pages[1], seed,
+                     std, attn_splits, ctypes.byref(h))
+            else:
+                idbuf = None
+                if nccl_id is not None:
+                    idbuf = ctypes.create_string_buffer(bytes(nccl_id), len(nccl_id))
+                call("infernt_batch_engine_create_tp", ctypes.byref(self._c), batch, seed, std, attn_splits, rank,
+                     world, idbuf, ctypes.byref(h))
+            self._h = h
         v0, vl = ctypes.c_int(), ctypes.c_int()
         call("infernt_batch_engine_vocab_range", self._h, ctypes.byref(v0), ctypes.byref(vl))
         self.vocab_range = (v0.value, v0.value + vl.value)
 
     def close(self):
         if self._h:
-            lib().infernt_batch_engine_destroy(self._h)
+            if self._owned:
+                lib().infernt_batch_engine_destroy(self._h)
             self._h = None
 
     def __del__(self):
@@ -420,6 +453,25 @@ class BatchEngine:
             self.close()
         except Exception:
             pass
+
+    def set_pages(self, seq: int, pages):
+        """Pages of sequence `seq` for its positions [0, len(pages) x page_size)."""
+        arr = (ctypes.c_int * max(1, len(pages)))(*[int(p) for p in pages])
+        call("infernt_batch_engine_set_pages", self._h, seq, arr, len(pages))
+
+    def paging(self):
+        """(page_size, num_pages, max_pages per sequence); zeros when contiguous."""
+        a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        call("infernt_batch_engine_paging", self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return a.value, b.value, c.value
+
+    def set_salts(self, salts):
+        """Per-sequence sampling salts (None: none)."""
+        if salts is None:
+            call("infernt_batch_engine_set_salts", self._h, None)
+            return
+        arr = (ctypes.c_uint64 * self.T)(*[int(x) for x in salts])
+        call("infernt_batch_engine_set_salts", self._h, arr)
 
     def fill_kv(self, seq: int, seed: int, n_pos: int, std: float = 1.0):
         call("infernt_batch_engine_fill_kv", self._h, seq, seed, n_pos, std)
@@ -491,6 +543,164 @@ class BatchEngine:
         """KV splits per (sequence, KV head), least positions per split and
         copy stages per warp of the attention; results do not change."""
         call("infernt_batch_engine_set_attention", self._h, splits, min_chunk, stages)
+
+
+class SchedPlan(ctypes.Structure):
+    """``infernt_sched_plan`` (include/infernt_capi.h)."""
+    _fields_ = [("n_prefill", ctypes.c_int), ("prefill_slot", ctypes.POINTER(ctypes.c_int)),
+                ("prefill_offset", ctypes.POINTER(ctypes.c_int)), ("prefill_len", ctypes.POINTER(ctypes.c_int)),
+                ("prefill_tokens", ctypes.POINTER(ctypes.c_int)), ("n_decode", ctypes.c_int),
+                ("tokens", ctypes.POINTER(ctypes.c_int)), ("positions", ctypes.POINTER(ctypes.c_int)),
+                ("n_changed", ctypes.c_int), ("changed_slot", ctypes.POINTER(ctypes.c_int)),
+                ("pages", ctypes.POINTER(ctypes.c_int)), ("n_pages", ctypes.POINTER(ctypes.c_int)),
+                ("max_pages", ctypes.c_int), ("n_preempted", ctypes.c_int)]
+
+
+class SchedStats(ctypes.Structure):
+    """``infernt_sched_stats`` (include/infernt_capi.h)."""
+    _fields_ = [("waiting", ctypes.c_int), ("running", ctypes.c_int), ("finished", ctypes.c_int),
+                ("free_pages", ctypes.c_int), ("steps", ctypes.c_longlong), ("preemptions", ctypes.c_longlong),
+                ("prefill_tokens", ctypes.c_longlong), ("decode_tokens", ctypes.c_longlong)]
+
+    def as_dict(self):
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+REQUEST_STATES = {0: "waiting", 1: "running", 2: "finished", 3: "cancelled"}
+
+
+def _request_result(fn, handle, rid):
+    n, state, pre = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    call(fn, handle, rid, None, 0, ctypes.byref(n), ctypes.byref(state), ctypes.byref(pre))
+    buf = (ctypes.c_int * max(1, n.value))()
+    call(fn, handle, rid, buf, n.value, ctypes.byref(n), ctypes.byref(state), ctypes.byref(pre))
+    return list(buf[:n.value]), REQUEST_STATES[state.value], pre.value
+
+
+class Scheduler:
+    """Iteration-level scheduler over paged KV (infernt_scheduler_*; host
+    logic only): plan() gives a step's prefills, decode inputs and page
+    tables, commit() takes the step's tokens."""
+
+    def __init__(self, slots: int, page_size: int, num_pages: int, max_seq_len: int):
+        h = ctypes.c_void_p()
+        call("infernt_scheduler_create", slots, page_size, num_pages, max_seq_len, ctypes.byref(h))
+        self._h = h
+        self.slots = slots
+
+    def close(self):
+        if self._h:
+            lib().infernt_scheduler_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def submit(self, prompt, max_new_tokens: int, eos: int = -1) -> int:
+        arr = (ctypes.c_int * len(prompt))(*[int(t) for t in prompt])
+        rid = ctypes.c_int64()
+        call("infernt_scheduler_submit", self._h, arr, len(prompt), max_new_tokens, eos, ctypes.byref(rid))
+        return rid.value
+
+    def cancel(self, rid: int):
+        call("infernt_scheduler_cancel", self._h, rid)
+
+    def plan(self):
+        """The next step as a dict of Python lists."""
+        p = SchedPlan()
+        call("infernt_scheduler_plan", self._h, ctypes.byref(p))
+        S, mp = self.slots, p.max_pages
+        ntok = sum(p.prefill_len[i] for i in range(p.n_prefill))
+        return {
+            "prefill": [(p.prefill_slot[i],
+                         [p.prefill_tokens[p.prefill_offset[i] + j] for j in range(p.prefill_len[i])])
+                        for i in range(p.n_prefill)],
+            "prefill_tokens": ntok,
+            "n_decode": p.n_decode,
+            "tokens": [p.tokens[i] for i in range(S)],
+            "positions": [p.positions[i] for i in range(S)],
+            "changed": [p.changed_slot[i] for i in range(p.n_changed)],
+            "pages": [[p.pages[i * mp + j] for j in range(p.n_pages[i])] for i in range(S)],
+            "max_pages": mp,
+            "n_preempted": p.n_preempted,
+        }
+
+    def commit(self, prefill_next, decode_next):
+        a = (ctypes.c_int * max(1, len(prefill_next)))(*[int(t) for t in prefill_next])
+        b = (ctypes.c_int * self.slots)(*[int(t) for t in decode_next])
+        call("infernt_scheduler_commit", self._h, a, b)
+
+    def result(self, rid: int):
+        """(generated tokens, state name, preemptions)."""
+        return _request_result("infernt_scheduler_result", self._h, rid)
+
+    def release(self, rid: int):
+        call("infernt_scheduler_release", self._h, rid)
+
+    def stats(self):
+        st = SchedStats()
+        call("infernt_scheduler_stats", self._h, ctypes.byref(st))
+        return st.as_dict()
+
+
+class Server:
+    """Continuous batching on a paged batched engine (infernt_server_*)."""
+
+    def __init__(self, cfg: ModelConfig, slots: int, page_size: int, num_pages: int, seed: int = 0,
+                 std: float = 0.02):
+        self.cfg = cfg
+        self._c = cfg.c()
+        h = ctypes.c_void_p()
+        call("infernt_server_create_seeded", ctypes.byref(self._c), slots, page_size, num_pages, seed, std,
+             ctypes.byref(h))
+        self._h = h
+        e = ctypes.c_void_p()
+        call("infernt_server_engine", self._h, ctypes.byref(e))
+        self.engine = BatchEngine(cfg, slots, _handle=e)
+        self.slots = slots
+
+    def close(self):
+        if self._h:
+            self.engine.close()
+            lib().infernt_server_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def submit(self, prompt, max_new_tokens: int, eos: int = -1) -> int:
+        arr = (ctypes.c_int * len(prompt))(*[int(t) for t in prompt])
+        rid = ctypes.c_int64()
+        call("infernt_server_submit", self._h, arr, len(prompt), max_new_tokens, eos, ctypes.byref(rid))
+        return rid.value
+
+    def step(self) -> int:
+        n = ctypes.c_int()
+        call("infernt_server_step", self._h, ctypes.byref(n))
+        return n.value
+
+    def run(self) -> float:
+        """Steps until every request finished; host milliseconds."""
+        ms = ctypes.c_double()
+        call("infernt_server_run", self._h, ctypes.byref(ms))
+        return ms.value
+
+    def result(self, rid: int):
+        return _request_result("infernt_server_result", self._h, rid)
+
+    def stats(self):
+        st = SchedStats()
+        call("infernt_server_stats", self._h, ctypes.byref(st))
+        return st.as_dict()
+
+    def set_sampling(self, temperature: float, seed: int = 0):
+        call("infernt_server_set_sampling", self._h, temperature, seed)
 
 
 class Checkpoint:

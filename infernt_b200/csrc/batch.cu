@@ -397,7 +397,22 @@ struct BtAttnArgs {
     float* attn_f32;
     unsigned* err;
     unsigned* tickets;  // [T][nkv] zeros, or NULL (S > 1: a separate merge launch)
+    // paged caches (block_table set): kc / vc are pools of pages
+    // [page][nkv][page_size][D]; position p of sequence t lives in page
+    // block_table[t][p / page_size] at row p % page_size.  A sequence at
+    // position -1 is an empty slot: skipped without an error.
+    const int* block_table;
+    int page_size, max_pages;
 };
+
+// Address of cache row p of (sequence t, KV head kvh): contiguous
+// [T][nkv][max_seq][D], or its page (paged caches).
+template <int D>
+__device__ __forceinline__ size_t bt_row_off(const BtAttnArgs& a, int t, int kvh, int p) {
+    if (!a.block_table) return (((size_t)t * a.nkv + kvh) * a.max_seq + p) * D;
+    const int page = a.block_table[(size_t)t * a.max_pages + p / a.page_size];
+    return (((size_t)page * a.nkv + kvh) * a.page_size + p % a.page_size) * D;
+}
 
 template <int D>
 constexpr int attn_extra_bytes() {
@@ -424,7 +439,7 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
     // copies may start before the projection this kernel depends on
     const int pos = a.positions[t];
     if (pos < 0 || pos >= max_seq) {
-        if (FUSED && tid == 0 && a.err) atomicOr(a.err, kErrPosition);
+        if (FUSED && tid == 0 && a.err && !(a.block_table && pos == -1)) atomicOr(a.err, kErrPosition);
         return;
     }
     const int seq = pos + 1;
@@ -434,10 +449,8 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
     const int c0 = split * chunk, c1 = min(seq, c0 + chunk);
     const bool own_row = FUSED && split == active - 1;  // this split holds position pos
     const int ntiles = (c1 - c0 + kAttnTile - 1) / kAttnTile;
-    uint16_t* kcache = a.kc + ((size_t)t * nkv + kvh) * max_seq * D;
-    uint16_t* vcache = a.vc + ((size_t)t * nkv + kvh) * max_seq * D;
-    const unsigned char* kb = reinterpret_cast<const unsigned char*>(kcache);
-    const unsigned char* vb = reinterpret_cast<const unsigned char*>(vcache);
+    const unsigned char* kb = reinterpret_cast<const unsigned char*>(a.kc);
+    const unsigned char* vb = reinterpret_cast<const unsigned char*>(a.vc);
     const uint32_t ring = smem_addr(att_smem) + (uint32_t)warp * NST * 2 * TILEB;
 
     // this warp's tile i of the split -> stage i % NST (K at +0, V at +TILEB)
@@ -450,7 +463,7 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
             for (int e = 0; e < kAttnTile * CH / 32; ++e) {
                 const int idx = e * 32 + lane, row = idx / CH, ch = idx % CH;
                 const bool ok = p0 + row < c1;
-                const size_t off = (size_t)(ok ? p0 + row : c0) * ROWB + (size_t)ch * 16;
+                const size_t off = bt_row_off<D>(a, t, kvh, ok ? p0 + row : c0) * 2 + (size_t)ch * 16;
                 const uint32_t dst = st + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4));
                 cp_async16(dst, kb + off, ok ? 16u : 0u);
                 cp_async16(dst + TILEB, vb + off, ok ? 16u : 0u);
@@ -511,7 +524,7 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
         if (own_row && tid < 2 * CH) {
             // the rows for later steps (16 bytes per thread)
             const uint16_t* src = tid < CH ? newk : newv;
-            uint16_t* dst = (tid < CH ? kcache : vcache) + (size_t)pos * D;
+            uint16_t* dst = (tid < CH ? a.kc : a.vc) + bt_row_off<D>(a, t, kvh, pos);
             const int c = tid % CH;
             *reinterpret_cast<uint4*>(dst + 8 * c) = *reinterpret_cast<const uint4*>(src + 8 * c);
         }
@@ -740,7 +753,7 @@ constexpr int kArgChunks = 8;
 
 __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int* tokens, int* positions, int* hist,
                                                  float* cand_v, int* cand_i, unsigned* tickets, float inv_t,
-                                                 uint64_t seed) {
+                                                 uint64_t seed, const uint64_t* salts) {
     pdl_wait();  // the previous kernel of the step has completed
     pdl_launch_dependents();
     __shared__ float bv[8];
@@ -751,9 +764,13 @@ __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int
     const float4* lt = reinterpret_cast<const float4*>(logits + (size_t)t * V);
     // temperature sampling (inv_t > 0): Gumbel scores keyed by (seed, the
     // sequence's position), so chained steps draw fresh noise without a host
-    // counter; every chunk reads the position before the last one advances it
+    // counter; every chunk reads the position before the last one advances it.
+    // With salts (a value per sequence, e.g. its request id) the key is
+    // (stream_key(seed, salt), position): sequences at one position draw
+    // independent noise
     const bool sample = inv_t > 0.0f;
-    const uint64_t key = sample ? infernt_stream_key(seed, (uint64_t)positions[t]) : 0;
+    const uint64_t base = salts ? infernt_stream_key(seed, salts[t]) : seed;
+    const uint64_t key = sample ? infernt_stream_key(base, (uint64_t)positions[t]) : 0;
     float v = -INFINITY;
     int id = 4 * c0;  // equal to the old single-pass start (index 0) once chunks combine in order
 #pragma unroll 4
@@ -809,23 +826,47 @@ __global__ void __launch_bounds__(256) bt_argmax(const float* logits, int V, int
     }
     tokens[t] = id;
     if (hist) hist[t] = id;
-    positions[t] += 1;
+    if (positions[t] >= 0) positions[t] += 1;  // an empty slot (position -1) stays empty
 }
 
 // Rows [0, n_pos) of sequence `seq`'s cache of one layer, [T][Nkv][max_seq][D]
 // bf16: element (layer, h0 + h, p, d) of the seeded KV stream of a model with
 // nkv_all KV heads (include/infernt_seed.h; h0 > 0 on a tensor-parallel rank
 // holding heads [h0, h0 + nkv)), the values infernt_fill_kv writes in FP32,
-// rounded to bf16.
+// rounded to bf16.  Paged caches (pages set): the pool [page][Nkv][P][D],
+// position p in page pages[p / P] at row p % P.
 __global__ void bt_fill_kv(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos,
-                           uint64_t key, float std_dev, int h0, int nkv_all) {
+                           uint64_t key, float std_dev, int h0, int nkv_all, const int* pages, int page_size) {
     const size_t n = (size_t)nkv * n_pos * D;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int d = (int)(i % D);
         const int p = (int)((i / D) % n_pos);
         const int h = (int)(i / ((size_t)D * n_pos));
         const uint64_t gi = ((((uint64_t)layer * nkv_all + h0 + h) << 20) + (uint64_t)p) * (uint64_t)D + d;
-        cache[(((size_t)seq * nkv + h) * max_seq + p) * D + d] = bf16_bits(infernt_normal_std(key, gi, std_dev));
+        const size_t row = pages ? ((size_t)pages[p / page_size] * nkv + h) * page_size + p % page_size
+                                 : ((size_t)seq * nkv + h) * max_seq + p;
+        cache[row * D + d] = bf16_bits(infernt_normal_std(key, gi, std_dev));
+    }
+}
+
+// Rows [p0, p1) of one sequence between a contiguous cache [Nkv][max_seq][D]
+// and its pages of a pool [page][Nkv][P][D] (to_pages: contiguous -> pages),
+// 16 bytes per thread and step.
+__global__ void bt_page_copy(uint16_t* pool, uint16_t* flat, const int* pages, int page_size, int nkv, int max_seq,
+                             int D, int p0, int p1, int to_pages) {
+    const int ch = D / 8;  // 16-byte chunks per row
+    const size_t n = (size_t)nkv * (p1 - p0) * ch;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % ch);
+        const int p = p0 + (int)((i / ch) % (p1 - p0));
+        const int h = (int)(i / ((size_t)ch * (p1 - p0)));
+        uint4* a = reinterpret_cast<uint4*>(flat + ((size_t)h * max_seq + p) * D) + c;
+        uint4* b = reinterpret_cast<uint4*>(
+                       pool + (((size_t)pages[p / page_size] * nkv + h) * page_size + p % page_size) * D) + c;
+        if (to_pages)
+            *b = *a;
+        else
+            *a = *b;
     }
 }
 
@@ -1190,8 +1231,11 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
 int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
                               const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
                               int stages, float* part, uint16_t* attn, unsigned* err, unsigned* tickets,
-                              cudaStream_t st) {
+                              cudaStream_t st, const int* block_table, int page_size, int max_pages) {
     const int G = nq / nkv;
+    INFERNT_REQUIRE(!block_table || (page_size >= 1 && (long long)page_size * max_pages >= max_seq),
+                    "fused batched attention: pages of %d positions, %d per sequence, max_seq %d", page_size,
+                    max_pages, max_seq);
     INFERNT_REQUIRE(G >= 1 && G <= 8 && nq % nkv == 0 && (D == 64 || D == 128),
                     "fused batched attention: group size %d, head_dim %d", G, D);
     INFERNT_REQUIRE(S >= 1 && min_chunk >= 1 && qkv_splits >= 1 && qkv_splits <= kMaxSplits,
@@ -1215,15 +1259,30 @@ int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float
     a.attn = attn;
     a.err = err;
     a.tickets = tickets;
+    a.block_table = block_table;
+    a.page_size = page_size;
+    a.max_pages = max_pages;
     if (int s = attn_mma_dispatch<true>(a, D, stages, st)) return s;
     INFERNT_CUDA_TRY(cudaGetLastError());
     return attn_merge(a, D, st);
 }
 
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
-                      float std_dev, int h0, int nkv_all, cudaStream_t st) {
+                      float std_dev, int h0, int nkv_all, cudaStream_t st, const int* pages, int page_size) {
     if (n_pos <= 0) return INFERNT_OK;
-    bt_fill_kv<<<256, 256, 0, st>>>(cache, seq, layer, nkv, max_seq, D, n_pos, key, std_dev, h0, nkv_all);
+    bt_fill_kv<<<256, 256, 0, st>>>(cache, seq, layer, nkv, max_seq, D, n_pos, key, std_dev, h0, nkv_all, pages,
+                                    page_size);
+    INFERNT_CUDA_TRY(cudaGetLastError());
+    return INFERNT_OK;
+}
+
+int bt_page_copy_launch(uint16_t* pool, uint16_t* flat, const int* pages, int page_size, int nkv, int max_seq, int D,
+                        int p0, int p1, bool to_pages, cudaStream_t st) {
+    INFERNT_REQUIRE(pool && flat && pages && page_size >= 1 && D % 8 == 0 && 0 <= p0 && p0 <= p1 && p1 <= max_seq,
+                    "page copy: rows [%d, %d) of %d, pages of %d", p0, p1, max_seq, page_size);
+    if (p0 == p1) return INFERNT_OK;
+    bt_page_copy<<<2 * sm_count(), 256, 0, st>>>(pool, flat, pages, page_size, nkv, max_seq, D, p0, p1,
+                                                 to_pages ? 1 : 0);
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }
@@ -1276,10 +1335,11 @@ int tp_argmax_pick_launch(const int2* cand_all, int world, int T, int* tokens, i
 }
 
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
-                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st) {
+                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st,
+                     const uint64_t* salts) {
     INFERNT_REQUIRE(V % 4 == 0 && V / 4 >= kArgChunks, "batched argmax: vocabulary %d", V);
     INFERNT_CUDA_TRY(launch_pdl(bt_argmax, dim3(kArgChunks, T), dim3(256), st, logits, V, tokens, positions, hist,
-                                cand_v, cand_i, tickets, inv_t, seed));
+                                cand_v, cand_i, tickets, inv_t, seed, salts));
     INFERNT_CUDA_TRY(cudaGetLastError());
     return INFERNT_OK;
 }

@@ -42,11 +42,14 @@ int bt_attention_launch(const float* q, const uint16_t* kc, const uint16_t* vc, 
 int bt_attention_fused_launch(const float* qkv_part, int qkv_splits, const float2* rope, uint16_t* kc, uint16_t* vc,
                               const int* positions, int T, int nq, int nkv, int D, int max_seq, int S, int min_chunk,
                               int stages, float* part, uint16_t* attn, unsigned* err, unsigned* tickets,
-                              cudaStream_t st);
+                              cudaStream_t st, const int* block_table, int page_size, int max_pages);
 int bt_fill_kv_launch(uint16_t* cache, int seq, int layer, int nkv, int max_seq, int D, int n_pos, uint64_t key,
-                      float std_dev, int h0, int nkv_all, cudaStream_t st);
+                      float std_dev, int h0, int nkv_all, cudaStream_t st, const int* pages, int page_size);
+int bt_page_copy_launch(uint16_t* pool, uint16_t* flat, const int* pages, int page_size, int nkv, int max_seq, int D,
+                        int p0, int p1, bool to_pages, cudaStream_t st);
 int bt_argmax_launch(const float* logits, int T, int V, int* tokens, int* positions, int* hist, float* cand_v,
-                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st);
+                     int* cand_i, unsigned* tickets, float inv_t, uint64_t seed, cudaStream_t st,
+                     const uint64_t* salts);
 int pgemm_launch(const void* W, int N, int K, const void* X, int T, float* Y, int ldy, unsigned* err,
                  cudaStream_t st);
 int pgemm_swiglu_launch(const void* W_gu, int I, int K, const void* X, int T, uint16_t* act, int ldy, unsigned* err,
@@ -188,6 +191,20 @@ struct infernt_batch_engine {
     // Gumbel-max inside the argmax kernels, keyed by (sample_seed, position)
     float sample_inv_t = 0.0f;
     uint64_t sample_seed = 0;
+    // paged KV caches (page_size > 0): kc / vc of a layer are pools
+    // [num_pages][nkv][page_size][D]; sequence t's position p lives in page
+    // table[t][p / page_size] (table [T][max_pages], -1: no page; the host
+    // copy is uploaded before a step once it changed).  A sequence at
+    // position -1 is an empty slot.  Prefill runs on contiguous staging
+    // caches st_k / st_v [nkv][max_seq][D] per layer (allocated by the first
+    // paged prefill) and copies the rows into the pages.  salts [T]: the
+    // per-sequence sampling keys (set_salts), or none.
+    int page_size = 0, num_pages = 0, max_pages = 0;
+    int* table = nullptr;
+    std::vector<int> table_host;
+    bool table_dirty = false;
+    std::vector<uint16_t*> st_k, st_v;
+    uint64_t* salts = nullptr;
 
     ~infernt_batch_engine() {
         if (graph) cudaGraphExecDestroy(graph);  // before the communicator its NCCL nodes use
@@ -301,7 +318,8 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         if (int s = window(p, H, il, il, I, 0, (long long)r * il, INFERNT_STREAM_LAYER(l, 6))) return s;
         ly.down = p;
         e->layers.push_back(ly);
-        const size_t cache = (size_t)T * nkv * c.max_seq_len * D * 2;
+        const size_t cache = e->page_size ? (size_t)e->num_pages * nkv * e->page_size * D * 2
+                                          : (size_t)T * nkv * c.max_seq_len * D * 2;
         void* k = nullptr;
         void* v = nullptr;
         if (int s = alloc(e, cache, &k)) return s;
@@ -356,6 +374,13 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
         if (int s = alloc(e, sizeof(float) * (size_t)T * H, reinterpret_cast<void**>(&e->ysum))) return s;
         if (int s = alloc(e, sizeof(int2) * (size_t)T, reinterpret_cast<void**>(&e->cand))) return s;
         if (int s = alloc(e, sizeof(int2) * (size_t)T * e->world, reinterpret_cast<void**>(&e->cand_all))) return s;
+    }
+    if (e->page_size) {
+        e->max_pages = (c.max_seq_len + e->page_size - 1) / e->page_size;
+        const size_t tb = sizeof(int) * (size_t)T * e->max_pages;
+        if (int s = alloc(e, tb, reinterpret_cast<void**>(&e->table))) return s;
+        INFERNT_CUDA_TRY(cudaMemsetAsync(e->table, 0xff, tb, e->stream));
+        e->table_host.assign((size_t)T * e->max_pages, -1);
     }
     if (int s = alloc(e, sizeof(float2) * (size_t)c.max_seq_len * (D / 2), reinterpret_cast<void**>(&e->rope)))
         return s;
@@ -413,7 +438,8 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
             // Q|K|V finishing inside the tensor-core attention
             if (int s = bt_attention_fused_launch(e->part, e->sp_qkv, e->rope, e->kc[l], e->vc[l], e->positions, T, nq,
                                                   nkv, D, c.max_seq_len, e->S, e->min_chunk, e->stages, e->apart,
-                                                  e->attn, e->err, e->tickets, st))
+                                                  e->attn, e->err, e->tickets, st, e->table, e->page_size,
+                                                  e->max_pages))
                 return s;
         } else {
             if (int s = bt_qkv_finish_launch(e->part, e->sp_qkv, T, nq, nkv, D, e->positions, e->rope, c.max_seq_len,
@@ -435,7 +461,7 @@ int record_step(infernt_batch_engine* e, cudaStream_t st) {
     // the LM head runs unsplit: part[0] holds the logits [T][vlp]
     if (e->world == 1)
         return bt_argmax_launch(e->part, T, V, e->tokens, e->positions, nullptr, e->cand_v, e->cand_i, e->am_tickets,
-                                e->sample_inv_t, e->sample_seed, st);
+                                e->sample_inv_t, e->sample_seed, st, e->salts);
     if (int s = tp_argmax_local_launch(e->part, T, e->vlp, e->vl, e->v0, e->cand, e->positions, e->sample_inv_t,
                                        e->sample_seed, st))
         return s;
@@ -556,6 +582,39 @@ int grow_prefill(infernt_batch_engine* e, int C) {
     return INFERNT_OK;
 }
 
+// Staging caches of a paged engine's prefill: [nkv][max_seq][D] K and V per
+// layer.
+int grow_staging(infernt_batch_engine* e) {
+    if (!e->st_k.empty()) return INFERNT_OK;
+    const infernt_llama_config& c = e->cfg;
+    const size_t bytes = (size_t)e->nkv_l * c.max_seq_len * c.head_dim * 2;
+    for (int l = 0; l < c.num_layers; ++l) {
+        void* k = nullptr;
+        void* v = nullptr;
+        if (int s = alloc(e, bytes, &k)) return s;
+        if (int s = alloc(e, bytes, &v)) return s;
+        e->st_k.push_back(static_cast<uint16_t*>(k));
+        e->st_v.push_back(static_cast<uint16_t*>(v));
+    }
+    return INFERNT_OK;
+}
+
+// Rows [p0, p1) of sequence seq, every layer, from its pages into the
+// staging caches (to_pages false) or back.
+int stage_rows(infernt_batch_engine* e, int seq, int p0, int p1, bool to_pages) {
+    const infernt_llama_config& c = e->cfg;
+    const int* pages = e->table + (size_t)seq * e->max_pages;
+    for (int l = 0; l < c.num_layers; ++l) {
+        if (int s = infernt::bt_page_copy_launch(e->kc[l], e->st_k[l], pages, e->page_size, e->nkv_l, c.max_seq_len,
+                                                 c.head_dim, p0, p1, to_pages, e->stream))
+            return s;
+        if (int s = infernt::bt_page_copy_launch(e->vc[l], e->st_v[l], pages, e->page_size, e->nkv_l, c.max_seq_len,
+                                                 c.head_dim, p0, p1, to_pages, e->stream))
+            return s;
+    }
+    return INFERNT_OK;
+}
+
 // Prefill of sequence `seq`: prompt tokens pf_tokens[0, n) at positions
 // [start, start + n) in chunks of C, every layer per chunk; then the LM head
 // and argmax of the last token (its logits in pf_y[0, V), the greedy token
@@ -566,7 +625,12 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
     const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, S = c.max_seq_len;
     const int qs = nq * D, nqkv = qs + 2 * nkv * D;
     const float eps = c.rms_norm_eps;
-    const size_t seq_off = (size_t)seq * nkv * S * D;
+    // the sequence's contiguous caches: its rows of [T][nkv][S][D], or the
+    // staging caches of a paged engine
+    const bool paged = e->page_size > 0;
+    const size_t seq_off = paged ? 0 : (size_t)seq * nkv * S * D;
+    const std::vector<uint16_t*>& kcs = paged ? e->st_k : e->kc;
+    const std::vector<uint16_t*>& vcs = paged ? e->st_v : e->vc;
     using namespace infernt;
     int m = 0;
     for (int c0 = 0; c0 < n; c0 += C) {
@@ -577,8 +641,8 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
             return s;
         for (int l = 0; l < L; ++l) {
             const auto& ly = e->layers[l];
-            uint16_t* kc = e->kc[l] + seq_off;
-            uint16_t* vc = e->vc[l] + seq_off;
+            uint16_t* kc = kcs[l] + seq_off;
+            uint16_t* vc = vcs[l] + seq_off;
             if (int s = pgemm_launch(ly.qkv, nqkv, H, e->pf_x, m, e->pf_y, nqkv, e->err, st)) return s;
             if (int s = pf_qkv_rope_launch(e->pf_y, m, p0, nq, nkv, D, e->rope, S, e->pf_q, kc, vc, st)) return s;
             if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, e->err, 1, st)) return s;
@@ -594,17 +658,43 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
     // the last token's final-normed row is row m - 1 of the last chunk
     if (int s = bgemm_launch(e->lm, V, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
     return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket,
-                            e->sample_inv_t, e->sample_seed, st);
+                            e->sample_inv_t, e->sample_seed, st, e->salts ? e->salts + seq : nullptr);
 }
 
-int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions) {
+// Whether the block table gives sequence t pages for positions [0, last].
+bool pages_cover(const infernt_batch_engine* e, int t, int last) {
+    const int* row = e->table_host.data() + (size_t)t * e->max_pages;
+    for (int i = 0; i <= last / e->page_size; ++i)
+        if (row[i] < 0) return false;
+    return true;
+}
+
+// The host block table on the device (before a step that reads it).
+int upload_table(infernt_batch_engine* e) {
+    if (!e->page_size || !e->table_dirty) return INFERNT_OK;
+    INFERNT_CUDA_TRY(cudaMemcpyAsync(e->table, e->table_host.data(), sizeof(int) * e->table_host.size(),
+                                     cudaMemcpyHostToDevice, e->stream));
+    e->table_dirty = false;
+    return INFERNT_OK;
+}
+
+// Token and position per sequence for the next steps (`steps` of them);
+// a paged engine takes position -1 for an empty slot and needs pages
+// through the last position the steps write.
+int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions, int steps = 1) {
+    const bool paged = e->page_size > 0;
     for (int t = 0; t < e->T; ++t) {
         INFERNT_REQUIRE(tokens[t] >= 0 && tokens[t] < e->cfg.vocab_size, "batch engine: token %d of sequence %d",
                         tokens[t], t);
+        if (paged && positions[t] == -1) continue;
         INFERNT_REQUIRE(positions[t] >= 0 && positions[t] < e->cfg.max_seq_len,
                         "batch engine: position %d of sequence %d outside [0, %d)", positions[t], t,
                         e->cfg.max_seq_len);
+        INFERNT_REQUIRE(!paged || pages_cover(e, t, positions[t] + steps - 1),
+                        "batch engine: sequence %d has no page for a position in [0, %d]", t,
+                        positions[t] + steps - 1);
     }
+    if (int s = upload_table(e)) return s;
     INFERNT_CUDA_TRY(cudaMemcpyAsync(e->tokens, tokens, sizeof(int) * e->T, cudaMemcpyHostToDevice, e->stream));
     INFERNT_CUDA_TRY(cudaMemcpyAsync(e->positions, positions, sizeof(int) * e->T, cudaMemcpyHostToDevice, e->stream));
     return INFERNT_OK;
@@ -614,9 +704,14 @@ int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions)
 
 extern "C" {
 
-int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
-                                   int attn_splits, int rank, int world, const void* nccl_id,
-                                   infernt_batch_engine** out) {
+}  // extern "C"
+
+namespace {
+
+// An engine of `batch` sequences: contiguous caches (page_size 0) or pools
+// of num_pages pages of page_size positions.
+int create_engine(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev, int attn_splits, int rank,
+                  int world, const void* nccl_id, int page_size, int num_pages, infernt_batch_engine** out) {
     INFERNT_REQUIRE(cfg && out, "batch_engine_create: null argument");
     *out = nullptr;
     INFERNT_REQUIRE(cfg->weight_dtype == INFERNT_DTYPE_BF16, "batch engine: bf16 weights only");
@@ -669,6 +764,8 @@ int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, u
         if (S > 64) S = 64;
     }
     e->S = S < 1 ? 1 : S;
+    e->page_size = page_size;
+    e->num_pages = num_pages;
     int s = build(e, seed, std_dev);
     if (!s && world > 1) {
         ncclUniqueId id;
@@ -689,9 +786,82 @@ int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, u
     return INFERNT_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int infernt_batch_engine_create_tp(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
+                                   int attn_splits, int rank, int world, const void* nccl_id,
+                                   infernt_batch_engine** out) {
+    return create_engine(cfg, batch, seed, std_dev, attn_splits, rank, world, nccl_id, 0, 0, out);
+}
+
 int infernt_batch_engine_create_seeded(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev,
                                        int attn_splits, infernt_batch_engine** out) {
-    return infernt_batch_engine_create_tp(cfg, batch, seed, std_dev, attn_splits, 0, 1, nullptr, out);
+    return create_engine(cfg, batch, seed, std_dev, attn_splits, 0, 1, nullptr, 0, 0, out);
+}
+
+int infernt_batch_engine_create_paged(const infernt_llama_config* cfg, int batch, int page_size, int num_pages,
+                                      uint64_t seed, float std_dev, int attn_splits, infernt_batch_engine** out) {
+    INFERNT_REQUIRE(cfg && out, "batch_engine_create_paged: null argument");
+    *out = nullptr;
+    INFERNT_REQUIRE(page_size >= 1 && page_size <= cfg->max_seq_len && num_pages >= 1,
+                    "batch_engine_create_paged: %d pages of %d positions (max_seq_len %d)", num_pages, page_size,
+                    cfg->max_seq_len);
+    INFERNT_REQUIRE(cfg->num_key_value_heads >= 1 && cfg->num_attention_heads % cfg->num_key_value_heads == 0 &&
+                        cfg->num_attention_heads / cfg->num_key_value_heads <= 8,
+                    "batch_engine_create_paged: paged caches need query groups of at most 8 heads");
+    INFERNT_REQUIRE((long long)num_pages * cfg->num_key_value_heads * page_size <= (1ll << 40),
+                    "batch_engine_create_paged: pool of %d pages too large", num_pages);
+    return create_engine(cfg, batch, seed, std_dev, attn_splits, 0, 1, nullptr, page_size, num_pages, out);
+}
+
+int infernt_batch_engine_set_pages(infernt_batch_engine* e, int seq, const int* pages, int n_pages) {
+    INFERNT_REQUIRE(e, "batch_engine_set_pages: null engine");
+    INFERNT_REQUIRE(e->page_size > 0, "batch_engine_set_pages: the engine's caches are not paged");
+    INFERNT_REQUIRE(seq >= 0 && seq < e->T, "batch_engine_set_pages: sequence %d outside [0, %d)", seq, e->T);
+    INFERNT_REQUIRE(n_pages >= 0 && n_pages <= e->max_pages && (n_pages == 0 || pages),
+                    "batch_engine_set_pages: %d pages (at most %d per sequence)", n_pages, e->max_pages);
+    for (int i = 0; i < n_pages; ++i)
+        INFERNT_REQUIRE(pages[i] >= 0 && pages[i] < e->num_pages, "batch_engine_set_pages: page %d outside [0, %d)",
+                        pages[i], e->num_pages);
+    int* row = e->table_host.data() + (size_t)seq * e->max_pages;
+    for (int i = 0; i < e->max_pages; ++i) row[i] = i < n_pages ? pages[i] : -1;
+    e->table_dirty = true;
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_paging(infernt_batch_engine* e, int* page_size, int* num_pages, int* max_pages) {
+    INFERNT_REQUIRE(e && page_size && num_pages && max_pages, "batch_engine_paging: null argument");
+    *page_size = e->page_size;
+    *num_pages = e->num_pages;
+    *max_pages = e->max_pages;
+    return INFERNT_OK;
+}
+
+int infernt_batch_engine_set_salts(infernt_batch_engine* e, const uint64_t* salts) {
+    INFERNT_REQUIRE(e, "batch_engine_set_salts: null engine");
+    INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if (!salts) {
+        if (e->salts) {
+            release(e, e->salts);
+            e->salts = nullptr;
+            if (e->graph) {
+                cudaGraphExecDestroy(e->graph);
+                e->graph = nullptr;  // captured again at the next step
+            }
+        }
+        return INFERNT_OK;
+    }
+    if (!e->salts) {
+        if (int s = alloc(e, sizeof(uint64_t) * (size_t)e->T, reinterpret_cast<void**>(&e->salts))) return s;
+        if (e->graph) {
+            cudaGraphExecDestroy(e->graph);
+            e->graph = nullptr;
+        }
+    }
+    INFERNT_CUDA_TRY(cudaMemcpy(e->salts, salts, sizeof(uint64_t) * (size_t)e->T, cudaMemcpyHostToDevice));
+    return INFERNT_OK;
 }
 
 int infernt_nccl_unique_id(void* out, size_t n) {
@@ -720,13 +890,22 @@ int infernt_batch_engine_destroy(infernt_batch_engine* e) {
 int infernt_batch_engine_fill_kv(infernt_batch_engine* e, int seq, uint64_t seed, int n_pos, float std_dev) {
     INFERNT_REQUIRE(e && seq >= 0 && seq < e->T && n_pos >= 0 && n_pos <= e->cfg.max_seq_len,
                     "batch_engine_fill_kv: bad arguments");
+    const int* pages = nullptr;
+    if (e->page_size && n_pos > 0) {
+        INFERNT_REQUIRE(pages_cover(e, seq, n_pos - 1), "batch_engine_fill_kv: sequence %d has no page for a position "
+                        "below %d", seq, n_pos);
+        if (int s = upload_table(e)) return s;
+        pages = e->table + (size_t)seq * e->max_pages;
+    }
     const uint64_t kk = infernt_stream_key(seed, INFERNT_STREAM_KV_K), vk = infernt_stream_key(seed, INFERNT_STREAM_KV_V);
     for (int l = 0; l < e->cfg.num_layers; ++l) {
         if (int s = infernt::bt_fill_kv_launch(e->kc[l], seq, l, e->nkv_l, e->cfg.max_seq_len, e->cfg.head_dim, n_pos,
-                                               kk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream))
+                                               kk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream,
+                                               pages, e->page_size))
             return s;
         if (int s = infernt::bt_fill_kv_launch(e->vc[l], seq, l, e->nkv_l, e->cfg.max_seq_len, e->cfg.head_dim, n_pos,
-                                               vk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream))
+                                               vk, std_dev, e->rank * e->nkv_l, e->cfg.num_key_value_heads, e->stream,
+                                               pages, e->page_size))
             return s;
     }
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
@@ -748,7 +927,7 @@ int infernt_batch_engine_decode(infernt_batch_engine* e, const int* tokens, cons
     for (int t = 0; t < e->T; ++t)
         INFERNT_REQUIRE((long long)positions[t] + steps <= e->cfg.max_seq_len,
                         "batch_engine_decode: sequence %d would pass max_seq_len", t);
-    if (int s = set_inputs(e, tokens, positions)) return s;
+    if (int s = set_inputs(e, tokens, positions, steps)) return s;
     if (int s = ensure_graph(e)) return s;
     int* hist = nullptr;
     if (tokens_out) {
@@ -834,6 +1013,16 @@ int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* to
                         tokens[i], i);
     int C = chunk > 0 ? chunk : 4096;
     if (C > n_tokens) C = n_tokens;
+    const bool paged = e->page_size > 0;
+    if (paged) {
+        INFERNT_REQUIRE(pages_cover(e, seq, start_pos + n_tokens - 1),
+                        "batch_engine_prefill: sequence %d has no page for a position in [0, %d]", seq,
+                        start_pos + n_tokens - 1);
+        if (int s = grow_staging(e)) return s;
+        if (int s = upload_table(e)) return s;
+        // earlier rows of the sequence into the staging caches
+        if (int s = stage_rows(e, seq, 0, start_pos, false)) return s;
+    }
     if (int s = grow_prefill(e, C)) return s;
     INFERNT_CUDA_TRY(
         cudaMemcpyAsync(e->pf_tokens, tokens, sizeof(int) * (size_t)n_tokens, cudaMemcpyHostToDevice, e->stream));
@@ -841,6 +1030,8 @@ int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* to
     INFERNT_CUDA_TRY(cudaMemcpyAsync(e->pf_tok, tp, sizeof(tp), cudaMemcpyHostToDevice, e->stream));
     INFERNT_CUDA_TRY(cudaEventRecord(e->ev[0], e->stream));
     if (int s = record_prefill(e, seq, n_tokens, start_pos, C, e->stream)) return s;
+    if (paged)
+        if (int s = stage_rows(e, seq, start_pos, start_pos + n_tokens, true)) return s;
     INFERNT_CUDA_TRY(cudaEventRecord(e->ev[1], e->stream));
     int out[2] = {0, 0};
     INFERNT_CUDA_TRY(cudaMemcpyAsync(out, e->pf_tok, sizeof(out), cudaMemcpyDeviceToHost, e->stream));
@@ -864,6 +1055,24 @@ int infernt_batch_engine_read_kv(infernt_batch_engine* e, int seq, int layer, in
     const int nkv = e->nkv_l, D = c.head_dim, S = c.max_seq_len;
     const size_t row = (size_t)n_pos * D * 2;
     INFERNT_CUDA_TRY(cudaStreamSynchronize(e->stream));
+    if (e->page_size) {
+        // page by page: rows [i P, min(n_pos, (i + 1) P)) of each KV head
+        const int P = e->page_size;
+        INFERNT_REQUIRE(n_pos == 0 || pages_cover(e, seq, n_pos - 1),
+                        "batch_engine_read_kv: sequence %d has no page for a position below %d", seq, n_pos);
+        const int* tab = e->table_host.data() + (size_t)seq * e->max_pages;
+        for (int h = 0; h < nkv; ++h)
+            for (int p0 = 0; p0 < n_pos; p0 += P) {
+                const int rows = n_pos - p0 < P ? n_pos - p0 : P;
+                const size_t src = (((size_t)tab[p0 / P] * nkv + h) * P) * D;
+                const size_t dst = (size_t)h * row + (size_t)p0 * D * 2;
+                INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(k_host) + dst, e->kc[layer] + src,
+                                            (size_t)rows * D * 2, cudaMemcpyDeviceToHost));
+                INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(v_host) + dst, e->vc[layer] + src,
+                                            (size_t)rows * D * 2, cudaMemcpyDeviceToHost));
+            }
+        return INFERNT_OK;
+    }
     for (int h = 0; h < nkv; ++h) {
         const size_t off = ((size_t)seq * nkv + h) * S * D;
         INFERNT_CUDA_TRY(cudaMemcpy(static_cast<char*>(k_host) + h * row, e->kc[layer] + off, row,
