@@ -712,8 +712,20 @@ def run_batched(args, longctx=False, tp=False):
         lo, hi = n_seq * rank // world, n_seq * (rank + 1) // world
     mine = ctx[lo:hi]
     T = hi - lo
+    page = getattr(args, "paged", 0)
     if not tp:
-        eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
+        if page:
+            # paged caches: each sequence's pages drawn from a shuffled pool
+            # that holds exactly the positions the run reaches
+            need = [-(-(int(c) + W + K + 16) // page) for c in mine]
+            order = np.random.default_rng(99).permutation(sum(need)).tolist()
+            eng = ib.BatchEngine(cfg, T, seed=seed, std=STD, pages=(page, sum(need)))
+            at = 0
+            for b in range(T):
+                eng.set_pages(b, order[at:at + need[b]])
+                at += need[b]
+        else:
+            eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
     tokens = ib.prompt(n_seq, seed, 3, cfg.vocab_size)[lo:hi]
     prefill = None
     if longctx and getattr(args, "real_prefill", False) and not tp:
@@ -814,6 +826,8 @@ def run_batched(args, longctx=False, tp=False):
                    "contexts_mean": round(float(np.mean(ctx)), 1),
                    "parallelism": ("tp%d" if tp else "dp%d") % world,
                    "splits_qkv_o_gateup_down_lm_attn": sp,
+                   "kv_layout": ("paged: pages of %d positions from a shuffled pool, block table per sequence"
+                                 % page if page else "contiguous [sequence][kv head][max_seq][head_dim]"),
                    "l2": "no flush: %.2f GB of weights + %.2f GB of KV per GPU per step"
                    % (wbytes / 1e9, kv_bytes / 1e9)},
         "e2e": {"value": round(n_seq * ne / e2e_s, 1), "unit": "tok/s",
@@ -836,6 +850,119 @@ def run_batched(args, longctx=False, tp=False):
                           "seeded prompt prefilled by the engine (time under 'prefill'), then decoded from "
                           "the token it produced")
     eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_serving(args):
+    """Continuous batching of TinyLlama-shaped bf16 requests through the
+    server C ABI (infernt_server_*: iteration-level scheduler, paged KV
+    caches, prefill per admitted request on the tensor cores, one batched
+    decode step of every running request per iteration): 256 requests with
+    seeded prompts of uniform length in [512, 2048] and uniform
+    max_new_tokens in [16, 512] (numpy seed 4321), 64 slots, pages of 32
+    positions, a pool of 80% of the positions the slots could hold at
+    max_seq_len.  value: generated tokens per second over the whole run
+    (prefills, decode steps and host scheduling inside the host-timed
+    region: the call a user makes, so it is also the e2e figure).  Beside
+    it, static batching of the same requests on the contiguous batched
+    engine and the same kernels: waves of 64, each prompt prefilled, then
+    every wave decoded until its longest request is done.  With N ranks
+    each serves its own share of the requests on a full replica (replicas,
+    no collective); value = all ranks' generated tokens / the slowest
+    rank's time."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import numpy as np
+    import infernt_b200 as ib
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    slots, page = 64, 32
+    n_req = 256
+    rng = np.random.default_rng(4321)
+    plen = rng.integers(512, 2049, size=n_req)
+    new = rng.integers(16, 513, size=n_req)
+    lo, hi = n_req * rank // world, n_req * (rank + 1) // world
+    cfg = ib.TINYLLAMA.with_(weight_dtype=ib.DTYPE_BF16, max_seq_len=2048 + 512 + 16)
+    prompts = [ib.prompt(int(plen[i]), 7000 + i, 3, cfg.vocab_size) for i in range(lo, hi)]
+    n_pages = int(0.8 * slots * cfg.max_seq_len / page)
+    srv = ib.Server(cfg, slots, page, n_pages, seed=SEED, std=STD)
+    # warm-up: graph capture, prefill scratch, staging caches
+    for i in range(args.warmup):
+        srv.submit(prompts[i % len(prompts)][:512], 8)
+    srv.run()
+    w0 = srv.stats()
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ids = [srv.submit(prompts[i], int(new[lo + i])) for i in range(hi - lo)]
+    srv.run()
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    clocks = sampler.stop()
+    st = srv.stats()
+    outs = [srv.result(r) for r in ids]
+    assert all(o[1] == "finished" and len(o[0]) == int(new[lo + i]) for i, o in enumerate(outs))
+    srv.close()
+    gen = int(np.sum(new[lo:hi]))
+    secs_max = max_over_ranks(torch, secs * 1e3, "cuda") / 1e3
+    total_gen = int(np.sum(new))
+    value = total_gen / secs_max
+    steps = st["steps"] - w0["steps"]
+    dec = st["decode_tokens"] - w0["decode_tokens"]
+    # static batching on the contiguous engine: waves of `slots` requests
+    eng = ib.BatchEngine(cfg, slots, seed=SEED, std=STD)
+    eng.prefill(0, prompts[0][:512])
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    for w0i in range(0, hi - lo, slots):
+        wave = list(range(w0i, min(hi - lo, w0i + slots)))
+        toks = [0] * slots
+        pos = [0] * slots
+        for j, i in enumerate(wave):
+            toks[j], _, _ = eng.prefill(j, prompts[i])
+            pos[j] = len(prompts[i])
+        longest = max(int(new[lo + i]) for i in wave)
+        if longest > 1:
+            eng.decode(toks, pos, longest - 1)
+    torch.cuda.synchronize()
+    static_s = max_over_ranks(torch, (time.perf_counter() - t1) * 1e3, "cuda") / 1e3
+    eng.close()
+    result = {
+        "metric": "served tok/s (TinyLlama-1.1B shape, bf16, continuous batching of 256 requests)",
+        "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": int(steps),
+        "warmup": args.warmup, "ms_per_step": round(secs_max * 1e3 / max(1, steps), 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 weights and projection inputs, f32 accumulation, bf16 KV",
+        "data": ("synthetic: seeded weights N(0,0.02) seed 0, norms 1.0; 256 seeded prompts, lengths uniform "
+                 "in [512, 2048], max_new_tokens uniform in [16, 512] (numpy seed 4321), greedy"),
+        "config": {"workload": "tinyllama-bf16-serving-256req-64slots", "slots": slots, "page_size": page,
+                   "pool_pages": n_pages, "requests": n_req, "parallelism": "replicas%d" % world,
+                   "prompt_tokens": int(np.sum(plen)), "generated_tokens": total_gen,
+                   "l2": "no flush: 2.07 GB of weights per step"},
+        "serving": {"decode_steps": int(steps), "mean_running": round(dec / max(1, steps), 1),
+                    "preemptions": st["preemptions"] - w0["preemptions"],
+                    "prefill_tokens": st["prefill_tokens"] - w0["prefill_tokens"],
+                    "rank0_generated": gen},
+        "static_batching": {"tok_s": round(total_gen / static_s, 1), "s": round(static_s, 3),
+                            "how": "contiguous batched engine, waves of 64 requests, each wave decoded "
+                                   "until its longest request finishes"},
+        "e2e": {"value": round(value, 1), "unit": "tok/s", "h2d_bytes_per_step": 8 * slots,
+                "d2h_bytes_per_step": 4 * slots,
+                "api": "infernt_server_submit / infernt_server_run (C ABI); host-timed, prefills included"},
+        "gpu_launches": None,
+        "clocks": clocks,
+    }
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1062,7 +1189,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "layer-ops", "llama8b-tp", "batched", "longctx", "longctx-tp",
-                                           "prefill", "profile-case"],
+                                           "prefill", "serving", "profile-case"],
                     default="decode",
                     help="decode: the TinyLlama decode benchmark; layer-ops: every op of one layer "
                          "at position 4095, timed alone; llama8b-tp: the 8B-shaped bf16 decode, "
@@ -1072,7 +1199,11 @@ def main():
                          "data-parallel over the torchrun ranks; longctx-tp: the same 16 sequences, "
                          "tensor-parallel over the torchrun ranks; prefill: the 32768-token prompts of "
                          "those sequences (one prompt per step), data-parallel over the torchrun ranks; "
+                         "serving: continuous batching of 256 TinyLlama-shaped bf16 requests over paged KV "
+                         "(infernt_server_*), static batching beside it; "
                          "profile-case: a run sized for profilers (see run_profile_case), no JSON line")
+    ap.add_argument("--paged", type=int, default=0,
+                    help="batched / longctx: page size of paged KV caches (0: contiguous caches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-llama8b", action="store_true",
                     help="decode: skip the Llama-3-8B-shaped tensor-parallel measurement")
@@ -1106,6 +1237,8 @@ def main():
         run_batched(args, longctx=True, tp=True)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "serving":
+        run_serving(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

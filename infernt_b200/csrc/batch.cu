@@ -453,17 +453,34 @@ __global__ void __launch_bounds__(128) bt_attn_mma(const BtAttnArgs a) {
     const unsigned char* vb = reinterpret_cast<const unsigned char*>(a.vc);
     const uint32_t ring = smem_addr(att_smem) + (uint32_t)warp * NST * 2 * TILEB;
 
-    // this warp's tile i of the split -> stage i % NST (K at +0, V at +TILEB)
+    // this warp's tile i of the split -> stage i % NST (K at +0, V at +TILEB).
+    // Row of position p: off0 + p below `bound`, else off1 + p — one base
+    // for contiguous caches, and for pages of at least a tile the tile's
+    // one or two pages (looked up once per tile); smaller pages look up
+    // every row.  Rows past the split (ok false) copy nothing from p0's row.
+    const bool row_pages = a.block_table && a.page_size < kAttnTile;
     auto issue = [&](int i) {
         const int tile = warp + NW * i;
         if (tile < ntiles) {
             const int p0 = c0 + tile * kAttnTile;
             const uint32_t st = ring + (uint32_t)(i % NST) * 2 * TILEB;
+            long long off0 = ((long long)t * nkv + kvh) * max_seq, off1 = off0;
+            int bound = max_seq;
+            if (a.block_table && !row_pages) {
+                const int P = a.page_size, pi = p0 / P, last = min(p0 + kAttnTile, c1) - 1;
+                const int* tab = a.block_table + (size_t)t * a.max_pages;
+                bound = (pi + 1) * P;
+                off0 = ((long long)tab[pi] * nkv + kvh) * P - (long long)pi * P;
+                if (last >= bound) off1 = ((long long)tab[pi + 1] * nkv + kvh) * P - (long long)bound;
+            }
 #pragma unroll
             for (int e = 0; e < kAttnTile * CH / 32; ++e) {
                 const int idx = e * 32 + lane, row = idx / CH, ch = idx % CH;
                 const bool ok = p0 + row < c1;
-                const size_t off = bt_row_off<D>(a, t, kvh, ok ? p0 + row : c0) * 2 + (size_t)ch * 16;
+                const int pp = ok ? p0 + row : p0;
+                const size_t r = row_pages ? bt_row_off<D>(a, t, kvh, pp) / D
+                                           : (size_t)((pp < bound ? off0 : off1) + pp);
+                const size_t off = r * ROWB + (size_t)ch * 16;
                 const uint32_t dst = st + (uint32_t)(row * ROWB + ((ch ^ (row & 7)) << 4));
                 cp_async16(dst, kb + off, ok ? 16u : 0u);
                 cp_async16(dst + TILEB, vb + off, ok ? 16u : 0u);
