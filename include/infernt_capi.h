@@ -597,6 +597,17 @@ INFERNT_API void* infernt_plan_xchg_region(infernt_plan* plan);
  * the launch returns, and the next synchronising call reports
  * INFERNT_ERR_DEVICE; the plan stays usable. */
 INFERNT_API int infernt_plan_set_wait_budget(infernt_plan* plan, long long microseconds);
+/* Weight-stream slots (16 KB each) the persistent decode kernel keeps in
+ * flight per SM: the producer issues a slot's bulk copy only when the slot
+ * `slots` earlier has landed.  Landed slots still fill the whole ring ahead
+ * of the consumers; the limit only bounds the copies queued in the memory
+ * system, behind which the reads of tagged activations at a phase boundary
+ * wait.  0 or more than the ring: no limit beyond the ring.  Plans of the
+ * other modes accept and ignore it.  No reference counterpart (the
+ * reference streams its weights through cuBLAS). */
+INFERNT_API int infernt_plan_set_stream_depth(infernt_plan* plan, int slots);
+/* The in-flight limit and the ring size in slots. */
+INFERNT_API int infernt_plan_stream_depth(const infernt_plan* plan, int* slots, int* ring_slots);
 
 /* One rank of a tensor-parallel decoder with seeded synthetic weights: the
  * rank's shards are windows of the matrices infernt_engine_create_seeded

@@ -20,8 +20,9 @@ DTYPE_BF16 = 1
 
 # Phase-timeline fields (infernt_plan_set_trace): phase start, input loaded,
 # work done, barrier passed, producer issued last tile (ns); consumer wait
-# cycles, producer wait cycles.
-TRACE_FIELDS = 7
+# cycles, producer wait cycles; thread 0's input words current, input and
+# constants in shared memory (ns).
+TRACE_FIELDS = 9
 
 MODE_EAGER = 0
 MODE_GRAPH = 1
@@ -235,6 +236,8 @@ _SIGS = {
     "infernt_plan_xchg_region": (_P, [_P]),
     "infernt_plan_set_peer_regions": (_I, [_P, ctypes.POINTER(_P)]),
     "infernt_plan_set_wait_budget": (_I, [_P, ctypes.c_longlong]),
+    "infernt_plan_set_stream_depth": (_I, [_P, _I]),
+    "infernt_plan_stream_depth": (_I, [_P, _P, _P]),
 }
 
 IPC_HANDLE_BYTES = 64
@@ -273,7 +276,7 @@ def call(name, *args):
 
 
 def _trace(cfg, fn, handle, token, position, steps):
-    """Runs a traced decode chain through `fn`; [cta][step][phase][7] int64."""
+    """Runs a traced decode chain through `fn`; [cta][step][phase][TRACE_FIELDS] int64."""
     import numpy as np
     nph = 5 * cfg.num_layers + 1
     ctas = lib().infernt_persistent_ctas()
@@ -387,7 +390,7 @@ class Engine:
 
     def trace_chain(self, token: int, position: int, steps: int):
         """Device-chained decode with the persistent kernel's phase timeline.
-        Returns an int64 array [cta][step][phase][7] over every CTA of the
+        Returns an int64 array [cta][step][phase][9] over every CTA of the
         launch: %globaltimer ns of phase start, input loaded, work done,
         barrier passed, producer issued the phase's last slot; then the SM
         cycles the CTA's first consumer waited for slots and its producer
@@ -834,3 +837,14 @@ class TPEngine:
     def set_wait_budget(self, microseconds: int):
         """Time budget of every wait inside the decode kernel."""
         call("infernt_plan_set_wait_budget", self._plan(), int(microseconds))
+
+    def set_stream_depth(self, slots: int):
+        """Weight-stream slots the decode kernel keeps in flight per SM
+        (infernt_plan_set_stream_depth; 0: the whole ring)."""
+        call("infernt_plan_set_stream_depth", self._plan(), int(slots))
+
+    def stream_depth(self):
+        """(slots in flight, ring slots) of the decode kernel."""
+        a, b = ctypes.c_int(), ctypes.c_int()
+        call("infernt_plan_stream_depth", self._plan(), ctypes.byref(a), ctypes.byref(b))
+        return a.value, b.value

@@ -97,6 +97,12 @@ __device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint3
         : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no destination, no
+// completion); src and bytes multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (TMA) writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

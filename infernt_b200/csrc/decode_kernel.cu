@@ -303,6 +303,54 @@ __device__ __noinline__ void ll_read_vec(const unsigned long long* src, float* d
     if ((n & 1) && tid == 0) dst[n - 1] = ll_val(wt.one<SYS>(src + n - 1, ld_ll1<SYS>(src + n - 1), tag));
 }
 
+// A run of tagged words src[0, n) read into dst[0, n) (n even, src 16-byte
+// and dst 8-byte aligned).
+struct LLSeg {
+    const unsigned long long* src;
+    float* dst;
+    int n;
+};
+
+// ll_read_vec over three runs at once: the word pairs of all three are
+// loaded in the same batches, so runs that land together cost one round
+// trip instead of one each.  Batches of kSegBatch pairs per thread (the
+// attention inputs are a few thousand words at most).
+constexpr int kSegBatch = 4;
+__device__ __noinline__ void ll_read_segs(const LLSeg s0, const LLSeg s1, const LLSeg s2, unsigned tag, int tid,
+                                          const LLWait wt) {
+    constexpr int STEP = kMegaConsumers * 2;
+    const int n01 = s0.n + s1.n, total = n01 + s2.n;
+    auto src_of = [&](int i) {
+        return i < s0.n ? s0.src + i : (i < n01 ? s1.src + (i - s0.n) : s2.src + (i - n01));
+    };
+    auto dst_of = [&](int i) {
+        return i < s0.n ? s0.dst + i : (i < n01 ? s1.dst + (i - s0.n) : s2.dst + (i - n01));
+    };
+    for (int base = tid * 2; base < total; base += STEP * kSegBatch) {
+        ulonglong2 w[kSegBatch];
+#pragma unroll
+        for (int k = 0; k < kSegBatch; ++k)
+            if (base + k * STEP < total) w[k] = ld_ll2<false>(src_of(base + k * STEP));
+        const long long t0 = clock64();
+        unsigned spins = 0;
+        while (true) {
+            bool ok = true;
+#pragma unroll
+            for (int k = 0; k < kSegBatch; ++k)
+                if (base + k * STEP < total && !(ll_is(w[k].x, tag) && ll_is(w[k].y, tag))) ok = false;
+            if (ok || wt.give_up(t0, spins)) break;
+#pragma unroll
+            for (int k = 0; k < kSegBatch; ++k)
+                if (base + k * STEP < total && !(ll_is(w[k].x, tag) && ll_is(w[k].y, tag)))
+                    w[k] = ld_ll2<false>(src_of(base + k * STEP));
+        }
+#pragma unroll
+        for (int k = 0; k < kSegBatch; ++k)
+            if (base + k * STEP < total)
+                *reinterpret_cast<float2*>(dst_of(base + k * STEP)) = make_float2(ll_val(w[k].x), ll_val(w[k].y));
+    }
+}
+
 // Output units [u0, u1) of this CTA: [U b / P, U (b + 1) / P).
 __device__ __forceinline__ void unit_range(const MegaPhase& P, int& u0, int& u1) {
     u0 = (int)((long long)P.units * blockIdx.x / gridDim.x);
@@ -362,7 +410,7 @@ __device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4
 // Residual phases also stage the (tagged) residual rows of the CTA's units
 // in sh.res.
 __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaShared& sh, int tid, int u0, int u1,
-                       uint32_t& xphase, int tok, unsigned ts, unsigned tag) {
+                       uint32_t& xphase, int tok, unsigned ts, unsigned tag, long long tb) {
     const int warp = tid >> 5, lane = tid & 31;
     const LLWait wt{p.err, &sh.abort};
     const int K = P.K;
@@ -380,12 +428,12 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
             plain = p.emb + (size_t)t * K;
         }
     }
-    // constant inputs (norm weights, the embedding row) by bulk copy, issued
-    // first so the tagged reads below overlap them
+    // constant inputs (norm weights, the embedding row, the launch's input
+    // vector) by bulk copy, issued first so the tagged reads below overlap
+    // them; nothing in this launch writes them, so no proxy fence is needed
     const uint32_t vbytes = (uint32_t)K * 4u;
     const uint32_t bytes = (plain ? vbytes : 0u) + (P.norm_w ? vbytes : 0u);
     if (tid == 0 && bytes) {
-        fence_proxy_async_global();
         mbar_arrive_expect_tx(&sh.xbar, bytes);
         if (plain) bulk_g2s_plain(xs, plain, vbytes, &sh.xbar);
         if (P.norm_w) bulk_g2s_plain(xs + K, P.norm_w, vbytes, &sh.xbar);
@@ -426,11 +474,13 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
         for (int i = P.kx + tid; i < K; i += kMegaConsumers) xs[i] = 0.0f;
     }
     if (my_res) sh.res[tid] = ll_val(wt.one<false>(P.res + u0 + tid, res_w, ts + (unsigned)P.res_ph));
+    trace_mark(p, tb, 7);
     if (bytes) {
         mega_wait(&sh.xbar, xphase & 1u, &sh.abort, p.err);
         ++xphase;
     }
     named_sync(1, kMegaConsumers);  // every thread's tagged reads into xs
+    trace_mark(p, tb, 8);
     if (plain && P.xout)
         for (int i = s0 + tid; i < s1; i += kMegaConsumers) st_ll(P.xout + i, xs[i], tag);
     constexpr int STRIDE = kMegaConsumers * 4;
@@ -949,13 +999,38 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
     if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i, tag);
 }
 
+// The cached K/V rows of this CTA's items in the attention phase that
+// follows (caches P.kc / P.vc), and the RoPE row of `pos`, into L2: issued
+// when the Q|K|V phase starts, so the attention phase's bulk copies of them
+// hit L2 instead of waiting for HBM behind the weight stream.
+__device__ void attention_prefetch(const MegaParams& p, const MegaPhase& P, int pos) {
+    const AttnArgs& a = p.attn;
+    if (pos < 0 || pos >= a.max_seq) return;
+    int chunk, active;
+    attn_chunk(pos + 1, a.splits, chunk, active);
+    const uint32_t row_bytes = (uint32_t)a.D * 4u;
+    bool any = false;
+    for (int it = blockIdx.x; it < a.nkv * a.splits; it += gridDim.x) {
+        const int kvh = it / a.splits, split = it % a.splits;
+        if (split >= active) continue;
+        any = true;
+        const int c0 = split * chunk, c1 = min(pos, c0 + chunk);  // row pos is this step's
+        if (c1 <= c0) continue;
+        const size_t off = ((size_t)kvh * a.max_seq + c0) * a.D;
+        bulk_prefetch_l2(P.kc + off, (uint32_t)(c1 - c0) * row_bytes);
+        bulk_prefetch_l2(P.vc + off, (uint32_t)(c1 - c0) * row_bytes);
+    }
+    if (any && a.rope) bulk_prefetch_l2(a.rope + (size_t)pos * (a.D / 2), row_bytes);
+}
+
 template <typename WT, int NS>
 __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned char* ring, uint64_t* full,
                            uint64_t* empty, RingPos& rp, uint32_t& xphase, float* xs, MegaShared& sh, int tid,
-                           long long tb, int tok, unsigned ts, unsigned tag) {
+                           long long tb, int tok, int pos, unsigned ts, unsigned tag) {
+    if (P.kc && tid == 0) attention_prefetch(p, P, pos);
     int u0, u1;
     unit_range(P, u0, u1);
-    load_x(p, P, xs, sh, tid, u0, u1, xphase, tok, ts, tag);
+    load_x(p, P, xs, sh, tid, u0, u1, xphase, tok, ts, tag, tb);
     if (tid == 0) trace_mark(p, tb, 1);
     SlotReader rd{ring, full, empty, &rp, p.ring_slots, &sh.abort, p.err, tb >= 0, 0};
     // widths that divide a slot's pieces keep their input columns in
@@ -1025,20 +1100,21 @@ __device__ void attention_item_bulk(const AttnArgs& a, const AttnLL& ll, int kvh
 
     // first round: the RoPE row and the first K/V tile by bulk copy, while
     // the threads read the tagged q rows and new K/V rows as they land
+    // (the cached rows were written by generic stores of earlier steps; the
+    // proxy fence after the step's acquire orders them before these copies)
     int t0 = c0, tl = min(T, c1 - c0);
     if (tid == 0) {
-        fence_proxy_async_global();
         const uint32_t bytes = row_bytes + 2u * (uint32_t)tl * row_bytes;
         mbar_arrive_expect_tx(&sh.xbar, bytes);
         bulk_g2s_plain(rope, a.rope + (size_t)pos * half, row_bytes, &sh.xbar);
         bulk_g2s_plain(kt, kbase + (size_t)t0 * D, (uint32_t)tl * row_bytes, &sh.xbar);
         bulk_g2s_plain(vt, vbase + (size_t)t0 * D, (uint32_t)tl * row_bytes, &sh.xbar);
     }
-    ll_read_vec<false>(ll.qkv + (size_t)kvh * G * D, qs, G * D, ll.tin, tid, wt);
-    if (owns_new) {
-        ll_read_vec<false>(ll.qkv + (size_t)a.nq * D + (size_t)kvh * D, knew, D, ll.tin, tid, wt);
-        ll_read_vec<false>(ll.qkv + (size_t)(a.nq + a.nkv) * D + (size_t)kvh * D, vnew, D, ll.tin, tid, wt);
-    }
+    // the group's q rows and (last split) the new K and V rows, in one round
+    const int nn = owns_new ? D : 0;
+    ll_read_segs(LLSeg{ll.qkv + (size_t)kvh * G * D, qs, G * D},
+                 LLSeg{ll.qkv + (size_t)a.nq * D + (size_t)kvh * D, knew, nn},
+                 LLSeg{ll.qkv + (size_t)(a.nq + a.nkv) * D + (size_t)kvh * D, vnew, nn}, ll.tin, tid, wt);
     mega_wait(&sh.xbar, xphase & 1u, &sh.abort, err);
     ++xphase;
     named_sync(1, kMegaConsumers);
@@ -1463,6 +1539,7 @@ template <typename WT>
 __device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full, uint64_t* empty, MegaShared& sh) {
     volatile int* abort = &sh.abort;
     const int slots = p.ring_slots;
+    const int depth = p.stream_depth > 0 && p.stream_depth < slots ? p.stream_depth : slots;
     const uint64_t pol = l2_evict_first_policy();
     uint32_t sl = 0;  // slots armed so far
     bool ok = true;
@@ -1476,6 +1553,15 @@ __device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full
         if (sl >= (uint32_t)slots && !mega_wait(&empty[wp.s], wp.ph ^ 1u, abort, p.err)) {
             ok = false;
             break;
+        }
+        // at most `depth` slots in flight: slot sl - depth must have landed
+        // (its full barrier is not re-armed before slot sl - depth + slots)
+        if (depth < slots && sl >= (uint32_t)depth) {
+            const uint32_t q = sl - (uint32_t)depth;
+            if (!mega_wait(&full[q % (uint32_t)slots], (q / (uint32_t)slots) & 1u, abort, p.err)) {
+                ok = false;
+                break;
+            }
         }
         pwait += clock64() - c0;
         mbar_arrive_expect_tx(&full[wp.s], sb);
@@ -1568,6 +1654,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             while ((int)(unsigned)(st >> 32) != pos0 + step && !wt.give_up(t0, spins)) st = ld_acquire64(stw);
         }
         const int tok = (int)(unsigned)(st & 0xffffffffull), pos = (int)(unsigned)(st >> 32);
+        // the KV-cache rows of earlier steps (generic stores, made visible by
+        // the acquire) before this step's bulk copies of them: thread 0
+        // issues every attention copy of the CTA
+        if (tid == 0) fence_proxy_async_global();
         // read after the first phase's opening barrier, so no thread of the
         // previous step still uses the old key
         if (tid == 0) sh.skey = infernt_stream_key(p.sample_seed, (uint64_t)(unsigned)pos);
@@ -1598,9 +1688,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             if (P.kind == kPhAttn) {
                 attention_phase(p, P, xs, sh, tid, tb, xphase, pos, ts, tag);
             } else if (P.ns == 2) {
-                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, ts, tag);
+                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
             } else {
-                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, ts, tag);
+                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
             }
             trace_mark(p, tb, 2);
             trace_mark(p, tb, 3);

@@ -37,8 +37,9 @@ struct alignas(16) MegaPhase {
     unsigned long long* xout;       // this CTA's share [K b/P, K (b+1)/P) of the input (layer 0's raw
                                     // embedding row, or the summed input) is published here, or NULL
     int layer;          // attention phases: KV-cache layer
-    float* kc;          // attention phases: the layer's K and V caches [N_kv, max_seq, D]
-    float* vc;
+    float* kc;          // attention phases: the layer's K and V caches [N_kv, max_seq, D]; the
+    float* vc;          // Q|K|V phase before one: the same caches, whose cached rows the CTAs
+                        // owning attention items prefetch into L2 when the phase starts
     // tensor parallelism
     int nsum;           // > 0: x = the xout vector of shares xbase + the nsum partials (rank order)
     const unsigned long long* xbase;  // this CTA's earlier share of the residual stream (phase xbase_ph)
@@ -85,7 +86,9 @@ struct MegaParams {
     // per (step, phase): [phase start, input loaded, work done, phase end,
     // producer issued the phase's last slot, SM cycles consumer warp 0
     // waited for full slots, SM cycles the producer waited for free slots
-    // while issuing the phase's slots]; attention phases record the item's
+    // while issuing the phase's slots, GEMV phases: thread 0's tagged input
+    // words current, every thread's input and the bulk-copied constants in
+    // shared memory (before RMSNorm)]; attention phases record the item's
     // inputs landed (1), partial computed (4), merge start and end (5, 6)
     unsigned long long* trace;
     // SM clock cycles any single wait may take before the kernel gives up
@@ -96,9 +99,12 @@ struct MegaParams {
     // (sample_seed, the step's position, the vocabulary id)
     float inv_temp;
     unsigned long long sample_seed;
+    // weight-stream slots the producer keeps in flight (issued, not yet
+    // landed); ring_slots: no limit beyond the ring
+    int stream_depth;
 };
 
-constexpr int kTraceFields = 7;
+constexpr int kTraceFields = 9;
 
 // Exchange region layout (one per rank, cudaMalloc'd, shared by IPC):
 // argmax slots [8] u64 (float value bits | index << 32 | tag << 56), then

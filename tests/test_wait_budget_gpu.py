@@ -64,3 +64,21 @@ def test_wait_budget_is_validated():
     with pytest.raises(ib.InferntError):
         eng.set_wait_budget(0)
     eng.close()
+
+
+def test_stream_depth_changes_no_result():
+    """The in-flight limit of the weight stream only reorders bulk copies in
+    time: every setting decodes the same tokens and the same logits bits."""
+    eng = ib.TPEngine(CFG, 0, 1, seed=5)
+    depth, ring = eng.stream_depth()
+    assert 1 <= depth <= ring
+    runs = []
+    for d in (0, 1, 3, ring):
+        eng.set_stream_depth(d)
+        assert eng.stream_depth()[0] == (ring if d == 0 else d)
+        toks, _ = eng.decode_chain(7, 0, 12)
+        runs.append((toks, eng.logits().tobytes()))
+    assert all(r == runs[0] for r in runs), [r[0] for r in runs]
+    with pytest.raises(ib.InferntError):
+        eng.set_stream_depth(-1)
+    eng.close()
