@@ -397,8 +397,22 @@ __device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4
     return acc;
 }
 
+// RMSNorm folded into the GEMV: for the widths whose input columns stay in
+// registers (K = 2048, 4096) the phase reads the raw input, each thread
+// multiplies its columns by the norm weights and sums their squares, and the
+// epilogue scales every row sum by rsqrt(sum x^2 / K + eps):
+// W (x * w * r) = r (W (x * w)) (cuda/rmsnorm.cu:10-26, with the factor r
+// applied once per output instead of once per input element).  This takes
+// the norm's two barriers and passes over the input off the critical path
+// at the phase start.
+__device__ __forceinline__ bool norm_folded(const MegaPhase& P) {
+    return P.norm_w != nullptr && (P.cb == 4 || P.cb == 8);
+}
+
+
 // Input vector of a GEMV phase into shared memory (RMSNorm applied when
-// set), `ts` the tag of phase 0 of this step, `tag` this phase's.
+// set, unless folded), `ts` the tag of phase 0 of this step, `tag` this
+// phase's.
 //
 // * Tagged input (P.x): read as it lands (phase P.x_ph's tag).
 // * Layer 0: the embedding row of the step's token (or the launch's input
@@ -483,6 +497,9 @@ __device__ void load_x(const MegaParams& p, const MegaPhase& P, float* xs, MegaS
     trace_mark(p, tb, 8);
     if (plain && P.xout)
         for (int i = s0 + tid; i < s1; i += kMegaConsumers) st_ll(P.xout + i, xs[i], tag);
+    // widths whose input columns stay in registers fold RMSNorm into the
+    // GEMV (norm_folded): xs keeps the raw input, nothing more to do here
+    if (norm_folded(P)) return;
     constexpr int STRIDE = kMegaConsumers * 4;
     if (P.norm_w) {
         float ss = 0.0f;
@@ -560,14 +577,18 @@ template <typename WT, int NS, bool TWO>
 __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaShared& sh, int ub, int n, int u1,
                                 int tid, float& am_v, int& am_i, unsigned ts, unsigned tag) {
     constexpr int BU = MegaRows<WT>::R / NS;
+    // folded RMSNorm (norm_folded): the factor from team 0's sums of squares
+    float r = 1.0f;
+    if (!TWO && P.norm_w)
+        r = rsqrtf((((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3]) / (float)P.K + P.eps);
     for (int idx = tid; idx < n * BU; idx += kMegaConsumers) {
         const int sl = idx / BU, i = idx % BU;
         const int row = ub + idx;
         if (row >= u1) continue;
-        const float v = gpart_sum<TWO>(sh, sl, i);
+        const float v = gpart_sum<TWO>(sh, sl, i) * r;
         if (NS == 2) {
             const int u = BU + i;
-            const float yu = gpart_sum<TWO>(sh, sl, u);
+            const float yu = gpart_sum<TWO>(sh, sl, u) * r;
             st_ll(P.out + row, silu_mul(v, yu), tag);
         } else if (P.epi == kEpiStore) {
             st_ll(P.out + row, v, tag);
@@ -953,6 +974,27 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
     if (CB > 0) {
 #pragma unroll
         for (int c = 0; c < NXR; ++c) xr[c] = *reinterpret_cast<const float4*>(xt + c * kPiece);
+        if (P.norm_w) {
+            // folded RMSNorm: a team covers every column once; team 0's warps
+            // publish their sums of squares for the epilogue's factor
+            const float* wn = xs + P.K + ctid * 4;
+            float ss = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NXR; ++c) {
+                const float4 w = *reinterpret_cast<const float4*>(wn + c * kPiece);
+                float4& v = xr[c];
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+                v.x *= w.x;
+                v.y *= w.y;
+                v.z *= w.z;
+                v.w *= w.w;
+            }
+            ss = warp_sum(ss);
+            if (team == 0 && lane == 0) sh.ss[cwarp] = ss;
+        }
     }
     const bool split = CB == 0 && P.cb >= PT;
     float am_v = -1e30f;
@@ -1138,6 +1180,7 @@ __device__ void attention_item_bulk(const AttnArgs& a, const AttnLL& ll, int kvh
         for (int d = tid; d < D; d += kMegaConsumers) vdst[d] = vnew[d];
     }
     named_sync(1, kMegaConsumers);
+    mark(7);
 
     // this warp's heads h = warp + j NW (warp-uniform validity)
     bool hv[MAXH];
@@ -1208,6 +1251,7 @@ __device__ void attention_item_bulk(const AttnArgs& a, const AttnLL& ll, int kvh
             }
         }
         __syncwarp();
+        if (t0 == c0) mark(8);
         // P V: each value row is read once for all heads; every output
         // column's sum runs over the positions in order
         float acc[MAXH][MAXDL];

@@ -89,7 +89,8 @@ struct MegaParams {
     // while issuing the phase's slots, GEMV phases: thread 0's tagged input
     // words current, every thread's input and the bulk-copied constants in
     // shared memory (before RMSNorm)]; attention phases record the item's
-    // inputs landed (1), partial computed (4), merge start and end (5, 6)
+    // inputs landed (1), partial computed (4), merge start and end (5, 6),
+    // RoPE and cache append done (7), first tile's softmax done (8)
     unsigned long long* trace;
     // SM clock cycles any single wait may take before the kernel gives up
     // (kErrWaitTimeout in the error word, every CTA returns)
