@@ -369,7 +369,13 @@ INFERNT_API int infernt_batch_engine_logits(infernt_batch_engine* e, float* logi
  * its logits into logits_host [vocab] (or NULL), and *ms the device time
  * of the prefill (or NULL).  Synchronous.  The first call (and a later call
  * with a larger chunk) allocates the prefill scratch: about chunk x (hidden
- * x 10 + max(Q|K|V rows, 2 x intermediate) x 4 + intermediate x 2) bytes. */
+ * x 10 + max(Q|K|V rows, 2 x intermediate) x 4 + intermediate x 2) bytes.
+ * Tensor-parallel engines (infernt_batch_engine_create_tp): every rank calls
+ * it with the same arguments; each runs its shards of the heads,
+ * intermediate rows and vocabulary, ncclAllReduce sums the O and down
+ * projections' partial rows of a chunk, every rank returns the same token,
+ * and logits_host receives this rank's vocabulary rows
+ * (infernt_batch_engine_vocab_range) at its start. */
 INFERNT_API int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* tokens,
                                              int n_tokens, int start_pos, int chunk, int* next_token,
                                              float* logits_host, float* ms);

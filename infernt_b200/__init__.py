@@ -425,6 +425,7 @@ class BatchEngine:
         pages)."""
         self.cfg = cfg
         self.T = batch
+        self.world = world
         self._c = cfg.c()
         self._owned = _handle is None
         if _handle is not None:
@@ -506,7 +507,9 @@ class BatchEngine:
     def prefill(self, seq: int, tokens, start_pos: int = 0, chunk: int = 0, want_logits: bool = False):
         """Prompt prefill of sequence `seq` (infernt_batch_engine_prefill):
         writes its K/V rows of positions [start_pos, start_pos + len(tokens))
-        and returns (greedy next token, last token's logits or None, device ms)."""
+        and returns (greedy next token, last token's logits or None, device
+        ms).  Tensor-parallel ranks all call it with the same arguments; the
+        logits are then this rank's vocabulary rows (vocab_range)."""
         import numpy as np
         toks = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         nxt = ctypes.c_int()
@@ -514,13 +517,16 @@ class BatchEngine:
         logits = np.empty(self.cfg.vocab_size, dtype=np.float32) if want_logits else None
         call("infernt_batch_engine_prefill", self._h, seq, toks.ctypes.data, toks.size, start_pos, chunk,
              ctypes.byref(nxt), None if logits is None else logits.ctypes.data, ctypes.byref(ms))
+        if logits is not None:
+            logits = logits[:self.vocab_range[1] - self.vocab_range[0]].copy()
         return nxt.value, logits, ms.value
 
     def read_kv(self, seq: int, layer: int, n_pos: int):
         """Rows [0, n_pos) of the sequence's K and V caches of one layer as
-        float32 arrays [nkv][n_pos][head_dim] (exact bf16 values)."""
+        float32 arrays [nkv][n_pos][head_dim] (exact bf16 values; a
+        tensor-parallel rank's own KV heads)."""
         import numpy as np
-        shape = (self.cfg.num_key_value_heads, n_pos, self.cfg.head_dim)
+        shape = (self.cfg.num_key_value_heads // self.world, n_pos, self.cfg.head_dim)
         k = np.zeros(shape, dtype=np.uint16)
         v = np.zeros(shape, dtype=np.uint16)
         call("infernt_batch_engine_read_kv", self._h, seq, layer, n_pos, k.ctypes.data, v.ctypes.data)

@@ -392,10 +392,10 @@ int build(infernt_batch_engine* e, uint64_t seed, float std_dev) {
 }
 
 // The sum over the ranks of y [T][H] in place (tensor parallelism).
-int all_reduce(infernt_batch_engine* e, float* y, cudaStream_t st) {
+int all_reduce(infernt_batch_engine* e, float* y, cudaStream_t st, size_t count = 0) {
     const NcclApi* n = nccl_api();
-    const ncclResult_t r = n->all_reduce(y, y, (size_t)e->T * e->cfg.hidden_size, ncclFloat32, ncclSum,
-                                         static_cast<ncclComm_t>(e->comm), st);
+    if (!count) count = (size_t)e->T * e->cfg.hidden_size;
+    const ncclResult_t r = n->all_reduce(y, y, count, ncclFloat32, ncclSum, static_cast<ncclComm_t>(e->comm), st);
     return r == ncclSuccess ? INFERNT_OK : fail(INFERNT_ERR_CUDA, "ncclAllReduce: %s", n->err_str(r));
 }
 
@@ -618,12 +618,19 @@ int stage_rows(infernt_batch_engine* e, int seq, int p0, int p1, bool to_pages) 
 // Prefill of sequence `seq`: prompt tokens pf_tokens[0, n) at positions
 // [start, start + n) in chunks of C, every layer per chunk; then the LM head
 // and argmax of the last token (its logits in pf_y[0, V), the greedy token
-// in pf_tok[0]).  Launches only.
+// in pf_tok[0]).  A tensor-parallel rank runs its shards (query and KV
+// heads, intermediate rows, vocabulary rows) and sums the O and down
+// projections' partial rows [m][H] over the ranks with ncclAllReduce before
+// each residual add (the chunk's rows are too many for the decode step's
+// peer-memory exchange region); the last token's argmax candidates of every
+// rank meet by ncclAllGather, as in the decode step.  Every rank must call
+// it with the same arguments.  Launches only.
 int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cudaStream_t st) {
     const infernt_llama_config& c = e->cfg;
-    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = c.intermediate_size;
-    const int nq = c.num_attention_heads, nkv = c.num_key_value_heads, S = c.max_seq_len;
+    const int H = c.hidden_size, V = c.vocab_size, D = c.head_dim, L = c.num_layers, I = e->il;
+    const int nq = e->nq_l, nkv = e->nkv_l, S = c.max_seq_len;
     const int qs = nq * D, nqkv = qs + 2 * nkv * D;
+    const bool tp = e->world > 1;
     const float eps = c.rms_norm_eps;
     // the sequence's contiguous caches: its rows of [T][nkv][S][D], or the
     // staging caches of a paged engine
@@ -647,18 +654,35 @@ int record_prefill(infernt_batch_engine* e, int seq, int n, int start, int C, cu
             if (int s = pf_qkv_rope_launch(e->pf_y, m, p0, nq, nkv, D, e->rope, S, e->pf_q, kc, vc, st)) return s;
             if (int s = pf_attention_launch(e->pf_q, kc, vc, m, p0, nq, nkv, D, S, e->pf_x, e->err, 1, st)) return s;
             if (int s = pgemm_launch(ly.o, H, qs, e->pf_x, m, e->pf_y, H, e->err, st)) return s;
+            if (tp)
+                if (int s = all_reduce(e, e->pf_y, st, (size_t)m * H)) return s;
             if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, ly.ffn_norm, eps, e->pf_x, st)) return s;
             // gate/up with SwiGLU in its epilogue: bf16 activations, no FP32 gate/up rows
             if (int s = pgemm_swiglu_launch(ly.gu, I, H, e->pf_x, m, e->pf_act, I, e->err, st)) return s;
             if (int s = pgemm_launch(ly.down, H, I, e->pf_act, m, e->pf_y, H, e->err, st)) return s;
+            if (tp)
+                if (int s = all_reduce(e, e->pf_y, st, (size_t)m * H)) return s;
             const float* next_norm = l + 1 < L ? e->layers[l + 1].attn_norm : e->final_norm;
             if (int s = bt_resid_norm_launch(e->pf_y, 1, m, H, e->pf_h, next_norm, eps, e->pf_x, st)) return s;
         }
     }
     // the last token's final-normed row is row m - 1 of the last chunk
-    if (int s = bgemm_launch(e->lm, V, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
-    return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket,
-                            e->sample_inv_t, e->sample_seed, st, e->salts ? e->salts + seq : nullptr);
+    if (!tp) {
+        if (int s = bgemm_launch(e->lm, V, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
+        return bt_argmax_launch(e->pf_y, 1, V, e->pf_tok, e->pf_tok + 1, nullptr, e->cand_v, e->cand_i, e->pf_ticket,
+                                e->sample_inv_t, e->sample_seed, st, e->salts ? e->salts + seq : nullptr);
+    }
+    // this rank's vocabulary rows (zero-padded to vlp), its candidate, then
+    // the winner over the ranks' candidates
+    if (int s = bgemm_launch(e->lm, e->vlp, H, e->pf_x + (size_t)(m - 1) * H, 1, e->pf_y, 1, e->err, st)) return s;
+    if (int s = tp_argmax_local_launch(e->pf_y, 1, e->vlp, e->vl, e->v0, e->cand, e->pf_tok + 1, e->sample_inv_t,
+                                       e->sample_seed, st))
+        return s;
+    const NcclApi* nc = nccl_api();
+    const ncclResult_t r =
+        nc->all_gather(e->cand, e->cand_all, (size_t)2, ncclInt32, static_cast<ncclComm_t>(e->comm), st);
+    if (r != ncclSuccess) return fail(INFERNT_ERR_CUDA, "ncclAllGather: %s", nc->err_str(r));
+    return tp_argmax_pick_launch(e->cand_all, e->world, 1, e->pf_tok, e->pf_tok + 1, st);
 }
 
 // Whether the block table gives sequence t pages for positions [0, last].
@@ -1001,7 +1025,6 @@ int infernt_batch_engine_set_attention(infernt_batch_engine* e, int splits, int 
 int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* tokens, int n_tokens, int start_pos,
                                  int chunk, int* next_token, float* logits_host, float* ms) {
     INFERNT_REQUIRE(e && tokens, "batch_engine_prefill: null argument");
-    if (e->world > 1) return fail(INFERNT_ERR_UNSUPPORTED, "batch_engine_prefill: tensor-parallel engines decode only");
     const infernt_llama_config& c = e->cfg;
     INFERNT_REQUIRE(seq >= 0 && seq < e->T, "batch_engine_prefill: sequence %d outside [0, %d)", seq, e->T);
     INFERNT_REQUIRE(n_tokens >= 1 && start_pos >= 0 && (long long)start_pos + n_tokens <= c.max_seq_len,
@@ -1036,8 +1059,8 @@ int infernt_batch_engine_prefill(infernt_batch_engine* e, int seq, const int* to
     int out[2] = {0, 0};
     INFERNT_CUDA_TRY(cudaMemcpyAsync(out, e->pf_tok, sizeof(out), cudaMemcpyDeviceToHost, e->stream));
     if (logits_host)
-        INFERNT_CUDA_TRY(cudaMemcpyAsync(logits_host, e->pf_y, sizeof(float) * (size_t)c.vocab_size,
-                                         cudaMemcpyDeviceToHost, e->stream));
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(logits_host, e->pf_y, sizeof(float) * (size_t)e->vl, cudaMemcpyDeviceToHost,
+                                         e->stream));
     const int s = check_err(e);
     if (s) return s;
     if (next_token) *next_token = out[0];

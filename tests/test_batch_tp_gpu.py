@@ -139,3 +139,86 @@ def test_batch_tp2_matches_oracle(peer):
 @pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
 def test_batch_tp2_head_dim_128_padded_vocab():
     check_against_oracle(CFG_D128, 2)
+
+
+PF_PROMPT, PF_CHUNK, PF_STEPS = 40, 16, 3
+
+
+def _prefill_rank(rank, world, port, cfg, out):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        obj = [ib.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        prompt = [int(t) for t in O.prompt(PF_PROMPT, SEED + 1, 3, cfg.vocab_size)]
+
+        def run(eng):
+            tok, logits, _ = eng.prefill(0, prompt, 0, chunk=PF_CHUNK, want_logits=True)
+            kv = [eng.read_kv(0, l, PF_PROMPT) for l in range(cfg.num_layers)]
+            tokens, positions, toks = [tok, 11], [PF_PROMPT, 0], []
+            for _ in range(PF_STEPS):
+                tokens = eng.step(tokens, positions)
+                positions = [p + 1 for p in positions]
+                toks.append(tokens)
+            return tok, logits, kv, toks
+
+        eng = ib.BatchEngine(cfg, 2, seed=SEED, rank=rank, world=world, nccl_id=obj[0])
+        res = run(eng) + (eng.vocab_range,)
+        eng.close()
+        dist.barrier()
+        if rank == 0:
+            one = ib.BatchEngine(cfg, 2, seed=SEED)
+            out["one"] = run(one)
+            one.close()
+        out[rank] = res
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif("_gpus() < 2", reason="needs two GPUs")
+@pytest.mark.parametrize("cfg", [CFG, CFG_D128], ids=["d64", "d128-padded-vocab"])
+def test_batch_tp2_prefill_matches_one_gpu(cfg):
+    """Prompt prefill on a two-rank engine (ncclAllReduce of each chunk's O
+    and down rows) against the one-GPU engine with the same seeded weights:
+    both ranks return the same next token, the ranks' logits slices and KV
+    heads put together match the one-GPU prefill (layer 0's K/V rows exactly:
+    no sum over ranks precedes them; later layers within the batched
+    tolerance), and the decode steps that follow agree."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_prefill_rank, args=(r, 2, port, cfg, out)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(600)
+        assert [p.exitcode for p in procs] == [0, 0]
+        res = dict(out)
+    tok1, logits1, kv1, toks1 = res["one"]
+    assert res[0][0] == res[1][0], "ranks disagree on the prefill token"
+    full = np.concatenate([res[0][1], res[1][1]])
+    assert full.shape == logits1.shape
+    err = float(np.abs(full - logits1).max())
+    scale = float(np.abs(logits1).max())
+    assert err <= 1e-2 * scale, (err, scale)
+    if res[0][0] != tok1:
+        assert top2_gap(logits1) < 2 * err, (res[0][0], tok1)
+    nkv_l = cfg.num_key_value_heads // 2
+    for l in range(cfg.num_layers):
+        for which in (0, 1):  # K, V
+            mine = np.concatenate([res[r][2][l][which] for r in range(2)])
+            want = kv1[l][which]
+            if l == 0:
+                np.testing.assert_array_equal(mine, want)
+            else:
+                assert float(np.abs(mine - want).max()) <= 2e-2 * float(np.abs(want).max()), (l, which)
+        assert res[0][2][l][0].shape[0] == nkv_l
+    assert res[0][3] == res[1][3], "ranks disagree on the decode tokens"
+    agree = sum(a == b for s, t in zip(res[0][3], toks1) for a, b in zip(s, t))
+    assert agree >= len(toks1) * 2 - 1, (res[0][3], toks1)
