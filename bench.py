@@ -728,7 +728,7 @@ def run_batched(args, longctx=False, tp=False):
             eng = ib.BatchEngine(cfg, T, seed=seed, std=STD)
     tokens = ib.prompt(n_seq, seed, 3, cfg.vocab_size)[lo:hi]
     prefill = None
-    if longctx and getattr(args, "real_prefill", False) and not tp:
+    if longctx and getattr(args, "real_prefill", False):
         # the prompts run through the engine's prefill (tensor-core chunks) and
         # each sequence decodes from the token its prompt produced
         pf_ms = 0.0
@@ -740,7 +740,9 @@ def run_batched(args, longctx=False, tp=False):
         pf_max = max_over_ranks(torch, pf_ms, "cuda")
         prefill = {"ms": round(pf_max, 1), "prompt_tokens": int(np.sum(ctx)),
                    "tok_s": round(float(np.sum(ctx)) / (pf_max / 1e3), 1),
-                   "api": "infernt_batch_engine_prefill, one sequence after another"}
+                   "api": "infernt_batch_engine_prefill, one sequence after another" +
+                          (" (tensor parallel: every rank its shards, ncclAllReduce of each chunk's O and down "
+                           "rows)" if tp and world > 1 else "")}
     else:
         for b in range(T):
             eng.fill_kv(b, 1000 + lo + b, int(mine[b]))
