@@ -1683,7 +1683,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
     long long n = 0;  // phases started so far
     const long long total = (long long)p.steps * p.nphases;
     const unsigned long long* stw = reinterpret_cast<const unsigned long long*>(p.state);
-    const unsigned long long st0 = ld_acquire64(stw);
+    // the first step's (token, position): launch parameters, or the state
+    // a previous launch or kernel left
+    const unsigned long long st0 =
+        p.init_pos >= 0 ? ((unsigned long long)(unsigned)p.init_token | ((unsigned long long)(unsigned)p.init_pos << 32))
+                        : ld_acquire64(stw);
+    if (p.init_pos >= 0 && blockIdx.x == 0 && tid == 0) {
+        // the state the LM-head phase reads and advances; ordered before its
+        // reads through the argmax ticket every CTA takes
+        p.state[0] = p.init_token;
+        p.state[1] = p.init_pos;
+        p.state[2] = 0;
+    }
     const int pos0 = (int)(unsigned)(st0 >> 32);
     for (int step = 0; step < p.steps; ++step) {
         // this step's token and position: published (release) by the last

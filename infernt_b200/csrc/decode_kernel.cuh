@@ -103,6 +103,9 @@ struct MegaParams {
     // weight-stream slots the producer keeps in flight (issued, not yet
     // landed); ring_slots: no limit beyond the ring
     int stream_depth;
+    // the first step's token and position (init_pos >= 0): taken from here
+    // instead of the state word, which CTA 0 initialises; -1: read the state
+    int init_token, init_pos;
 };
 
 constexpr int kTraceFields = 9;

@@ -73,7 +73,8 @@ struct infernt_plan {
     float* logits = nullptr;
     float2* rope = nullptr;  // (cos, sin) table [max_seq][D/2]
     int* state = nullptr;  // {token, position, step, last token}
-    unsigned* err = nullptr;
+    unsigned* err = nullptr;  // 64 bytes after state
+    int* host_rb = nullptr;   // pinned host copy of state .. err (one readback per step)
     float* attn_part = nullptr;
     unsigned* attn_counter = nullptr;
     LmWs* lm_ws = nullptr;
@@ -268,8 +269,16 @@ int run_graph_step(infernt_plan* p, cudaStream_t st, int mode, const float* inpu
 }
 
 // `steps` decode steps from the current device state.
-int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist, int steps) {
+// Steps of the plan from the device state; (token, position) with
+// position >= 0 set the first step's instead (the persistent kernel takes
+// them as launch parameters, the kernel sequences from set_state_kernel).
+int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, float* logits, int* hist, int steps,
+              int token = 0, int position = -1) {
     if (!logits) logits = p->logits;
+    if (p->mode != INFERNT_MODE_PERSISTENT && position >= 0) {
+        set_state_kernel<<<1, 1, 0, st>>>(p->state, token, position);
+        INFERNT_CUDA_TRY(cudaGetLastError());
+    }
     if (p->mode == INFERNT_MODE_PERSISTENT) {
         INFERNT_REQUIRE(p->tp_size == 1 || p->peers_set,
                         "tensor-parallel plan: infernt_plan_set_peers has not been called");
@@ -278,6 +287,8 @@ int run_steps(infernt_plan* p, cudaStream_t st, int mode, const float* input, fl
         m.logits = logits;
         m.hist = hist;
         m.steps = steps;
+        m.init_token = token;
+        m.init_pos = position;
         // every phase instance has its own tag (the same sequence on every
         // rank); 32-bit tags bound a plan's lifetime
         const unsigned long long used = (unsigned long long)steps * (unsigned long long)m.nphases;
@@ -603,6 +614,10 @@ int plan_create_impl(const infernt_llama_config* cfg, const void* const* weights
     p->state = reinterpret_cast<int*>(b);
     p->err = reinterpret_cast<unsigned*>(b + 64);
     b += b_state;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&p->host_rb), 128, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        p->host_rb = nullptr;  // read_token falls back to pageable copies
+    }
     const size_t part = (size_t)cfg->num_key_value_heads * p->splits *
                         (cfg->num_attention_heads / cfg->num_key_value_heads) * (cfg->head_dim + 2) * 4;
     p->attn_part = reinterpret_cast<float*>(b);
@@ -813,6 +828,7 @@ int infernt_plan_destroy(infernt_plan* p) {
     cudaFree(p->mega_mem);
     cudaFree(p->ll_mem);
     cudaFree(p->scratch);
+    if (p->host_rb) cudaFreeHost(p->host_rb);
     delete p;
     return INFERNT_OK;
 }
@@ -825,9 +841,7 @@ int infernt_plan_forward(infernt_plan* p, const float* input_embedding, int posi
                     position, p->cfg.max_seq_len);
     INFERNT_REQUIRE(aligned16(input_embedding), "plan_forward: input must be 16-byte aligned");
     cudaStream_t st = (cudaStream_t)stream;
-    set_state_kernel<<<1, 1, 0, st>>>(p->state, 0, position);
-    INFERNT_CUDA_TRY(cudaGetLastError());
-    return run_steps(p, st, kInputVector, input_embedding, logits, nullptr, 1);
+    return run_steps(p, st, kInputVector, input_embedding, logits, nullptr, 1, 0, position);
 }
 
 int infernt_plan_decode(infernt_plan* p, int token, int position, float* logits, void* stream) {
@@ -837,9 +851,7 @@ int infernt_plan_decode(infernt_plan* p, int token, int position, float* logits,
     INFERNT_REQUIRE(position >= 0 && position < p->cfg.max_seq_len, "plan_decode: position %d outside [0, %d)",
                     position, p->cfg.max_seq_len);
     cudaStream_t st = (cudaStream_t)stream;
-    set_state_kernel<<<1, 1, 0, st>>>(p->state, token, position);
-    INFERNT_CUDA_TRY(cudaGetLastError());
-    return run_steps(p, st, kInputToken, nullptr, logits, nullptr, 1);
+    return run_steps(p, st, kInputToken, nullptr, logits, nullptr, 1, token, position);
 }
 
 int infernt_plan_decode_chain(infernt_plan* p, int token, int position, int steps, int* tokens_dev, void* stream) {
@@ -850,9 +862,7 @@ int infernt_plan_decode_chain(infernt_plan* p, int token, int position, int step
                     p->cfg.max_seq_len);
     if (steps == 0) return INFERNT_OK;
     cudaStream_t st = (cudaStream_t)stream;
-    set_state_kernel<<<1, 1, 0, st>>>(p->state, token, position);
-    INFERNT_CUDA_TRY(cudaGetLastError());
-    return run_steps(p, st, kInputToken, nullptr, nullptr, tokens_dev, steps);
+    return run_steps(p, st, kInputToken, nullptr, nullptr, tokens_dev, steps, token, position);
 }
 
 int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
@@ -860,9 +870,18 @@ int infernt_plan_read_token(infernt_plan* p, int* token_host, void* stream) {
     cudaStream_t st = (cudaStream_t)stream;
     int buf[4];
     unsigned err = 0;
-    INFERNT_CUDA_TRY(cudaMemcpyAsync(buf, p->state, sizeof(buf), cudaMemcpyDeviceToHost, st));
-    INFERNT_CUDA_TRY(cudaMemcpyAsync(&err, p->err, sizeof(err), cudaMemcpyDeviceToHost, st));
-    INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
+    if (p->host_rb) {
+        // state and error word in one copy into pinned memory (the error
+        // word sits 64 bytes after the state)
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(p->host_rb, p->state, 68, cudaMemcpyDeviceToHost, st));
+        INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
+        memcpy(buf, p->host_rb, sizeof(buf));
+        memcpy(&err, reinterpret_cast<const char*>(p->host_rb) + 64, sizeof(err));
+    } else {
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(buf, p->state, sizeof(buf), cudaMemcpyDeviceToHost, st));
+        INFERNT_CUDA_TRY(cudaMemcpyAsync(&err, p->err, sizeof(err), cudaMemcpyDeviceToHost, st));
+        INFERNT_CUDA_TRY(cudaStreamSynchronize(st));
+    }
     if (err) {
         cudaMemsetAsync(p->err, 0, sizeof(unsigned), st);
         cudaStreamSynchronize(st);
