@@ -874,31 +874,32 @@ __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int
     int q0 = 0;  // column block of the slot's first piece
     int s = 0;   // stream row of the slot's first piece
     float run = 0.0f;
+#pragma unroll 1
     for (int p0 = 0; p0 < npieces; p0 += PT) {
         const int n = min(PT, npieces - p0);
         const int split = cb - q0;  // pieces of row s in this slot (>= 1)
-        float pv[PT];
+        float nxt = 0.0f;
         if ((rd.rp->s & 1) == team) {
             const unsigned char* wp = rd.take(ctid, EB);
+            // inputs of piece i: column block q0 + i of row s (i < split),
+            // else block i - split of row s + 1; each an immediate offset
+            // from one of two bases
+            const float* xa = xt + q0 * kPiece;
+            const float* xb = xt - split * kPiece;
 #pragma unroll
             for (int i = 0; i < PT; ++i) {
-                const int q = q0 + i >= cb ? q0 + i - cb : q0 + i;
-                pv[i] = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xt + q * kPiece));
+                const float* xp = i < split ? xa + i * kPiece : xb + i * kPiece;
+                const float d = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xp));
+                const float v = i < n ? d : 0.0f;
+                if (i < split)
+                    run += v;
+                else
+                    nxt += v;
             }
             rd.release(lane);
         } else {
-#pragma unroll
-            for (int i = 0; i < PT; ++i) pv[i] = 0.0f;
+            // the other team's slot: nothing to add, only the row bookkeeping
             rd.skip(1);
-        }
-        float nxt = 0.0f;
-#pragma unroll
-        for (int i = 0; i < PT; ++i) {
-            const float v = i < n ? pv[i] : 0.0f;
-            if (i < split)
-                run += v;
-            else
-                nxt += v;
         }
         if (split <= n) {  // row s ends in this slot
             acc_set<R>(acc, stream_row_acc<NS, BU>(s, nb), run);
