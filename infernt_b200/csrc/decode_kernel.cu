@@ -883,18 +883,19 @@ __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int
             const unsigned char* wp = rd.take(ctid, EB);
             // inputs of piece i: column block q0 + i of row s (i < split),
             // else block i - split of row s + 1; each an immediate offset
-            // from one of two bases
+            // from one of two bases.  Pieces past n (the batch's last slot,
+            // where row s is the batch's last row and split == n) are stale
+            // and land in nxt, which is not used after that slot.
             const float* xa = xt + q0 * kPiece;
             const float* xb = xt - split * kPiece;
 #pragma unroll
             for (int i = 0; i < PT; ++i) {
                 const float* xp = i < split ? xa + i * kPiece : xb + i * kPiece;
                 const float d = piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xp));
-                const float v = i < n ? d : 0.0f;
                 if (i < split)
-                    run += v;
+                    run += d;
                 else
-                    nxt += v;
+                    nxt += d;
             }
             rd.release(lane);
         } else {
