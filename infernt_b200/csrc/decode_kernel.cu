@@ -42,6 +42,7 @@
 // sets kErrWaitTimeout in the error word, marks itself aborted and runs the
 // remaining control flow without waiting, so the kernel always terminates
 // and the host reports INFERNT_ERR_DEVICE.
+#include <array>
 #include <cstring>
 
 #include "decode_kernel.cuh"
@@ -573,13 +574,13 @@ __device__ __forceinline__ float gpart_sum(const MegaShared& sh, int sl, int a) 
 // candidate.  All consumer threads take part; called between named
 // barriers.  Units of a Q|K|V phase are rows of the stacked [q | k | v]
 // output, so the stacked row is the output index.
-template <typename WT, int NS, bool TWO>
+template <typename WT, int NS, bool TWO, bool FOLD>
 __device__ void combine_batches(const MegaParams& p, const MegaPhase& P, MegaShared& sh, int ub, int n, int u1,
                                 int tid, float& am_v, int& am_i, unsigned ts, unsigned tag) {
     constexpr int BU = MegaRows<WT>::R / NS;
     // folded RMSNorm (norm_folded): the factor from team 0's sums of squares
     float r = 1.0f;
-    if (!TWO && P.norm_w)
+    if (FOLD && P.norm_w)
         r = rsqrtf((((sh.ss[0] + sh.ss[1]) + sh.ss[2]) + sh.ss[3]) / (float)P.K + P.eps);
     for (int idx = tid; idx < n * BU; idx += kMegaConsumers) {
         const int sl = idx / BU, i = idx % BU;
@@ -913,6 +914,67 @@ __device__ __forceinline__ void batch_split(SlotReader& rd, const float* xt, int
     }
 }
 
+// A batch when the slot holds pieces of up to MB + 1 rows (MB row ends:
+// MB x K / 512 >= the pieces of a slot, K / 512 smaller than them): the
+// shape of batch_split with MB + 1 running sums.  Piece i belongs to row
+// s + k, k the row ends before it (b0 = K / 512 - q0, b0 + K / 512, ...), and
+// reads column block q0 + i - k K / 512; the sums are kept in stream order
+// and each finished row's goes to its accumulator.  Stale pieces of a
+// batch's last slot (past its last row end) land in a later sum, which is
+// not used.
+template <typename WT, int NS, int MB>
+__device__ __forceinline__ void batch_rows(SlotReader& rd, const float* xt, int cb, int rows, int nb, float* acc,
+                                           int ctid, int lane, int team) {
+    constexpr int R = MegaRows<WT>::R, BU = R / NS;
+    constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB, EB = MegaRows<WT>::EB;
+    const int npieces = rows * cb;
+    int q0 = 0;  // column block of the slot's first piece
+    int s = 0;   // stream row of the slot's first piece
+    float run = 0.0f;
+#pragma unroll 1
+    for (int p0 = 0; p0 < npieces; p0 += PT) {
+        const int n = min(PT, npieces - p0);
+        const int b0 = cb - q0;  // pieces of row s in this slot (>= 1)
+        float sum[MB + 1];
+        sum[0] = run;
+#pragma unroll
+        for (int e = 1; e <= MB; ++e) sum[e] = 0.0f;
+        if ((rd.rp->s & 1) == team) {
+            const unsigned char* wp = rd.take(ctid, EB);
+            const float* xq = xt + q0 * kPiece;
+#pragma unroll
+            for (int i = 0; i < PT; ++i) {
+                int k = 0;
+#pragma unroll
+                for (int e = 0; e < MB; ++e) k += i >= b0 + e * cb ? 1 : 0;
+                const float d =
+                    piece_dot<WT>(wp + i * PB, *reinterpret_cast<const float4*>(xq + (i - k * cb) * kPiece));
+#pragma unroll
+                for (int e = 0; e <= MB; ++e)
+                    if (k == e) sum[e] += d;
+            }
+            rd.release(lane);
+        } else {
+            // the other team's slot: nothing to add, only the row bookkeeping
+            rd.skip(1);
+        }
+        int ends = 0;  // rows that end in this slot
+#pragma unroll
+        for (int e = 0; e < MB; ++e)
+            if (b0 + e * cb <= n) ends = e + 1;
+#pragma unroll
+        for (int e = 0; e < MB; ++e)
+            if (e < ends) acc_set<R>(acc, stream_row_acc<NS, BU>(s + e, nb), sum[e]);
+        float nr = sum[0];
+#pragma unroll
+        for (int e = 1; e <= MB; ++e)
+            if (e == ends) nr = sum[e];
+        run = nr;
+        q0 = ends ? n - (b0 + (ends - 1) * cb) : q0 + n;
+        s += ends;
+    }
+}
+
 // Any batch, any cb: the pieces of each slot as independent products, added
 // to a running row sum in stream order; a finished row moves to its
 // accumulator.  Pieces past the batch's end (a short last batch) are not
@@ -961,7 +1023,7 @@ __device__ void batch_generic(SlotReader& rd, const float* xt, int cb, int nb, f
     }
 }
 
-template <typename WT, int NS, int CB>
+template <typename WT, int NS, int CB, bool NARROW>
 __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& rd, const float* xs, MegaShared& sh,
                           int tid, int u0, int u1, unsigned ts, unsigned tag) {
     constexpr int R = MegaRows<WT>::R, PT = MegaRows<WT>::PT;
@@ -976,7 +1038,7 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
     if (CB > 0) {
 #pragma unroll
         for (int c = 0; c < NXR; ++c) xr[c] = *reinterpret_cast<const float4*>(xt + c * kPiece);
-        if (P.norm_w) {
+        if ((CB == 4 || CB == 8) && P.norm_w) {
             // folded RMSNorm: a team covers every column once; team 0's warps
             // publish their sums of squares for the epilogue's factor
             const float* wn = xs + P.K + ctid * 4;
@@ -1019,6 +1081,10 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
             for (int a = 0; a < R; ++a) acc[a] = 0.0f;
             if (split)
                 batch_split<WT, NS>(rd, xt, P.cb, rows, nb, acc, ctid, lane, team);
+            else if (NARROW && 2 * P.cb >= PT)
+                batch_rows<WT, NS, 2>(rd, xt, P.cb, rows, nb, acc, ctid, lane, team);
+            else if (NARROW && 3 * P.cb >= PT)
+                batch_rows<WT, NS, 3>(rd, xt, P.cb, rows, nb, acc, ctid, lane, team);
             else
                 batch_generic<WT, NS>(rd, xt, P.cb, nb, acc, ctid, lane, team);
             // the warp's sum of each row; lane L holds row L / (32 / R)
@@ -1030,15 +1096,16 @@ __device__ void gemv_body(const MegaParams& p, const MegaPhase& P, SlotReader& r
         // their epilogue before the row-sum slots are reused
         if (++bi % kGroupBatch == 0) {
             named_sync(1, kMegaConsumers);
-            combine_batches<WT, NS, CB == 0>(p, P, sh, u0 + (bi - kGroupBatch) * BU, kGroupBatch, u1, tid, am_v,
-                                             am_i, ts, tag);
+            combine_batches<WT, NS, CB == 0, CB == 4 || CB == 8>(p, P, sh, u0 + (bi - kGroupBatch) * BU,
+                                                                 kGroupBatch, u1, tid, am_v, am_i, ts, tag);
             named_sync(1, kMegaConsumers);
         }
     }
     const int rest = bi % kGroupBatch;
     if (rest) {
         named_sync(1, kMegaConsumers);
-        combine_batches<WT, NS, CB == 0>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v, am_i, ts, tag);
+        combine_batches<WT, NS, CB == 0, CB == 4 || CB == 8>(p, P, sh, u0 + (bi - rest) * BU, rest, u1, tid, am_v,
+                                                             am_i, ts, tag);
     }
     if (P.epi == kEpiArgmax) argmax_phase_end(p, sh, tid, am_v, am_i, tag);
 }
@@ -1067,7 +1134,7 @@ __device__ void attention_prefetch(const MegaParams& p, const MegaPhase& P, int 
     if (any && a.rope) bulk_prefetch_l2(a.rope + (size_t)pos * (a.D / 2), row_bytes);
 }
 
-template <typename WT, int NS>
+template <typename WT, int NS, bool NARROW>
 __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned char* ring, uint64_t* full,
                            uint64_t* empty, RingPos& rp, uint32_t& xphase, float* xs, MegaShared& sh, int tid,
                            long long tb, int tok, int pos, unsigned ts, unsigned tag) {
@@ -1079,10 +1146,20 @@ __device__ void gemv_phase(const MegaParams& p, const MegaPhase& P, unsigned cha
     SlotReader rd{ring, full, empty, &rp, p.ring_slots, &sh.abort, p.err, tb >= 0, 0};
     // widths that divide a slot's pieces keep their input columns in
     // registers (every thread takes the same branch: P is shared)
-    switch (P.cb) {
-        case 4: gemv_body<WT, NS, 4>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
-        case 8: gemv_body<WT, NS, 8>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
-        default: gemv_body<WT, NS, 0>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+    if constexpr (NARROW) {
+        switch (P.cb) {
+            case 1: gemv_body<WT, NS, 1, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            case 2: gemv_body<WT, NS, 2, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            case 4: gemv_body<WT, NS, 4, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            case 8: gemv_body<WT, NS, 8, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            default: gemv_body<WT, NS, 0, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+        }
+    } else {
+        switch (P.cb) {
+            case 4: gemv_body<WT, NS, 4, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            case 8: gemv_body<WT, NS, 8, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+            default: gemv_body<WT, NS, 0, NARROW>(p, P, rd, xs, sh, tid, u0, u1, ts, tag); break;
+        }
     }
     if (tb >= 0) p.trace[tb + 5] = (unsigned long long)rd.waited;
 }
@@ -1646,7 +1723,13 @@ __device__ void produce(const MegaParams& p, unsigned char* ring, uint64_t* full
     }
 }
 
-template <typename WT>
+// NARROW: the instantiation for plans with rows narrower than a slot other
+// than the widths 2048 and 4096 (tensor-parallel shards, small models): it
+// adds register-resident inputs for rows of 512 and 1024 columns and the
+// slots holding several row ends (batch_rows).  The plain instantiation
+// goes without them, so their code and registers do not weigh on the other
+// plans' loops.
+template <typename WT, bool NARROW>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const MegaParams p) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ MegaShared sh;
@@ -1745,9 +1828,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
             if (P.kind == kPhAttn) {
                 attention_phase(p, P, xs, sh, tid, tb, xphase, pos, ts, tag);
             } else if (P.ns == 2) {
-                gemv_phase<WT, 2>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
+                gemv_phase<WT, 2, NARROW>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
             } else {
-                gemv_phase<WT, 1>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
+                gemv_phase<WT, 1, NARROW>(p, P, ring, full, empty, rp, xphase, xs, sh, tid, tb, tok, pos, ts, tag);
             }
             trace_mark(p, tb, 2);
             trace_mark(p, tb, 3);
@@ -1765,6 +1848,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega_kernel(const Mega
 
 }  // namespace
 
+// Both instantiations of a weight type (the plan's limits hold for either).
+std::array<const void*, 2> mega_kernels(int weight_dtype) {
+    if (weight_dtype == INFERNT_DTYPE_BF16)
+        return {reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16, false>),
+                reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16, true>)};
+    return {reinterpret_cast<const void*>(decode_mega_kernel<float, false>),
+            reinterpret_cast<const void*>(decode_mega_kernel<float, true>)};
+}
+
 int mega_smem_bytes(int ring_slots, int x_floats) {
     return ring_slots * kMegaSlot + x_floats * 4 + 2 * ring_slots * 8;
 }
@@ -1772,23 +1864,26 @@ int mega_smem_bytes(int ring_slots, int x_floats) {
 int mega_max_ring_slots() { return kMaxRingSlots; }
 
 int mega_static_smem(int weight_dtype) {
-    cudaFuncAttributes fa;
-    const void* k = weight_dtype == INFERNT_DTYPE_BF16
-                        ? reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(decode_mega_kernel<float>);
-    if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) {
-        cudaGetLastError();
-        return 48 * 1024;
+    int most = 0;
+    for (const void* k : mega_kernels(weight_dtype)) {
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, k) != cudaSuccess) {
+            cudaGetLastError();
+            return 48 * 1024;
+        }
+        if ((int)fa.sharedSizeBytes > most) most = (int)fa.sharedSizeBytes;
     }
-    return (int)fa.sharedSizeBytes;
+    return most;
 }
 
 cudaError_t mega_prepare() {
     // the register split assumes the launch holds kLaunchRegs per thread: a
     // build that allocated fewer could not satisfy setmaxnreg.inc, so it is
     // refused here rather than launched
-    for (const void* k : {reinterpret_cast<const void*>(decode_mega_kernel<float>),
-                          reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16>)}) {
+    for (const void* k : {reinterpret_cast<const void*>(decode_mega_kernel<float, false>),
+                          reinterpret_cast<const void*>(decode_mega_kernel<float, true>),
+                          reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16, false>),
+                          reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16, true>)}) {
         cudaFuncAttributes fa;
         cudaError_t e = cudaFuncGetAttributes(&fa, k);
         if (e != cudaSuccess) return e;
@@ -1801,15 +1896,16 @@ cudaError_t mega_prepare() {
 }
 
 int mega_occupancy(int weight_dtype, int smem_bytes) {
-    int n = 0;
-    const void* k = weight_dtype == INFERNT_DTYPE_BF16
-                        ? reinterpret_cast<const void*>(decode_mega_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(decode_mega_kernel<float>);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kMegaThreads, smem_bytes) != cudaSuccess) {
-        cudaGetLastError();
-        return 0;
+    int least = 1 << 30;
+    for (const void* k : mega_kernels(weight_dtype)) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kMegaThreads, smem_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        if (n < least) least = n;
     }
-    return n;
+    return least;
 }
 
 cudaError_t launch_mega(const MegaParams& p, int weight_dtype, int ctas, cudaStream_t stream) {
@@ -1823,8 +1919,11 @@ cudaError_t launch_mega(const MegaParams& p, int weight_dtype, int ctas, cudaStr
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (weight_dtype == INFERNT_DTYPE_BF16) return cudaLaunchKernelEx(&cfg, decode_mega_kernel<__nv_bfloat16>, p);
-    return cudaLaunchKernelEx(&cfg, decode_mega_kernel<float>, p);
+    if (weight_dtype == INFERNT_DTYPE_BF16)
+        return p.narrow ? cudaLaunchKernelEx(&cfg, decode_mega_kernel<__nv_bfloat16, true>, p)
+                        : cudaLaunchKernelEx(&cfg, decode_mega_kernel<__nv_bfloat16, false>, p);
+    return p.narrow ? cudaLaunchKernelEx(&cfg, decode_mega_kernel<float, true>, p)
+                    : cudaLaunchKernelEx(&cfg, decode_mega_kernel<float, false>, p);
 }
 
 }  // namespace infernt

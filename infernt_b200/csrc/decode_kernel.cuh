@@ -106,6 +106,9 @@ struct MegaParams {
     // the first step's token and position (init_pos >= 0): taken from here
     // instead of the state word, which CTA 0 initialises; -1: read the state
     int init_token, init_pos;
+    // 1: some GEMV phase has rows narrower than a slot other than 2048 and
+    // 4096 columns: launch the instantiation with the narrow-row paths
+    int narrow;
 };
 
 constexpr int kTraceFields = 9;

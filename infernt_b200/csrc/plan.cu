@@ -536,6 +536,12 @@ int build_mega(infernt_plan* p) {
     // only lengthens the phase boundaries' reads (TinyLlama FP32 1.009 ->
     // 0.993 ms per step, 8B bf16 3.227 -> 3.187; 6 to 10 slots all equal)
     m.stream_depth = slots < 8 ? slots : 8;
+    // rows narrower than a slot other than 2048 / 4096 columns: the kernel
+    // instantiation with the narrow-row paths
+    const int pt = dt == INFERNT_DTYPE_BF16 ? 16 : 8;
+    m.narrow = 0;
+    for (const MegaPhase& P : ph)
+        if (P.kind == kPhGemv && P.cb < pt && P.cb != 4 && P.cb != 8) m.narrow = 1;
     p->mega_ctas = ctas;
     return INFERNT_OK;
 }
