@@ -376,26 +376,44 @@ __device__ __forceinline__ void trace_mark(const MegaParams& p, long long base, 
 
 // -------------------------------------------------------------- consumers
 
-// The dot product of 4 weights at wp with 4 inputs, in element order.
+// (a.x, a.y) = (fma(w0, x0, a.x), fma(w1, x1, a.y)): one packed FP32 FMA
+// (two lanes, each rounded as fmaf).  The consumers are bound by issue
+// latency, so halving their FMA instructions shortens every slot.
+__device__ __forceinline__ void fma2(float2& a, float w0, float w1, float x0, float x1) {
+    asm("{\n\t.reg .b64 pw, px, pa;\n\t"
+        "mov.b64 pw, {%2, %3};\n\t"
+        "mov.b64 px, {%4, %5};\n\t"
+        "mov.b64 pa, {%0, %1};\n\t"
+        "fma.rn.f32x2 pa, pw, px, pa;\n\t"
+        "mov.b64 {%0, %1}, pa;\n\t}"
+        : "+f"(a.x), "+f"(a.y)
+        : "f"(w0), "f"(w1), "f"(x0), "f"(x1));
+}
+
+// The 4 weights at wp (FP32, or bf16 widened: a bf16 value is the top half
+// of the FP32 with the same bits, so widening is a shift for the low
+// element and a mask for the high one), multiplied into the two lanes of a:
+// lane 0 takes elements 0 and 2, lane 1 elements 1 and 3.
 template <typename WT>
-__device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4& xv) {
-    float acc = 0.0f;
+__device__ __forceinline__ void piece_fma2(float2& a, const unsigned char* wp, const float4& xv) {
     if (WeightTraits<WT>::kBytes == 4) {
         const float4 w = *reinterpret_cast<const float4*>(wp);
-        acc = fmaf(w.x, xv.x, acc);
-        acc = fmaf(w.y, xv.y, acc);
-        acc = fmaf(w.z, xv.z, acc);
-        acc = fmaf(w.w, xv.w, acc);
+        fma2(a, w.x, w.y, xv.x, xv.y);
+        fma2(a, w.z, w.w, xv.z, xv.w);
     } else {
-        // a bf16 value is the top half of the FP32 with the same bits, so
-        // widening is a shift (low element) or a mask (high element)
         const uint2 raw = *reinterpret_cast<const uint2*>(wp);
-        acc = fmaf(__uint_as_float(raw.x << 16), xv.x, acc);
-        acc = fmaf(__uint_as_float(raw.x & 0xffff0000u), xv.y, acc);
-        acc = fmaf(__uint_as_float(raw.y << 16), xv.z, acc);
-        acc = fmaf(__uint_as_float(raw.y & 0xffff0000u), xv.w, acc);
+        fma2(a, __uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u), xv.x, xv.y);
+        fma2(a, __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u), xv.z, xv.w);
     }
-    return acc;
+}
+
+// The dot product of 4 weights at wp with 4 inputs: (w0 x0 + w2 x2) +
+// (w1 x1 + w3 x3), each lane of the packed FMA rounded as fmaf.
+template <typename WT>
+__device__ __forceinline__ float piece_dot(const unsigned char* wp, const float4& xv) {
+    float2 a = make_float2(0.0f, 0.0f);
+    piece_fma2<WT>(a, wp, xv);
+    return a.x + a.y;
 }
 
 // RMSNorm folded into the GEMV: for the widths whose input columns stay in
@@ -804,16 +822,14 @@ template <typename WT, int CB>
 __device__ __forceinline__ void slot_row_sums(const unsigned char* wp, const float4* xr, float* v) {
     constexpr int PT = MegaRows<WT>::PT, PB = MegaRows<WT>::PB;
     constexpr int RS = PT / CB;
-    float pv[PT];
+    // packed FMAs: per row two accumulators (even / odd pieces), two lanes each
+    float2 a[RS][2];
 #pragma unroll
-    for (int i = 0; i < PT; ++i) pv[i] = piece_dot<WT>(wp + i * PB, xr[i % CB]);
+    for (int k = 0; k < RS; ++k) a[k][0] = a[k][1] = make_float2(0.0f, 0.0f);
 #pragma unroll
-    for (int k = 0; k < RS; ++k) {
-        float t = 0.0f;
+    for (int i = 0; i < PT; ++i) piece_fma2<WT>(a[i / CB][(i % CB) & 1], wp + i * PB, xr[i % CB]);
 #pragma unroll
-        for (int c = 0; c < CB; ++c) t += pv[k * CB + c];
-        v[k] = t;
-    }
+    for (int k = 0; k < RS; ++k) v[k] = (a[k][0].x + a[k][0].y) + (a[k][1].x + a[k][1].y);
 }
 
 template <typename WT, int NS, int CB>
