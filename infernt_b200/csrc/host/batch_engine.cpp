@@ -724,14 +724,6 @@ int set_inputs(infernt_batch_engine* e, const int* tokens, const int* positions,
     return INFERNT_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-}  // extern "C"
-
-namespace {
-
 // An engine of `batch` sequences: contiguous caches (page_size 0) or pools
 // of num_pages pages of page_size positions.
 int create_engine(const infernt_llama_config* cfg, int batch, uint64_t seed, float std_dev, int attn_splits, int rank,
