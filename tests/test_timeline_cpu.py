@@ -49,3 +49,14 @@ def test_summary_of_known_marks():
     assert abs(s["step_us"] - (2 * (4 * 3.5 + 3.0) + 3.5)) < 1e-9
     text = T.format_summary(s, 2)
     assert "layer critical path 17.00 us x 2 layers" in text
+
+
+def test_cli_summarises_a_saved_trace(tmp_path, capsys):
+    # a TinyLlama-shaped trace (22 layers, 111 phases) through the --load path
+    tr = make_trace(num_layers=22, steps=2, ctas=3)
+    path = tmp_path / "trace.npy"
+    np.save(path, tr)
+    assert T.main(["--load", str(path), "--shape", "tinyllama"]) == 0
+    out = capsys.readouterr().out
+    assert "| qkv | 3.40 | 1.00 |" in out  # 1.2 + 2.2 us: the third CTA is the last
+    assert "x 22 layers" in out
